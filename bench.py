@@ -1,0 +1,370 @@
+"""Batch-1 Qwen3 decode benchmark (tokens/s and HBM roofline) on 1..8 B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+
+One bench step = one full greedy decode window of the workload: the cursor
+is set back to the end of the prompt (prefilled once) and the engine decodes
+to the context limit, (capacity - prompt) tokens, as Generator::generate's
+loop does (src/lib/inference/generator.cpp:47-56, EOS ignored).  Weights are
+synthetic N(0, 0.02) BF16 from seed 0, prompt ids uniform from seed 1.  With
+N > 1 the model is tensor-parallel over N GPUs (strong scaling: the same
+model and window, the work split by heads / MLP columns / vocabulary).
+
+Rank 0 prints one JSON line.  `--impl reference` times the reference's own
+CPU implementation (its AVX-512 backend compiled from its sources,
+oracle/_ref/libref_cpu.so) on bounded samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 decode tok/s and HBM GB/s vs roofline, 1/2/4/8 B200"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--workload", default="qwen3-8b-ctx4096")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
+    ap.add_argument("--window", type=int, default=0, help="profiling only: decode this many tokens per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--cpu-sample-tokens", type=int, default=3)
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_ids):
+        self.gpu_ids = gpu_ids
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={','.join(str(g) for g in self.gpu_ids)}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"], stdout=open(self.path, "w"),
+                stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except Exception:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except Exception:
+                pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() == "active":
+                    reasons.add(name)
+        load = [s for s in sm if s >= 0.5 * max(sm)] if sm else []
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+class CpuSampler:
+    """The reference's own CPU backend (oracle/_ref/libref_cpu.so) -- or, where
+    it was not built, the oracle's C port -- holding one model of the workload
+    with its KV cache prefilled to context `pos` by synthetic values, timing
+    Model::forward calls there."""
+
+    def __init__(self, cfg, pos, max_tokens, threads):
+        os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+        from oracle import ModelConfig
+
+        mc = ModelConfig.make(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, 128, cfg.vocab,
+                              pos + max_tokens + 1, tied=cfg.tied)
+        try:
+            from oracle import RefLib
+
+            impl, self.kind = RefLib("cpu"), "reference"
+        except (FileNotFoundError, OSError):
+            from oracle import Oracle
+
+            impl, self.kind = Oracle(), "port"
+        self.pos = pos
+        self.m = impl.model(mc, seed=0)
+        if self.kind == "reference":
+            self.m.fill_kv(pos, seed=7)
+
+    def sample(self, n_tokens):
+        self.m.token_count = self.pos
+        tok = 1000
+        t0 = time.perf_counter()
+        for _ in range(n_tokens):
+            tok = self.m.forward(tok)
+        return n_tokens / (time.perf_counter() - t0)
+
+    def close(self):
+        self.m.close()
+
+
+def run_reference(a, cfg, prompt_len, capacity, workload):
+    """--impl reference: the reference's CPU implementation, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    mid = prompt_len + (capacity - prompt_len) // 2
+    n_tok = max(1, a.cpu_sample_tokens)
+    cs = CpuSampler(cfg, mid, n_tok, threads)
+    kind = cs.kind
+    vals = [cs.sample(n_tok) for _ in range(a.warmup + a.steps)][a.warmup:]
+    cs.close()
+    value = statistics.mean(vals)
+    sample = (f"{n_tok} decode steps (Model::forward) of {cfg.name} at context {mid} (mid-window of "
+              f"{prompt_len}->{capacity}), KV cache prefilled with synthetic values, per bench step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": a.gpus,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(n_tok / value * 1000, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
+                   "global_batch": 1, "parallelism": "cpu", "l2_flush": "weights (GBs) exceed every cache"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- GPU leg
+def main():
+    a = parse_args()
+    from inference_b200.config import WORKLOADS
+
+    if a.workload not in WORKLOADS:
+        raise SystemExit(f"unknown workload {a.workload}; choose from {sorted(WORKLOADS)}")
+    cfg, prompt_len, capacity = WORKLOADS[a.workload]
+    workload = a.workload
+    if a.layers:
+        cfg = cfg.with_layers(a.layers)
+        workload += f"-L{a.layers}(profiling)"
+    if a.impl == "reference":
+        return run_reference(a, cfg, prompt_len, capacity, workload)
+    if a.warmup < 3:
+        print("note: fewer than 3 warm-up steps", file=sys.stderr)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != a.gpus:
+        raise SystemExit(f"--gpus {a.gpus} but WORLD_SIZE {world}")
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    import inference_b200 as ib
+
+    eng = ib.Engine(cfg, capacity=capacity, device=local, tp_rank=rank, tp_size=world)
+    eng.init_synthetic(0)
+    if world > 1:
+        obj = [ib.Engine.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        eng.attach_nccl(obj[0])
+
+    window = capacity - prompt_len if not a.window else min(a.window, capacity - prompt_len)
+    prompt = ib.prompt_ids(prompt_len, seed=1, vocab=cfg.vocab)
+    eng.set_tokens(prompt)
+    eng.step(prompt_len - 1)  # prefill: every prompt id but the last (qwen3.hpp:168-173)
+    eng.sync()
+    start_pos = prompt_len - 1
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+
+    def one_window():
+        eng.set_position(start_pos)
+        eng.step(window)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(a.warmup):
+        one_window()
+    eng.sync()
+    barrier()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gpu_ids = list(range(world)) if world > 1 else [local]
+    with ClockSampler(gpu_ids) as clocks:
+        ev0.record(stream)
+        for _ in range(a.steps):
+            one_window()
+        ev1.record(stream)
+        eng.sync()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clock = clocks.summary()
+    tokens = a.steps * window
+    tok_s = tokens / (ms / 1000.0)
+
+    # ---- end-to-end through the public API (host buffers, H2D + D2H inside)
+    e2e = None
+    if not a.no_e2e:
+        pin_prompt = torch.from_numpy(prompt.astype(np.int32)).pin_memory()
+        pin_out = torch.empty(window, dtype=torch.int32).pin_memory()
+        import ctypes as C
+
+        n_out = C.c_size_t()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            ib._lib.check(ib.lib().q3_engine_generate(eng.h, pin_prompt.data_ptr(), prompt_len, window, 0,
+                                                      pin_out.data_ptr(), C.byref(n_out)))
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        if dist:
+            t = torch.tensor([dt], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            dt = float(t.item())
+        e2e = {"value": round(a.steps * window / dt, 3), "unit": "tok/s", "h2d_bytes_per_step": int(prompt_len * 4 + 4),
+               "d2h_bytes_per_step": int(window * 4),
+               "includes": "prompt H2D, prefill of the prompt, decode, token D2H"}
+
+    # ---- dominant kernel (GEMV) roofline: one eager step, CUDA events around each launch
+    mid = start_pos + window // 2
+    eng.set_position(mid)
+    g_ms, g_launch, g_bytes = eng.profile_step(0)
+    eng.set_position(mid)
+    at_ms, at_launch, at_bytes = eng.profile_step(1)
+    peak, peak_kind = measured_peaks()
+    achieved = g_bytes / (g_ms / 1000.0) / 1e9
+    traffic = None
+    tr_path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tr_path):
+        try:
+            tr = json.load(open(tr_path)).get(cfg.name)
+            if tr:  # measured DRAM bytes / algorithmic bytes of the same launches, applied per launch here
+                traffic = round(tr["ratio"] * g_bytes / g_launch)
+        except Exception:
+            traffic = None
+    roofline = {"kernel": "gemv_kernel (every GEMV launch of one decode step; per-launch averages)",
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": traffic, "algorithmic_bytes_per_launch": round(g_bytes / g_launch),
+                "launch_ms_avg": round(g_ms / g_launch, 5), "launches_per_step": g_launch,
+                "attention": {"achieved_gbs": round(at_bytes / (at_ms / 1000.0) / 1e9, 1),
+                              "launch_ms_avg": round(at_ms / max(1, at_launch), 5)}}
+    # whole-step roofline: weights + average KV read per token over the window, all ranks
+    avg_pos = start_pos + (window - 1) / 2.0
+    bytes_tok = cfg.weight_bytes() + cfg.kv_bytes_per_position() * (avg_pos + 1)
+    step_roof = {"bytes_per_token": int(bytes_tok), "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1),
+                 "peak_gbs": peak * world, "frac": round(bytes_tok * tok_s / 1e9 / (peak * world), 4)}
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        try:
+            cs = CpuSampler(cfg, mid, a.cpu_sample_tokens, threads)
+            cs.sample(1)
+            v, kind = cs.sample(a.cpu_sample_tokens), cs.kind
+            cs.close()
+            cpu = {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": kind,
+                   "sample": f"{a.cpu_sample_tokens} decode steps of {cfg.name} at context {mid}, KV prefilled "
+                             f"with synthetic values"}
+        except Exception as exc:  # report, never fail the GPU number
+            cpu = {"value": None, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": f"failed: {exc}"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
+                       "decode_tokens_per_step": window, "global_batch": 1,
+                       "parallelism": f"tp{world}", "weights": "random N(0,0.02) seed 0, ids seed 1",
+                       "l2_flush": f"not needed: {cfg.weight_bytes() / 1e9:.1f} GB of weights streamed per token "
+                                   f">> 126 MB L2"},
+            "clocks": clock, "e2e": e2e, "gpu_launches": int((cfg.layers * 5 + 1) * window * a.steps),
+            "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

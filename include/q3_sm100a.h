@@ -1,0 +1,221 @@
+/*
+ * q3_sm100a.h -- C ABI of the B200 (sm_100a) Qwen3 batch-1 decode library
+ * (libq3_sm100a.so).
+ *
+ * Plain pointers and sizes only.  BF16 tensors are passed as `uint16_t*`
+ * holding bfloat16 bit patterns; every pointer named *_dev is device memory.
+ * Every call returns a q3_status; q3_last_error() describes the last failure
+ * on the calling thread.  Streams are `cudaStream_t` passed as `void*`
+ * (NULL = the legacy default stream).
+ *
+ * Each entry point names the reference interface it replaces
+ * (pind0s/inference, paths relative to that project).
+ */
+#ifndef Q3_SM100A_H
+#define Q3_SM100A_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define Q3_API __attribute__((visibility("default")))
+#else
+#define Q3_API
+#endif
+
+typedef enum q3_status {
+    Q3_OK = 0,
+    Q3_ERR_INVALID = 1,     /* bad shape, alignment or argument */
+    Q3_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+    Q3_ERR_UNSUPPORTED = 3, /* valid request this build does not handle */
+    Q3_ERR_OOM = 4,         /* device allocation failed */
+    Q3_ERR_DEVICE = 5,      /* a kernel recorded an error (e.g. a bounded wait ran out) */
+    Q3_ERR_NCCL = 6,        /* a NCCL call failed */
+} q3_status;
+
+Q3_API const char* q3_last_error(void);
+Q3_API int q3_version(void);
+
+/* ------------------------------------------------------------------------
+ * Op-level entry points: one per reference Backend op
+ * (src/lib/backend/backend.hpp:26-36), with the reference's semantics and the
+ * aliasing it relies on (src/lib/model/qwen3/qwen3.hpp:143-159).  Shapes follow
+ * the reference's tensors; all are BF16 except the fp32 RoPE tables.
+ * ---------------------------------------------------------------------- */
+
+/* Backend::embedding (backend.hpp:26; cuda/kernels/embedding.cuh:9-30):
+ * out[hidden] = table[token, :]. */
+Q3_API int q3_embedding(const uint16_t* table_dev, size_t vocab, size_t hidden, uint32_t token, uint16_t* out_dev,
+                        void* stream);
+
+/* Backend::matmul (backend.hpp:27; cuda/kernels/matmul.cuh:8-18 cublasGemmEx):
+ * y[n_out] = W[n_out, n_in] . x[n_in], fp32 accumulation, BF16 out.
+ * n_in % 8 == 0 and 16-byte aligned x, W. */
+Q3_API int q3_gemv(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* y_dev, size_t n_out, size_t n_in,
+                   void* stream);
+
+/* Backend::rmsnorm (backend.hpp:28; cuda/kernels/rmsnorm.cuh:12-46,83-89). */
+Q3_API int q3_rmsnorm(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* out_dev, size_t n, float eps,
+                      void* stream);
+
+/* Backend::rmsnorm_add (backend.hpp:29; cuda/kernels/rmsnorm.cuh:48-80,91-95):
+ * res = bf16(res + upd); out = rmsnorm(res).  `upd` may alias `out`. */
+Q3_API int q3_rmsnorm_add(uint16_t* res_dev, const uint16_t* upd_dev, const uint16_t* w_dev, uint16_t* out_dev,
+                          size_t n, float eps, void* stream);
+
+/* Backend::rope (backend.hpp:30; cuda/kernels/rope.cuh:10-58): rotate-half
+ * RoPE in place on values[heads, head_dim] at `pos`; cos/sin are the
+ * [max_pos, head_dim/2] fp32 tables of backend/util/rope_cache.hpp:23-45. */
+Q3_API int q3_rope(uint16_t* values_dev, const float* cos_dev, const float* sin_dev, size_t heads, size_t head_dim,
+                   size_t pos, void* stream);
+
+/* Backend::qk_norm_rope (backend.hpp:33-34; cuda/kernels/qk_norm_rope.cuh:14-100):
+ * per-head RMSNorm with q_norm / k_norm then RoPE at `pos`, in place. */
+Q3_API int q3_qk_norm_rope(uint16_t* q_dev, uint16_t* k_dev, const uint16_t* q_norm_dev, const uint16_t* k_norm_dev,
+                           const float* cos_dev, const float* sin_dev, size_t q_heads, size_t kv_heads,
+                           size_t head_dim, size_t pos, float eps, void* stream);
+
+/* Backend::self_attention (backend.hpp:31; cuda/backend.cu:86-95,124-134;
+ * cuda/kernels/flash_attention.cuh:38-184): softmax(q K^T / sqrt(hd)) V over
+ * positions 0..pos with the GQA map kv = qh / (q_heads / kv_heads).  K and V
+ * use the reference KV layout [capacity, kv_heads, head_dim].  `out` may
+ * alias `q`.  head_dim must be 128; q_heads / kv_heads in {1, 2, 4, 8}.
+ * `workspace` holds the split partials: q3_attention_workspace_bytes(). */
+Q3_API size_t q3_attention_workspace_bytes(size_t q_heads, size_t kv_heads, size_t max_positions);
+Q3_API int q3_attention(const uint16_t* q_dev, const uint16_t* k_dev, const uint16_t* v_dev, uint16_t* out_dev,
+                        size_t q_heads, size_t kv_heads, size_t head_dim, size_t pos, void* workspace_dev,
+                        size_t workspace_bytes, void* stream);
+
+/* The same attention over the paged KV layout this library uses:
+ * k_pages / v_pages are [num_pages, kv_heads, page_size, head_dim] and
+ * page_table maps logical page -> physical page.  page_size is 64. */
+Q3_API int q3_attention_paged(const uint16_t* q_dev, const uint16_t* k_pages_dev, const uint16_t* v_pages_dev,
+                              const int32_t* page_table_dev, uint16_t* out_dev, size_t q_heads, size_t kv_heads,
+                              size_t head_dim, size_t page_size, size_t pos, void* workspace_dev,
+                              size_t workspace_bytes, void* stream);
+
+/* Backend::add (backend.hpp:32; cuda/kernels/add.cuh:10-31); out may alias a. */
+Q3_API int q3_add(const uint16_t* a_dev, const uint16_t* b_dev, uint16_t* out_dev, size_t n, void* stream);
+
+/* Backend::silu (backend.hpp:33; cuda/kernels/silu.cuh:9-32):
+ * out = bf16(g / (1 + exp(-g)) * u); out may alias gate. */
+Q3_API int q3_silu_mul(const uint16_t* gate_dev, const uint16_t* up_dev, uint16_t* out_dev, size_t n, void* stream);
+
+/* Backend::argmax (backend.hpp:35; cuda/backend.cu:107-112 thrust::max_element):
+ * first index of the largest BF16 logit, written to *index_dev. */
+Q3_API int q3_argmax(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, void* stream);
+
+/* make_rope_cache (src/lib/backend/util/rope_cache.hpp:23-45) on the host:
+ * fp32 cos/sin tables [max_pos, head_dim/2], the same bits the engine uses. */
+Q3_API int q3_rope_tables(size_t max_pos, size_t head_dim, float theta, float* cos_host, float* sin_host);
+
+/* ------------------------------------------------------------------------
+ * Synthetic inputs (no reference counterpart: the reference loads
+ * safetensors).  Bit-identical to oracle/q3_oracle.c q3o_fill_normal /
+ * q3o_prompt_ids on any IEEE machine.
+ * ---------------------------------------------------------------------- */
+Q3_API int q3_fill_normal(uint16_t* dst_dev, uint64_t seed, uint64_t tensor_id, size_t rows, size_t cols,
+                          size_t row0, size_t col0, size_t full_cols, size_t dst_row_stride, void* stream);
+Q3_API void q3_prompt_ids(uint32_t* dst_host, size_t n, uint64_t seed, uint32_t vocab);
+
+/* ------------------------------------------------------------------------
+ * Decode engine: Model + KVCache + Generator loop
+ * (src/lib/model/qwen3/qwen3.hpp:105-173, src/lib/kv_cache/kv_cache.hpp:6-29,
+ * src/lib/inference/generator.cpp:37-63), one engine per GPU / TP rank.
+ * ---------------------------------------------------------------------- */
+typedef struct q3_model_config {
+    /* src/lib/model/qwen3/config.hpp:8-23 */
+    uint32_t hidden;      /* hidden_size */
+    uint32_t inter;       /* intermediate_size */
+    uint32_t layers;      /* num_hidden_layers */
+    uint32_t q_heads;     /* num_attention_heads */
+    uint32_t kv_heads;    /* num_key_value_heads */
+    uint32_t head_dim;    /* head_dim (128) */
+    uint32_t vocab;       /* vocab_size */
+    uint32_t tied;        /* tie_word_embeddings */
+    float eps;            /* rms_norm_eps */
+    float theta;          /* rope_theta */
+    uint32_t capacity;    /* KV-cache capacity (context size) */
+    uint32_t eos;         /* eos_token_id (used only when stop_at_eos) */
+} q3_model_config;
+
+typedef struct q3_engine q3_engine;
+
+/* Tensor-parallel placement: rank `tp_rank` of `tp_size` on CUDA device
+ * `device`.  tp_size 1 needs no communicator. */
+Q3_API int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp_size, q3_engine** out);
+Q3_API int q3_engine_destroy(q3_engine* e);
+
+/* Weights: synthetic N(0, 0.02) BF16 from `seed` (norm weights 1.0), each
+ * rank generating its own shard of the full tensors. */
+Q3_API int q3_engine_init_synthetic(q3_engine* e, uint64_t seed);
+
+/* Weights::insert + Backend::make_tensor (src/lib/model/weights.hpp:16-37,
+ * cuda/backend.cu:39-50) for one full (unsharded) tensor named as in the
+ * Hugging Face checkpoint (model.layers.N.self_attn.q_proj.weight, ...).
+ * The engine packs / shards it into its own layout. */
+Q3_API int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, size_t rows, size_t cols);
+
+/* KVCache::reset (kv_cache.hpp:26-28) and prompt installation. */
+Q3_API int q3_engine_reset(q3_engine* e);
+
+/* Tokens: installs ids[0..n) as the forced prefix (prompt or a teacher-forced
+ * sequence).  Steps at positions < n consume these ids; later steps consume
+ * the greedy argmax of the previous step. */
+Q3_API int q3_engine_set_tokens(q3_engine* e, const uint32_t* ids_host, size_t n);
+
+/* Runs `n` decode steps (Model::forward each) on the engine's stream without
+ * host synchronisation.  Replays one CUDA graph per step. */
+Q3_API int q3_engine_step(q3_engine* e, size_t n);
+
+/* Blocks until queued steps finish; returns Q3_ERR_DEVICE if a kernel
+ * recorded an error. */
+Q3_API int q3_engine_sync(q3_engine* e);
+
+/* Model::forward(token) with a host round trip, as the reference
+ * Backend-based loop does (qwen3.hpp:131-166): returns the greedy token. */
+Q3_API int q3_engine_forward(q3_engine* e, uint32_t token, uint32_t* next_token);
+
+/* Generator::generate (generator.cpp:37-63) on ids: prefill the prompt, then
+ * greedy-decode until the KV cache is full (capacity - 1 positions) or
+ * `max_new` tokens; EOS stops it only if stop_at_eos.  Prompt and output are
+ * host arrays.  Returns the number of tokens written to out_host. */
+Q3_API int q3_engine_generate(q3_engine* e, const uint32_t* prompt_host, size_t n_prompt, size_t max_new,
+                              int stop_at_eos, uint32_t* out_host, size_t* n_out);
+
+/* Moves the decode cursor (KVCache::token_count) back to `pos`, which must
+ * not exceed the furthest position already computed; KV entries from `pos`
+ * on are overwritten by the following steps.  Used to re-run a decode window
+ * after one prefill. */
+Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
+
+/* State readers (the reference keeps these as public members). */
+Q3_API int q3_engine_position(q3_engine* e, size_t* pos);
+Q3_API int q3_engine_logits(q3_engine* e, uint16_t* out_host);  /* this rank's vocab shard */
+Q3_API int q3_engine_argmax_history(q3_engine* e, uint32_t* out_host, size_t n);
+Q3_API int q3_engine_kv_slot(q3_engine* e, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host);
+Q3_API int q3_engine_fill_kv(q3_engine* e, size_t upto, uint64_t seed); /* synthetic KV for timing windows */
+
+/* Device pointers / sizes for instrumentation and tests. */
+Q3_API int q3_engine_stream(q3_engine* e, void** stream);
+Q3_API size_t q3_engine_weight_bytes(q3_engine* e);      /* this rank's weight bytes read per step */
+Q3_API size_t q3_engine_kv_bytes_per_position(q3_engine* e);
+
+/* Per-kernel-class timing of one eager step with CUDA events (kernel class:
+ * 0 all GEMVs, 1 attention, 2 everything).  Reports total milliseconds,
+ * launches and algorithmic bytes. */
+Q3_API int q3_engine_profile_step(q3_engine* e, int kernel_class, double* ms, size_t* launches, double* bytes);
+
+/* Tensor parallelism over NCCL: rank 0 calls q3_nccl_unique_id, the id is
+ * shared by the caller (e.g. torch.distributed), then every rank attaches. */
+Q3_API int q3_nccl_unique_id(void* id_out_128_bytes);
+Q3_API int q3_engine_attach_nccl(q3_engine* e, const void* id_128_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* Q3_SM100A_H */

@@ -1,0 +1,870 @@
+// engine.cu -- the decode engine: Qwen3 Model + paged KVCache + greedy loop on
+// one GPU (one tensor-parallel rank), behind the q3_engine_* C ABI.
+//
+// Reference semantics followed: Model::build / forward / prefill
+// (src/lib/model/qwen3/qwen3.hpp:105-173), KVCache (src/lib/kv_cache/
+// kv_cache.hpp:6-29), make_rope_cache (src/lib/backend/util/rope_cache.hpp:
+// 23-45) and the Generator loop (src/lib/inference/generator.cpp:37-63).
+//
+// B200 design:
+//   * one decode step = 5 kernels per layer + 1 (QKV, attention, O, gate/up,
+//     down; lm_head+argmax), all PDL-launched, captured once into a CUDA graph
+//     and replayed per token; the token id, position and argmax live in device
+//     memory so consecutive steps run back to back with no host round trip;
+//   * weights are pre-packed once: q/k/v rows concatenated, gate/up rows
+//     interleaved (gate_j, up_j), each rank holding its tensor-parallel shard;
+//   * KV cache: per layer [pages, kv_heads, 64, 128] BF16 pages and a page
+//     table; a (page, head) block is one contiguous 16 KB TMA copy;
+//   * tensor parallel ranks run the row-parallel GEMVs (o_proj, down_proj)
+//     into fp32 partials, allreduce them with NCCL, and fold the residual add
+//     into the next GEMV's prologue; lm_head is vocab-sharded and the per-rank
+//     (value, index) keys are all-gathered and resolved in the next step.
+#include <nccl.h>
+
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "host_util.hpp"
+#include "kernels.cuh"
+
+namespace q3 {
+
+namespace {
+
+constexpr int kPageSize = 64;
+
+struct LayerW {
+    bf16 *w_qkv, *w_o, *w_gu, *w_down;
+    bf16 *in_norm, *post_norm, *q_norm, *k_norm;
+    bf16 *k_pages, *v_pages;
+};
+
+}  // namespace
+}  // namespace q3
+
+struct q3_engine {
+    q3_model_config cfg{};
+    int device = 0, rank = 0, world = 1, sms = 148;
+    cudaStream_t stream = nullptr;
+    // local (per-rank) dimensions
+    int H = 0, qh = 0, kvh = 0, qd = 0, kd = 0, il = 0, vl = 0;
+    uint32_t voff = 0;
+    // weights
+    q3::bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
+    std::vector<q3::LayerW> layers;
+    int n_pages = 0;
+    int32_t* page_table = nullptr;
+    float *rope_cos = nullptr, *rope_sin = nullptr;
+    // activations
+    q3::bf16 *hs[2] = {nullptr, nullptr}, *q = nullptr, *attn = nullptr, *g = nullptr, *logits = nullptr;
+    float *vsum = nullptr, *partial = nullptr;
+    // control state
+    int32_t *pos = nullptr, *n_forced = nullptr, *tokens = nullptr, *argmax_hist = nullptr;
+    uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
+    uint32_t *done_counter = nullptr, *head_counters = nullptr, *err = nullptr;
+    float* attn_ws = nullptr;
+    int attn_splits = 1;
+    size_t attn_slots = 0;
+    uint32_t* attn_counters = nullptr;
+    // graph / comms
+    cudaGraphExec_t graph = nullptr;
+    ncclComm_t comm = nullptr;
+    size_t host_pos = 0, host_forced = 0, host_max_pos = 0;
+    size_t weight_bytes = 0;
+    std::vector<void*> allocs;
+};
+
+namespace q3 {
+namespace {
+
+int dalloc(q3_engine* e, void** p, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    cudaError_t st = cudaMalloc(p, bytes);
+    if (st != cudaSuccess) {
+        set_error(std::string("cudaMalloc(") + std::to_string(bytes) + "): " + cudaGetErrorString(st));
+        return st == cudaErrorMemoryAllocation ? Q3_ERR_OOM : Q3_ERR_CUDA;
+    }
+    e->allocs.push_back(*p);
+    return Q3_OK;
+}
+
+template <class T>
+int dalloc_t(q3_engine* e, T** p, size_t count) {
+    return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T));
+}
+
+#define Q3_TRY(x)                  \
+    do {                           \
+        int rc_ = (x);             \
+        if (rc_ != Q3_OK) return rc_; \
+    } while (0)
+
+// ------------------------------------------------------------ one decode step
+struct Recorder {
+    q3_engine* e;
+    bool pdl;
+    // optional per-kernel timing (eager profiling)
+    int klass = -1;  // 0 GEMV, 1 attention, 2 all
+    std::vector<cudaEvent_t>* ev = nullptr;
+    double* bytes = nullptr;
+    size_t launches = 0;
+
+    void mark(bool begin, int kind) {
+        if (!ev || !(klass == 2 || klass == kind)) return;
+        cudaEvent_t x;
+        cudaEventCreate(&x);
+        cudaEventRecord(x, e->stream);
+        ev->push_back(x);
+        if (!begin) ++launches;
+    }
+};
+
+GemvArgs base_args(q3_engine* e) {
+    GemvArgs a{};
+    a.eps = e->cfg.eps;
+    a.err = e->err;
+    a.capacity = static_cast<int>(e->cfg.capacity);
+    a.pos_ptr = e->pos;
+    return a;
+}
+
+int gemv(Recorder& r, int pro, int epi, GemvArgs a, const bf16* W, int N, int K, int pos_for_bytes) {
+    (void)pos_for_bytes;
+    a.W = W;
+    a.N = N;
+    a.K = K;
+    a.plan = plan_gemv(N, K, epi, r.e->sms);
+    r.mark(true, 0);
+    cudaError_t st = launch_gemv(pro, epi, a, r.e->stream, r.pdl);
+    r.mark(false, 0);
+    if (r.bytes && (r.klass == 0 || r.klass == 2)) *r.bytes += static_cast<double>(N) * K * 2 + K * 2.0 + N * 2.0;
+    if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("gemv launch: ") + cudaGetErrorString(st));
+    return Q3_OK;
+}
+
+int attention(Recorder& r, const LayerW& L, size_t pos_now) {
+    q3_engine* e = r.e;
+    AttnArgs a{};
+    a.q = e->q;
+    a.k = L.k_pages;
+    a.v = L.v_pages;
+    a.page_table = e->page_table;
+    a.out = e->attn;
+    a.q_heads = e->qh;
+    a.kv_heads = e->kvh;
+    a.page_size = kPageSize;
+    a.paged = 1;
+    a.pos_ptr = e->pos;
+    a.splits = e->attn_splits;
+    a.part_ml = e->attn_ws;
+    a.part_acc = e->attn_ws + e->attn_slots * 2;
+    a.counters = e->attn_counters;
+    a.err = e->err;
+    r.mark(true, 1);
+    cudaError_t st = launch_attention(a, e->stream, r.pdl);
+    r.mark(false, 1);
+    if (r.bytes && (r.klass == 1 || r.klass == 2))
+        *r.bytes += 2.0 * (pos_now + 1) * e->kvh * 128 * 2 + 2.0 * e->qd * 2;
+    if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(st));
+    return Q3_OK;
+}
+
+int allreduce(q3_engine* e, float* buf, size_t n) {
+    ncclResult_t nr = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, e->stream);
+    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+    return Q3_OK;
+}
+
+int record_step(Recorder& r, size_t pos_now) {
+    q3_engine* e = r.e;
+    const q3_model_config& c = e->cfg;
+    const bool tp = e->world > 1;
+    int cur = 0;  // residual buffer holding hs (tensor-parallel ping-pong)
+    for (size_t l = 0; l < e->layers.size(); ++l) {
+        const LayerW& L = e->layers[l];
+        // ---- QKV (+ embedding / residual / RMSNorm prologue, qk-norm + RoPE + KV write epilogue)
+        GemvArgs a = base_args(e);
+        a.norm_w = L.in_norm;
+        a.q_rows = e->qd;
+        a.kv_rows = e->kd;
+        a.head_dim = 128;
+        a.kv_heads_local = e->kvh;
+        a.page_size = kPageSize;
+        a.q_out = e->q;
+        a.k_pages = L.k_pages;
+        a.v_pages = L.v_pages;
+        a.page_table = e->page_table;
+        a.q_norm = L.q_norm;
+        a.k_norm = L.k_norm;
+        a.rope_cos = e->rope_cos;
+        a.rope_sin = e->rope_sin;
+        a.head_counters = e->head_counters;
+        int pro;
+        if (l == 0) {
+            pro = PRO_EMBED_NORM;
+            a.embed = e->embed;
+            a.vocab = static_cast<int>(c.vocab);
+            a.tokens = e->tokens;
+            a.argmax_hist = e->argmax_hist;
+            a.n_forced = e->n_forced;
+            a.keys = e->keys;
+            a.n_keys = e->world;
+            a.hs_out = e->hs[0];
+            cur = 0;
+        } else if (tp) {
+            pro = PRO_RESID_NORM;
+            a.hs = e->hs[cur];
+            a.hs_out = e->hs[cur ^ 1];
+            a.vsum = e->partial;
+            a.ss_unrounded = 0;  // qwen3.hpp:159 add, then :137 rmsnorm of the rounded residual
+            cur ^= 1;
+        } else {
+            pro = PRO_NORM;
+            a.hs = e->hs[0];
+        }
+        Q3_TRY(gemv(r, pro, EPI_QKV, a, L.w_qkv, e->qd + 2 * e->kd, e->H, 0));
+        // ---- attention
+        Q3_TRY(attention(r, L, pos_now));
+        // ---- o_proj (+ residual add)
+        GemvArgs o = base_args(e);
+        o.x = e->attn;
+        if (tp) {
+            o.yf = e->partial;
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, o, L.w_o, e->H, e->qd, 0));
+            Q3_TRY(allreduce(e, e->partial, e->H));
+        } else {
+            o.hs = e->hs[0];
+            o.vsum_out = e->vsum;
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID_F32, o, L.w_o, e->H, e->qd, 0));
+        }
+        // ---- gate/up (+ RMSNorm prologue, SwiGLU epilogue)
+        GemvArgs gu = base_args(e);
+        gu.norm_w = L.post_norm;
+        gu.y = e->g;
+        if (tp) {
+            gu.hs = e->hs[cur];
+            gu.hs_out = e->hs[cur ^ 1];
+            gu.vsum = e->partial;
+            gu.ss_unrounded = 1;  // rmsnorm_add (rmsnorm.cuh:58-60) squares the unrounded sums
+            cur ^= 1;
+            Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_SWIGLU, gu, L.w_gu, 2 * e->il, e->H, 0));
+        } else {
+            gu.hs = e->hs[0];
+            gu.vsum = e->vsum;
+            Q3_TRY(gemv(r, PRO_NORM_F32, EPI_SWIGLU, gu, L.w_gu, 2 * e->il, e->H, 0));
+        }
+        // ---- down_proj (+ residual add)
+        GemvArgs d = base_args(e);
+        d.x = e->g;
+        if (tp) {
+            d.yf = e->partial;
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, d, L.w_down, e->H, e->il, 0));
+            Q3_TRY(allreduce(e, e->partial, e->H));
+        } else {
+            d.hs = e->hs[0];
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID, d, L.w_down, e->H, e->il, 0));
+        }
+    }
+    // ---- final RMSNorm + lm_head + argmax (vocab shard)
+    GemvArgs h = base_args(e);
+    h.norm_w = e->final_norm;
+    h.y = e->logits;
+    h.key_slot = e->key_slot;
+    h.done_counter = e->done_counter;
+    h.key_out = tp ? e->key_send : e->keys;
+    h.pos_inc = e->pos;
+    h.vocab_offset = e->voff;
+    if (tp) {
+        h.hs = e->hs[cur];
+        h.hs_out = e->hs[cur ^ 1];
+        h.vsum = e->partial;
+        h.ss_unrounded = 0;
+        Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
+        ncclResult_t nr = ncclAllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
+        if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+    } else {
+        h.hs = e->hs[0];
+        Q3_TRY(gemv(r, PRO_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
+    }
+    return Q3_OK;
+}
+
+int build_graph(q3_engine* e) {
+    if (e->graph) return Q3_OK;
+    if (e->world > 1 && !e->comm) return fail(Q3_ERR_INVALID, "tensor-parallel engine needs q3_engine_attach_nccl");
+    Recorder r{e, true};
+    cudaGraph_t g = nullptr;
+    Q3_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = record_step(r, 0);
+    cudaError_t st = cudaStreamEndCapture(e->stream, &g);
+    if (rc != Q3_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(st));
+    st = cudaGraphInstantiate(&e->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(st));
+    return Q3_OK;
+}
+
+int check_device_error(q3_engine* e) {
+    uint32_t err = 0;
+    Q3_CUDA(cudaMemcpy(&err, e->err, sizeof(err), cudaMemcpyDeviceToHost));
+    if (err != 0) {
+        static const char* names[] = {"ok", "TMA wait timed out", "peer wait timed out", "token id out of range",
+                                      "position out of range"};
+        return fail(Q3_ERR_DEVICE, std::string("device error: ") + (err < 5 ? names[err] : "unknown"));
+    }
+    return Q3_OK;
+}
+
+// Host rope tables exactly as make_rope_cache (rope_cache.hpp:29-41): fp32,
+// inv_freq = 1/pow(theta, 2i/hd), cos/sin(float(p) * inv_freq).
+void rope_tables(size_t max_pos, size_t hd, float theta, std::vector<float>& c, std::vector<float>& s) {
+    const size_t half = hd / 2;
+    std::vector<float> inv(half);
+    for (size_t i = 0; i < half; ++i) {
+        const float ex = 2.0F * static_cast<float>(i) / static_cast<float>(hd);
+        inv[i] = 1.0F / std::pow(theta, ex);
+    }
+    c.resize(max_pos * half);
+    s.resize(max_pos * half);
+    for (size_t p = 0; p < max_pos; ++p)
+        for (size_t i = 0; i < half; ++i) {
+            const float ang = static_cast<float>(p) * inv[i];
+            c[p * half + i] = std::cos(ang);
+            s[p * half + i] = std::sin(ang);
+        }
+}
+
+}  // namespace
+}  // namespace q3
+
+using namespace q3;
+
+extern "C" {
+
+int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp_size, q3_engine** out) {
+    Q3_CHECK(cfg && out, "q3_engine_create: null argument");
+    *out = nullptr;
+    const q3_model_config& c = *cfg;
+    Q3_CHECK(tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size, "q3_engine_create: bad tensor-parallel rank");
+    if (c.head_dim != 128) return fail(Q3_ERR_UNSUPPORTED, "q3_engine_create: head_dim must be 128");
+    Q3_CHECK(c.layers > 0 && c.hidden > 0 && c.vocab > 0 && c.capacity > 1, "q3_engine_create: empty config");
+    Q3_CHECK(c.kv_heads > 0 && c.q_heads % c.kv_heads == 0, "q3_engine_create: q_heads % kv_heads != 0");
+    const uint32_t G = c.q_heads / c.kv_heads;
+    if (!(G == 1 || G == 2 || G == 4 || G == 8)) return fail(Q3_ERR_UNSUPPORTED, "GQA group must be 1/2/4/8");
+    Q3_CHECK(c.kv_heads % tp_size == 0, "kv_heads must divide by the tensor-parallel size");
+    Q3_CHECK(c.inter % tp_size == 0 && (c.inter / tp_size) % 8 == 0, "intermediate/tp must be a multiple of 8");
+    Q3_CHECK(c.vocab % tp_size == 0, "vocab must divide by the tensor-parallel size");
+    Q3_CHECK(c.hidden % 8 == 0 && c.hidden <= 32768, "hidden must be a multiple of 8 (<= 32768)");
+    Q3_CHECK(c.capacity < (1u << 24), "capacity too large");
+
+    auto* e = new q3_engine();
+    e->cfg = c;
+    e->device = device;
+    e->rank = tp_rank;
+    e->world = tp_size;
+    int rc = Q3_OK;
+    auto bail = [&](int code) {
+        q3_engine_destroy(e);
+        return code;
+    };
+    if (cudaSetDevice(device) != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "cudaSetDevice failed"));
+    e->sms = num_sms(device);
+    if (configure_kernels() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "kernel attribute setup failed"));
+    if (cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking) != cudaSuccess)
+        return bail(fail(Q3_ERR_CUDA, "cudaStreamCreate failed"));
+
+    e->H = static_cast<int>(c.hidden);
+    e->qh = static_cast<int>(c.q_heads / tp_size);
+    e->kvh = static_cast<int>(c.kv_heads / tp_size);
+    e->qd = e->qh * 128;
+    e->kd = e->kvh * 128;
+    e->il = static_cast<int>(c.inter / tp_size);
+    e->vl = static_cast<int>(c.vocab / tp_size);
+    e->voff = static_cast<uint32_t>(e->vl) * static_cast<uint32_t>(tp_rank);
+    const size_t H = e->H;
+
+    // ---- weights
+    if ((rc = dalloc_t(e, &e->embed, static_cast<size_t>(c.vocab) * H)) != Q3_OK) return bail(rc);
+    if (c.tied) {
+        e->lm_head = e->embed + static_cast<size_t>(e->voff) * H;
+    } else if ((rc = dalloc_t(e, &e->lm_head, static_cast<size_t>(e->vl) * H)) != Q3_OK) {
+        return bail(rc);
+    }
+    if ((rc = dalloc_t(e, &e->final_norm, H)) != Q3_OK) return bail(rc);
+    e->n_pages = static_cast<int>((c.capacity + kPageSize - 1) / kPageSize);
+    const size_t page_elems = static_cast<size_t>(e->n_pages) * e->kvh * kPageSize * 128;
+    e->layers.resize(c.layers);
+    for (auto& L : e->layers) {
+        if ((rc = dalloc_t(e, &L.w_qkv, static_cast<size_t>(e->qd + 2 * e->kd) * H)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.w_o, H * e->qd)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.w_gu, 2 * static_cast<size_t>(e->il) * H)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.w_down, H * e->il)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.in_norm, H)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.post_norm, H)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.q_norm, 128)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.k_norm, 128)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.k_pages, page_elems)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &L.v_pages, page_elems)) != Q3_OK) return bail(rc);
+        if (cudaMemset(L.k_pages, 0, page_elems * 2) != cudaSuccess ||
+            cudaMemset(L.v_pages, 0, page_elems * 2) != cudaSuccess)
+            return bail(fail(Q3_ERR_CUDA, "KV cache memset failed"));
+    }
+    // bytes streamed per decode step by this rank (weights read by the GEMVs + norms + one embedding row)
+    const size_t per_layer = (static_cast<size_t>(e->qd + 2 * e->kd) * H + H * e->qd + 2 * static_cast<size_t>(e->il) * H +
+                              H * e->il + 2 * H + 256) * 2;
+    e->weight_bytes = per_layer * c.layers + static_cast<size_t>(e->vl) * H * 2 + H * 2 + H * 2;
+
+    // ---- page table (identity for a single sequence) and RoPE tables
+    std::vector<int32_t> pt(e->n_pages);
+    for (int i = 0; i < e->n_pages; ++i) pt[i] = i;
+    if ((rc = dalloc_t(e, &e->page_table, pt.size())) != Q3_OK) return bail(rc);
+    if (cudaMemcpy(e->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail(fail(Q3_ERR_CUDA, "page table upload failed"));
+    std::vector<float> cs, sn;
+    rope_tables(c.capacity, 128, c.theta, cs, sn);
+    if ((rc = dalloc_t(e, &e->rope_cos, cs.size())) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->rope_sin, sn.size())) != Q3_OK) return bail(rc);
+    if (cudaMemcpy(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(e->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+        return bail(fail(Q3_ERR_CUDA, "rope table upload failed"));
+
+    // ---- activations and control
+    if ((rc = dalloc_t(e, &e->hs[0], H)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->hs[1], H)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->q, e->qd)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->attn, e->qd)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->g, e->il)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->logits, e->vl)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->vsum, H)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->partial, H)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->pos, 4)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->n_forced, 4)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->tokens, c.capacity + 1)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->argmax_hist, c.capacity + 1)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->key_slot, 2)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->key_send, 2)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->keys, static_cast<size_t>(tp_size) + 1)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->done_counter, 4)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->head_counters, static_cast<size_t>(e->qh + e->kvh) + 4)) != Q3_OK) return bail(rc);
+    if ((rc = dalloc_t(e, &e->err, 4)) != Q3_OK) return bail(rc);
+    cudaMemset(e->pos, 0, 16);
+    cudaMemset(e->n_forced, 0, 16);
+    cudaMemset(e->tokens, 0, (c.capacity + 1) * 4);
+    cudaMemset(e->argmax_hist, 0xFF, (c.capacity + 1) * 4);
+    cudaMemset(e->key_slot, 0, 16);
+    cudaMemset(e->key_send, 0, 16);
+    cudaMemset(e->keys, 0, (tp_size + 1) * 8);
+    cudaMemset(e->done_counter, 0, 16);
+    cudaMemset(e->head_counters, 0, (e->qh + e->kvh + 4) * 4);
+    cudaMemset(e->err, 0, 4);
+
+    // ---- attention split workspace, sized for the full context
+    e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
+    const int Gl = e->qh / e->kvh;
+    const int HG = Gl >= 4 ? 4 : Gl;
+    e->attn_slots = static_cast<size_t>(e->kvh) * (Gl / HG) * e->attn_splits * HG;
+    const size_t ws = attn_workspace_bytes(e->qh, e->kvh, e->attn_splits);
+    if ((rc = dalloc(e, reinterpret_cast<void**>(&e->attn_ws), ws)) != Q3_OK) return bail(rc);
+    e->attn_counters = reinterpret_cast<uint32_t*>(e->attn_ws + e->attn_slots * 2 + e->attn_slots * 128);
+    cudaMemset(e->attn_ws, 0, ws);
+    if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "engine setup failed"));
+    *out = e;
+    return Q3_OK;
+}
+
+int q3_engine_destroy(q3_engine* e) {
+    if (!e) return Q3_OK;
+    cudaSetDevice(e->device);
+    if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    if (e->comm) ncclCommDestroy(e->comm);
+    for (void* p : e->allocs) cudaFree(p);
+    if (e->stream) cudaStreamDestroy(e->stream);
+    delete e;
+    return Q3_OK;
+}
+
+int q3_engine_init_synthetic(q3_engine* e, uint64_t seed) {
+    Q3_CHECK(e, "null engine");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const q3_model_config& c = e->cfg;
+    const size_t H = e->H;
+    cudaStream_t s = e->stream;
+    const size_t qfull = static_cast<size_t>(c.q_heads) * 128;
+    const size_t kfull = static_cast<size_t>(c.kv_heads) * 128;
+    // tensor ids: embed 1, lm_head 2, layer l: 16 + 16 l + {q,k,v,o,gate,up,down}
+    Q3_CUDA(launch_fill_normal(e->embed, seed, 1, c.vocab, H, 0, 0, H, H, s));
+    if (!c.tied) Q3_CUDA(launch_fill_normal(e->lm_head, seed, 2, e->vl, H, e->voff, 0, H, H, s));
+    Q3_CUDA(launch_fill_const(e->final_norm, H, 1.0f, s));
+    for (size_t l = 0; l < e->layers.size(); ++l) {
+        const LayerW& L = e->layers[l];
+        const uint64_t b = 16 + 16 * l;
+        const size_t qr0 = static_cast<size_t>(e->rank) * e->qd, kr0 = static_cast<size_t>(e->rank) * e->kd;
+        Q3_CUDA(launch_fill_normal(L.w_qkv, seed, b + 0, e->qd, H, qr0, 0, H, H, s));
+        Q3_CUDA(launch_fill_normal(L.w_qkv + e->qd * H, seed, b + 1, e->kd, H, kr0, 0, H, H, s));
+        Q3_CUDA(launch_fill_normal(L.w_qkv + (e->qd + e->kd) * H, seed, b + 2, e->kd, H, kr0, 0, H, H, s));
+        Q3_CUDA(launch_fill_normal(L.w_o, seed, b + 3, H, e->qd, 0, qr0, qfull, e->qd, s));
+        const size_t ir0 = static_cast<size_t>(e->rank) * e->il;
+        Q3_CUDA(launch_fill_normal(L.w_gu, seed, b + 4, e->il, H, ir0, 0, H, 2 * H, s));
+        Q3_CUDA(launch_fill_normal(L.w_gu + H, seed, b + 5, e->il, H, ir0, 0, H, 2 * H, s));
+        Q3_CUDA(launch_fill_normal(L.w_down, seed, b + 6, H, e->il, 0, ir0, c.inter, e->il, s));
+        Q3_CUDA(launch_fill_const(L.in_norm, H, 1.0f, s));
+        Q3_CUDA(launch_fill_const(L.post_norm, H, 1.0f, s));
+        Q3_CUDA(launch_fill_const(L.q_norm, 128, 1.0f, s));
+        Q3_CUDA(launch_fill_const(L.k_norm, 128, 1.0f, s));
+        (void)kfull;
+    }
+    Q3_CUDA(cudaStreamSynchronize(s));
+    return Q3_OK;
+}
+
+int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, size_t rows, size_t cols) {
+    Q3_CHECK(e && name && host, "q3_engine_set_weight: null argument");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const q3_model_config& c = e->cfg;
+    const std::string n(name);
+    const size_t H = e->H;
+    auto expect = [&](size_t r, size_t cc) { return rows == r && cols == cc; };
+    auto copy2d = [&](void* dst, size_t dpitch_elems, const uint16_t* src, size_t spitch_elems, size_t width_elems,
+                      size_t height) -> int {
+        Q3_CUDA(cudaMemcpy2D(dst, dpitch_elems * 2, src, spitch_elems * 2, width_elems * 2, height,
+                             cudaMemcpyHostToDevice));
+        return Q3_OK;
+    };
+    if (n == "model.embed_tokens.weight") {
+        Q3_CHECK(expect(c.vocab, H), "embed_tokens shape");
+        return copy2d(e->embed, H, host, H, H, c.vocab);
+    }
+    if (n == "lm_head.weight") {
+        Q3_CHECK(expect(c.vocab, H), "lm_head shape");
+        if (c.tied) return fail(Q3_ERR_INVALID, "lm_head.weight given for a tied-embedding model");
+        return copy2d(e->lm_head, H, host + static_cast<size_t>(e->voff) * H, H, H, e->vl);
+    }
+    if (n == "model.norm.weight") {
+        Q3_CHECK(expect(1, H) || expect(H, 1), "norm shape");
+        return copy2d(e->final_norm, H, host, H, H, 1);
+    }
+    const std::string pre = "model.layers.";
+    Q3_CHECK(n.rfind(pre, 0) == 0, "unknown weight name: " + n);
+    size_t dot = n.find('.', pre.size());
+    Q3_CHECK(dot != std::string::npos, "bad weight name: " + n);
+    const size_t l = std::stoul(n.substr(pre.size(), dot - pre.size()));
+    Q3_CHECK(l < e->layers.size(), "layer index out of range: " + n);
+    const std::string leaf = n.substr(dot + 1);
+    const LayerW& L = e->layers[l];
+    const size_t qfull = static_cast<size_t>(c.q_heads) * 128, kfull = static_cast<size_t>(c.kv_heads) * 128;
+    const size_t qr0 = static_cast<size_t>(e->rank) * e->qd, kr0 = static_cast<size_t>(e->rank) * e->kd;
+    const size_t ir0 = static_cast<size_t>(e->rank) * e->il;
+    if (leaf == "self_attn.q_proj.weight") {
+        Q3_CHECK(expect(qfull, H), "q_proj shape");
+        return copy2d(L.w_qkv, H, host + qr0 * H, H, H, e->qd);
+    }
+    if (leaf == "self_attn.k_proj.weight") {
+        Q3_CHECK(expect(kfull, H), "k_proj shape");
+        return copy2d(L.w_qkv + e->qd * H, H, host + kr0 * H, H, H, e->kd);
+    }
+    if (leaf == "self_attn.v_proj.weight") {
+        Q3_CHECK(expect(kfull, H), "v_proj shape");
+        return copy2d(L.w_qkv + (e->qd + e->kd) * H, H, host + kr0 * H, H, H, e->kd);
+    }
+    if (leaf == "self_attn.o_proj.weight") {
+        Q3_CHECK(expect(H, qfull), "o_proj shape");
+        return copy2d(L.w_o, e->qd, host + qr0, qfull, e->qd, H);
+    }
+    if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight") {
+        Q3_CHECK(expect(c.inter, H), "gate/up shape");
+        bf16* dst = L.w_gu + (leaf == "mlp.up_proj.weight" ? H : 0);
+        return copy2d(dst, 2 * H, host + ir0 * H, H, H, e->il);
+    }
+    if (leaf == "mlp.down_proj.weight") {
+        Q3_CHECK(expect(H, c.inter), "down_proj shape");
+        return copy2d(L.w_down, e->il, host + ir0, c.inter, e->il, H);
+    }
+    auto vec = [&](bf16* dst, size_t len) -> int {
+        Q3_CHECK(rows * cols == len, "norm weight shape: " + n);
+        Q3_CUDA(cudaMemcpy(dst, host, len * 2, cudaMemcpyHostToDevice));
+        return Q3_OK;
+    };
+    if (leaf == "input_layernorm.weight") return vec(L.in_norm, H);
+    if (leaf == "post_attention_layernorm.weight") return vec(L.post_norm, H);
+    if (leaf == "self_attn.q_norm.weight") return vec(L.q_norm, 128);
+    if (leaf == "self_attn.k_norm.weight") return vec(L.k_norm, 128);
+    return fail(Q3_ERR_INVALID, "unknown weight name: " + n);
+}
+
+int q3_engine_reset(q3_engine* e) {
+    Q3_CHECK(e, "null engine");
+    Q3_CUDA(cudaSetDevice(e->device));
+    Q3_CUDA(cudaMemsetAsync(e->pos, 0, 4, e->stream));
+    Q3_CUDA(cudaMemsetAsync(e->n_forced, 0, 4, e->stream));
+    Q3_CUDA(cudaMemsetAsync(e->argmax_hist, 0xFF, (e->cfg.capacity + 1) * 4, e->stream));
+    e->host_pos = 0;
+    e->host_forced = 0;
+    e->host_max_pos = 0;
+    return Q3_OK;
+}
+
+int q3_engine_set_tokens(q3_engine* e, const uint32_t* ids, size_t n) {
+    Q3_CHECK(e && (ids || n == 0), "q3_engine_set_tokens: null argument");
+    Q3_CHECK(n <= e->cfg.capacity, "q3_engine_set_tokens: more tokens than KV capacity");
+    for (size_t i = 0; i < n; ++i) Q3_CHECK(ids[i] < e->cfg.vocab, "q3_engine_set_tokens: token id >= vocab");
+    Q3_CUDA(cudaSetDevice(e->device));
+    if (n) Q3_CUDA(cudaMemcpyAsync(e->tokens, ids, n * 4, cudaMemcpyHostToDevice, e->stream));
+    const int32_t nf = static_cast<int32_t>(n);
+    Q3_CUDA(cudaMemcpyAsync(e->n_forced, &nf, 4, cudaMemcpyHostToDevice, e->stream));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    e->host_forced = n;
+    return Q3_OK;
+}
+
+int q3_engine_step(q3_engine* e, size_t n) {
+    Q3_CHECK(e, "null engine");
+    if (n == 0) return Q3_OK;
+    Q3_CHECK(e->host_forced >= 1 || e->host_pos >= 1, "q3_engine_step: no input token (set_tokens first)");
+    if (e->host_pos + n > e->cfg.capacity)
+        return fail(Q3_ERR_INVALID, "q3_engine_step: KV cache capacity exceeded");
+    Q3_CUDA(cudaSetDevice(e->device));
+    Q3_TRY(build_graph(e));
+    for (size_t i = 0; i < n; ++i) Q3_CUDA(cudaGraphLaunch(e->graph, e->stream));
+    e->host_pos += n;
+    if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
+    return Q3_OK;
+}
+
+int q3_engine_sync(q3_engine* e) {
+    Q3_CHECK(e, "null engine");
+    Q3_CUDA(cudaSetDevice(e->device));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    return check_device_error(e);
+}
+
+static int finish_last(q3_engine* e) {
+    Q3_CUDA(launch_resolve_tokens(e->keys, e->world, e->tokens, e->argmax_hist, e->pos, e->n_forced,
+                                  static_cast<int>(e->cfg.vocab), e->err, e->stream));
+    return Q3_OK;
+}
+
+int q3_engine_forward(q3_engine* e, uint32_t token, uint32_t* next_token) {
+    Q3_CHECK(e && next_token, "q3_engine_forward: null argument");
+    Q3_CHECK(token < e->cfg.vocab, "q3_engine_forward: token id >= vocab");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const size_t p = e->host_pos;
+    Q3_CHECK(p < e->cfg.capacity, "q3_engine_forward: KV cache full");
+    const int32_t t = static_cast<int32_t>(token), nf = static_cast<int32_t>(p + 1);
+    Q3_CUDA(cudaMemcpyAsync(e->tokens + p, &t, 4, cudaMemcpyHostToDevice, e->stream));
+    Q3_CUDA(cudaMemcpyAsync(e->n_forced, &nf, 4, cudaMemcpyHostToDevice, e->stream));
+    e->host_forced = p + 1;
+    Q3_TRY(q3_engine_step(e, 1));
+    Q3_TRY(finish_last(e));
+    std::vector<uint64_t> k(e->world);
+    Q3_CUDA(cudaMemcpyAsync(k.data(), e->keys, 8 * e->world, cudaMemcpyDeviceToHost, e->stream));
+    Q3_TRY(q3_engine_sync(e));
+    uint64_t best = 0;
+    for (uint64_t v : k) best = v > best ? v : best;
+    *next_token = 0xFFFFFFFFu - static_cast<uint32_t>(best & 0xFFFFFFFFull);
+    return Q3_OK;
+}
+
+int q3_engine_generate(q3_engine* e, const uint32_t* prompt, size_t n_prompt, size_t max_new, int stop_at_eos,
+                       uint32_t* out, size_t* n_out) {
+    Q3_CHECK(e && prompt && out && n_out, "q3_engine_generate: null argument");
+    Q3_CHECK(n_prompt >= 1, "q3_engine_generate: empty prompt");
+    // generator.cpp:42-44
+    if (n_prompt >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "prompt does not fit in the model context");
+    Q3_TRY(q3_engine_reset(e));
+    Q3_TRY(q3_engine_set_tokens(e, prompt, n_prompt));
+    // prefill forwards every prompt id but the last (qwen3.hpp:168-173); the
+    // loop then runs while token_count + 1 < capacity (generator.cpp:49).
+    const size_t room = e->cfg.capacity - n_prompt;
+    const size_t n_gen = max_new < room ? max_new : room;
+    const size_t steps = n_prompt - 1 + n_gen;
+    if (!stop_at_eos) {
+        Q3_TRY(q3_engine_step(e, steps));
+    } else {
+        // EOS needs the host to look at tokens: run in chunks.
+        size_t done = 0;
+        const size_t chunk = 32;
+        while (done < steps) {
+            const size_t k = (steps - done) < chunk ? (steps - done) : chunk;
+            Q3_TRY(q3_engine_step(e, k));
+            done += k;
+            if (done >= n_prompt) {
+                Q3_TRY(finish_last(e));
+                std::vector<int32_t> t(done + 1);
+                Q3_CUDA(cudaMemcpyAsync(t.data(), e->tokens, (done + 1) * 4, cudaMemcpyDeviceToHost, e->stream));
+                Q3_TRY(q3_engine_sync(e));
+                bool eos = false;
+                for (size_t i = n_prompt; i <= done; ++i)
+                    if (static_cast<uint32_t>(t[i]) == e->cfg.eos) eos = true;
+                if (eos) break;
+            }
+        }
+        const size_t produced = done + 1 - n_prompt;
+        std::vector<int32_t> t(done + 1);
+        Q3_TRY(finish_last(e));
+        Q3_CUDA(cudaMemcpyAsync(t.data(), e->tokens, (done + 1) * 4, cudaMemcpyDeviceToHost, e->stream));
+        Q3_TRY(q3_engine_sync(e));
+        size_t k = 0;
+        for (; k < produced && k < n_gen; ++k) {
+            const uint32_t v = static_cast<uint32_t>(t[n_prompt + k]);
+            if (v == e->cfg.eos) break;  // generator.cpp:52-54: EOS is not emitted
+            out[k] = v;
+        }
+        *n_out = k;
+        return Q3_OK;
+    }
+    Q3_TRY(finish_last(e));
+    Q3_CUDA(cudaMemcpyAsync(out, e->tokens + n_prompt, n_gen * 4, cudaMemcpyDeviceToHost, e->stream));
+    Q3_TRY(q3_engine_sync(e));
+    *n_out = n_gen;
+    return Q3_OK;
+}
+
+int q3_engine_set_position(q3_engine* e, size_t pos) {
+    Q3_CHECK(e, "null engine");
+    const size_t reached = e->host_max_pos > e->host_pos ? e->host_max_pos : e->host_pos;
+    Q3_CHECK(pos <= reached && pos < e->cfg.capacity, "q3_engine_set_position: position not reached yet");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const int32_t p = static_cast<int32_t>(pos);
+    Q3_CUDA(cudaMemcpyAsync(e->pos, &p, 4, cudaMemcpyHostToDevice, e->stream));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    e->host_max_pos = reached;
+    e->host_pos = pos;
+    return Q3_OK;
+}
+
+int q3_engine_position(q3_engine* e, size_t* pos) {
+    Q3_CHECK(e && pos, "null argument");
+    *pos = e->host_pos;
+    return Q3_OK;
+}
+
+int q3_engine_logits(q3_engine* e, uint16_t* out) {
+    Q3_CHECK(e && out, "null argument");
+    Q3_CUDA(cudaSetDevice(e->device));
+    Q3_CUDA(cudaMemcpyAsync(out, e->logits, static_cast<size_t>(e->vl) * 2, cudaMemcpyDeviceToHost, e->stream));
+    return q3_engine_sync(e);
+}
+
+int q3_engine_argmax_history(q3_engine* e, uint32_t* out, size_t n) {
+    Q3_CHECK(e && out, "null argument");
+    Q3_CHECK(n <= e->cfg.capacity, "argmax history longer than capacity");
+    Q3_CUDA(cudaSetDevice(e->device));
+    Q3_TRY(finish_last(e));
+    Q3_CUDA(cudaMemcpyAsync(out, e->argmax_hist, n * 4, cudaMemcpyDeviceToHost, e->stream));
+    return q3_engine_sync(e);
+}
+
+int q3_engine_kv_slot(q3_engine* e, size_t layer, size_t pos, uint16_t* k_out, uint16_t* v_out) {
+    Q3_CHECK(e && k_out && v_out, "null argument");
+    Q3_CHECK(layer < e->layers.size() && pos < e->cfg.capacity, "kv slot out of range");
+    Q3_CUDA(cudaSetDevice(e->device));
+    int32_t page = 0;
+    Q3_CUDA(cudaMemcpy(&page, e->page_table + pos / kPageSize, 4, cudaMemcpyDeviceToHost));
+    const LayerW& L = e->layers[layer];
+    for (int h = 0; h < e->kvh; ++h) {
+        const size_t off = ((static_cast<size_t>(page) * e->kvh + h) * kPageSize + pos % kPageSize) * 128;
+        Q3_CUDA(cudaMemcpy(k_out + h * 128, L.k_pages + off, 256, cudaMemcpyDeviceToHost));
+        Q3_CUDA(cudaMemcpy(v_out + h * 128, L.v_pages + off, 256, cudaMemcpyDeviceToHost));
+    }
+    return Q3_OK;
+}
+
+int q3_engine_fill_kv(q3_engine* e, size_t upto, uint64_t seed) {
+    Q3_CHECK(e, "null engine");
+    Q3_CHECK(upto < e->cfg.capacity, "q3_engine_fill_kv: upto must be < capacity");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const size_t pages = (upto + kPageSize - 1) / kPageSize;
+    const size_t rows = pages * e->kvh * kPageSize;
+    for (size_t l = 0; l < e->layers.size(); ++l) {
+        if (rows == 0) break;
+        Q3_CUDA(launch_fill_normal(e->layers[l].k_pages, seed, 0x4B00 + 2 * l, rows, 128, 0, 0, 128, 128, e->stream));
+        Q3_CUDA(launch_fill_normal(e->layers[l].v_pages, seed, 0x4B01 + 2 * l, rows, 128, 0, 0, 128, 128, e->stream));
+    }
+    const int32_t p = static_cast<int32_t>(upto);
+    Q3_CUDA(cudaMemcpyAsync(e->pos, &p, 4, cudaMemcpyHostToDevice, e->stream));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    e->host_pos = upto;
+    if (upto > e->host_max_pos) e->host_max_pos = upto;
+    return Q3_OK;
+}
+
+int q3_engine_stream(q3_engine* e, void** stream) {
+    Q3_CHECK(e && stream, "null argument");
+    *stream = e->stream;
+    return Q3_OK;
+}
+
+size_t q3_engine_weight_bytes(q3_engine* e) { return e ? e->weight_bytes : 0; }
+
+size_t q3_engine_kv_bytes_per_position(q3_engine* e) {
+    return e ? e->layers.size() * 2 * static_cast<size_t>(e->kvh) * 128 * 2 : 0;
+}
+
+int q3_engine_profile_step(q3_engine* e, int klass, double* ms, size_t* launches, double* bytes) {
+    Q3_CHECK(e && ms && launches && bytes, "null argument");
+    Q3_CHECK(e->host_pos < e->cfg.capacity, "q3_engine_profile_step: KV cache full");
+    Q3_CHECK(e->host_forced >= 1 || e->host_pos >= 1, "q3_engine_profile_step: no input token");
+    if (e->world > 1 && !e->comm) return fail(Q3_ERR_INVALID, "tensor-parallel engine needs NCCL");
+    Q3_CUDA(cudaSetDevice(e->device));
+    std::vector<cudaEvent_t> ev;
+    double b = 0;
+    Recorder r{e, false, klass, &ev, &b};
+    Q3_TRY(record_step(r, e->host_pos));
+    e->host_pos += 1;
+    if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    double total = 0;
+    for (size_t i = 0; i + 1 < ev.size(); i += 2) {
+        float t = 0;
+        cudaEventElapsedTime(&t, ev[i], ev[i + 1]);
+        total += t;
+    }
+    for (auto x : ev) cudaEventDestroy(x);
+    *ms = total;
+    *launches = r.launches;
+    *bytes = b;
+    return check_device_error(e);
+}
+
+int q3_rope_tables(size_t max_pos, size_t head_dim, float theta, float* cos_host, float* sin_host) {
+    Q3_CHECK(cos_host && sin_host && head_dim % 2 == 0, "q3_rope_tables: bad argument");
+    std::vector<float> c, s;
+    rope_tables(max_pos, head_dim, theta, c, s);
+    std::memcpy(cos_host, c.data(), c.size() * 4);
+    std::memcpy(sin_host, s.data(), s.size() * 4);
+    return Q3_OK;
+}
+
+int q3_nccl_unique_id(void* id_out) {
+    Q3_CHECK(id_out, "null argument");
+    ncclUniqueId id;
+    ncclResult_t nr = ncclGetUniqueId(&id);
+    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(nr));
+    static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
+    std::memcpy(id_out, &id, sizeof(id));
+    return Q3_OK;
+}
+
+int q3_engine_attach_nccl(q3_engine* e, const void* id_in) {
+    Q3_CHECK(e && id_in, "null argument");
+    if (e->world == 1) return Q3_OK;
+    Q3_CUDA(cudaSetDevice(e->device));
+    ncclUniqueId id;
+    std::memcpy(&id, id_in, sizeof(id));
+    ncclResult_t nr = ncclCommInitRank(&e->comm, e->world, id, e->rank);
+    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(nr));
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;
+    }
+    return Q3_OK;
+}
+
+}  // extern "C"

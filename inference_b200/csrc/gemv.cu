@@ -1,0 +1,447 @@
+// gemv.cu -- batch-1 BF16 GEMV for B200, the weight-streaming kernel of the
+// decode step.  Replaces the reference's cuBLAS call
+// (src/lib/backend/cuda/kernels/matmul.cuh:8-18) and fuses the small ops
+// around each matmul of Model::forward (src/lib/model/qwen3/qwen3.hpp:131-166).
+//
+// Design (one CTA per SM, 8 consumer warps + 1 producer warp):
+//   * The CTA owns a contiguous band of weight rows.  The producer lane streams
+//     it as tiles of rb rows x kc columns with 1-D TMA bulk copies
+//     (cp.async.bulk, one per row segment, L2 evict-first) into a ring of
+//     shared-memory stages guarded by full/empty mbarriers.
+//   * Weights do not depend on the previous kernel, so the producer starts
+//     before griddepcontrol.wait: with programmatic dependent launch the next
+//     GEMV's weight prefetch overlaps the tail of the current kernel.
+//   * Consumers build x in shared memory (the prologue: copy, RMSNorm,
+//     embedding lookup, residual add), then each warp dots its row segment
+//     with 16-byte vectors, fp32 FMA, warp-shuffle reduction, and a fixed-order
+//     cross-warp sum, so results are deterministic.
+//   * Epilogues apply the reference's BF16 rounding points exactly: matmul
+//     output rounded to BF16, then the following op on the rounded value.
+#include <algorithm>
+
+#include "kernels.cuh"
+
+namespace q3 {
+
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 32;
+constexpr int kStageTarget = 16384;
+constexpr size_t kSmemBudget = 110 * 1024;
+constexpr int kMaxDynSmem = 200 * 1024;
+
+struct SmemLayout {
+    size_t stage_off, x_off, bar_off, red_off, misc_off, total;
+};
+
+__host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K) {
+    SmemLayout L;
+    const size_t stage_bytes = static_cast<size_t>(p.rb) * p.kc * 2;
+    L.stage_off = 0;
+    L.x_off = stage_bytes * p.stages;
+    L.bar_off = (L.x_off + static_cast<size_t>(K) * 2 + 15) / 16 * 16;
+    L.red_off = L.bar_off + 2 * static_cast<size_t>(p.stages) * 8;
+    L.misc_off = L.red_off + 2 * 8 * 8 * sizeof(float);
+    L.total = L.misc_off + 128;
+    return L;
+}
+
+__device__ __forceinline__ size_t kv_slot(const GemvArgs& a, int pos, int head) {
+    const int page = a.page_table[pos / a.page_size];
+    return ((static_cast<size_t>(page) * a.kv_heads_local + head) * a.page_size + (pos % a.page_size)) * 128;
+}
+
+// Sum of per-thread values over the 256 consumer threads, fixed order.
+__device__ __forceinline__ float consumers_sum(float v, float* scratch8) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_sum(v);
+    if (lane == 0) scratch8[warp] = v;
+    named_bar(1, kConsumers);
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) t += scratch8[w];
+    named_bar(1, kConsumers);
+    return t;
+}
+
+template <int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const GemvPlan& p = a.plan;
+    const SmemLayout L = smem_layout(p, a.K);
+    uint8_t* stage_base = smem + L.stage_off;
+    bf16* xs = reinterpret_cast<bf16*>(smem + L.x_off);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+    uint64_t* empty = full + p.stages;
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
+    float* misc = reinterpret_cast<float*>(smem + L.misc_off);
+    unsigned long long* cta_key = reinterpret_cast<unsigned long long*>(misc + 16);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int units = a.N / p.row_gran;
+    const int u0 = static_cast<int>(static_cast<long long>(blockIdx.x) * units / gridDim.x);
+    const int u1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * units / gridDim.x);
+    const int r0 = u0 * p.row_gran, r1 = u1 * p.row_gran;
+    const int nrb = (r1 - r0 + p.rb - 1) / p.rb;
+    const int ntiles = nrb * p.ncb;
+    const uint32_t kc_bytes = static_cast<uint32_t>(p.kc) * 2;
+    const size_t stage_bytes = static_cast<size_t>(p.rb) * kc_bytes;
+
+    if (tid == 0) {
+        for (int s = 0; s < p.stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        *cta_key = 0ull;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    // ------------------------------------------------------------ producer
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();
+            for (int t = 0; t < ntiles; ++t) {
+                const int s = t % p.stages;
+                if (t >= p.stages &&
+                    !mbar_wait(&empty[s], ((t / p.stages) - 1) & 1, a.err, DEV_TMA_WAIT_TIMEOUT))
+                    break;
+                const int rbk = t / p.ncb, cb = t % p.ncb;
+                const int row = r0 + rbk * p.rb;
+                const int rows = min(p.rb, r1 - row);
+                mbar_arrive_expect_tx(&full[s], rows * kc_bytes);
+                uint8_t* dst = stage_base + s * stage_bytes;
+                const bf16* src = a.W + static_cast<size_t>(row) * a.K + static_cast<size_t>(cb) * p.kc;
+                for (int r = 0; r < rows; ++r)
+                    bulk_g2s(dst + r * kc_bytes, src + static_cast<size_t>(r) * a.K, kc_bytes, &full[s], pol);
+            }
+        }
+        return;
+    }
+
+    // ------------------------------------------------------------ consumers
+    pdl_wait();
+    int pos = 0;
+    if (EPI == EPI_QKV || PRO == PRO_EMBED_NORM) {
+        pos = *a.pos_ptr;
+        if (pos < 0 || pos >= a.capacity) {
+            if (tid == 0) record_error(a.err, DEV_BAD_POSITION);
+            pos = 0;
+        }
+    }
+
+    // ---- prologue: x in shared memory
+    const int kv8 = a.K / 8;
+    if constexpr (PRO == PRO_PLAIN) {
+        const uint4* src = reinterpret_cast<const uint4*>(a.x);
+        uint4* dst = reinterpret_cast<uint4*>(xs);
+        for (int i = tid; i < kv8; i += kConsumers) dst[i] = src[i];
+    } else {
+        const bf16* src = a.hs;
+        if constexpr (PRO == PRO_EMBED_NORM) {
+            int token;
+            const int nf = *a.n_forced;
+            uint64_t best = 0;
+            for (int r = 0; r < a.n_keys; ++r) best = max(best, static_cast<uint64_t>(a.keys[r]));
+            const uint32_t greedy = argmax_key_index(best);
+            token = (pos < nf) ? a.tokens[pos] : static_cast<int>(greedy);
+            if (token < 0 || token >= a.vocab) {
+                if (tid == 0) record_error(a.err, DEV_BAD_TOKEN);
+                token = 0;
+            }
+            if (blockIdx.x == 0 && tid == 0) {
+                if (pos >= 1) a.argmax_hist[pos - 1] = static_cast<int32_t>(greedy);
+                if (pos >= nf) a.tokens[pos] = token;
+            }
+            src = a.embed + static_cast<size_t>(token) * a.K;
+        }
+        float ss = 0.f;
+        for (int i = tid; i < kv8; i += kConsumers) {
+            uint4 h = reinterpret_cast<const uint4*>(src)[i];
+            if constexpr (PRO == PRO_NORM_F32) {
+                const float4 v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
+                const float4 v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
+                ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
+                ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
+            } else if constexpr (PRO == PRO_RESID_NORM) {
+                const float4 v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
+                const float4 v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
+                const float rs[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float a0 = bf_lo(hw[j]) + round_bf(rs[2 * j]);
+                    const float a1 = bf_hi(hw[j]) + round_bf(rs[2 * j + 1]);
+                    const bf16 b0 = f2bf(a0), b1 = f2bf(a1);
+                    const float s0 = a.ss_unrounded ? a0 : bf2f(b0);
+                    const float s1 = a.ss_unrounded ? a1 : bf2f(b1);
+                    ss += s0 * s0 + s1 * s1;
+                    hw[j] = static_cast<uint32_t>(__bfloat16_as_ushort(b0)) |
+                            (static_cast<uint32_t>(__bfloat16_as_ushort(b1)) << 16);
+                }
+            } else {
+                const uint32_t* hw = reinterpret_cast<const uint32_t*>(&h);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const float lo = bf_lo(hw[j]), hi = bf_hi(hw[j]);
+                    ss += lo * lo + hi * hi;
+                }
+            }
+            reinterpret_cast<uint4*>(xs)[i] = h;
+            if constexpr (PRO == PRO_EMBED_NORM || PRO == PRO_RESID_NORM) {
+                if (blockIdx.x == 0) reinterpret_cast<uint4*>(a.hs_out)[i] = h;
+            }
+        }
+        ss = consumers_sum(ss, misc);
+        const float scale = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
+        for (int i = tid; i < kv8; i += kConsumers) {
+            uint4 h = reinterpret_cast<uint4*>(xs)[i];
+            const uint4 w = reinterpret_cast<const uint4*>(a.norm_w)[i];
+            uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
+            const uint32_t* ww = reinterpret_cast<const uint32_t*>(&w);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const bf16 b0 = f2bf(bf_lo(hw[j]) * scale * bf_lo(ww[j]));
+                const bf16 b1 = f2bf(bf_hi(hw[j]) * scale * bf_hi(ww[j]));
+                hw[j] = static_cast<uint32_t>(__bfloat16_as_ushort(b0)) |
+                        (static_cast<uint32_t>(__bfloat16_as_ushort(b1)) << 16);
+            }
+            reinterpret_cast<uint4*>(xs)[i] = h;
+        }
+    }
+    named_bar(1, kConsumers);
+
+    // ---- main loop
+    const int wpr = kConsumerWarps / p.rb;
+    const int tr = warp / wpr, part = warp % wpr;
+    const int nv = p.kc / 8;
+    const int vstep = wpr * 32;
+    float acc0 = 0.f, acc1 = 0.f;
+    uint64_t best_key = 0;
+    bool failed = false;
+
+    for (int t = 0; t < ntiles; ++t) {
+        const int s = t % p.stages;
+        const bool ok = !failed && mbar_wait(&full[s], (t / p.stages) & 1, a.err, DEV_TMA_WAIT_TIMEOUT);
+        failed = failed || !ok;
+        const int rbk = t / p.ncb, cb = t % p.ncb;
+        const int row = r0 + rbk * p.rb;
+        const int rows = min(p.rb, r1 - row);
+        if (ok && tr < rows) {
+            const uint4* wv = reinterpret_cast<const uint4*>(stage_base + s * stage_bytes + tr * kc_bytes);
+            const uint4* xv = reinterpret_cast<const uint4*>(xs + static_cast<size_t>(cb) * p.kc);
+            int v = part * 32 + lane;
+            for (; v + vstep < nv; v += 2 * vstep) {
+                acc0 = dot8(wv[v], xv[v], acc0);
+                acc1 = dot8(wv[v + vstep], xv[v + vstep], acc1);
+            }
+            if (v < nv) acc0 = dot8(wv[v], xv[v], acc0);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+
+        if (cb == p.ncb - 1) {
+            const float wsum = warp_sum(acc0 + acc1);
+            acc0 = acc1 = 0.f;
+            float* rd = red + (rbk & 1) * 64;
+            if (lane == 0) rd[tr * 8 + part] = wsum;
+            named_bar(1, kConsumers);
+            if constexpr (EPI == EPI_SWIGLU) {
+                if (tid < rows / 2) {
+                    float g = 0.f, u = 0.f;
+                    for (int q = 0; q < wpr; ++q) g += rd[(2 * tid) * 8 + q];
+                    for (int q = 0; q < wpr; ++q) u += rd[(2 * tid + 1) * 8 + q];
+                    // qwen3.hpp:154-156 -> silu.cuh:18-20 on the BF16-rounded matmul outputs
+                    const float gv = round_bf(g), uv = round_bf(u);
+                    const float silu = gv / (1.0f + expf(-gv));
+                    a.y[(row >> 1) + tid] = f2bf(silu * uv);
+                }
+            } else {
+                if (tid < rows) {
+                    float r = 0.f;
+                    for (int q = 0; q < wpr; ++q) r += rd[tid * 8 + q];
+                    const int gr = row + tid;
+                    if constexpr (EPI == EPI_STORE) {
+                        a.y[gr] = f2bf(r);
+                    } else if constexpr (EPI == EPI_PARTIAL) {
+                        a.yf[gr] = r;
+                    } else if constexpr (EPI == EPI_RESID) {
+                        // qwen3.hpp:158-159: hidden = bf16(down); hs = bf16(hs + hidden)
+                        a.hs[gr] = f2bf(bf2f(a.hs[gr]) + round_bf(r));
+                    } else if constexpr (EPI == EPI_RESID_F32) {
+                        // qwen3.hpp:151-152 -> rmsnorm.cuh:58-60
+                        const float v = bf2f(a.hs[gr]) + round_bf(r);
+                        a.hs[gr] = f2bf(v);
+                        a.vsum_out[gr] = v;
+                    } else if constexpr (EPI == EPI_QKV) {
+                        const bf16 b = f2bf(r);
+                        if (gr < a.q_rows) {
+                            a.q_out[gr] = b;
+                        } else if (gr < a.q_rows + a.kv_rows) {
+                            const int k = gr - a.q_rows;
+                            a.k_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
+                        } else {
+                            const int k = gr - a.q_rows - a.kv_rows;
+                            a.v_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
+                        }
+                    } else if constexpr (EPI == EPI_ARGMAX) {
+                        const bf16 b = f2bf(r);
+                        a.y[gr] = b;
+                        best_key = max(best_key, argmax_key(bf2f(b), static_cast<uint32_t>(gr) + a.vocab_offset));
+                    }
+                }
+            }
+        }
+    }
+
+    // ---- post-loop finishers
+    if constexpr (EPI == EPI_QKV) {
+        // qk_norm_rope (qk_norm_rope.cuh:14-90) for every q / k head whose last
+        // rows this CTA produced: the CTA that completes a head normalises it.
+        __threadfence();
+        named_bar(1, kConsumers);
+        if (warp == 0) {
+            const int nqk = a.q_rows + a.kv_rows;
+            const int hi_row = min(r1, nqk);
+            for (int h = r0 / 128; h * 128 < hi_row; ++h) {
+                const int lo = max(r0, h * 128), hi = min(hi_row, (h + 1) * 128);
+                if (hi <= lo) continue;
+                uint32_t old = 0;
+                if (lane == 0) old = atomicAdd(&a.head_counters[h], static_cast<uint32_t>(hi - lo));
+                old = __shfl_sync(0xffffffffu, old, 0);
+                if (old + static_cast<uint32_t>(hi - lo) != 128u) continue;
+                __threadfence();
+                const bool is_q = h * 128 < a.q_rows;
+                bf16* base = is_q ? a.q_out + h * 128 : a.k_pages + kv_slot(a, pos, h - a.q_rows / 128);
+                const bf16* nw = is_q ? a.q_norm : a.k_norm;
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    v[j] = __uint_as_float(static_cast<uint32_t>(
+                                               __ldcg(reinterpret_cast<const unsigned short*>(base) + lane + 32 * j))
+                                           << 16);
+                const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+                const float scale = 1.0f / sqrtf(ss / 128.0f + a.eps);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const int i = lane + 32 * j;
+                    const float c = a.rope_cos[static_cast<size_t>(pos) * 64 + i];
+                    const float sn = a.rope_sin[static_cast<size_t>(pos) * 64 + i];
+                    const float x = v[j] * bf2f(nw[i]) * scale;
+                    const float y = v[j + 2] * bf2f(nw[i + 64]) * scale;
+                    base[i] = f2bf(x * c - y * sn);
+                    base[i + 64] = f2bf(y * c + x * sn);
+                }
+                if (lane == 0) a.head_counters[h] = 0u;
+            }
+        }
+    }
+    if constexpr (EPI == EPI_ARGMAX) {
+        if (best_key) atomicMax(cta_key, static_cast<unsigned long long>(best_key));
+        named_bar(1, kConsumers);
+        if (tid == 0) {
+            atomicMax(reinterpret_cast<unsigned long long*>(a.key_slot), *cta_key);
+            __threadfence();
+            const uint32_t old = atomicAdd(a.done_counter, 1u);
+            if (old == gridDim.x - 1) {
+                __threadfence();
+                const unsigned long long k = atomicExch(reinterpret_cast<unsigned long long*>(a.key_slot), 0ull);
+                *a.key_out = k;
+                *a.done_counter = 0u;
+                atomicAdd(a.pos_inc, 1);
+            }
+        }
+    }
+}
+
+template <int PRO, int EPI>
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
+    auto* fn = gemv_kernel<PRO, EPI>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.plan.grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = a.plan.smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, fn, a);
+}
+
+}  // namespace
+
+cudaError_t configure_gemv_kernels() {
+    const void* fns[] = {
+        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_STORE>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_RESID>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_RESID_F32>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_PARTIAL>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM, EPI_STORE>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM, EPI_QKV>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_EMBED_NORM, EPI_QKV>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_RESID_NORM, EPI_QKV>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM_F32, EPI_SWIGLU>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_RESID_NORM, EPI_SWIGLU>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM, EPI_ARGMAX>),
+        reinterpret_cast<const void*>(gemv_kernel<PRO_RESID_NORM, EPI_ARGMAX>),
+    };
+    for (const void* f : fns) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+GemvPlan plan_gemv(int N, int K, int epi, int sms) {
+    GemvPlan p{};
+    p.row_gran = (epi == EPI_SWIGLU) ? 2 : 1;
+    const int row_bytes = K * 2;
+    const int min_rb = (epi == EPI_SWIGLU) ? 2 : 1;
+    if (row_bytes * min_rb <= kStageTarget) {
+        int rb = 8;
+        while (rb > min_rb && rb * row_bytes > kStageTarget) rb >>= 1;
+        p.rb = rb;
+        p.kc = K;
+        p.ncb = 1;
+    } else {
+        p.rb = min_rb;
+        int ncb = (row_bytes * p.rb + kStageTarget - 1) / kStageTarget;
+        while (K % (8 * ncb) != 0) ++ncb;
+        p.ncb = ncb;
+        p.kc = K / ncb;
+    }
+    const size_t stage_bytes = static_cast<size_t>(p.rb) * p.kc * 2;
+    const size_t fixed = (static_cast<size_t>(K) * 2 + 15) / 16 * 16 + 1024;
+    long st = kSmemBudget > fixed ? static_cast<long>((kSmemBudget - fixed) / stage_bytes) : 2;
+    p.stages = static_cast<int>(std::min(8L, std::max(2L, st)));
+    const int units = N / p.row_gran;
+    p.grid = std::max(1, std::min(sms, units));
+    p.smem = smem_layout(p, K).total;
+    return p;
+}
+
+cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl) {
+#define Q3_CASE(P, E) \
+    if (pro == P && epi == E) return launch_t<P, E>(a, s, pdl);
+    Q3_CASE(PRO_PLAIN, EPI_STORE)
+    Q3_CASE(PRO_PLAIN, EPI_RESID)
+    Q3_CASE(PRO_PLAIN, EPI_RESID_F32)
+    Q3_CASE(PRO_PLAIN, EPI_PARTIAL)
+    Q3_CASE(PRO_NORM, EPI_STORE)
+    Q3_CASE(PRO_NORM, EPI_QKV)
+    Q3_CASE(PRO_EMBED_NORM, EPI_QKV)
+    Q3_CASE(PRO_RESID_NORM, EPI_QKV)
+    Q3_CASE(PRO_NORM_F32, EPI_SWIGLU)
+    Q3_CASE(PRO_RESID_NORM, EPI_SWIGLU)
+    Q3_CASE(PRO_NORM, EPI_ARGMAX)
+    Q3_CASE(PRO_RESID_NORM, EPI_ARGMAX)
+#undef Q3_CASE
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace q3

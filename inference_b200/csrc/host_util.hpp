@@ -1,0 +1,39 @@
+// host_util.hpp -- status codes and the thread-local error message behind
+// q3_last_error().
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <string>
+
+#include "../../include/q3_sm100a.h"
+
+namespace q3 {
+
+void set_error(const std::string& msg);
+
+struct Failure {
+    int status;
+};
+
+inline int fail(int status, const std::string& msg) {
+    set_error(msg);
+    return status;
+}
+
+#define Q3_CUDA(call)                                                                                         \
+    do {                                                                                                      \
+        cudaError_t e_ = (call);                                                                              \
+        if (e_ != cudaSuccess) {                                                                              \
+            ::q3::set_error(std::string(#call) + ": " + cudaGetErrorString(e_));                              \
+            return Q3_ERR_CUDA;                                                                               \
+        }                                                                                                     \
+    } while (0)
+
+#define Q3_CHECK(cond, msg)                                \
+    do {                                                   \
+        if (!(cond)) return ::q3::fail(Q3_ERR_INVALID, msg); \
+    } while (0)
+
+}  // namespace q3

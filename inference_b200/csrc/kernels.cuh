@@ -1,0 +1,138 @@
+// kernels.cuh -- argument blocks and host launchers of the sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace q3 {
+
+// ---------------------------------------------------------------- GEMV
+// y = W x for one token, W row-major [N, K] BF16, fp32 accumulation.
+// The prologue builds x in shared memory; the epilogue consumes each row sum.
+enum GemvPro : int {
+    PRO_PLAIN = 0,       // x = src (BF16 vector of K)
+    PRO_NORM = 1,        // x = rmsnorm(hs) over rounded hs
+    PRO_NORM_F32 = 2,    // x = rmsnorm with sum of squares over fp32 vsum, values bf16(vsum)
+    PRO_EMBED_NORM = 3,  // token -> hs = embed[token]; x = rmsnorm(hs)
+    PRO_RESID_NORM = 4,  // hs' = bf16(hs + bf16(reduced)); x = rmsnorm(hs') (tensor parallel)
+};
+enum GemvEpi : int {
+    EPI_STORE = 0,      // y[r] = bf16(acc)
+    EPI_RESID = 1,      // hs[r] = bf16(hs[r] + bf16(acc))
+    EPI_RESID_F32 = 2,  // v = hs[r] + bf16(acc); hs[r] = bf16(v); vsum[r] = v
+    EPI_SWIGLU = 3,     // rows (2j, 2j+1) = (gate_j, up_j): y[j] = bf16(silu(bf16 g) * bf16 u)
+    EPI_QKV = 4,        // q / k / v rows to q_out and the paged KV slot; q,k heads then norm + RoPE
+    EPI_ARGMAX = 5,     // logits[r] = bf16(acc); running (max, first index) across the grid
+    EPI_PARTIAL = 6,    // yf[r] = acc (fp32 partial for a tensor-parallel reduction)
+};
+
+struct GemvPlan {
+    int rb;        // rows per tile: 1, 2, 4 or 8
+    int kc;        // columns per tile (multiple of 8, divides K)
+    int ncb;       // column tiles per row block (K / kc)
+    int stages;    // shared-memory ring depth
+    int grid;      // CTAs
+    int row_gran;  // rows assigned to CTAs in units of this many (2 for SWIGLU)
+    size_t smem;   // dynamic shared memory bytes
+};
+
+struct GemvArgs {
+    const bf16* W;
+    int N, K;
+    GemvPlan plan;
+    // ---- prologue
+    const bf16* x;             // PRO_PLAIN source
+    bf16* hs;                  // residual stream read by PRO_NORM*/PRO_RESID_NORM, updated by EPI_RESID*
+    bf16* hs_out;              // PRO_EMBED_NORM / PRO_RESID_NORM: residual written by CTA 0
+    const bf16* norm_w;        // RMSNorm weight [K]
+    float eps;
+    const float* vsum;         // PRO_NORM_F32 fp32 sums; PRO_RESID_NORM: fp32 reduced partials
+    int ss_unrounded;          // PRO_RESID_NORM: sum of squares over unrounded (rmsnorm_add) values
+    const bf16* embed;         // PRO_EMBED_NORM table [vocab, K]
+    int vocab;                 // full vocabulary
+    int32_t* tokens;           // tokens by position (forced prefix + greedy)
+    int32_t* argmax_hist;      // greedy argmax by position
+    const int32_t* n_forced;   // forced prefix length
+    const uint64_t* keys;      // per-rank argmax keys of the previous step
+    int n_keys;
+    const int32_t* pos_ptr;    // current position
+    int capacity;
+    // ---- epilogue
+    bf16* y;
+    float* yf;
+    float* vsum_out;
+    // EPI_QKV
+    int q_rows, kv_rows, head_dim, kv_heads_local, page_size;
+    bf16* q_out;
+    bf16* k_pages;
+    bf16* v_pages;
+    const int32_t* page_table;
+    const bf16* q_norm;
+    const bf16* k_norm;
+    const float* rope_cos;
+    const float* rope_sin;
+    uint32_t* head_counters;
+    // EPI_ARGMAX
+    uint64_t* key_slot;
+    uint32_t* done_counter;
+    uint64_t* key_out;
+    int32_t* pos_inc;          // incremented once by the last CTA
+    uint32_t vocab_offset;
+    // ---- errors
+    uint32_t* err;
+};
+
+GemvPlan plan_gemv(int N, int K, int epi, int num_sms);
+cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+    const bf16* q;            // [q_heads, 128]
+    const bf16* k;            // paged: [pages, kvh, page, 128]; flat: [capacity, kvh, 128]
+    const bf16* v;
+    const int32_t* page_table;
+    bf16* out;                // [q_heads, 128]
+    int q_heads, kv_heads, page_size;
+    int paged;                // 1 = paged layout, 0 = reference layout
+    const int32_t* pos_ptr;   // device position (or null -> pos_host)
+    int pos_host;
+    int splits;               // grid.y
+    float* part_ml;           // [kvh, splits, G, 2]
+    float* part_acc;          // [kvh, splits, G, 128]
+    uint32_t* counters;       // [kvh]
+    uint32_t* err;
+};
+int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
+size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
+cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// ---------------------------------------------------------------- small ops
+cudaError_t launch_embedding(const bf16* table, int hidden, uint32_t token, bf16* out, cudaStream_t s);
+cudaError_t launch_rmsnorm(const bf16* x, const bf16* w, bf16* out, int n, float eps, cudaStream_t s);
+cudaError_t launch_rmsnorm_add(bf16* res, const bf16* upd, const bf16* w, bf16* out, int n, float eps,
+                               cudaStream_t s);
+cudaError_t launch_qk_norm_rope(bf16* q, bf16* k, const bf16* qn, const bf16* kn, const float* cos_t,
+                                const float* sin_t, int q_heads, int kv_heads, int pos, float eps, cudaStream_t s);
+cudaError_t launch_rope(bf16* v, const float* cos_t, const float* sin_t, int heads, int head_dim, int pos,
+                        cudaStream_t s);
+cudaError_t launch_add(const bf16* a, const bf16* b, bf16* out, size_t n, cudaStream_t s);
+cudaError_t launch_silu_mul(const bf16* g, const bf16* u, bf16* out, size_t n, cudaStream_t s);
+cudaError_t launch_argmax(const bf16* logits, size_t n, uint32_t* index, uint64_t* scratch, cudaStream_t s);
+cudaError_t launch_fill_normal(bf16* dst, uint64_t seed, uint64_t tensor_id, size_t rows, size_t cols, size_t row0,
+                               size_t col0, size_t full_cols, size_t dst_row_stride, cudaStream_t s);
+cudaError_t launch_fill_const(bf16* dst, size_t n, float value, cudaStream_t s);
+cudaError_t launch_resolve_tokens(const uint64_t* keys, int n_keys, int32_t* tokens, int32_t* argmax_hist,
+                                  const int32_t* pos_ptr, const int32_t* n_forced, int vocab, uint32_t* err,
+                                  cudaStream_t s);
+
+uint64_t seed_key(uint64_t seed);
+// Shared-memory opt-in of every kernel instantiation on the current device;
+// called once per device before any launch (and before graph capture).
+cudaError_t configure_kernels();
+cudaError_t configure_gemv_kernels();
+cudaError_t configure_attention_kernels();
+int num_sms(int device);
+
+}  // namespace q3

@@ -1,0 +1,142 @@
+"""Python handle on the decode engine (q3_engine_* in include/q3_sm100a.h).
+
+Mirrors the reference's Generator / Model / KVCache surface
+(src/lib/inference/generator.cpp:26-63, src/lib/model/qwen3/qwen3.hpp:131-173,
+src/lib/kv_cache/kv_cache.hpp:6-29): ``forward`` is Model::forward with a
+host round trip, ``generate`` is Generator::generate on token ids, ``reset``
+is KVCache::reset.  ``step`` is the device-resident loop used for timing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ._lib import ModelConfig, check, lib
+from .config import Qwen3Config
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class Engine:
+    def __init__(self, cfg: Qwen3Config, capacity: int, device: int = 0, tp_rank: int = 0, tp_size: int = 1):
+        self.cfg, self.capacity, self.tp_rank, self.tp_size = cfg, capacity, tp_rank, tp_size
+        mc = ModelConfig(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.vocab,
+                         int(cfg.tied), cfg.eps, cfg.theta, capacity, cfg.eos)
+        h = C.c_void_p()
+        check(lib().q3_engine_create(C.byref(mc), device, tp_rank, tp_size, C.byref(h)))
+        self.h = h
+
+    # ---- lifecycle
+    def close(self):
+        if getattr(self, "h", None):
+            lib().q3_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # ---- weights
+    def init_synthetic(self, seed: int = 0):
+        check(lib().q3_engine_init_synthetic(self.h, seed))
+
+    def set_weight(self, name: str, w: np.ndarray):
+        w = np.ascontiguousarray(w, dtype=np.uint16)
+        rows, cols = (w.shape[0], w.shape[1]) if w.ndim == 2 else (1, w.shape[0])
+        check(lib().q3_engine_set_weight(self.h, name.encode(), _ptr(w), rows, cols))
+
+    @staticmethod
+    def nccl_unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        check(lib().q3_nccl_unique_id(buf))
+        return buf.raw
+
+    def attach_nccl(self, uid: bytes):
+        buf = C.create_string_buffer(bytes(uid), 128)
+        check(lib().q3_engine_attach_nccl(self.h, buf))
+
+    # ---- decode
+    def reset(self):
+        check(lib().q3_engine_reset(self.h))
+
+    def set_tokens(self, ids):
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        check(lib().q3_engine_set_tokens(self.h, _ptr(ids), ids.size))
+
+    def step(self, n: int = 1):
+        check(lib().q3_engine_step(self.h, n))
+
+    def sync(self):
+        check(lib().q3_engine_sync(self.h))
+
+    def forward(self, token: int) -> int:
+        out = C.c_uint32()
+        check(lib().q3_engine_forward(self.h, token, C.byref(out)))
+        return int(out.value)
+
+    def generate(self, prompt, max_new: int, stop_at_eos: bool = False) -> np.ndarray:
+        prompt = np.ascontiguousarray(prompt, dtype=np.uint32)
+        out = np.empty(max(1, max_new), np.uint32)
+        n = C.c_size_t()
+        check(lib().q3_engine_generate(self.h, _ptr(prompt), prompt.size, max_new, int(stop_at_eos), _ptr(out),
+                                       C.byref(n)))
+        return out[: n.value].copy()
+
+    def set_position(self, pos: int):
+        check(lib().q3_engine_set_position(self.h, pos))
+
+    def fill_kv(self, upto: int, seed: int = 7):
+        check(lib().q3_engine_fill_kv(self.h, upto, seed))
+
+    # ---- state
+    @property
+    def position(self) -> int:
+        p = C.c_size_t()
+        check(lib().q3_engine_position(self.h, C.byref(p)))
+        return int(p.value)
+
+    def logits(self) -> np.ndarray:
+        out = np.empty(self.cfg.vocab // self.tp_size, np.uint16)
+        check(lib().q3_engine_logits(self.h, _ptr(out)))
+        return out
+
+    def argmax_history(self, n: int) -> np.ndarray:
+        out = np.empty(n, np.uint32)
+        check(lib().q3_engine_argmax_history(self.h, _ptr(out), n))
+        return out
+
+    def kv_slot(self, layer: int, pos: int):
+        kvh = self.cfg.kv_heads // self.tp_size
+        k = np.empty((kvh, 128), np.uint16)
+        v = np.empty((kvh, 128), np.uint16)
+        check(lib().q3_engine_kv_slot(self.h, layer, pos, _ptr(k), _ptr(v)))
+        return k, v
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        check(lib().q3_engine_stream(self.h, C.byref(s)))
+        return s.value or 0
+
+    def weight_bytes(self) -> int:
+        return int(lib().q3_engine_weight_bytes(self.h))
+
+    def kv_bytes_per_position(self) -> int:
+        return int(lib().q3_engine_kv_bytes_per_position(self.h))
+
+    def profile_step(self, kernel_class: int = 0):
+        """One eager step with CUDA events around each kernel of the class
+        (0 GEMVs, 1 attention, 2 all): (milliseconds, launches, bytes)."""
+        ms, n, b = C.c_double(), C.c_size_t(), C.c_double()
+        check(lib().q3_engine_profile_step(self.h, kernel_class, C.byref(ms), C.byref(n), C.byref(b)))
+        return ms.value, int(n.value), b.value

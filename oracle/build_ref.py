@@ -89,7 +89,6 @@ def build_ref_cpu(reference: str, force: bool = False) -> str | None:
 def build_ref_cuda(reference: str, force: bool = False) -> str | None:
     lib = os.path.join(reference, "src", "lib")
     backend_cu = os.path.join(lib, "backend", "cuda", "backend.cu")
-    backend_cpp = os.path.join(lib, "backend", "cpu", "backend.cpp")
     nl = _nlohmann_include()
     cccl = _cccl3_includes()
     if not os.path.isfile(backend_cu) or nl is None or cccl is None or shutil.which("nvcc") is None:
@@ -103,24 +102,21 @@ def build_ref_cuda(reference: str, force: bool = False) -> str | None:
         os.makedirs(obj_dir, exist_ok=True)
         inc = []
         for p in cccl:
-            inc += ["-isystem", p]
+            inc += ["-I", p]
         common = ["-std=c++20", "-O3", "-gencode", "arch=compute_100a,code=sm_100a", "--expt-relaxed-constexpr",
                   "--extended-lambda", "-Xcompiler", "-fPIC", "-I", lib, "-I", nl] + inc
-        # The harness is plain C++ but includes CUDA headers; compile it with
-        # nvcc as a .cu so the CCCL 3 headers see the same configuration.
-        harness_cu = os.path.join(obj_dir, "ref_harness_cuda.cu")
-        with open(harness_cu, "w") as f:
-            f.write('#include "%s"\n' % harness)
         o1 = os.path.join(obj_dir, "backend_cuda.o")
         o2 = os.path.join(obj_dir, "harness_cuda.o")
+        # backend.cu is the reference's only CUDA translation unit (C++20,
+        # src/lib/backend/cuda/CMakeLists.txt:18-22); the model code is host
+        # C++23 (std::views::zip), compiled by g++ as the reference's CMake does.
         _run(["nvcc"] + common + ["-c", backend_cu, "-o", o1])
-        _run(["nvcc"] + common + ["-DREF_CUDA", "-c", harness_cu, "-o", o2])
-        # The CUDA harness also instantiates the CPU backend singleton
-        # (tensor.hpp's Storage frees through Backend&, and the harness never
-        # calls it), so link only the CUDA backend and the harness.
-        _run(["nvcc", "-shared", "-gencode", "arch=compute_100a,code=sm_100a", o1, o2, "-o", out,
-              "-L", HERE, "-lq3_oracle", "-Xlinker", "-rpath,$ORIGIN/..", "-lcublas", "-lcudart"])
-        del backend_cpp
+        cuda_inc = os.path.join(os.path.dirname(os.path.dirname(shutil.which("nvcc"))), "include")
+        _run(["g++", "-std=c++23", "-O2", "-fPIC", "-DREF_CUDA", "-I", lib, "-I", nl, "-I", cuda_inc, "-c", harness,
+              "-o", o2])
+        cuda_lib = os.path.join(os.path.dirname(cuda_inc), "lib64")
+        _run(["g++", "-shared", o1, o2, "-o", out, "-L", HERE, "-lq3_oracle", "-Wl,-rpath,$ORIGIN/..",
+              "-L", cuda_lib, "-lcublas", "-lcudart"])
     return out
 
 

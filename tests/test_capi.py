@@ -1,0 +1,68 @@
+"""CPU-side checks of the C ABI: the library loads, exports every symbol
+include/q3_sm100a.h declares, and rejects bad arguments before touching a
+GPU.  No compute calls here."""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    src = open(os.path.join(ROOT, "include", "q3_sm100a.h")).read()
+    return sorted(set(re.findall(r"Q3_API\s+[\w\s\*]+?\b(q3_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from inference_b200 import lib
+    from inference_b200._lib import SIGNATURES
+
+    L = lib()
+    syms = header_symbols()
+    assert len(syms) >= 30
+    for s in syms:
+        assert hasattr(L, s), s
+        assert s in SIGNATURES, f"{s} has no ctypes signature"
+    assert set(SIGNATURES) == set(syms)
+
+
+def test_invalid_arguments_fail_before_the_gpu():
+    from inference_b200 import Q3Error, lib
+    from inference_b200._lib import ModelConfig, check
+
+    L = lib()
+    assert L.q3_gemv(None, None, None, 4, 8, None) == 1
+    assert b"null" in L.q3_last_error()
+    x = C.c_void_p(16)  # never dereferenced: validation fails first
+    assert L.q3_gemv(x, x, x, 4, 12, None) == 1  # n_in % 8
+    assert L.q3_qk_norm_rope(x, x, x, x, x, x, 8, 8, 64, 0, 1e-6, None) == 3  # head_dim 64 unsupported
+    assert L.q3_attention(x, x, x, x, 12, 8, 128, 5, x, 1 << 20, None) == 1  # 12 % 8
+    bad = ModelConfig(1024, 3072, 28, 16, 8, 64, 151936, 1, 1e-6, 1e6, 64, 0)
+    h = C.c_void_p()
+    assert L.q3_engine_create(C.byref(bad), 0, 0, 1, C.byref(h)) == 3
+    odd = ModelConfig(1024, 3072, 28, 16, 8, 128, 151936, 1, 1e-6, 1e6, 64, 0)
+    assert L.q3_engine_create(C.byref(odd), 0, 0, 3, C.byref(h)) == 1  # 8 kv heads over 3 ranks
+    with pytest.raises(Q3Error):
+        check(1)
+
+
+def test_prompt_ids_and_rope_tables_match_oracle(oracle):
+    from inference_b200 import prompt_ids, rope_tables
+
+    np.testing.assert_array_equal(prompt_ids(4096, seed=1), oracle.prompt_ids(4096, seed=1))
+    c1, s1 = rope_tables(8192)
+    c2, s2 = oracle.rope_cache(8192)
+    np.testing.assert_array_equal(c1, c2)
+    np.testing.assert_array_equal(s1, s2)
+
+
+def test_workspace_size_is_monotone():
+    from inference_b200 import lib
+
+    L = lib()
+    sizes = [L.q3_attention_workspace_bytes(32, 8, p) for p in (0, 63, 64, 1000, 8191, 100000)]
+    assert all(a <= b for a, b in zip(sizes, sizes[1:]))
+    assert L.q3_attention_workspace_bytes(12, 8, 100) == 0
