@@ -84,7 +84,9 @@ Q3_API int q3_qk_norm_rope(uint16_t* q_dev, uint16_t* k_dev, const uint16_t* q_n
  * positions 0..pos with the GQA map kv = qh / (q_heads / kv_heads).  K and V
  * use the reference KV layout [capacity, kv_heads, head_dim].  `out` may
  * alias `q`.  head_dim must be 128; q_heads / kv_heads in {1, 2, 4, 8}.
- * `workspace` holds the split partials: q3_attention_workspace_bytes(). */
+ * The KV splits merge inside a thread-block cluster through distributed
+ * shared memory, so no global scratch is needed: `workspace` may be NULL
+ * (q3_attention_workspace_bytes() reports the size kept for ABI stability). */
 Q3_API size_t q3_attention_workspace_bytes(size_t q_heads, size_t kv_heads, size_t max_positions);
 Q3_API int q3_attention(const uint16_t* q_dev, const uint16_t* k_dev, const uint16_t* v_dev, uint16_t* out_dev,
                         size_t q_heads, size_t kv_heads, size_t head_dim, size_t pos, void* workspace_dev,

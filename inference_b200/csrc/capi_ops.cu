@@ -139,20 +139,17 @@ size_t q3_attention_workspace_bytes(size_t q_heads, size_t kv_heads, size_t max_
 static int attention_common(const uint16_t* q, const uint16_t* k, const uint16_t* v, const int32_t* page_table,
                             uint16_t* out, size_t q_heads, size_t kv_heads, size_t head_dim, size_t page_size,
                             size_t pos, void* ws, size_t ws_bytes, void* stream, int paged) {
-    Q3_CHECK(q && k && v && out && ws, "q3_attention: null pointer");
+    Q3_CHECK(q && k && v && out, "q3_attention: null pointer");
+    (void)ws;
+    (void)ws_bytes;  // splits merge in distributed shared memory; the workspace is unused
     if (head_dim != 128) return fail(Q3_ERR_UNSUPPORTED, "q3_attention: head_dim must be 128");
     Q3_CHECK(kv_heads > 0 && q_heads % kv_heads == 0, "q3_attention: q_heads must be a multiple of kv_heads");
     const size_t G = q_heads / kv_heads;
     if (!(G == 1 || G == 2 || G == 4 || G == 8)) return fail(Q3_ERR_UNSUPPORTED, "q3_attention: GQA group 1/2/4/8");
     if (paged) Q3_CHECK(page_size == 64 && page_table, "q3_attention_paged: page_size must be 64");
     Q3_CHECK(aligned16(k) && aligned16(v) && aligned16(q), "q3_attention: 16-byte alignment required");
-    const int sms = current_sms();
-    // Size the split count from this call's position (the workspace must hold it).
-    const int splits = attn_splits(static_cast<int>(kv_heads), static_cast<int>(pos), 64, sms);
-    const size_t need = attn_workspace_bytes(static_cast<int>(q_heads), static_cast<int>(kv_heads), splits);
-    Q3_CHECK(ws_bytes >= need, "q3_attention: workspace too small (q3_attention_workspace_bytes)");
-    const int HG = G >= 4 ? 4 : static_cast<int>(G);
-    const size_t slots = kv_heads * (G / HG) * splits * HG;
+    Q3_CHECK(pos < (1u << 24), "q3_attention: position too large");
+    const int splits = attn_splits(static_cast<int>(kv_heads), static_cast<int>(pos), 64, current_sms());
     AttnArgs a{};
     a.q = cb(q);
     a.k = cb(k);
@@ -166,13 +163,8 @@ static int attention_common(const uint16_t* q, const uint16_t* k, const uint16_t
     a.pos_ptr = nullptr;
     a.pos_host = static_cast<int>(pos);
     a.splits = splits;
-    a.part_ml = static_cast<float*>(ws);
-    a.part_acc = a.part_ml + slots * 2;
-    a.counters = reinterpret_cast<uint32_t*>(a.part_acc + slots * 128);
     a.err = nullptr;
     cudaStream_t s = as_stream(stream);
-    cudaError_t e = cudaMemsetAsync(a.counters, 0, kv_heads * (G / HG) * sizeof(uint32_t), s);
-    if (e != cudaSuccess) return launch_status(e, "q3_attention");
     return launch_status(launch_attention(a, s, false), "q3_attention");
 }
 

@@ -64,10 +64,7 @@ struct q3_engine {
     int32_t *pos = nullptr, *n_forced = nullptr, *tokens = nullptr, *argmax_hist = nullptr;
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
     uint32_t *done_counter = nullptr, *head_counters = nullptr, *err = nullptr;
-    float* attn_ws = nullptr;
     int attn_splits = 1;
-    size_t attn_slots = 0;
-    uint32_t* attn_counters = nullptr;
     // graph / comms
     cudaGraphExec_t graph = nullptr;
     ncclComm_t comm = nullptr;
@@ -158,9 +155,6 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.paged = 1;
     a.pos_ptr = e->pos;
     a.splits = e->attn_splits;
-    a.part_ml = e->attn_ws;
-    a.part_acc = e->attn_ws + e->attn_slots * 2;
-    a.counters = e->attn_counters;
     a.err = e->err;
     r.mark(true, 1);
     cudaError_t st = launch_attention(a, e->stream, r.pdl);
@@ -464,15 +458,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     cudaMemset(e->head_counters, 0, (e->qh + e->kvh + 4) * 4);
     cudaMemset(e->err, 0, 4);
 
-    // ---- attention split workspace, sized for the full context
+    // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
-    const int Gl = e->qh / e->kvh;
-    const int HG = Gl >= 4 ? 4 : Gl;
-    e->attn_slots = static_cast<size_t>(e->kvh) * (Gl / HG) * e->attn_splits * HG;
-    const size_t ws = attn_workspace_bytes(e->qh, e->kvh, e->attn_splits);
-    if ((rc = dalloc(e, reinterpret_cast<void**>(&e->attn_ws), ws)) != Q3_OK) return bail(rc);
-    e->attn_counters = reinterpret_cast<uint32_t*>(e->attn_ws + e->attn_slots * 2 + e->attn_slots * 128);
-    cudaMemset(e->attn_ws, 0, ws);
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "engine setup failed"));
     *out = e;
     return Q3_OK;

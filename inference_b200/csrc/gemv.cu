@@ -25,25 +25,24 @@ namespace q3 {
 
 namespace {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;
-constexpr int kThreads = kConsumers + 32;
-constexpr int kStageTarget = 16384;
-constexpr size_t kSmemBudget = 110 * 1024;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kChunk = 2048;            // columns per item: 4 KB of BF16 weights
+constexpr int kMaxItems = 4096;         // (row, chunk) partial sums per CTA
+constexpr size_t kSmemBudget = 112 * 1024;  // two CTAs per SM: the next kernel's prefetch overlaps this one
 constexpr int kMaxDynSmem = 200 * 1024;
 
 struct SmemLayout {
-    size_t stage_off, x_off, bar_off, red_off, misc_off, total;
+    size_t stage_off, x_off, part_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K) {
+__host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K, int max_rows) {
     SmemLayout L;
-    const size_t stage_bytes = static_cast<size_t>(p.rb) * p.kc * 2;
     L.stage_off = 0;
-    L.x_off = stage_bytes * p.stages;
-    L.bar_off = (L.x_off + static_cast<size_t>(K) * 2 + 15) / 16 * 16;
-    L.red_off = L.bar_off + 2 * static_cast<size_t>(p.stages) * 8;
-    L.misc_off = L.red_off + 2 * 8 * 8 * sizeof(float);
+    L.x_off = static_cast<size_t>(kWarps) * p.stages * p.kc * 2;
+    L.part_off = L.x_off + (static_cast<size_t>(K) * 2 + 15) / 16 * 16;
+    L.bar_off = L.part_off + (static_cast<size_t>(max_rows) * p.nch * 4 + 15) / 16 * 16;
+    L.misc_off = L.bar_off + static_cast<size_t>(kWarps) * p.stages * 8;
     L.total = L.misc_off + 128;
     return L;
 }
@@ -53,77 +52,72 @@ __device__ __forceinline__ size_t kv_slot(const GemvArgs& a, int pos, int head) 
     return ((static_cast<size_t>(page) * a.kv_heads_local + head) * a.page_size + (pos % a.page_size)) * 128;
 }
 
-// Sum of per-thread values over the 256 consumer threads, fixed order.
-__device__ __forceinline__ float consumers_sum(float v, float* scratch8) {
+// Sum over the CTA's threads, fixed order.
+__device__ __forceinline__ float cta_sum(float v, float* scratch) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     v = warp_sum(v);
-    if (lane == 0) scratch8[warp] = v;
-    named_bar(1, kConsumers);
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) t += scratch8[w];
-    named_bar(1, kConsumers);
+    for (int w = 0; w < kWarps; ++w) t += scratch[w];
+    __syncthreads();
     return t;
 }
 
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& p = a.plan;
-    const SmemLayout L = smem_layout(p, a.K);
-    uint8_t* stage_base = smem + L.stage_off;
-    bf16* xs = reinterpret_cast<bf16*>(smem + L.x_off);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-    uint64_t* empty = full + p.stages;
-    float* red = reinterpret_cast<float*>(smem + L.red_off);
-    float* misc = reinterpret_cast<float*>(smem + L.misc_off);
-    unsigned long long* cta_key = reinterpret_cast<unsigned long long*>(misc + 16);
-
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    // ---- this CTA's rows and this warp's contiguous run of (row, chunk) items
     const int units = a.N / p.row_gran;
     const int u0 = static_cast<int>(static_cast<long long>(blockIdx.x) * units / gridDim.x);
     const int u1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * units / gridDim.x);
     const int r0 = u0 * p.row_gran, r1 = u1 * p.row_gran;
-    const int nrb = (r1 - r0 + p.rb - 1) / p.rb;
-    const int ntiles = nrb * p.ncb;
-    const uint32_t kc_bytes = static_cast<uint32_t>(p.kc) * 2;
-    const size_t stage_bytes = static_cast<size_t>(p.rb) * kc_bytes;
+    const int nrows = r1 - r0;
+    const int max_rows = (units + gridDim.x - 1) / gridDim.x * p.row_gran;
+    const SmemLayout L = smem_layout(p, a.K, max_rows);
+    bf16* xs = reinterpret_cast<bf16*>(smem + L.x_off);
+    float* part = reinterpret_cast<float*>(smem + L.part_off);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off) + warp * p.stages;
+    float* misc = reinterpret_cast<float*>(smem + L.misc_off);
+    unsigned long long* cta_key = reinterpret_cast<unsigned long long*>(misc + 16);
+    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * p.kc * 2;
 
-    if (tid == 0) {
-        for (int s = 0; s < p.stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        *cta_key = 0ull;
+    const int n_items = nrows * p.nch;
+    const int i0 = static_cast<int>(static_cast<long long>(warp) * n_items / kWarps);
+    const int i1 = static_cast<int>(static_cast<long long>(warp + 1) * n_items / kWarps);
+    const int cnt = i1 - i0;
+
+    if (lane == 0) {
+        for (int s = 0; s < p.stages; ++s) mbar_init(&bars[s], 1);
         fence_barrier_init();
     }
-    __syncthreads();
-    pdl_trigger();
+    __syncwarp();
 
-    // ------------------------------------------------------------ producer
-    if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            const uint64_t pol = policy_evict_first();
-            for (int t = 0; t < ntiles; ++t) {
-                const int s = t % p.stages;
-                if (t >= p.stages &&
-                    !mbar_wait(&empty[s], ((t / p.stages) - 1) & 1, a.err, DEV_TMA_WAIT_TIMEOUT))
-                    break;
-                const int rbk = t / p.ncb, cb = t % p.ncb;
-                const int row = r0 + rbk * p.rb;
-                const int rows = min(p.rb, r1 - row);
-                mbar_arrive_expect_tx(&full[s], rows * kc_bytes);
-                uint8_t* dst = stage_base + s * stage_bytes;
-                const bf16* src = a.W + static_cast<size_t>(row) * a.K + static_cast<size_t>(cb) * p.kc;
-                for (int r = 0; r < rows; ++r)
-                    bulk_g2s(dst + r * kc_bytes, src + static_cast<size_t>(r) * a.K, kc_bytes, &full[s], pol);
-            }
-        }
-        return;
+    uint64_t pol = 0;
+    auto issue = [&](int item, int slot) {
+        const int row = r0 + item / p.nch, c = item % p.nch;
+        const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
+        const uint32_t bytes = static_cast<uint32_t>(cols) * 2;
+        mbar_arrive_expect_tx(&bars[slot], bytes);
+        bulk_g2s(ring + static_cast<size_t>(slot) * p.kc * 2, a.W + static_cast<size_t>(row) * a.K + c * p.kc,
+                 bytes, &bars[slot], pol);
+    };
+    // Weights never depend on earlier kernels: start streaming before the wait.
+    if (lane == 0) {
+        pol = policy_evict_first();
+        for (int j = 0; j < p.stages && j < cnt; ++j) issue(i0 + j, j);
     }
+    for (int i = tid; i < nrows * p.nch; i += kThreads) part[i] = 0.f;
+    if (tid == 0) *cta_key = 0ull;
 
-    // ------------------------------------------------------------ consumers
     pdl_wait();
+    pdl_trigger();
     int pos = 0;
     if (EPI == EPI_QKV || PRO == PRO_EMBED_NORM) {
         pos = *a.pos_ptr;
@@ -138,16 +132,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     if constexpr (PRO == PRO_PLAIN) {
         const uint4* src = reinterpret_cast<const uint4*>(a.x);
         uint4* dst = reinterpret_cast<uint4*>(xs);
-        for (int i = tid; i < kv8; i += kConsumers) dst[i] = src[i];
+        for (int i = tid; i < kv8; i += kThreads) dst[i] = src[i];
     } else {
         const bf16* src = a.hs;
         if constexpr (PRO == PRO_EMBED_NORM) {
-            int token;
             const int nf = *a.n_forced;
             uint64_t best = 0;
             for (int r = 0; r < a.n_keys; ++r) best = max(best, static_cast<uint64_t>(a.keys[r]));
             const uint32_t greedy = argmax_key_index(best);
-            token = (pos < nf) ? a.tokens[pos] : static_cast<int>(greedy);
+            int token = (pos < nf) ? a.tokens[pos] : static_cast<int>(greedy);
             if (token < 0 || token >= a.vocab) {
                 if (tid == 0) record_error(a.err, DEV_BAD_TOKEN);
                 token = 0;
@@ -159,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             src = a.embed + static_cast<size_t>(token) * a.K;
         }
         float ss = 0.f;
-        for (int i = tid; i < kv8; i += kConsumers) {
+        for (int i = tid; i < kv8; i += kThreads) {
             uint4 h = reinterpret_cast<const uint4*>(src)[i];
             if constexpr (PRO == PRO_NORM_F32) {
                 const float4 v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
@@ -195,9 +188,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
                 if (blockIdx.x == 0) reinterpret_cast<uint4*>(a.hs_out)[i] = h;
             }
         }
-        ss = consumers_sum(ss, misc);
+        ss = cta_sum(ss, misc);
         const float scale = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
-        for (int i = tid; i < kv8; i += kConsumers) {
+        for (int i = tid; i < kv8; i += kThreads) {
             uint4 h = reinterpret_cast<uint4*>(xs)[i];
             const uint4 w = reinterpret_cast<const uint4*>(a.norm_w)[i];
             uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
@@ -212,87 +205,88 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
             reinterpret_cast<uint4*>(xs)[i] = h;
         }
     }
-    named_bar(1, kConsumers);
+    __syncthreads();
 
-    // ---- main loop
-    const int wpr = kConsumerWarps / p.rb;
-    const int tr = warp / wpr, part = warp % wpr;
-    const int nv = p.kc / 8;
-    const int vstep = wpr * 32;
+    // ---- main loop: each warp streams its own items; no CTA-wide barrier
     float acc0 = 0.f, acc1 = 0.f;
-    uint64_t best_key = 0;
     bool failed = false;
-
-    for (int t = 0; t < ntiles; ++t) {
-        const int s = t % p.stages;
-        const bool ok = !failed && mbar_wait(&full[s], (t / p.stages) & 1, a.err, DEV_TMA_WAIT_TIMEOUT);
+    for (int j = 0; j < cnt; ++j) {
+        const int slot = j % p.stages;
+        const bool ok = !failed && mbar_wait(&bars[slot], (j / p.stages) & 1, a.err, DEV_TMA_WAIT_TIMEOUT);
         failed = failed || !ok;
-        const int rbk = t / p.ncb, cb = t % p.ncb;
-        const int row = r0 + rbk * p.rb;
-        const int rows = min(p.rb, r1 - row);
-        if (ok && tr < rows) {
-            const uint4* wv = reinterpret_cast<const uint4*>(stage_base + s * stage_bytes + tr * kc_bytes);
-            const uint4* xv = reinterpret_cast<const uint4*>(xs + static_cast<size_t>(cb) * p.kc);
-            int v = part * 32 + lane;
-            for (; v + vstep < nv; v += 2 * vstep) {
+        const int item = i0 + j;
+        const int rl = item / p.nch, c = item % p.nch;
+        if (ok) {
+            const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
+            const int nv = cols / 8;
+            const uint4* wv = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(slot) * p.kc * 2);
+            const uint4* xv = reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c) * p.kc);
+            int v = lane;
+            for (; v + 32 < nv; v += 64) {
                 acc0 = dot8(wv[v], xv[v], acc0);
-                acc1 = dot8(wv[v + vstep], xv[v + vstep], acc1);
+                acc1 = dot8(wv[v + 32], xv[v + 32], acc1);
             }
             if (v < nv) acc0 = dot8(wv[v], xv[v], acc0);
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-
-        if (cb == p.ncb - 1) {
-            const float wsum = warp_sum(acc0 + acc1);
+        // flush at the end of this warp's part of a row
+        if (c == p.nch - 1 || j == cnt - 1) {
+            const float sum = warp_sum(acc0 + acc1);
             acc0 = acc1 = 0.f;
-            float* rd = red + (rbk & 1) * 64;
-            if (lane == 0) rd[tr * 8 + part] = wsum;
-            named_bar(1, kConsumers);
-            if constexpr (EPI == EPI_SWIGLU) {
-                if (tid < rows / 2) {
-                    float g = 0.f, u = 0.f;
-                    for (int q = 0; q < wpr; ++q) g += rd[(2 * tid) * 8 + q];
-                    for (int q = 0; q < wpr; ++q) u += rd[(2 * tid + 1) * 8 + q];
-                    // qwen3.hpp:154-156 -> silu.cuh:18-20 on the BF16-rounded matmul outputs
-                    const float gv = round_bf(g), uv = round_bf(u);
-                    const float silu = gv / (1.0f + expf(-gv));
-                    a.y[(row >> 1) + tid] = f2bf(silu * uv);
+            if (lane == 0) part[rl * p.nch + c] = sum;
+        }
+        __syncwarp();
+        if (lane == 0 && !failed && j + p.stages < cnt) {
+            fence_proxy_async();  // generic-proxy reads of this slot precede the async refill
+            issue(i0 + j + p.stages, slot);
+        }
+    }
+    __syncthreads();
+
+    // ---- epilogue: row sums in fixed chunk order
+    auto row_sum = [&](int rl) {
+        float r = 0.f;
+        for (int c = 0; c < p.nch; ++c) r += part[rl * p.nch + c];
+        return r;
+    };
+    uint64_t best_key = 0;
+    if constexpr (EPI == EPI_SWIGLU) {
+        for (int m = tid; m < nrows / 2; m += kThreads) {
+            // qwen3.hpp:154-156 -> silu.cuh:18-20 on the BF16-rounded matmul outputs
+            const float gv = round_bf(row_sum(2 * m)), uv = round_bf(row_sum(2 * m + 1));
+            const float silu = gv / (1.0f + expf(-gv));
+            a.y[(r0 >> 1) + m] = f2bf(silu * uv);
+        }
+    } else {
+        for (int rl = tid; rl < nrows; rl += kThreads) {
+            const float r = row_sum(rl);
+            const int gr = r0 + rl;
+            if constexpr (EPI == EPI_STORE) {
+                a.y[gr] = f2bf(r);
+            } else if constexpr (EPI == EPI_PARTIAL) {
+                a.yf[gr] = r;
+            } else if constexpr (EPI == EPI_RESID) {
+                // qwen3.hpp:158-159: hidden = bf16(down); hs = bf16(hs + hidden)
+                a.hs[gr] = f2bf(bf2f(a.hs[gr]) + round_bf(r));
+            } else if constexpr (EPI == EPI_RESID_F32) {
+                // qwen3.hpp:151-152 -> rmsnorm.cuh:58-60
+                const float v = bf2f(a.hs[gr]) + round_bf(r);
+                a.hs[gr] = f2bf(v);
+                a.vsum_out[gr] = v;
+            } else if constexpr (EPI == EPI_QKV) {
+                const bf16 b = f2bf(r);
+                if (gr < a.q_rows) {
+                    a.q_out[gr] = b;
+                } else if (gr < a.q_rows + a.kv_rows) {
+                    const int k = gr - a.q_rows;
+                    a.k_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
+                } else {
+                    const int k = gr - a.q_rows - a.kv_rows;
+                    a.v_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
                 }
-            } else {
-                if (tid < rows) {
-                    float r = 0.f;
-                    for (int q = 0; q < wpr; ++q) r += rd[tid * 8 + q];
-                    const int gr = row + tid;
-                    if constexpr (EPI == EPI_STORE) {
-                        a.y[gr] = f2bf(r);
-                    } else if constexpr (EPI == EPI_PARTIAL) {
-                        a.yf[gr] = r;
-                    } else if constexpr (EPI == EPI_RESID) {
-                        // qwen3.hpp:158-159: hidden = bf16(down); hs = bf16(hs + hidden)
-                        a.hs[gr] = f2bf(bf2f(a.hs[gr]) + round_bf(r));
-                    } else if constexpr (EPI == EPI_RESID_F32) {
-                        // qwen3.hpp:151-152 -> rmsnorm.cuh:58-60
-                        const float v = bf2f(a.hs[gr]) + round_bf(r);
-                        a.hs[gr] = f2bf(v);
-                        a.vsum_out[gr] = v;
-                    } else if constexpr (EPI == EPI_QKV) {
-                        const bf16 b = f2bf(r);
-                        if (gr < a.q_rows) {
-                            a.q_out[gr] = b;
-                        } else if (gr < a.q_rows + a.kv_rows) {
-                            const int k = gr - a.q_rows;
-                            a.k_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
-                        } else {
-                            const int k = gr - a.q_rows - a.kv_rows;
-                            a.v_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
-                        }
-                    } else if constexpr (EPI == EPI_ARGMAX) {
-                        const bf16 b = f2bf(r);
-                        a.y[gr] = b;
-                        best_key = max(best_key, argmax_key(bf2f(b), static_cast<uint32_t>(gr) + a.vocab_offset));
-                    }
-                }
+            } else if constexpr (EPI == EPI_ARGMAX) {
+                const bf16 b = f2bf(r);
+                a.y[gr] = b;
+                best_key = max(best_key, argmax_key(bf2f(b), static_cast<uint32_t>(gr) + a.vocab_offset));
             }
         }
     }
@@ -302,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
         // qk_norm_rope (qk_norm_rope.cuh:14-90) for every q / k head whose last
         // rows this CTA produced: the CTA that completes a head normalises it.
         __threadfence();
-        named_bar(1, kConsumers);
+        __syncthreads();
         if (warp == 0) {
             const int nqk = a.q_rows + a.kv_rows;
             const int hi_row = min(r1, nqk);
@@ -341,7 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant
     }
     if constexpr (EPI == EPI_ARGMAX) {
         if (best_key) atomicMax(cta_key, static_cast<unsigned long long>(best_key));
-        named_bar(1, kConsumers);
+        __syncthreads();
         if (tid == 0) {
             atomicMax(reinterpret_cast<unsigned long long*>(a.key_slot), *cta_key);
             __threadfence();
@@ -400,28 +394,19 @@ cudaError_t configure_gemv_kernels() {
 GemvPlan plan_gemv(int N, int K, int epi, int sms) {
     GemvPlan p{};
     p.row_gran = (epi == EPI_SWIGLU) ? 2 : 1;
-    const int row_bytes = K * 2;
-    const int min_rb = (epi == EPI_SWIGLU) ? 2 : 1;
-    if (row_bytes * min_rb <= kStageTarget) {
-        int rb = 8;
-        while (rb > min_rb && rb * row_bytes > kStageTarget) rb >>= 1;
-        p.rb = rb;
-        p.kc = K;
-        p.ncb = 1;
-    } else {
-        p.rb = min_rb;
-        int ncb = (row_bytes * p.rb + kStageTarget - 1) / kStageTarget;
-        while (K % (8 * ncb) != 0) ++ncb;
-        p.ncb = ncb;
-        p.kc = K / ncb;
-    }
-    const size_t stage_bytes = static_cast<size_t>(p.rb) * p.kc * 2;
-    const size_t fixed = (static_cast<size_t>(K) * 2 + 15) / 16 * 16 + 1024;
-    long st = kSmemBudget > fixed ? static_cast<long>((kSmemBudget - fixed) / stage_bytes) : 2;
-    p.stages = static_cast<int>(std::min(8L, std::max(2L, st)));
+    p.kc = K < kChunk ? K : kChunk;
+    p.nch = (K + p.kc - 1) / p.kc;
     const int units = N / p.row_gran;
-    p.grid = std::max(1, std::min(sms, units));
-    p.smem = smem_layout(p, K).total;
+    // one CTA per SM, more only if the per-CTA partial sums would not fit
+    const long long items = static_cast<long long>(N) * p.nch;
+    int grid = std::min(sms, units);
+    const long long min_grid = (items + kMaxItems - 1) / kMaxItems;
+    if (grid < min_grid) grid = static_cast<int>(std::min<long long>(min_grid, units));
+    p.grid = std::max(1, grid);
+    const int max_rows = (units + p.grid - 1) / p.grid * p.row_gran;
+    for (p.stages = 4; p.stages > 2; --p.stages)
+        if (smem_layout(p, K, max_rows).total <= kSmemBudget) break;
+    p.smem = smem_layout(p, K, max_rows).total;
     return p;
 }
 

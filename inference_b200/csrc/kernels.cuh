@@ -29,10 +29,9 @@ enum GemvEpi : int {
 };
 
 struct GemvPlan {
-    int rb;        // rows per tile: 1, 2, 4 or 8
-    int kc;        // columns per tile (multiple of 8, divides K)
-    int ncb;       // column tiles per row block (K / kc)
-    int stages;    // shared-memory ring depth
+    int kc;        // columns per (row, chunk) work item: min(K, 2048), a multiple of 8
+    int nch;       // chunks per row, ceil(K / kc); the last may be shorter
+    int stages;    // per-warp shared-memory ring depth
     int grid;      // CTAs
     int row_gran;  // rows assigned to CTAs in units of this many (2 for SWIGLU)
     size_t smem;   // dynamic shared memory bytes
@@ -98,10 +97,7 @@ struct AttnArgs {
     int paged;                // 1 = paged layout, 0 = reference layout
     const int32_t* pos_ptr;   // device position (or null -> pos_host)
     int pos_host;
-    int splits;               // grid.y
-    float* part_ml;           // [kvh, splits, G, 2]
-    float* part_acc;          // [kvh, splits, G, 128]
-    uint32_t* counters;       // [kvh]
+    int splits;               // grid.x = cluster size: a power of two <= 16
     uint32_t* err;
 };
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);

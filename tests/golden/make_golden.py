@@ -107,6 +107,8 @@ def model_case(ref: RefLib, o: Oracle, name: str) -> dict:
     prompt = o.prompt_ids(plen, seed=1, vocab=cfg.vocab)
     t0 = time.time()
     m = ref.model(cfg, seed=0)
+    om = o.model(cfg, seed=0)  # the oracle in lockstep: the envelope two fp32 implementations span
+    env_max, env_cos = [], []
     seq = list(int(t) for t in prompt)
     argmax, topi, topv, s1, s2 = [], [], [], [], []
     kv_layers = sorted({0, cfg.layers - 1})
@@ -116,6 +118,10 @@ def model_case(ref: RefLib, o: Oracle, name: str) -> dict:
         nxt = m.forward(seq[i])
         lg = m.logits()
         f = (lg.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        om.forward(seq[i])
+        fo = (om.logits().astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        env_max.append(float(np.abs(f - fo).max()))
+        env_cos.append(float(f @ fo / (np.linalg.norm(f) * np.linalg.norm(fo))))
         idx = np.argsort(-f, kind="stable")[:TOPK]
         argmax.append(nxt)
         topi.append(idx.astype(np.int64))
@@ -129,7 +135,9 @@ def model_case(ref: RefLib, o: Oracle, name: str) -> dict:
         if i >= plen - 1 and len(seq) < n_fwd:
             seq.append(nxt)
     m.close()
-    print(f"  {name}: {n_fwd} forwards in {time.time() - t0:.1f}s", flush=True)
+    om.close()
+    print(f"  {name}: {n_fwd} forwards in {time.time() - t0:.1f}s; reference CPU vs oracle: max |dlogit| "
+          f"{max(env_max):.4f}, min cosine {min(env_cos):.6f}", flush=True)
     d = {
         "config": np.array([cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.vocab,
                             cfg.capacity, cfg.tied], np.int64),
@@ -141,6 +149,11 @@ def model_case(ref: RefLib, o: Oracle, name: str) -> dict:
         "logit_sum": np.array(s1),
         "logit_sumsq": np.array(s2),
         "kv_layers": np.array(kv_layers, np.int64),
+        # per step: max |logit difference| and cosine between the reference
+        # CPU backend and the oracle -- how far apart two correct fp32
+        # implementations of the same model land
+        "env_maxabs": np.array(env_max),
+        "env_cos": np.array(env_cos),
     }
     for lay in kv_layers:
         d[f"k_l{lay}"] = np.stack(kv[lay][0])

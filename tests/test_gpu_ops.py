@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 import make_golden as G
-from gpu_util import assert_bf16_close, dev, empty_bf16, host
+from gpu_util import assert_bf16_close, dev, empty_bf16, host, ulps
 from inputs import uniform_bf16
 
 pytestmark = pytest.mark.gpu
@@ -126,12 +126,15 @@ def test_silu_and_add_aliased(be, oracle, golden_ops, n):
     b = uniform_bf16(G.seed_of("elem.b", n), (n,))
     g = dev(a)
     be.silu(g, dev(b), g)  # qwen3.hpp:156 aliases gate and output
-    np.testing.assert_array_equal(host(g), oracle.silu(a, b))
+    # CUDA expf and glibc expf may differ in the last fp32 bit: a BF16
+    # rounding flip on at most a few elements per million
+    d = ulps(host(g), oracle.silu(a, b))
+    assert d.max() <= 1 and (d > 0).sum() <= max(1, n // 100000)
     l_ = dev(a)
     be.add(l_, dev(b), l_)  # qwen3.hpp:159 aliases left and output
     np.testing.assert_array_equal(host(l_), oracle.add(a, b))
     if f"silu/{n}" in golden_ops:
-        np.testing.assert_array_equal(host(g), golden_ops[f"silu/{n}"])
+        assert ulps(host(g), golden_ops[f"silu/{n}"]).max() <= 1
         np.testing.assert_array_equal(host(l_), golden_ops[f"add/{n}"])
 
 
