@@ -25,12 +25,30 @@ namespace q3 {
 
 namespace {
 
-constexpr int kWarps = 8;
+#ifndef Q3_GEMV_WARPS
+#define Q3_GEMV_WARPS 16
+#endif
+#ifndef Q3_GEMV_CHUNK
+#define Q3_GEMV_CHUNK 2048
+#endif
+#ifndef Q3_GEMV_SMEM_KB
+#define Q3_GEMV_SMEM_KB 210
+#endif
+#ifndef Q3_GEMV_MAX_STAGES
+#define Q3_GEMV_MAX_STAGES 3
+#endif
+#ifndef Q3_GEMV_MIN_BLOCKS
+#define Q3_GEMV_MIN_BLOCKS 1
+#endif
+constexpr int kWarps = Q3_GEMV_WARPS;
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = 2048;            // columns per item: 4 KB of BF16 weights
+constexpr int kChunk = Q3_GEMV_CHUNK;   // columns per item: 4 KB of BF16 weights
 constexpr int kMaxItems = 4096;         // (row, chunk) partial sums per CTA
-constexpr size_t kSmemBudget = 112 * 1024;  // two CTAs per SM: the next kernel's prefetch overlaps this one
-constexpr int kMaxDynSmem = 200 * 1024;
+// One CTA per SM with a ~192 KB ring: loaded HBM latency needs well over
+// 100 KB in flight per SM to sustain its share of the bandwidth (measured:
+// 8 warps x 3 x 4 KB reached 71% of peak on a 201 MB GEMV, 16 x 3 x 4 KB 85%).
+constexpr size_t kSmemBudget = Q3_GEMV_SMEM_KB * 1024;
+constexpr int kMaxDynSmem = 220 * 1024;
 
 struct SmemLayout {
     size_t stage_off, x_off, part_off, bar_off, misc_off, total;
@@ -68,7 +86,7 @@ __device__ __forceinline__ float cta_sum(float v, float* scratch) {
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 template <int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& p = a.plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -404,7 +422,7 @@ GemvPlan plan_gemv(int N, int K, int epi, int sms) {
     if (grid < min_grid) grid = static_cast<int>(std::min<long long>(min_grid, units));
     p.grid = std::max(1, grid);
     const int max_rows = (units + p.grid - 1) / p.grid * p.row_gran;
-    for (p.stages = 4; p.stages > 2; --p.stages)
+    for (p.stages = Q3_GEMV_MAX_STAGES; p.stages > 2; --p.stages)
         if (smem_layout(p, K, max_rows).total <= kSmemBudget) break;
     p.smem = smem_layout(p, K, max_rows).total;
     return p;
