@@ -42,6 +42,7 @@ def parse_args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=0, help="profiling only: override the layer count")
     ap.add_argument("--window", type=int, default=0, help="profiling only: decode this many tokens per step")
+    ap.add_argument("--prompt", type=int, default=0, help="profiling only: override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=3)
@@ -206,6 +207,11 @@ def main():
     if a.layers:
         cfg = cfg.with_layers(a.layers)
         workload += f"-L{a.layers}(profiling)"
+    if a.prompt:
+        prompt_len = a.prompt
+        workload += f"-P{a.prompt}(profiling)"
+    if a.window:
+        workload += f"-W{a.window}(profiling)"
     if a.impl == "reference":
         return run_reference(a, cfg, prompt_len, capacity, workload)
     if a.warmup < 3:

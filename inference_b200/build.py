@@ -3,7 +3,8 @@
     python -m inference_b200.build [--force] [-j N]
 
 Each .cu under csrc/ compiles to an object under inference_b200/_build/, then
-all link into inference_b200/libq3_sm100a.so against the CUDA runtime and NCCL.
+all link into inference_b200/libq3_sm100a.so against the CUDA runtime (NCCL is
+loaded at run time, only for tensor parallelism).
 """
 from __future__ import annotations
 
@@ -76,7 +77,7 @@ def build(force: bool = False, jobs: int = 8, verbose: bool = True, extra: list[
             print(f"--- {src}\n{log}", file=sys.stderr)
         raise RuntimeError(f"{len(failed)} CUDA source(s) failed to compile")
     if force or todo or _stale(LIB, objs):
-        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lnccl", "-lcudart"]
+        cmd = [nvcc()] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcudart", "-ldl"]
         if verbose:
             print("link", os.path.relpath(LIB, ROOT), flush=True)
         subprocess.run(cmd, check=True)

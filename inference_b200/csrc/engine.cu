@@ -19,7 +19,6 @@
 //     into fp32 partials, allreduce them with NCCL, and fold the residual add
 //     into the next GEMV's prologue; lm_head is vocab-sharded and the per-rank
 //     (value, index) keys are all-gathered and resolved in the next step.
-#include <nccl.h>
 
 #include <cmath>
 #include <cstring>
@@ -28,6 +27,7 @@
 
 #include "host_util.hpp"
 #include "kernels.cuh"
+#include "nccl_dyn.hpp"
 
 namespace q3 {
 
@@ -166,8 +166,8 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
 }
 
 int allreduce(q3_engine* e, float* buf, size_t n) {
-    ncclResult_t nr = ncclAllReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, e->stream);
-    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+    ncclResult_t nr = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, e->stream);
+    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().GetErrorString(nr));
     return Q3_OK;
 }
 
@@ -276,8 +276,8 @@ int record_step(Recorder& r, size_t pos_now) {
         h.vsum = e->partial;
         h.ss_unrounded = 0;
         Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
-        ncclResult_t nr = ncclAllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
-        if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+        ncclResult_t nr = nccl().AllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
+        if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + nccl().GetErrorString(nr));
     } else {
         h.hs = e->hs[0];
         Q3_TRY(gemv(r, PRO_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
@@ -470,7 +470,7 @@ int q3_engine_destroy(q3_engine* e) {
     cudaSetDevice(e->device);
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->graph) cudaGraphExecDestroy(e->graph);
-    if (e->comm) ncclCommDestroy(e->comm);
+    if (e->comm) nccl().CommDestroy(e->comm);
     for (void* p : e->allocs) cudaFree(p);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -831,9 +831,10 @@ int q3_rope_tables(size_t max_pos, size_t head_dim, float theta, float* cos_host
 
 int q3_nccl_unique_id(void* id_out) {
     Q3_CHECK(id_out, "null argument");
+    if (!nccl().ok) return fail(Q3_ERR_NCCL, nccl().error);
     ncclUniqueId id;
-    ncclResult_t nr = ncclGetUniqueId(&id);
-    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclGetUniqueId: ") + ncclGetErrorString(nr));
+    ncclResult_t nr = nccl().GetUniqueId(&id);
+    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclGetUniqueId: ") + nccl().GetErrorString(nr));
     static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
     std::memcpy(id_out, &id, sizeof(id));
     return Q3_OK;
@@ -845,8 +846,9 @@ int q3_engine_attach_nccl(q3_engine* e, const void* id_in) {
     Q3_CUDA(cudaSetDevice(e->device));
     ncclUniqueId id;
     std::memcpy(&id, id_in, sizeof(id));
-    ncclResult_t nr = ncclCommInitRank(&e->comm, e->world, id, e->rank);
-    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclCommInitRank: ") + ncclGetErrorString(nr));
+    if (!nccl().ok) return fail(Q3_ERR_NCCL, nccl().error);
+    ncclResult_t nr = nccl().CommInitRank(&e->comm, e->world, id, e->rank);
+    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl().GetErrorString(nr));
     if (e->graph) {
         cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;
