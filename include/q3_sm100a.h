@@ -111,6 +111,18 @@ Q3_API int q3_silu_mul(const uint16_t* gate_dev, const uint16_t* up_dev, uint16_
  * first index of the largest BF16 logit, written to *index_dev. */
 Q3_API int q3_argmax(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, void* stream);
 
+/* q3_argmax without any device allocation (no counterpart in the reference).
+ * For callers that must not let the library allocate: serving runtimes that
+ * plan all device memory themselves, code recording into a CUDA graph under
+ * global stream capture (where cudaMalloc is not allowed), latency-critical
+ * loops that cannot take cudaMalloc's implicit synchronisation.  Its scratch
+ * is a 32 KB array compiled into the library (kept by every GPU that loads
+ * it until the process exits), so n is limited to 16,777,216 logits; larger
+ * inputs return Q3_ERR_INVALID.  The first call on a device looks up the
+ * array's device address: make it before any stream capture.  Calls share
+ * the array, so calls that overlap on the GPU (unordered streams) race. */
+Q3_API int q3_argmax_noalloc(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, void* stream);
+
 /* make_rope_cache (src/lib/backend/util/rope_cache.hpp:23-45) on the host:
  * fp32 cos/sin tables [max_pos, head_dim/2], the same bits the engine uses. */
 Q3_API int q3_rope_tables(size_t max_pos, size_t head_dim, float theta, float* cos_host, float* sin_host);

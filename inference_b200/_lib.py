@@ -32,6 +32,7 @@ SIGNATURES = {
     "q3_add": (C.c_int, [_u16p, _u16p, _u16p, _sz, _vp]),
     "q3_silu_mul": (C.c_int, [_u16p, _u16p, _u16p, _sz, _vp]),
     "q3_argmax": (C.c_int, [_u16p, _sz, _u32p, _vp]),
+    "q3_argmax_noalloc": (C.c_int, [_u16p, _sz, _u32p, _vp]),
     "q3_rope_tables": (C.c_int, [_sz, _sz, C.c_float, _vp, _vp]),
     "q3_fill_normal": (C.c_int, [_u16p, C.c_uint64, C.c_uint64, _sz, _sz, _sz, _sz, _sz, _sz, _vp]),
     "q3_prompt_ids": (None, [_u32p, _sz, C.c_uint64, C.c_uint32]),
