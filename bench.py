@@ -46,6 +46,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-sample-tokens", type=int, default=3)
+    ap.add_argument("--reference-cuda-tokens", type=int, default=0,
+                    help="also time the reference's own cuBLAS CUDA backend (oracle/_ref/libref_cuda.so) for this "
+                         "many Model::forward calls at mid-window context; reported as reference_cuda")
     return ap.parse_args()
 
 
@@ -351,6 +354,33 @@ def main():
         except Exception as exc:  # report, never fail the GPU number
             cpu = {"value": None, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": f"failed: {exc}"}
 
+    # ---- the reference's own CUDA backend on the same GPU (optional, rank 0, N = 1)
+    ref_cuda = None
+    if rank == 0 and world == 1 and a.reference_cuda_tokens > 0:
+        try:
+            from oracle import ModelConfig, RefLib
+
+            rl = RefLib("cuda")
+            n_tok = a.reference_cuda_tokens
+            mc = ModelConfig.make(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, 128, cfg.vocab,
+                                  mid + n_tok + 2, tied=cfg.tied)
+            rm = rl.model(mc, seed=0)
+            rm.fill_kv(mid, seed=7)
+            rm.forward(1000)  # first call allocates the reference's flash scratch
+            rm.token_count = mid
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            tok = 1000
+            for _ in range(n_tok):
+                tok = rm.forward(tok)  # Model::forward: host sync per token, as the reference generator runs
+            dt = time.perf_counter() - t0
+            rm.close()
+            ref_cuda = {"value": round(n_tok / dt, 3), "unit": "tok/s",
+                        "sample": f"{n_tok} Model::forward calls at context {mid}, reference cuBLAS CUDA backend "
+                                  f"built from its sources for sm_100a"}
+        except Exception as exc:
+            ref_cuda = {"value": None, "unit": "tok/s", "sample": f"failed: {exc}"}
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
@@ -364,6 +394,8 @@ def main():
             "clocks": clock, "e2e": e2e, "gpu_launches": int((cfg.layers * 5 + 1) * window * a.steps),
             "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu,
         }
+        if ref_cuda is not None:
+            line["reference_cuda"] = ref_cuda
         print(json.dumps(line), flush=True)
     eng.close()
     if dist:

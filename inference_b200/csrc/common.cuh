@@ -1,7 +1,7 @@
 // common.cuh -- device helpers shared by the sm_100a decode kernels.
 //
 // Everything here is plain inline PTX for sm_100a: mbarriers, the 1-D bulk
-// tensor-memory-accelerator copy (cp.async.bulk, never with .multicast),
+// tensor-memory-accelerator copy (cp.async.bulk, into this CTA only),
 // programmatic dependent launch (griddepcontrol) and L2 cache policies.
 #pragma once
 
@@ -126,7 +126,7 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
 
 // 1-D bulk copy global -> this CTA's shared memory, completion counted in
 // bytes on `bar`.  Both addresses 16-byte aligned, size a multiple of 16.
-// No .multicast form is ever used.
+// Each copy lands in the issuing CTA only.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
     asm volatile(
