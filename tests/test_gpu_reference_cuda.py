@@ -3,10 +3,11 @@ kernels), built from the reference sources for sm_100a by oracle/build_ref.py
 (oracle/_ref/libref_cuda.so), running on the same GPU.
 
 Teacher-forced: the reference's CUDA Model::forward and the engine consume
-the golden token sequence; per-step logits are compared with the same bound
-as against the oracle (max(3e-2, 1.5x the reference-CPU-vs-oracle envelope,
-one BF16 ulp); cosine), and the reference's CUDA-vs-CPU spread is reported
-beside it.
+the golden token sequence; per-step logits are compared.  Both sides now
+carry their own fp32-order noise (each within the reference-CPU-vs-oracle
+envelope of the fixture), so the bound is the sum of two envelopes: max
+|d| <= max(3e-2, 2.5x envelope, one BF16 ulp), cosine >= 1 - 2.5 (1 - env).
+The reference's own CUDA-vs-CPU spread is reported beside it.
 """
 import os
 
@@ -46,7 +47,11 @@ def test_reference_cuda_ops_match(refcuda):
         y = empty_bf16(o)
         be.matmul(dev(x), dev(w), y)
         assert_bf16_close(host(y), refcuda.gemv(x, w), rtol=1e-2, atol=1e-3 * np.sqrt(i), min_exact=0.85)
-    for qh, kvh, pos in [(32, 32, 1024), (32, 8, 4095), (16, 8, 777)]:
+    # Longest context first: the reference sizes its flash-attention scratch
+    # once, from its first call's key length and query heads
+    # (src/lib/backend/cuda/backend.cu:89-91,124-134); a later, longer call
+    # would overflow it.  This library derives the split count per call.
+    for qh, kvh, pos in [(32, 8, 4095), (32, 32, 1024), (16, 8, 777)]:
         q = uniform_bf16(G.seed_of("rc.attn.q", qh, kvh, pos), (qh, 128))
         kc = uniform_bf16(G.seed_of("rc.attn.k", qh, kvh, pos), (pos + 1, kvh, 128))
         vc = uniform_bf16(G.seed_of("rc.attn.v", qh, kvh, pos), (pos + 1, kvh, 128))
@@ -66,9 +71,10 @@ def test_engine_vs_reference_cuda_teacher_forced(refcuda, name):
                      tied=bool(tied))
     rm = refcuda.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)), seed=0)
     toks = g["tokens"].astype(np.uint32)
-    atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
-    min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
+    atol = max(3e-2, 2.5 * float(g["env_maxabs"].max()))
+    min_cos = min(0.9999, 1.0 - 2.5 * (1.0 - float(g["env_cos"].min())))
     worst = worst_ref = 0.0
+    worst_cos = 1.0
     agree = 0
     with Engine(qc, capacity=cap) as e:
         e.init_synthetic(0)
@@ -79,13 +85,15 @@ def test_engine_vs_reference_cuda_teacher_forced(refcuda, name):
             mine = e.logits()
             r_next = rm.forward(int(t))
             ref = rm.logits()
-            d, _ = assert_logits_close(mine, ref, atol=atol, n_ulp=1, min_cos=min_cos)
+            d, c = assert_logits_close(mine, ref, atol=atol, n_ulp=1, min_cos=min_cos)
             worst = max(worst, d)
+            worst_cos = min(worst_cos, c)
             # the reference's own CUDA vs CPU spread at this step (top-16 of the CPU run)
             ti = g["top_idx"][i]
             worst_ref = max(worst_ref, float(np.abs(bf(ref[ti]) - bf(g["top_val"][i])).max()))
             agree += int(int(np.argmax(bf(mine))) == r_next)
     rm.close()
     assert agree >= len(toks) - 1
-    print(f"{name}: engine vs reference CUDA max |dlogit| {worst:.4f}; reference CUDA vs reference CPU "
+    print(f"{name}: engine vs reference CUDA max |dlogit| {worst:.4f}, min cosine {worst_cos:.6f}; "
+          f"reference CUDA vs reference CPU "
           f"(top-16) {worst_ref:.4f}; argmax agreement {agree}/{len(toks)}")
