@@ -45,11 +45,26 @@ def parse_args():
     ap.add_argument("--prompt", type=int, default=0, help="profiling only: override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path instead of the "
+                                                          "persistent kernel (the tensor-parallel path)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=3)
     ap.add_argument("--reference-cuda-tokens", type=int, default=0,
                     help="also time the reference's own cuBLAS CUDA backend (oracle/_ref/libref_cuda.so) for this "
                          "many Model::forward calls at mid-window context; reported as reference_cuda")
     return ap.parse_args()
+
+
+def read_traffic_ratio(model_name):
+    """DRAM bytes / algorithmic bytes of the dominant kernel, from the committed
+    ncu summary profiles/traffic_<model>.md ("dram_bytes_per_algorithmic_byte: X")."""
+    p = os.path.join(ROOT, "profiles", f"traffic_{model_name}.md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("dram_bytes_per_algorithmic_byte:"):
+                return float(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
 
 
 def measured_peaks():
@@ -241,6 +256,8 @@ def main():
 
     eng = ib.Engine(cfg, capacity=capacity, device=local, tp_rank=rank, tp_size=world)
     eng.init_synthetic(0)
+    if a.graph and eng.persistent:
+        eng.persistent = False
     if world > 1:
         obj = [ib.Engine.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(obj, src=0)
@@ -309,33 +326,44 @@ def main():
                "d2h_bytes_per_step": int(window * 4),
                "includes": "prompt H2D, prefill of the prompt, decode, token D2H"}
 
-    # ---- dominant kernel (GEMV) roofline: one eager step, CUDA events around each launch
+    # ---- dominant kernel roofline
+    peak, peak_kind = measured_peaks()
+    avg_pos = start_pos + (window - 1) / 2.0
+    bytes_tok = cfg.weight_bytes() + cfg.kv_bytes_per_position() * (avg_pos + 1)
     mid = start_pos + window // 2
+    # the kernel-per-op path, one eager step with CUDA events around each launch (diagnostic)
     eng.set_position(mid)
     g_ms, g_launch, g_bytes = eng.profile_step(0)
     eng.set_position(mid)
     at_ms, at_launch, at_bytes = eng.profile_step(1)
-    peak, peak_kind = measured_peaks()
-    achieved = g_bytes / (g_ms / 1000.0) / 1e9
-    traffic = None
-    tr_path = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tr_path):
-        try:
-            tr = json.load(open(tr_path)).get(cfg.name)
-            if tr:  # measured DRAM bytes / algorithmic bytes of the same launches, applied per launch here
-                traffic = round(tr["ratio"] * g_bytes / g_launch)
-        except Exception:
-            traffic = None
-    roofline = {"kernel": "gemv_kernel (every GEMV launch of one decode step; per-launch averages)",
-                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                "traffic": traffic, "algorithmic_bytes_per_launch": round(g_bytes / g_launch),
-                "launch_ms_avg": round(g_ms / g_launch, 5), "launches_per_step": g_launch,
-                "attention": {"achieved_gbs": round(at_bytes / (at_ms / 1000.0) / 1e9, 1),
-                              "launch_ms_avg": round(at_ms / max(1, at_launch), 5)}}
+    eager = {"gemv_gbs": round(g_bytes / (g_ms / 1000.0) / 1e9, 1), "gemv_launch_ms_avg": round(g_ms / g_launch, 5),
+             "gemv_launches_per_step": g_launch,
+             "attention_gbs": round(at_bytes / (at_ms / 1000.0) / 1e9, 1),
+             "attention_launch_ms_avg": round(at_ms / max(1, at_launch), 5)}
+    traffic_ratio = read_traffic_ratio(cfg.name)
+    if eng.persistent:
+        # one cooperative launch per bench step: algorithmic bytes of the whole window / its device time
+        per_launch = bytes_tok * window / world
+        achieved = bytes_tok * tok_s / 1e9 / world
+        roofline = {"kernel": "persistent_decode_kernel (one cooperative launch = one decode window of "
+                              f"{window} tokens)",
+                    "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                    "traffic": round(traffic_ratio * per_launch) if traffic_ratio else None,
+                    "algorithmic_bytes_per_launch": round(per_launch), "launch_ms_avg": round(ms / a.steps, 3),
+                    "kernel_per_op_path": eager}
+        launches = a.steps
+    else:
+        achieved = g_bytes / (g_ms / 1000.0) / 1e9
+        roofline = {"kernel": "gemv_kernel (every GEMV launch of one decode step; per-launch averages)",
+                    "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                    "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                    "traffic": round(traffic_ratio * g_bytes / g_launch) if traffic_ratio else None,
+                    "algorithmic_bytes_per_launch": round(g_bytes / g_launch),
+                    "launch_ms_avg": round(g_ms / g_launch, 5), "launches_per_step": g_launch,
+                    "kernel_per_op_path": eager}
+        launches = (cfg.layers * 5 + 1) * window * a.steps
     # whole-step roofline: weights + average KV read per token over the window, all ranks
-    avg_pos = start_pos + (window - 1) / 2.0
-    bytes_tok = cfg.weight_bytes() + cfg.kv_bytes_per_position() * (avg_pos + 1)
     step_roof = {"bytes_per_token": int(bytes_tok), "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1),
                  "peak_gbs": peak * world, "frac": round(bytes_tok * tok_s / 1e9 / (peak * world), 4)}
 
@@ -356,7 +384,7 @@ def main():
 
     # ---- the reference's own CUDA backend on the same GPU (optional, rank 0, N = 1)
     ref_cuda = None
-    if rank == 0 and world == 1 and a.reference_cuda_tokens > 0:
+    if rank == 0 and world == 1 and a.reference_cuda_tokens > 0:  # noqa: SIM102
         try:
             from oracle import ModelConfig, RefLib
 
@@ -388,10 +416,11 @@ def main():
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
                        "decode_tokens_per_step": window, "global_batch": 1,
+                       "decode_path": "persistent kernel" if eng.persistent else "CUDA graph of fused kernels",
                        "parallelism": f"tp{world}", "weights": "random N(0,0.02) seed 0, ids seed 1",
                        "l2_flush": f"not needed: {cfg.weight_bytes() / 1e9:.1f} GB of weights streamed per token "
                                    f">> 126 MB L2"},
-            "clocks": clock, "e2e": e2e, "gpu_launches": int((cfg.layers * 5 + 1) * window * a.steps),
+            "clocks": clock, "e2e": e2e, "gpu_launches": int(launches),
             "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu,
         }
         if ref_cuda is not None:

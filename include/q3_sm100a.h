@@ -207,6 +207,22 @@ Q3_API int q3_engine_generate(q3_engine* e, const uint32_t* prompt_host, size_t 
  * after one prefill. */
 Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
 
+/* Decode-step implementation: 1 (default on a single GPU when the model's
+ * shared-memory plan fits) runs n steps as one persistent cooperative kernel
+ * (one CTA per SM streaming all weights through a TMA ring, grid barriers
+ * between phases); 0 replays the per-step CUDA graph of fused kernels (the
+ * tensor-parallel path).  Both produce the same tokens. */
+Q3_API int q3_engine_set_persistent(q3_engine* e, int enable);
+Q3_API int q3_engine_is_persistent(q3_engine* e);
+
+/* Phase timeline of the persistent kernel (tracing): with enable = 1 the next
+ * launches record, for the first step of each launch, per CTA and phase
+ * (5 per layer + lm_head) four %globaltimer stamps in ns: consumer start,
+ * consumer end, producer first issue, producer last issue.  out_host (if not
+ * NULL) receives the last record, [ctas][phases][4] uint64. */
+Q3_API int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases,
+                           size_t* n_ctas);
+
 /* State readers (the reference keeps these as public members). */
 Q3_API int q3_engine_position(q3_engine* e, size_t* pos);
 Q3_API int q3_engine_logits(q3_engine* e, uint16_t* out_host);  /* this rank's vocab shard */

@@ -24,6 +24,7 @@ enum DeviceError : uint32_t {
     DEV_PEER_WAIT_TIMEOUT = 2,
     DEV_BAD_TOKEN = 3,
     DEV_BAD_POSITION = 4,
+    DEV_GRID_TIMEOUT = 5,
 };
 
 // Upper bound on mbarrier polls before a kernel gives up (each try_wait

@@ -65,6 +65,13 @@ struct q3_engine {
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
     uint32_t *done_counter = nullptr, *head_counters = nullptr, *err = nullptr;
     int attn_splits = 1;
+    // persistent decode kernel (one launch per run of steps)
+    bool persistent = false;
+    q3::PersistentArgs pargs{};
+    q3::PersistentLayer* d_layers = nullptr;
+    unsigned long long* d_trace = nullptr;
+    uint32_t* gsync = nullptr;
+    uint32_t* abort_word = nullptr;
     // graph / comms
     cudaGraphExec_t graph = nullptr;
     ncclComm_t comm = nullptr;
@@ -309,8 +316,12 @@ int check_device_error(q3_engine* e) {
     Q3_CUDA(cudaMemcpy(&err, e->err, sizeof(err), cudaMemcpyDeviceToHost));
     if (err != 0) {
         static const char* names[] = {"ok", "TMA wait timed out", "peer wait timed out", "token id out of range",
-                                      "position out of range"};
-        return fail(Q3_ERR_DEVICE, std::string("device error: ") + (err < 5 ? names[err] : "unknown"));
+                                      "position out of range", "grid barrier timed out"};
+        // clear the error and the persistent kernel's barrier state so the engine stays usable
+        cudaMemset(e->err, 0, 4);
+        if (e->gsync) cudaMemset(e->gsync, 0, 8);
+        if (e->abort_word) cudaMemset(e->abort_word, 0, 4);
+        return fail(Q3_ERR_DEVICE, std::string("device error: ") + (err < 6 ? names[err] : "unknown"));
     }
     return Q3_OK;
 }
@@ -460,6 +471,74 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
+
+    // ---- persistent decode kernel (single GPU)
+    if (tp_size == 1) {
+        PersistentArgs& a = e->pargs;
+        a.H = e->H;
+        a.qd = e->qd;
+        a.kd = e->kd;
+        a.il = e->il;
+        a.vl = e->vl;
+        a.qh = e->qh;
+        a.kvh = e->kvh;
+        a.layers = static_cast<int>(c.layers);
+        a.vocab = static_cast<int>(c.vocab);
+        a.capacity = static_cast<int>(c.capacity);
+        a.voff = e->voff;
+        a.eps = c.eps;
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+        if (optin > 0 && plan_persistent(a, e->sms, static_cast<size_t>(optin))) {
+            std::vector<PersistentLayer> hl(c.layers);
+            for (size_t l = 0; l < c.layers; ++l) {
+                const LayerW& L = e->layers[l];
+                hl[l] = PersistentLayer{L.w_qkv, L.w_o, L.w_gu, L.w_down, L.in_norm, L.post_norm,
+                                        L.q_norm, L.k_norm, L.k_pages, L.v_pages};
+            }
+            const int Gl = e->qh / e->kvh;
+            const int HG = Gl >= 4 ? 4 : Gl;
+            float* att_part = nullptr;
+            uint32_t* att_cnt = nullptr;
+            if ((rc = dalloc_t(e, &e->d_layers, hl.size())) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &att_part, static_cast<size_t>(e->kvh) * a.nqb * a.splits * HG * 130)) != Q3_OK)
+                return bail(rc);
+            if ((rc = dalloc_t(e, &att_cnt, static_cast<size_t>(e->kvh) * a.nqb + 4)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &e->gsync, 4)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &e->abort_word, 4)) != Q3_OK) return bail(rc);
+            cudaMemcpy(e->d_layers, hl.data(), hl.size() * sizeof(PersistentLayer), cudaMemcpyHostToDevice);
+            cudaMemset(att_cnt, 0, (static_cast<size_t>(e->kvh) * a.nqb + 4) * 4);
+            cudaMemset(e->gsync, 0, 16);
+            cudaMemset(e->abort_word, 0, 16);
+            a.L = e->d_layers;
+            a.embed = e->embed;
+            a.lm_head = e->lm_head;
+            a.final_norm = e->final_norm;
+            a.page_table = e->page_table;
+            a.rope_cos = e->rope_cos;
+            a.rope_sin = e->rope_sin;
+            a.hs = e->hs[0];
+            a.q = e->q;
+            a.attn = e->attn;
+            a.g = e->g;
+            a.logits = e->logits;
+            a.vsum = e->vsum;
+            a.att_part = att_part;
+            a.att_counters = att_cnt;
+            a.pos = e->pos;
+            a.n_forced = e->n_forced;
+            a.tokens = e->tokens;
+            a.argmax_hist = e->argmax_hist;
+            a.key_slot = reinterpret_cast<unsigned long long*>(e->key_slot);
+            a.key_out = reinterpret_cast<unsigned long long*>(e->keys);
+            a.done_counter = e->done_counter;
+            a.head_counters = e->head_counters;
+            a.gsync = e->gsync;
+            a.err = e->err;
+            a.abort = e->abort_word;
+            // available; q3_engine_set_persistent selects it (the graph path is the default)
+        }
+    }
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "engine setup failed"));
     *out = e;
     return Q3_OK;
@@ -617,8 +696,18 @@ int q3_engine_step(q3_engine* e, size_t n) {
     if (e->host_pos + n > e->cfg.capacity)
         return fail(Q3_ERR_INVALID, "q3_engine_step: KV cache capacity exceeded");
     Q3_CUDA(cudaSetDevice(e->device));
-    Q3_TRY(build_graph(e));
-    for (size_t i = 0; i < n; ++i) Q3_CUDA(cudaGraphLaunch(e->graph, e->stream));
+    if (e->persistent) {
+        // one cooperative launch runs all n steps; bound a launch to 1 << 20 steps
+        for (size_t done = 0; done < n;) {
+            const size_t k = (n - done) < (1u << 20) ? (n - done) : (1u << 20);
+            e->pargs.n_steps = static_cast<int>(k);
+            Q3_CUDA(launch_persistent(e->pargs, e->stream));
+            done += k;
+        }
+    } else {
+        Q3_TRY(build_graph(e));
+        for (size_t i = 0; i < n; ++i) Q3_CUDA(cudaGraphLaunch(e->graph, e->stream));
+    }
     e->host_pos += n;
     if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
     return Q3_OK;
@@ -723,6 +812,44 @@ int q3_engine_set_position(q3_engine* e, size_t pos) {
     Q3_CUDA(cudaStreamSynchronize(e->stream));
     e->host_max_pos = reached;
     e->host_pos = pos;
+    return Q3_OK;
+}
+
+int q3_engine_set_persistent(q3_engine* e, int enable) {
+    Q3_CHECK(e, "null engine");
+    if (enable && !e->pargs.L) return fail(Q3_ERR_UNSUPPORTED, "persistent decode kernel unavailable for this engine");
+    e->persistent = enable != 0;
+    return Q3_OK;
+}
+
+int q3_engine_is_persistent(q3_engine* e) { return (e && e->persistent) ? 1 : 0; }
+
+int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases, size_t* n_ctas) {
+    Q3_CHECK(e && n_phases && n_ctas, "null argument");
+    if (!e->persistent) return fail(Q3_ERR_UNSUPPORTED, "the phase timeline needs the persistent decode kernel");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const size_t phases = e->layers.size() * 5 + 1;
+    const size_t n = static_cast<size_t>(e->pargs.grid) * phases * 4;
+    *n_phases = phases;
+    *n_ctas = static_cast<size_t>(e->pargs.grid);
+    if (enable) {
+        if (!e->pargs.trace) {
+            if (!e->d_trace) {
+                int rc = dalloc_t(e, &e->d_trace, n);
+                if (rc != Q3_OK) return rc;
+            }
+            Q3_CUDA(cudaMemset(e->d_trace, 0, n * 8));
+        }
+        e->pargs.trace = e->d_trace;
+        e->pargs.trace_phases = static_cast<int>(phases);
+    } else {
+        e->pargs.trace = nullptr;
+    }
+    if (out_host && e->d_trace) {
+        Q3_CHECK(capacity >= n, "q3_engine_trace: output buffer too small");
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_CUDA(cudaMemcpy(out_host, e->d_trace, n * 8, cudaMemcpyDeviceToHost));
+    }
     return Q3_OK;
 }
 

@@ -104,6 +104,46 @@ int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
 
+// ---------------------------------------------------------------- persistent decode
+struct PersistentLayer {
+    const bf16 *w_qkv, *w_o, *w_gu, *w_down;
+    const bf16 *in_norm, *post_norm, *q_norm, *k_norm;
+    bf16 *k_pages, *v_pages;
+};
+
+struct PersistentArgs {
+    // shapes (this rank)
+    int H, qd, kd, il, vl, qh, kvh, nqb, splits, layers, vocab, capacity, n_steps;
+    uint32_t voff;
+    float eps;
+    // weights and tables
+    const PersistentLayer* L;  // device array [layers]
+    const bf16 *embed, *lm_head, *final_norm;
+    const int32_t* page_table;
+    const float *rope_cos, *rope_sin;
+    // activations
+    bf16 *hs, *q, *attn, *g, *logits;
+    float* vsum;
+    float* att_part;          // [kvh * nqb][splits][HG][130]
+    uint32_t* att_counters;   // [kvh * nqb]
+    // control
+    int32_t *pos, *n_forced, *tokens, *argmax_hist;
+    unsigned long long *key_slot, *key_out;
+    uint32_t *done_counter, *head_counters;
+    uint32_t* gsync;          // [count, generation]
+    uint32_t *err, *abort;
+    // optional phase timeline of the first step: [grid][phases][4] globaltimer
+    // ns = consumer start, consumer end, producer first issue, producer last issue
+    unsigned long long* trace;
+    int trace_phases;
+    // launch / shared-memory plan (plan_persistent)
+    int grid;
+    uint32_t ring_slots;
+    size_t off_bars, off_x, off_part, off_misc, smem;
+};
+bool plan_persistent(PersistentArgs& a, int sms, size_t smem_limit);
+cudaError_t launch_persistent(const PersistentArgs& a, cudaStream_t s);
+
 // ---------------------------------------------------------------- small ops
 cudaError_t launch_embedding(const bf16* table, int hidden, uint32_t token, bf16* out, cudaStream_t s);
 cudaError_t launch_rmsnorm(const bf16* x, const bf16* w, bf16* out, int n, float eps, cudaStream_t s);

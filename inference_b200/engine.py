@@ -93,6 +93,27 @@ class Engine:
                                        C.byref(n)))
         return out[: n.value].copy()
 
+    @property
+    def persistent(self) -> bool:
+        return bool(lib().q3_engine_is_persistent(self.h))
+
+    @persistent.setter
+    def persistent(self, on: bool):
+        check(lib().q3_engine_set_persistent(self.h, int(bool(on))))
+
+    def trace(self, enable: bool = True):
+        """Turn the persistent kernel's phase timeline on/off."""
+        ph, ct = C.c_size_t(), C.c_size_t()
+        check(lib().q3_engine_trace(self.h, int(enable), None, 0, C.byref(ph), C.byref(ct)))
+
+    def read_trace(self) -> np.ndarray:
+        """[ctas, phases, 4] ns: consumer start/end, producer first/last issue (first step of the last launch)."""
+        ph, ct = C.c_size_t(), C.c_size_t()
+        check(lib().q3_engine_trace(self.h, 1, None, 0, C.byref(ph), C.byref(ct)))
+        out = np.zeros(ct.value * ph.value * 4, np.uint64)
+        check(lib().q3_engine_trace(self.h, 1, out.ctypes.data, out.size, C.byref(ph), C.byref(ct)))
+        return out.reshape(ct.value, ph.value, 4)
+
     def set_position(self, pos: int):
         check(lib().q3_engine_set_position(self.h, pos))
 
