@@ -217,9 +217,12 @@ Q3_API int q3_engine_is_persistent(q3_engine* e);
 
 /* Phase timeline of the persistent kernel (tracing): with enable = 1 the next
  * launches record, for the first step of each launch, per CTA and phase
- * (5 per layer + lm_head) four %globaltimer stamps in ns: consumer start,
- * consumer end, producer first issue, producer last issue.  out_host (if not
- * NULL) receives the last record, [ctas][phases][4] uint64. */
+ * (5 per layer + lm_head) eight uint64 words: [0] phase start and [1] phase
+ * end (%globaltimer ns), [2..7] inner marks of the phase (GEMV: input ready,
+ * dot products done, first item landed, ns spent waiting for items;
+ * attention: pages start, split state published, first page landed, pages
+ * done, split state written).  out_host (if not NULL) receives the last
+ * record, [ctas][phases][8]; capacity counts uint64 words. */
 Q3_API int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases,
                            size_t* n_ctas);
 

@@ -68,9 +68,9 @@ struct q3_engine {
     // persistent decode kernel (one launch per run of steps)
     bool persistent = false;
     q3::PersistentArgs pargs{};
-    q3::PersistentLayer* d_layers = nullptr;
+    uint32_t* d_layer_tab = nullptr;
     unsigned long long* d_trace = nullptr;
-    uint32_t* gsync = nullptr;
+    unsigned long long* gsync = nullptr;
     uint32_t* abort_word = nullptr;
     // graph / comms
     cudaGraphExec_t graph = nullptr;
@@ -319,7 +319,7 @@ int check_device_error(q3_engine* e) {
                                       "position out of range", "grid barrier timed out"};
         // clear the error and the persistent kernel's barrier state so the engine stays usable
         cudaMemset(e->err, 0, 4);
-        if (e->gsync) cudaMemset(e->gsync, 0, 8);
+        if (e->gsync) cudaMemset(e->gsync, 0, 16);
         if (e->abort_word) cudaMemset(e->abort_word, 0, 4);
         return fail(Q3_ERR_DEVICE, std::string("device error: ") + (err < 6 ? names[err] : "unknown"));
     }
@@ -442,7 +442,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     // ---- activations and control
     if ((rc = dalloc_t(e, &e->hs[0], H)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->hs[1], H)) != Q3_OK) return bail(rc);
-    if ((rc = dalloc_t(e, &e->q, e->qd)) != Q3_OK) return bail(rc);
+    // q, then this step's raw key rows (the persistent kernel normalises them in its attention phase)
+    if ((rc = dalloc_t(e, &e->q, static_cast<size_t>(e->qd) + e->kd)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->attn, e->qd)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->g, e->il)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->logits, e->vl)) != Q3_OK) return bail(rc);
@@ -496,47 +497,69 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
                 hl[l] = PersistentLayer{L.w_qkv, L.w_o, L.w_gu, L.w_down, L.in_norm, L.post_norm,
                                         L.q_norm, L.k_norm, L.k_pages, L.v_pages};
             }
-            const int Gl = e->qh / e->kvh;
-            const int HG = Gl >= 4 ? 4 : Gl;
+            const int HG = attention_head_group(e->qh, e->kvh);
             float* att_part = nullptr;
             uint32_t* att_cnt = nullptr;
-            if ((rc = dalloc_t(e, &e->d_layers, hl.size())) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_t(e, &att_part, static_cast<size_t>(e->kvh) * a.nqb * a.splits * HG * 130)) != Q3_OK)
-                return bail(rc);
-            if ((rc = dalloc_t(e, &att_cnt, static_cast<size_t>(e->kvh) * a.nqb + 4)) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_t(e, &e->gsync, 4)) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_t(e, &e->abort_word, 4)) != Q3_OK) return bail(rc);
-            cudaMemcpy(e->d_layers, hl.data(), hl.size() * sizeof(PersistentLayer), cudaMemcpyHostToDevice);
-            cudaMemset(att_cnt, 0, (static_cast<size_t>(e->kvh) * a.nqb + 4) * 4);
-            cudaMemset(e->gsync, 0, 16);
-            cudaMemset(e->abort_word, 0, 16);
-            a.L = e->d_layers;
-            a.embed = e->embed;
-            a.lm_head = e->lm_head;
-            a.final_norm = e->final_norm;
-            a.page_table = e->page_table;
-            a.rope_cos = e->rope_cos;
-            a.rope_sin = e->rope_sin;
-            a.hs = e->hs[0];
-            a.q = e->q;
-            a.attn = e->attn;
-            a.g = e->g;
-            a.logits = e->logits;
-            a.vsum = e->vsum;
-            a.att_part = att_part;
-            a.att_counters = att_cnt;
-            a.pos = e->pos;
-            a.n_forced = e->n_forced;
-            a.tokens = e->tokens;
-            a.argmax_hist = e->argmax_hist;
-            a.key_slot = reinterpret_cast<unsigned long long*>(e->key_slot);
-            a.key_out = reinterpret_cast<unsigned long long*>(e->keys);
-            a.done_counter = e->done_counter;
-            a.head_counters = e->head_counters;
-            a.gsync = e->gsync;
-            a.err = e->err;
-            a.abort = e->abort_word;
-            // available; q3_engine_set_persistent selects it (the graph path is the default)
+            // pointer table: 32-bit offsets in 256-byte units from the lowest pointer
+            unsigned long long base = ~0ull, top = 0;
+            bool aligned = true;
+            for (const PersistentLayer& L : hl) {
+                const void* const* ptrs = reinterpret_cast<const void* const*>(&L);
+                for (int i = 0; i < kLayerPtrs; ++i) {
+                    const auto v = reinterpret_cast<unsigned long long>(ptrs[i]);
+                    base = std::min(base, v);
+                    top = std::max(top, v);
+                    aligned = aligned && (v % 256 == 0);
+                }
+            }
+            std::vector<uint32_t> tab(hl.size() * kLayerPtrs);
+            for (size_t l = 0; l < hl.size(); ++l) {
+                const void* const* ptrs = reinterpret_cast<const void* const*>(&hl[l]);
+                for (int i = 0; i < kLayerPtrs; ++i)
+                    tab[l * kLayerPtrs + i] =
+                        static_cast<uint32_t>((reinterpret_cast<unsigned long long>(ptrs[i]) - base) >> 8);
+            }
+            // otherwise the persistent kernel stays unavailable (layer_tab null)
+            const bool fits = aligned && ((top - base) >> 8) < (1ull << 32);
+            if (fits) {
+                if ((rc = dalloc_t(e, &e->d_layer_tab, tab.size())) != Q3_OK) return bail(rc);
+                cudaMemcpy(e->d_layer_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
+                a.layer_tab = e->d_layer_tab;
+                a.layer_base = base;
+                if ((rc = dalloc_t(e, &att_part, static_cast<size_t>(e->kvh) * a.nqb * a.splits * HG * kAttRecord)) != Q3_OK)
+                    return bail(rc);
+                if ((rc = dalloc_t(e, &att_cnt, static_cast<size_t>(e->kvh) * a.nqb + 4)) != Q3_OK) return bail(rc);
+                if ((rc = dalloc_t(e, &e->gsync, 2)) != Q3_OK) return bail(rc);
+                if ((rc = dalloc_t(e, &e->abort_word, 4)) != Q3_OK) return bail(rc);
+                cudaMemset(att_cnt, 0, (static_cast<size_t>(e->kvh) * a.nqb + 4) * 4);
+                cudaMemset(e->gsync, 0, 16);
+                cudaMemset(e->abort_word, 0, 16);
+                a.embed = e->embed;
+                a.lm_head = e->lm_head;
+                a.final_norm = e->final_norm;
+                a.page_table = e->page_table;
+                a.rope_cos = e->rope_cos;
+                a.rope_sin = e->rope_sin;
+                a.hs = e->hs[0];
+                a.q = e->q;
+                a.attn = e->attn;
+                a.g = e->g;
+                a.logits = e->logits;
+                a.vsum = e->vsum;
+                a.att_part = att_part;
+                a.att_counters = att_cnt;
+                a.pos = e->pos;
+                a.n_forced = e->n_forced;
+                a.tokens = e->tokens;
+                a.argmax_hist = e->argmax_hist;
+                a.key_slot = reinterpret_cast<unsigned long long*>(e->key_slot);
+                a.key_out = reinterpret_cast<unsigned long long*>(e->keys);
+                a.done_counter = e->done_counter;
+                a.gsync = e->gsync;
+                a.err = e->err;
+                a.abort = e->abort_word;
+                // available; q3_engine_set_persistent selects it (the graph path is the default)
+            }
         }
     }
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "engine setup failed"));
@@ -817,7 +840,7 @@ int q3_engine_set_position(q3_engine* e, size_t pos) {
 
 int q3_engine_set_persistent(q3_engine* e, int enable) {
     Q3_CHECK(e, "null engine");
-    if (enable && !e->pargs.L) return fail(Q3_ERR_UNSUPPORTED, "persistent decode kernel unavailable for this engine");
+    if (enable && !e->pargs.layer_tab) return fail(Q3_ERR_UNSUPPORTED, "persistent decode kernel unavailable for this engine");
     e->persistent = enable != 0;
     return Q3_OK;
 }
@@ -829,7 +852,7 @@ int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacit
     if (!e->persistent) return fail(Q3_ERR_UNSUPPORTED, "the phase timeline needs the persistent decode kernel");
     Q3_CUDA(cudaSetDevice(e->device));
     const size_t phases = e->layers.size() * 5 + 1;
-    const size_t n = static_cast<size_t>(e->pargs.grid) * phases * 4;
+    const size_t n = static_cast<size_t>(e->pargs.grid) * phases * kTraceWords;
     *n_phases = phases;
     *n_ctas = static_cast<size_t>(e->pargs.grid);
     if (enable) {

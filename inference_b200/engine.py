@@ -107,12 +107,13 @@ class Engine:
         check(lib().q3_engine_trace(self.h, int(enable), None, 0, C.byref(ph), C.byref(ct)))
 
     def read_trace(self) -> np.ndarray:
-        """[ctas, phases, 4] ns: consumer start/end, producer first/last issue (first step of the last launch)."""
+        """[ctas, phases, 8] globaltimer ns of the first step of the last launch: [..., 0] phase start,
+        [..., 1] phase end, [..., 2:] inner marks (listed in csrc/persistent.cu)."""
         ph, ct = C.c_size_t(), C.c_size_t()
         check(lib().q3_engine_trace(self.h, 1, None, 0, C.byref(ph), C.byref(ct)))
-        out = np.zeros(ct.value * ph.value * 4, np.uint64)
+        out = np.zeros(ct.value * ph.value * 8, np.uint64)
         check(lib().q3_engine_trace(self.h, 1, out.ctypes.data, out.size, C.byref(ph), C.byref(ct)))
-        return out.reshape(ct.value, ph.value, 4)
+        return out.reshape(ct.value, ph.value, -1)
 
     def set_position(self, pos: int):
         check(lib().q3_engine_set_position(self.h, pos))
