@@ -123,7 +123,7 @@ inline int attention_head_group(int q_heads, int kv_heads) {
     return g % 4 == 0 ? 4 : (g % 2 == 0 ? 2 : 1);
 }
 
-constexpr int kTraceWords = 8;
+constexpr int kTraceWords = Q3_TRACE_WORDS;
 
 struct PersistentArgs {
     // shapes (this rank)

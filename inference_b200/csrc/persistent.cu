@@ -55,6 +55,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ void red_release_add(unsigned long long* p, unsigned long long v) {
     asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+__device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
     return *reinterpret_cast<const volatile uint32_t*>(p);
 }
@@ -73,20 +78,32 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Phase timeline of the first step of a launch, kTraceWords globaltimer marks
-// per (CTA, phase): [0] start, [1] end; GEMV: [2] input ready, [3] dot
-// products done, [4] first item landed (warp 0), [5] / [6] ns warp 0 spent
-// waiting for items / issuing refills; attention: [2] pages start, [3] split state published, [4] first
-// page landed, [5] pages done, [6] split state written, [7] ns spent issuing
-// refills.
-__device__ __forceinline__ void trace_mark(const PersistentArgs& a, int step, int phase, int what) {
-    if (a.trace && step == 0 && phase < a.trace_phases)
-        a.trace[(static_cast<size_t>(blockIdx.x) * a.trace_phases + phase) * kTraceWords + what] = now_ns();
+// Phase timeline of the first step of a launch, kTraceWords words per (CTA,
+// phase): [0] / [1] %globaltimer ns at phase start / end (comparable across
+// CTAs), [2] / [3] clock64 at phase start / end (cycles per ns), then SM
+// cycles of thread 0's view of the phase: GEMV [4] input ready, [5] waiting
+// for items, [6] issuing refills, [7] input ready -> dot products done;
+// attention [4] q/k norm, [5] page loop, [6] waiting for pages, [7] split
+// merge and publish, [9] computing on pages; [8] the SM the CTA runs on.
+__device__ __forceinline__ unsigned long long* trace_at(const PersistentArgs& a, int step, int phase) {
+    return (a.trace && step == 0 && phase < a.trace_phases)
+               ? a.trace + (static_cast<size_t>(blockIdx.x) * a.trace_phases + phase) * kTraceWords
+               : nullptr;
+}
+__device__ __forceinline__ void trace_edge(const PersistentArgs& a, int step, int phase, int end) {
+    if (unsigned long long* t = trace_at(a, step, phase)) {
+        t[end] = now_ns();
+        t[2 + end] = clock64();
+        if (!end) {
+            uint32_t sm;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+            t[8] = sm;
+        }
+    }
 }
 __device__ __forceinline__ void trace_put(const PersistentArgs& a, int step, int phase, int what,
                                           unsigned long long v) {
-    if (a.trace && step == 0 && phase < a.trace_phases)
-        a.trace[(static_cast<size_t>(blockIdx.x) * a.trace_phases + phase) * kTraceWords + what] = v;
+    if (unsigned long long* t = trace_at(a, step, phase)) t[what] = v;
 }
 
 // ----------------------------------------------------------------- work split
@@ -244,24 +261,28 @@ struct Ctx {
     uint32_t gi;               // global index of the current phase's first item
     unsigned long long nsync;  // grid barriers passed (thread 0)
     int tstep, tph;            // step and phase of the step (timeline)
+    unsigned long long tc0;    // clock64 at the phase start (thread 0, timeline)
 };
 
-__device__ __forceinline__ void tmark(const Ctx& c, int what) {
-    if (c.tid == 0) trace_mark(*c.a, c.tstep, c.tph, what);
-}
+// thread 0: cycles since the phase began (for the inner trace words)
+__device__ __forceinline__ unsigned long long tcyc(const Ctx& c) { return clock64() - c.tc0; }
 
 __device__ __forceinline__ void cbar(int id, int n) { named_bar(id, n); }
 
-// Issue item k of phase p into `slot` (whose previous item this thread's CTA consumed).
-__device__ __forceinline__ void issue(Ctx& c, int p, uint32_t k, uint32_t slot) {
-    const void* src;
-    uint32_t bytes;
-    const bool kv = c.seq.desc(p, k, &src, &bytes);
+// Copy `bytes` from src into `slot` (whose previous item this CTA consumed).
+__device__ __forceinline__ void issue_copy(Ctx& c, uint32_t slot, const void* src, uint32_t bytes, bool kv) {
     fence_proxy_async_smem();
     if (kv) fence_proxy_async_global();
     atomicAdd(&c.s.issued[slot], 1u);
     mbar_arrive_expect_tx(&c.s.full[slot], bytes);
     bulk_g2s(c.s.ring + static_cast<size_t>(slot) * kSlot, src, bytes, &c.s.full[slot], policy_evict_first());
+}
+// Issue item k of phase p into `slot`.
+__device__ __forceinline__ void issue(Ctx& c, int p, uint32_t k, uint32_t slot) {
+    const void* src;
+    uint32_t bytes;
+    const bool kv = c.seq.desc(p, k, &src, &bytes);
+    issue_copy(c, slot, src, bytes, kv);
 }
 
 // The item S after (p, k), if the launch has one, goes into `slot`.
@@ -386,24 +407,25 @@ __device__ Band gemv_consume(Ctx& c, int p, int N, int K, int row_gran) {
     const int nrows = b.r1 - b.r0;
     for (int i = c.tid; i < nrows * P; i += c.nt) c.s.part[i] = 0.f;
     cbar(1, c.nt);
-    tmark(c, 2);
+    const bool tw = a.trace && c.tid == 0;
+    const unsigned long long t_ready = tw ? tcyc(c) : 0ull;
     const uint32_t vpr = static_cast<uint32_t>(K) / 8;  // 16-byte vectors per row
     const uint32_t vtot = static_cast<uint32_t>(nrows) * vpr;
     const uint32_t nw = static_cast<uint32_t>(c.nw);
     const uint32_t k0 = (static_cast<uint32_t>(c.warp) + nw - c.gi % nw) % nw;
     const uint4* xv = reinterpret_cast<const uint4*>(c.s.x);
-    const bool tw = a.trace && c.tid == 0;
+    // refills that stay inside this phase need no sequence walk
+    int step_, layer_, kind_;
+    c.seq.locate(p, &step_, &layer_, &kind_);
+    const Geom geo = c.s.geo[kind_];
+    const uint8_t* wsrc = reinterpret_cast<const uint8_t*>(c.seq.weight(layer_, kind_)) + geo.off;
     unsigned long long t_wait = 0, t_refill = 0;
     for (uint32_t k = k0; k < n_items; k += nw) {
         const uint32_t g = c.gi + k;
         const uint32_t slot = g % c.S;
-        const unsigned long long w0 = tw ? now_ns() : 0ull;
+        const unsigned long long w0 = tw ? clock64() : 0ull;
         const bool ok = slot_wait(a, &c.s.full[slot], (g / c.S) & 1);
-        if (tw) {
-            const unsigned long long w1 = now_ns();
-            if (k == k0) trace_mark(a, c.tstep, c.tph, 4);
-            t_wait += w1 - w0;
-        }
+        if (tw) t_wait += clock64() - w0;
         const uint32_t v0 = k * (kSlot / 16);
         const uint32_t v1 = min(vtot, v0 + kSlot / 16);
         const uint4* wv = reinterpret_cast<const uint4*>(c.s.ring + static_cast<size_t>(slot) * kSlot) - v0;
@@ -428,18 +450,23 @@ __device__ Band gemv_consume(Ctx& c, int p, int N, int K, int row_gran) {
         }
         __syncwarp();
         if (c.lane == 0 && ok) {
-            const unsigned long long r0 = tw ? now_ns() : 0ull;
-            refill(c, p, k, slot);
-            if (tw) t_refill += now_ns() - r0;
+            const unsigned long long r0 = tw ? clock64() : 0ull;
+            const uint32_t kn = k + c.S;
+            if (kn < n_items)
+                issue_copy(c, slot, wsrc + static_cast<size_t>(kn) * kSlot, min(static_cast<uint32_t>(kSlot), geo.bytes - kn * kSlot), false);
+            else
+                refill(c, p, k, slot);
+            if (tw) t_refill += clock64() - r0;
         }
     }
     if (tw) {
+        trace_put(a, c.tstep, c.tph, 4, t_ready);
         trace_put(a, c.tstep, c.tph, 5, t_wait);
         trace_put(a, c.tstep, c.tph, 6, t_refill);
     }
     c.gi += n_items;
     cbar(1, c.nt);
-    tmark(c, 3);
+    if (tw) trace_put(a, c.tstep, c.tph, 7, tcyc(c) - t_ready);
     return b;
 }
 
@@ -571,13 +598,15 @@ __device__ void phase_attention(Ctx& c, int p, int layer, int pos) {
         }
     }
     const float qscale = (1.0f / sqrtf(128.0f)) * kLog2e;
-    unsigned long long t_refill = 0;
-    tmark(c, 2);
+    unsigned long long t_wait = 0;
+    const unsigned long long t_pages = c.tid == 0 ? tcyc(c) : 0ull;
+    unsigned long long t_bar = 0;
     for (int i = 0; i < np && att_warp; ++i) {
         const uint32_t g0 = c.gi + 4 * i;
         bool ok = true;
+        const unsigned long long w0 = c.tid == 0 && a.trace ? clock64() : 0ull;
         for (int qq = 0; qq < 4; ++qq) ok = slot_wait(a, &c.s.full[(g0 + qq) % c.S], ((g0 + qq) / c.S) & 1) && ok;
-        if (i == 0) tmark(c, 4);
+        if (c.tid == 0 && a.trace) t_wait += clock64() - w0;
         const int page = u.pb + i;
         if (page == live_page && c.warp == 0) {
             // the current position's row was written after this page's copy was issued
@@ -588,6 +617,7 @@ __device__ void phase_attention(Ctx& c, int p, int layer, int pos) {
             dst[c.lane & 15] = reinterpret_cast<const uint4*>(which ? vrow : krow)[c.lane & 15];
         }
         cbar(2, kAttWarps * 32);
+        const unsigned long long b0 = c.tid == 0 && a.trace ? clock64() : 0ull;
         const int valid = min(kPage, pos + 1 - page * kPage);
         const int j0 = hw * 4;  // 4 consecutive tokens, all in half j0 / 32 of the page
         const uint32_t kslot = (g0 + (j0 >> 5)) % c.S, vslot = (g0 + 2 + (j0 >> 5)) % c.S;
@@ -650,16 +680,19 @@ __device__ void phase_attention(Ctx& c, int p, int layer, int pos) {
                 for (int d = 0; d < 8; ++d) acc[g][d] = fmaf(pr, vf[d], acc[g][d]);
             }
         }
+        if (c.tid == 0 && a.trace) t_bar += clock64() - b0;
+        // every attention warp is done with the page: warps 0-3 refill its four slots
         cbar(2, kAttWarps * 32);
-        if (c.lane == 0 && c.warp < 4 && ok) {  // one refill per warp
-            const unsigned long long r0 = a.trace ? now_ns() : 0ull;
-            refill(c, p, static_cast<uint32_t>(4 * i + c.warp), (g0 + c.warp) % c.S);
-            if (a.trace) t_refill += now_ns() - r0;
-        }
+        if (c.lane == 0 && c.warp < 4 && ok) refill(c, p, static_cast<uint32_t>(4 * i + c.warp), (g0 + c.warp) % c.S);
     }
     c.gi += 4 * np;
-    tmark(c, 5);
-    if (c.tid == 0) trace_put(a, c.tstep, c.tph, 7, t_refill);
+    const unsigned long long t_done = c.tid == 0 ? tcyc(c) : 0ull;
+    if (c.tid == 0) {
+        trace_put(a, c.tstep, c.tph, 4, t_pages);
+        trace_put(a, c.tstep, c.tph, 5, t_done - t_pages);
+        trace_put(a, c.tstep, c.tph, 6, t_wait);
+        trace_put(a, c.tstep, c.tph, 9, t_bar);
+    }
     if (!u.valid) return;
     // ---- this split's state: half-warp pairs by shuffle, then the 8 warps in shared memory
     if (att_warp) {
@@ -704,57 +737,80 @@ __device__ void phase_attention(Ctx& c, int p, int layer, int pos) {
             dst[g * kAttRecord + 1] = Ls;
         }
     }
-    tmark(c, 6);
-    __threadfence();
+    // publish: the CTA barrier orders every thread's stores before thread 0's
+    // release; the last split's acquire makes all partials visible to its CTA
     cbar(1, c.nt);
     if (c.tid == 0) {
-        const uint32_t old = atomicAdd(&a.att_counters[kq], 1u);
+        const uint32_t old = atom_add_acq_rel(&a.att_counters[kq], 1u);
         c.s.flags[1] = (old == static_cast<uint32_t>(a.splits - 1)) ? 1u : 0u;
     }
     cbar(1, c.nt);
-    tmark(c, 3);
+    if (c.tid == 0) trace_put(a, c.tstep, c.tph, 7, tcyc(c) - t_done);
     if (!c.s.flags[1]) return;
     // ---- last split of the group: merge all splits (rows of att_part) in parallel
-    __threadfence();
+    // One round trip: every (m, l) to shared memory, and each thread's share
+    // of the accumulators (column cl = (head, 4 dims); R threads stripe the
+    // splits) with their m into registers, loaded together.
     const int SG = a.splits * HG;
-    float* fsc = S;                        // [splits][HG] m, then exp2(m - M)
-    float* lsc = fsc + SG;                 // [splits][HG] l
-    float* Mg = lsc + SG;                  // [HG]
-    float* Lg = Mg + 4;                    // [HG]
+    float* msh = S;          // [splits][HG] m
+    float* lsh = msh + SG;   // [splits][HG] l
+    float* Mg = lsh + SG;    // [HG]
+    float* Lg = Mg + 4;      // [HG]
     float4* red = reinterpret_cast<float4*>(S + ((2 * SG + 8 + 3) & ~3));  // [threads]
+    constexpr int C = HG * 32;
+    constexpr int kRegSplits = 6;
+    const int R = c.nt / C;
+    const bool comb = c.tid < R * C;
+    const int cl = c.tid % C, r = c.tid / C;
+    const int g = cl >> 5, d4 = cl & 31;
+    float4 va[kRegSplits];
+    float ma[kRegSplits];
+#pragma unroll
+    for (int j = 0; j < kRegSplits; ++j) {
+        const int sp = r + j * R;
+        ma[j] = -INFINITY;
+        if (comb && sp < a.splits) {
+            const float* e = grp + static_cast<size_t>(sp * HG + g) * kAttRecord;
+            ma[j] = __ldcg(e);
+            va[j] = __ldcg(reinterpret_cast<const float4*>(e + 4) + d4);
+        }
+    }
     for (int i = c.tid; i < SG; i += c.nt) {
-        fsc[i] = __ldcg(grp + static_cast<size_t>(i) * kAttRecord);
-        lsc[i] = __ldcg(grp + static_cast<size_t>(i) * kAttRecord + 1);
+        msh[i] = __ldcg(grp + static_cast<size_t>(i) * kAttRecord);
+        lsh[i] = __ldcg(grp + static_cast<size_t>(i) * kAttRecord + 1);
     }
     cbar(1, c.nt);
     if (c.tid < HG) {
         float M = -INFINITY;
-        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, fsc[sp * HG + c.tid]);
+        for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, msh[sp * HG + c.tid]);
         float Ls = 0.f;
         for (int sp = 0; sp < a.splits; ++sp) {
-            const float ms = fsc[sp * HG + c.tid];
-            if (ms != -INFINITY) Ls += lsc[sp * HG + c.tid] * exp2f(ms - M);
+            const float ms = msh[sp * HG + c.tid];
+            if (ms != -INFINITY) Ls += lsh[sp * HG + c.tid] * exp2f(ms - M);
         }
         Mg[c.tid] = M;
         Lg[c.tid] = Ls;
     }
     cbar(1, c.nt);
-    for (int i = c.tid; i < SG; i += c.nt) {
-        const float ms = fsc[i];
-        fsc[i] = (ms == -INFINITY) ? 0.f : exp2f(ms - Mg[i % HG]);
-    }
-    cbar(1, c.nt);
-    // column cl = (head, 4 dims) of the output; R threads per column stripe the splits
-    constexpr int C = HG * 32;
-    const int R = c.nt / C;
-    if (c.tid < R * C) {
-        const int cl = c.tid % C, r = c.tid / C;
-        const int g = cl >> 5, d4 = cl & 31;
+    if (comb) {
+        const float M = Mg[g];
         float4 s4 = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-        for (int sp = r; sp < a.splits; sp += R) {
-            const float f = fsc[sp * HG + g];
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(grp + static_cast<size_t>(sp * HG + g) * kAttRecord + 4) + d4);
+#pragma unroll
+        for (int j = 0; j < kRegSplits; ++j) {
+            if (ma[j] == -INFINITY) continue;
+            const float f = exp2f(ma[j] - M);
+            s4.x = fmaf(va[j].x, f, s4.x);
+            s4.y = fmaf(va[j].y, f, s4.y);
+            s4.z = fmaf(va[j].z, f, s4.z);
+            s4.w = fmaf(va[j].w, f, s4.w);
+        }
+        // more splits than registers hold: the rest in a second pass
+        for (int sp = r + kRegSplits * R; sp < a.splits; sp += R) {
+            const float* e = grp + static_cast<size_t>(sp * HG + g) * kAttRecord;
+            const float ms = __ldcg(e);
+            if (ms == -INFINITY) continue;
+            const float f = exp2f(ms - M);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(e + 4) + d4);
             s4.x = fmaf(v.x, f, s4.x);
             s4.y = fmaf(v.y, f, s4.y);
             s4.z = fmaf(v.z, f, s4.z);
@@ -764,19 +820,18 @@ __device__ void phase_attention(Ctx& c, int p, int layer, int pos) {
     }
     cbar(1, c.nt);
     if (c.tid < C) {
-        const int g = c.tid >> 5, d4 = c.tid & 31;
         float4 s4 = red[c.tid];
-        for (int r = 1; r < R; ++r) {
-            const float4 v = red[r * C + c.tid];
+        for (int rr = 1; rr < R; ++rr) {
+            const float4 v = red[rr * C + c.tid];
             s4.x += v.x;
             s4.y += v.y;
             s4.z += v.z;
             s4.w += v.w;
         }
-        const float inv_l = Lg[g];
+        const float L = Lg[g];
         uint2 o;
-        o.x = pack_bf2(s4.x / inv_l, s4.y / inv_l);
-        o.y = pack_bf2(s4.z / inv_l, s4.w / inv_l);
+        o.x = pack_bf2(s4.x / L, s4.y / L);
+        o.y = pack_bf2(s4.z / L, s4.w / L);
         reinterpret_cast<uint2*>(a.attn + static_cast<size_t>(qh0 + g) * 128)[d4] = o;
     }
     if (c.tid == 0) a.att_counters[kq] = 0u;
@@ -937,38 +992,43 @@ __global__ void __launch_bounds__(kMaxThreads, 1) persistent_decode_kernel(const
         int ph = 0;  // phase within the step (timeline)
         const bool t0 = c.tid == 0;
         c.tstep = step;
+        auto begin = [&]() {
+            c.tph = ph;
+            if (t0) {
+                c.tc0 = clock64();
+                trace_edge(a, step, ph, 0);
+            }
+        };
+        auto end = [&]() {
+            if (t0) trace_edge(a, step, ph, 1);
+            ++ph;
+        };
         for (int l = 0; l < a.layers && go; ++l) {
             if (l > 0 && !(go = grid_sync(c))) break;
-            c.tph = ph;
-            if (t0) trace_mark(a, step, ph, 0);
+            begin();
             phase_qkv(c, p++, l, pos);
-            if (t0) trace_mark(a, step, ph++, 1);
+            end();
             if (!(go = grid_sync(c))) break;
-            c.tph = ph;
-            if (t0) trace_mark(a, step, ph, 0);
+            begin();
             phase_attention<HG>(c, p++, l, pos);
-            if (t0) trace_mark(a, step, ph++, 1);
+            end();
             if (!(go = grid_sync(c))) break;
-            c.tph = ph;
-            if (t0) trace_mark(a, step, ph, 0);
+            begin();
             phase_o(c, p++);
-            if (t0) trace_mark(a, step, ph++, 1);
+            end();
             if (!(go = grid_sync(c))) break;
-            c.tph = ph;
-            if (t0) trace_mark(a, step, ph, 0);
+            begin();
             phase_gu(c, p++, l);
-            if (t0) trace_mark(a, step, ph++, 1);
+            end();
             if (!(go = grid_sync(c))) break;
-            c.tph = ph;
-            if (t0) trace_mark(a, step, ph, 0);
+            begin();
             phase_down(c, p++);
-            if (t0) trace_mark(a, step, ph++, 1);
+            end();
         }
         if (!go || !grid_sync(c)) break;
-        c.tph = ph;
-            if (t0) trace_mark(a, step, ph, 0);
+        begin();
         phase_lm(c, p++, pos, nf);
-        if (t0) trace_mark(a, step, ph, 1);
+        end();
     }
     // Leave no copy in flight: the last round issued into each slot must land
     // (it is the only one that can be outstanding; bounded wait).

@@ -15,6 +15,8 @@ import numpy as np
 from ._lib import ModelConfig, check, lib
 from .config import Qwen3Config
 
+TRACE_WORDS = 10  # Q3_TRACE_WORDS in include/q3_sm100a.h
+
 
 def _ptr(a: np.ndarray) -> int:
     return a.ctypes.data
@@ -107,11 +109,12 @@ class Engine:
         check(lib().q3_engine_trace(self.h, int(enable), None, 0, C.byref(ph), C.byref(ct)))
 
     def read_trace(self) -> np.ndarray:
-        """[ctas, phases, 8] globaltimer ns of the first step of the last launch: [..., 0] phase start,
-        [..., 1] phase end, [..., 2:] inner marks (listed in csrc/persistent.cu)."""
+        """[ctas, phases, TRACE_WORDS] record of the first step of the last launch: [..., 0:2] phase
+        start/end (globaltimer ns), [..., 2:4] clock64 there, [..., 4:8] SM cycles of parts of the
+        phase, [..., 8] SM id (include/q3_sm100a.h, q3_engine_trace)."""
         ph, ct = C.c_size_t(), C.c_size_t()
         check(lib().q3_engine_trace(self.h, 1, None, 0, C.byref(ph), C.byref(ct)))
-        out = np.zeros(ct.value * ph.value * 8, np.uint64)
+        out = np.zeros(ct.value * ph.value * TRACE_WORDS, np.uint64)
         check(lib().q3_engine_trace(self.h, 1, out.ctypes.data, out.size, C.byref(ph), C.byref(ct)))
         return out.reshape(ct.value, ph.value, -1)
 
