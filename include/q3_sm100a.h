@@ -58,6 +58,14 @@ Q3_API int q3_embedding(const uint16_t* table_dev, size_t vocab, size_t hidden, 
 Q3_API int q3_gemv(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* y_dev, size_t n_out, size_t n_in,
                    void* stream);
 
+/* Batched matmul for the prefill (no Backend counterpart: the reference
+ * prefills by calling matmul once per prompt token, qwen3.hpp:168-173):
+ * y[m, n] = x[m, k] . W[n, k]^T with W as stored (row-major [out, in]),
+ * tcgen05 tensor cores, fp32 accumulation, BF16 out.  n % 128 == 0,
+ * k % 64 == 0, 16-byte aligned pointers. */
+Q3_API int q3_gemm(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* y_dev, size_t m, size_t n, size_t k,
+                   void* stream);
+
 /* Backend::rmsnorm (backend.hpp:28; cuda/kernels/rmsnorm.cuh:12-46,83-89). */
 Q3_API int q3_rmsnorm(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* out_dev, size_t n, float eps,
                       void* stream);

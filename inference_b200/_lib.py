@@ -22,6 +22,7 @@ SIGNATURES = {
     "q3_version": (C.c_int, []),
     "q3_embedding": (C.c_int, [_u16p, _sz, _sz, C.c_uint32, _u16p, _vp]),
     "q3_gemv": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _vp]),
+    "q3_gemm": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _sz, _vp]),
     "q3_rmsnorm": (C.c_int, [_u16p, _u16p, _u16p, _sz, C.c_float, _vp]),
     "q3_rmsnorm_add": (C.c_int, [_u16p, _u16p, _u16p, _u16p, _sz, C.c_float, _vp]),
     "q3_rope": (C.c_int, [_u16p, _vp, _vp, _sz, _sz, _sz, _vp]),

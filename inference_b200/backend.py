@@ -58,6 +58,12 @@ class B200Backend:
     def matmul(self, input, weights, output):
         check(lib().q3_gemv(_p(input), _p(weights), _p(output), weights.shape[0], weights.shape[1], self._stream()))
 
+    def gemm(self, x, weights, output):
+        """Batched matmul of the prefill: output[m, n] = x[m, k] . weights[n, k]^T (q3_gemm)."""
+        m, k = x.shape
+        n = weights.shape[0]
+        check(lib().q3_gemm(_p(x), _p(weights), _p(output), m, n, k, self._stream()))
+
     # backend.hpp:28
     def rmsnorm(self, input, weight, output, epsilon: float):
         check(lib().q3_rmsnorm(_p(input), _p(weight), _p(output), input.numel(), epsilon, self._stream()))

@@ -96,6 +96,26 @@ int q3_gemv(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t n_out, siz
     return launch_status(launch_gemv(PRO_PLAIN, EPI_STORE, a, as_stream(stream), false), "q3_gemv");
 }
 
+int q3_gemm(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t m, size_t n, size_t k, void* stream) {
+    Q3_CHECK(x && w && y, "q3_gemm: null pointer");
+    Q3_CHECK(m > 0 && n > 0 && k > 0, "q3_gemm: empty shape");
+    Q3_CHECK(n % 128 == 0, "q3_gemm: n must be a multiple of 128");
+    Q3_CHECK(k % 64 == 0, "q3_gemm: k must be a multiple of 64");
+    Q3_CHECK(m < (1u << 24) && n < (1u << 24) && k < (1u << 20), "q3_gemm: shape too large");
+    Q3_CHECK(aligned16(x) && aligned16(w) && aligned16(y), "q3_gemm: x, W and y must be 16-byte aligned");
+    current_sms();
+    GemmArgs a{};
+    a.x = cb(x);
+    a.w = cb(w);
+    a.y = mb(y);
+    a.M = static_cast<int>(m);
+    a.N = static_cast<int>(n);
+    a.K = static_cast<int>(k);
+    a.ldy = a.N;
+    a.epi = GEMM_STORE;
+    return launch_status(launch_gemm(a, as_stream(stream)), "q3_gemm");
+}
+
 int q3_rmsnorm(const uint16_t* x, const uint16_t* w, uint16_t* out, size_t n, float eps, void* stream) {
     Q3_CHECK(x && w && out && n > 0, "q3_rmsnorm: bad argument");
     return launch_status(launch_rmsnorm(cb(x), cb(w), mb(out), static_cast<int>(n), eps, as_stream(stream)),

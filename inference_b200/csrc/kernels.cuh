@@ -159,6 +159,21 @@ struct PersistentArgs {
 bool plan_persistent(PersistentArgs& a, int sms, size_t smem_limit);
 cudaError_t launch_persistent(const PersistentArgs& a, cudaStream_t s);
 
+// ---------------------------------------------------------------- prefill GEMM (tcgen05)
+enum GemmEpi : int { GEMM_STORE = 0, GEMM_SWIGLU = 1, GEMM_RESID = 2 };
+struct GemmArgs {
+    const bf16* x;  // [M, K] row-major (tokens)
+    const bf16* w;  // [N, K] row-major (weights as stored)
+    bf16* y;        // STORE: [M, ldy] <- XW^T; SWIGLU: [M, ldy] <- swiglu of column pairs; RESID: [M, ldy] += XW^T
+    float* vsum;    // RESID only (optional): [M, ldy] fp32 sums before rounding
+    int M, N, K, ldy;
+    int epi;        // GemmEpi
+    int bn;         // output tile width 128 / 256, 0 = choose
+    uint32_t* err;
+};
+int gemm_tile_n(int M, int N, int sms);
+cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
+
 // ---------------------------------------------------------------- small ops
 cudaError_t launch_embedding(const bf16* table, int hidden, uint32_t token, bf16* out, cudaStream_t s);
 cudaError_t launch_rmsnorm(const bf16* x, const bf16* w, bf16* out, int n, float eps, cudaStream_t s);

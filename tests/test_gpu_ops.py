@@ -43,6 +43,29 @@ def test_gemv(be, oracle, golden_ops, i, o):
         assert_bf16_close(mine, golden_ops[key], rtol=1e-2, atol=1e-3 * np.sqrt(i), min_exact=0.9)
 
 
+GEMM_SHAPES = [(1, 1024, 128), (130, 1024, 4096), (257, 2560, 1024), (512, 4096, 24576), (300, 12288, 4096)]
+
+
+@pytest.mark.parametrize("m,k,n", GEMM_SHAPES)
+def test_gemm_tcgen05(be, m, k, n):
+    """Prefill GEMM (tcgen05, TMEM accumulator) against an fp32 product of the
+    same BF16 operands; (512, 4096, 24576) runs the 256-column tile, the rest
+    the 128-column tile, 130 / 257 / 300 rows exercise partial token tiles."""
+    import torch
+
+    x = uniform_bf16(G.seed_of("gemm.x", m, k, n), (m, k))
+    w = uniform_bf16(G.seed_of("gemm.w", m, k, n), (n, k))
+    y = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    be.gemm(dev(x).view(m, k), dev(w).view(n, k), y)
+    torch.cuda.synchronize()
+    xf = dev(x).view(m, k).float()
+    wf = dev(w).view(n, k).float()
+    ref = (xf.double() @ wf.double().T).float().to(torch.bfloat16)
+    mine = y.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+    gold = ref.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+    assert_bf16_close(mine, gold, rtol=1e-2, atol=1e-3 * np.sqrt(k), min_exact=0.9)
+
+
 @pytest.mark.parametrize("h", G.NORM)
 def test_rmsnorm(be, oracle, golden_ops, h):
     x = uniform_bf16(G.seed_of("norm.x", h), (h,))
