@@ -194,6 +194,14 @@ Q3_API int q3_engine_set_tokens(q3_engine* e, const uint32_t* ids_host, size_t n
  * host synchronisation.  Replays one CUDA graph per step. */
 Q3_API int q3_engine_step(q3_engine* e, size_t n);
 
+/* Model::prefill (qwen3.hpp:168-173) batched: writes the K/V cache of the set
+ * tokens at positions [position, position + n) -- tcgen05 GEMMs over up to
+ * 512 tokens at a time instead of n decode steps -- and advances the
+ * position by n.  No logits (the reference discards the prefill's).  The
+ * tokens must have been given with q3_engine_set_tokens.  Tensor-parallel
+ * engines run the n decode steps instead.  Asynchronous like step. */
+Q3_API int q3_engine_prefill(q3_engine* e, size_t n);
+
 /* Blocks until queued steps finish; returns Q3_ERR_DEVICE if a kernel
  * recorded an error. */
 Q3_API int q3_engine_sync(q3_engine* e);

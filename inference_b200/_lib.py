@@ -43,6 +43,7 @@ SIGNATURES = {
     "q3_engine_set_weight": (C.c_int, [_vp, C.c_char_p, _u16p, _sz, _sz]),
     "q3_engine_reset": (C.c_int, [_vp]),
     "q3_engine_set_tokens": (C.c_int, [_vp, _u32p, _sz]),
+    "q3_engine_prefill": (C.c_int, [_vp, _sz]),
     "q3_engine_step": (C.c_int, [_vp, _sz]),
     "q3_engine_sync": (C.c_int, [_vp]),
     "q3_engine_forward": (C.c_int, [_vp, C.c_uint32, C.POINTER(C.c_uint32)]),

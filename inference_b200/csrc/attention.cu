@@ -62,8 +62,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
     AttnSmem<HG>& S = *reinterpret_cast<AttnSmem<HG>*>(smem_raw);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int split = blockIdx.x, kvh = blockIdx.y, qb = blockIdx.z;
     const int G = a.q_heads / a.kv_heads;
+    const int nqb = G / HG;
+    const int split = blockIdx.x, kvh = blockIdx.y, qb = blockIdx.z % nqb, qi = blockIdx.z / nqb;
+    const bf16* qv = a.q + static_cast<size_t>(qi) * a.q_stride;
+    bf16* out = a.out + static_cast<size_t>(qi) * a.out_stride;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
@@ -77,7 +80,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
     // The position is final here: every kernel triggers its dependents only
     // after its own griddepcontrol.wait, so when this grid runs, the kernel
     // before the QKV GEMV (which advanced the position) has completed.
-    int pos = a.pos_ptr ? *a.pos_ptr : a.pos_host;
+    int pos = (a.pos_ptr ? *a.pos_ptr : a.pos_host) + qi;
     if (pos < 0) pos = 0;
     const int n_pages = pos / kPage + 1;
     const int pb = static_cast<int>(static_cast<long long>(split) * n_pages / a.splits);
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         float q[HG][8];
 #pragma unroll
         for (int g = 0; g < HG; ++g) {
-            const uint4 v = reinterpret_cast<const uint4*>(a.q + static_cast<size_t>(qh0 + g) * kHd)[hl];
+            const uint4 v = reinterpret_cast<const uint4*>(qv + static_cast<size_t>(qh0 + g) * kHd)[hl];
             const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
                 }
             }
             if (a.splits == 1) {
-                a.out[static_cast<size_t>(qh0 + g) * kHd + d] = f2bf(A / Lsum);
+                out[static_cast<size_t>(qh0 + g) * kHd + d] = f2bf(A / Lsum);
             } else {
                 S.cacc[g][d] = A;
                 if (d == 0) {
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
             }
             if (sub == 0) {
                 const int qh = kvh * G + qb * HG + g;
-                a.out[static_cast<size_t>(qh) * kHd + d] = f2bf(A / Lsum);
+                out[static_cast<size_t>(qh) * kHd + d] = f2bf(A / Lsum);
             }
         }
     }
@@ -301,7 +304,7 @@ cudaError_t launch_hg(const AttnArgs& a, cudaStream_t s, bool pdl, int nqb) {
     auto* fn = attn_kernel<HG>;
     const size_t smem = sizeof(AttnSmem<HG>);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.splits, a.kv_heads, nqb);
+    cfg.gridDim = dim3(a.splits, a.kv_heads, nqb * (a.n_queries > 1 ? a.n_queries : 1));
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
@@ -385,6 +388,8 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     const int G = a.q_heads / a.kv_heads;
     if (a.q_heads % a.kv_heads != 0 || !(G == 1 || G == 2 || G == 4 || G == 8)) return cudaErrorInvalidValue;
     if (a.splits < 1 || a.splits > 16 || (a.splits & (a.splits - 1)) != 0) return cudaErrorInvalidValue;
+    if (a.n_queries > 1 && static_cast<long long>(a.n_queries) * (G / heads_per_cta(G)) > 65535)
+        return cudaErrorInvalidValue;
     const int HG = heads_per_cta(G);
     const int nqb = G / HG;
     switch (HG) {

@@ -72,6 +72,10 @@ struct q3_engine {
     unsigned long long* d_trace = nullptr;
     unsigned long long* gsync = nullptr;
     uint32_t* abort_word = nullptr;
+    // batched prefill: token-row buffers of prefill_rows rows (allocated on first use)
+    int prefill_rows = 0;
+    q3::bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pg = nullptr;
+    float* pvsum = nullptr;
     // graph / comms
     cudaGraphExec_t graph = nullptr;
     ncclComm_t comm = nullptr;
@@ -736,6 +740,110 @@ int q3_engine_step(q3_engine* e, size_t n) {
     return Q3_OK;
 }
 
+// Batched prefill (qwen3.hpp:168-173 runs one decode forward per prompt token,
+// logits discarded): the K/V of the set tokens at positions [pos, pos + n),
+// up to 512 tokens per chunk.  Per layer: row RMSNorm, QKV GEMM (tcgen05),
+// q/k norm + RoPE with the cache writes, attention over each token's prefix,
+// then O (+ residual), RMSNorm of the fp32 sums, gate/up (SwiGLU epilogue) and
+// down (+ residual).  The last layer stops after its attention: its output
+// only feeds the discarded logits.
+int q3_engine_prefill(q3_engine* e, size_t n) {
+    Q3_CHECK(e, "null engine");
+    if (n == 0) return Q3_OK;
+    const size_t p0 = e->host_pos;
+    Q3_CHECK(p0 + n <= e->host_forced, "q3_engine_prefill: tokens not set (set_tokens first)");
+    if (p0 + n >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "q3_engine_prefill: KV cache capacity exceeded");
+    Q3_CUDA(cudaSetDevice(e->device));
+    if (e->world > 1) {
+        // tensor-parallel engines prefill through the per-token decode step
+        return q3_engine_step(e, n);
+    }
+    const int H = e->H, qd = e->qd, kd = e->kd, il = e->il;
+    const int ldqkv = qd + 2 * kd;
+    if (!e->prefill_rows) {
+        const int rows = static_cast<int>(std::min<size_t>(512, e->cfg.capacity));
+        int rc;
+        if ((rc = dalloc_t(e, &e->px, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+        if ((rc = dalloc_t(e, &e->pxn, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+        if ((rc = dalloc_t(e, &e->pqkv, static_cast<size_t>(rows) * ldqkv)) != Q3_OK) return rc;
+        if ((rc = dalloc_t(e, &e->pattn, static_cast<size_t>(rows) * qd)) != Q3_OK) return rc;
+        if ((rc = dalloc_t(e, &e->pg, static_cast<size_t>(rows) * il)) != Q3_OK) return rc;
+        if ((rc = dalloc_t(e, &e->pvsum, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+        e->prefill_rows = rows;
+    }
+    const float eps = e->cfg.eps;
+    cudaStream_t s = e->stream;
+    const int L = static_cast<int>(e->layers.size());
+    auto gemm = [&](const bf16* x, const bf16* w, bf16* y, float* vs, int m, int nn, int k, int ldy, int epi) {
+        GemmArgs g{};
+        g.x = x;
+        g.w = w;
+        g.y = y;
+        g.vsum = vs;
+        g.M = m;
+        g.N = nn;
+        g.K = k;
+        g.ldy = ldy;
+        g.epi = epi;
+        g.bn = gemm_tile_n(m, nn, e->sms);
+        g.err = e->err;
+        return launch_gemm(g, s);
+    };
+    for (size_t done = 0; done < n;) {
+        const int t = static_cast<int>(std::min<size_t>(n - done, static_cast<size_t>(e->prefill_rows)));
+        const int pc = static_cast<int>(p0 + done);
+        Q3_CUDA(launch_embed_rows(e->embed, e->tokens, pc, t, static_cast<int>(e->cfg.vocab), H, e->px, e->err, s));
+        for (int l = 0; l < L; ++l) {
+            const LayerW& W = e->layers[l];
+            Q3_CUDA(launch_rmsnorm_rows(e->px, nullptr, W.in_norm, e->pxn, t, H, eps, s));
+            Q3_CUDA(gemm(e->pxn, W.w_qkv, e->pqkv, nullptr, t, ldqkv, H, ldqkv, GEMM_STORE));
+            PrefillQkvArgs qa{};
+            qa.qkv = e->pqkv;
+            qa.ld = ldqkv;
+            qa.q_heads = e->qh;
+            qa.kv_heads = e->kvh;
+            qa.p0 = pc;
+            qa.q_norm = W.q_norm;
+            qa.k_norm = W.k_norm;
+            qa.rope_cos = e->rope_cos;
+            qa.rope_sin = e->rope_sin;
+            qa.k_pages = W.k_pages;
+            qa.v_pages = W.v_pages;
+            qa.page_table = e->page_table;
+            qa.eps = eps;
+            Q3_CUDA(launch_qkv_rows(qa, t, s));
+            AttnArgs aa{};
+            aa.q = e->pqkv;
+            aa.k = W.k_pages;
+            aa.v = W.v_pages;
+            aa.page_table = e->page_table;
+            aa.out = e->pattn;
+            aa.q_heads = e->qh;
+            aa.kv_heads = e->kvh;
+            aa.page_size = kPageSize;
+            aa.paged = 1;
+            aa.pos_host = pc;
+            aa.splits = attn_splits(e->kvh, pc + t - 1, kPageSize, e->sms);
+            aa.err = e->err;
+            aa.n_queries = t;
+            aa.q_stride = ldqkv;
+            aa.out_stride = qd;
+            Q3_CUDA(launch_attention(aa, s, false));
+            if (l == L - 1) break;
+            Q3_CUDA(gemm(e->pattn, W.w_o, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
+            Q3_CUDA(launch_rmsnorm_rows(e->px, e->pvsum, W.post_norm, e->pxn, t, H, eps, s));
+            Q3_CUDA(gemm(e->pxn, W.w_gu, e->pg, nullptr, t, 2 * il, H, il, GEMM_SWIGLU));
+            Q3_CUDA(gemm(e->pg, W.w_down, e->px, nullptr, t, H, il, H, GEMM_RESID));
+        }
+        done += static_cast<size_t>(t);
+    }
+    const int32_t np = static_cast<int32_t>(p0 + n);
+    Q3_CUDA(cudaMemcpyAsync(e->pos, &np, 4, cudaMemcpyHostToDevice, s));
+    e->host_pos = p0 + n;
+    if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
+    return Q3_OK;
+}
+
 int q3_engine_sync(q3_engine* e) {
     Q3_CHECK(e, "null engine");
     Q3_CUDA(cudaSetDevice(e->device));
@@ -783,11 +891,12 @@ int q3_engine_generate(q3_engine* e, const uint32_t* prompt, size_t n_prompt, si
     const size_t room = e->cfg.capacity - n_prompt;
     const size_t n_gen = max_new < room ? max_new : room;
     const size_t steps = n_prompt - 1 + n_gen;
+    Q3_TRY(q3_engine_prefill(e, n_prompt - 1));
     if (!stop_at_eos) {
-        Q3_TRY(q3_engine_step(e, steps));
+        Q3_TRY(q3_engine_step(e, n_gen));
     } else {
         // EOS needs the host to look at tokens: run in chunks.
-        size_t done = 0;
+        size_t done = n_prompt - 1;
         const size_t chunk = 32;
         while (done < steps) {
             const size_t k = (steps - done) < chunk ? (steps - done) : chunk;

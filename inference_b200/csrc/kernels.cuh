@@ -99,6 +99,10 @@ struct AttnArgs {
     int pos_host;
     int splits;               // grid.x = cluster size: a power of two <= 16
     uint32_t* err;
+    // batch of consecutive query positions (prefill): query i sits at position
+    // pos + i, reads q + i * q_stride and writes out + i * out_stride.  0 or 1 =
+    // the single decode query.
+    int n_queries, q_stride, out_stride;
 };
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
@@ -173,6 +177,22 @@ struct GemmArgs {
 };
 int gemm_tile_n(int M, int N, int sms);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
+
+// ---------------------------------------------------------------- prefill rows
+struct PrefillQkvArgs {
+    bf16* qkv;                  // [n, ld]: q heads, k heads, v heads of each token
+    int ld, q_heads, kv_heads, p0;
+    const bf16 *q_norm, *k_norm;
+    const float *rope_cos, *rope_sin;
+    bf16 *k_pages, *v_pages;
+    const int32_t* page_table;
+    float eps;
+};
+cudaError_t launch_embed_rows(const bf16* table, const int32_t* tokens, int p0, int n, int vocab, int H, bf16* x,
+                              uint32_t* err, cudaStream_t s);
+cudaError_t launch_rmsnorm_rows(const bf16* x, const float* vsum, const bf16* w, bf16* xn, int n, int H, float eps,
+                                cudaStream_t s);
+cudaError_t launch_qkv_rows(const PrefillQkvArgs& a, int n, cudaStream_t s);
 
 // ---------------------------------------------------------------- small ops
 cudaError_t launch_embedding(const bf16* table, int hidden, uint32_t token, bf16* out, cudaStream_t s);

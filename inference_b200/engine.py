@@ -76,6 +76,10 @@ class Engine:
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
         check(lib().q3_engine_set_tokens(self.h, _ptr(ids), ids.size))
 
+    def prefill(self, n: int):
+        """Batched prefill of the next n set tokens (K/V only), q3_engine_prefill."""
+        check(lib().q3_engine_prefill(self.h, n))
+
     def step(self, n: int = 1):
         check(lib().q3_engine_step(self.h, n))
 
