@@ -31,6 +31,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "batch-1 decode tok/s and HBM GB/s vs roofline, 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def parse_args():
@@ -75,6 +76,16 @@ def measured_peaks():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_bf16_peak():
+    """Burst cuBLAS bf16 TFLOP/s of MEASURED_PEAKS.json (a prefill GEMM is timed alone)."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
 
 
 class ClockSampler:
@@ -265,11 +276,26 @@ def main():
 
     window = capacity - prompt_len if not a.window else min(a.window, capacity - prompt_len)
     prompt = ib.prompt_ids(prompt_len, seed=1, vocab=cfg.vocab)
-    eng.set_tokens(prompt)
-    eng.step(prompt_len - 1)  # prefill: every prompt id but the last (qwen3.hpp:168-173)
-    eng.sync()
-    start_pos = prompt_len - 1
     stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    # prefill: every prompt id but the last (qwen3.hpp:168-173), batched through the
+    # tcgen05 GEMMs; timed here (device events, max over ranks) and left in place
+    pre_ms = []
+    for rep_ in range(4):
+        eng.reset()
+        eng.set_tokens(prompt)
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record(stream)
+        eng.prefill(prompt_len - 1)
+        p1.record(stream)
+        eng.sync()
+        if rep_:
+            pre_ms.append(p0.elapsed_time(p1))
+    pre_t = float(np.median(pre_ms))
+    if dist:
+        t = torch.tensor([pre_t], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        pre_t = float(t.item())
+    start_pos = prompt_len - 1
 
     def one_window():
         eng.set_position(start_pos)
@@ -325,6 +351,22 @@ def main():
         e2e = {"value": round(a.steps * window / dt, 3), "unit": "tok/s", "h2d_bytes_per_step": int(prompt_len * 4 + 4),
                "d2h_bytes_per_step": int(window * 4),
                "includes": "prompt H2D, prefill of the prompt, decode, token D2H"}
+
+    # ---- prefill (informational: the metric is decode tok/s)
+    n_pre = prompt_len - 1
+    # every layer's four GEMMs, but the last layer stops after its QKV GEMM
+    gemm_flop = 2.0 * n_pre * (cfg.layer_matmul_params() * (cfg.layers - 1) +
+                               (cfg.q_heads + 2 * cfg.kv_heads) * cfg.head_dim * cfg.hidden)
+    attn_flop = 4.0 * cfg.layers * cfg.q_heads * cfg.head_dim * n_pre * (n_pre + 1) / 2.0
+    bf16_peak, bf16_kind = measured_bf16_peak()
+    prefill = {"tokens": n_pre, "ms": round(pre_t, 3), "tok_s": round(n_pre / (pre_t / 1000.0), 1),
+               "path": ("batched: tcgen05 GEMMs (TMEM accumulators, TMA), batched split-KV attention"
+                        if world == 1 else "tensor parallel: per-token decode steps"),
+               "tflops": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world, 1),
+               "gemm_tflop": round(gemm_flop / 1e12, 3), "attention_tflop": round(attn_flop / 1e12, 3),
+               "peak_tflops": bf16_peak, "frac": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world /
+                                                      bf16_peak, 4),
+               "peak_kind": bf16_kind}
 
     # ---- dominant kernel roofline
     peak, peak_kind = measured_peaks()
@@ -421,7 +463,7 @@ def main():
                        "l2_flush": f"not needed: {cfg.weight_bytes() / 1e9:.1f} GB of weights streamed per token "
                                    f">> 126 MB L2"},
             "clocks": clock, "e2e": e2e, "gpu_launches": int(launches),
-            "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu,
+            "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu, "prefill": prefill,
         }
         if ref_cuda is not None:
             line["reference_cuda"] = ref_cuda

@@ -30,6 +30,12 @@ class Qwen3Config:
         per_layer = (qd + 2 * kd) * H + H * qd + 2 * I * H + H * I + 2 * H + 2 * self.head_dim
         return 2 * (per_layer * self.layers + self.vocab * H + H + H)
 
+    def layer_matmul_params(self) -> int:
+        """Weights of the QKV, O, gate/up and down matrices of one layer (GEMM FLOPs = 2 x tokens x this)."""
+        H, I = self.hidden, self.inter
+        qd, kd = self.q_heads * self.head_dim, self.kv_heads * self.head_dim
+        return (qd + 2 * kd) * H + H * qd + 2 * I * H + H * I
+
     def kv_bytes_per_position(self) -> int:
         return self.layers * 2 * self.kv_heads * self.head_dim * 2
 

@@ -823,7 +823,9 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
             aa.page_size = kPageSize;
             aa.paged = 1;
             aa.pos_host = pc;
-            aa.splits = attn_splits(e->kvh, pc + t - 1, kPageSize, e->sms);
+            // many queries already fill the GPU: a split gets at least 8 pages
+            const int pages = (pc + t - 1) / kPageSize + 1;
+            aa.splits = attn_splits(e->kvh, ((pages + 7) / 8) * kPageSize - 1, kPageSize, e->sms);
             aa.err = e->err;
             aa.n_queries = t;
             aa.q_stride = ldqkv;
