@@ -261,6 +261,21 @@ Q3_API size_t q3_engine_kv_bytes_per_position(q3_engine* e);
  * launches and algorithmic bytes. */
 Q3_API int q3_engine_profile_step(q3_engine* e, int kernel_class, double* ms, size_t* launches, double* bytes);
 
+/* Tensor parallelism through peer memory (the fast path): every rank exports
+ * its exchange buffer as a CUDA IPC handle of Q3_PEER_HANDLE_BYTES bytes,
+ * the handles are shared by any means (the tests use torch.distributed), and
+ * every rank attaches all of them, its own included, in rank order.  The
+ * o_proj / down_proj GEMVs then store their fp32 partial rows straight into
+ * every rank's buffer over NVLink and raise a flag; the next GEMV waits for
+ * all flags (bounded; Q3_ERR_DEVICE "peer wait timed out" otherwise) and sums
+ * the partials in rank order, so every rank holds the same bits.  The argmax
+ * keys of lm_head travel the same way.  Replaces the two allreduces and the
+ * allgather per layer that the NCCL path issues.  Requires peer access between
+ * the GPUs (NVLink). */
+#define Q3_PEER_HANDLE_BYTES 64
+Q3_API int q3_engine_peer_handle(q3_engine* e, void* handle_out);
+Q3_API int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n_ranks);
+
 /* Tensor parallelism over NCCL: rank 0 calls q3_nccl_unique_id, the id is
  * shared by the caller (e.g. torch.distributed), then every rank attaches. */
 Q3_API int q3_nccl_unique_id(void* id_out_128_bytes);

@@ -63,6 +63,8 @@ SIGNATURES = {
     "q3_engine_profile_step": (C.c_int, [_vp, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_size_t),
                                          C.POINTER(C.c_double)]),
     "q3_nccl_unique_id": (C.c_int, [_vp]),
+    "q3_engine_peer_handle": (C.c_int, [_vp, _vp]),
+    "q3_engine_attach_peers": (C.c_int, [_vp, _vp, _sz]),
     "q3_engine_attach_nccl": (C.c_int, [_vp, _vp]),
 }
 

@@ -76,6 +76,13 @@ struct q3_engine {
     int prefill_rows = 0;
     q3::bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pg = nullptr;
     float* pvsum = nullptr;
+    // tensor-parallel exchange through peer memory: this rank's buffer (shared
+    // with the peers by CUDA IPC), the peers' mappings, local counters
+    void* xbuf = nullptr;
+    size_t xbuf_bytes = 0;
+    void* xpeer[q3::kMaxRanks] = {};
+    q3::PeerLinks links{};
+    bool peer_mode = false;
     // graph / comms
     cudaGraphExec_t graph = nullptr;
     ncclComm_t comm = nullptr;
@@ -131,6 +138,7 @@ struct Recorder {
 
 GemvArgs base_args(q3_engine* e) {
     GemvArgs a{};
+    if (e->peer_mode) a.peer = e->links;
     a.eps = e->cfg.eps;
     a.err = e->err;
     a.capacity = static_cast<int>(e->cfg.capacity);
@@ -177,6 +185,7 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
 }
 
 int allreduce(q3_engine* e, float* buf, size_t n) {
+    if (e->peer_mode) return Q3_OK;  // the producing GEMV exchanged its partials through peer memory
     ncclResult_t nr = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, e->stream);
     if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().GetErrorString(nr));
     return Q3_OK;
@@ -287,8 +296,10 @@ int record_step(Recorder& r, size_t pos_now) {
         h.vsum = e->partial;
         h.ss_unrounded = 0;
         Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
-        ncclResult_t nr = nccl().AllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
-        if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + nccl().GetErrorString(nr));
+        if (!e->peer_mode) {
+            ncclResult_t nr = nccl().AllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
+            if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + nccl().GetErrorString(nr));
+        }
     } else {
         h.hs = e->hs[0];
         Q3_TRY(gemv(r, PRO_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
@@ -298,7 +309,8 @@ int record_step(Recorder& r, size_t pos_now) {
 
 int build_graph(q3_engine* e) {
     if (e->graph) return Q3_OK;
-    if (e->world > 1 && !e->comm) return fail(Q3_ERR_INVALID, "tensor-parallel engine needs q3_engine_attach_nccl");
+    if (e->world > 1 && !e->comm && !e->peer_mode)
+        return fail(Q3_ERR_INVALID, "tensor-parallel engine needs q3_engine_attach_peers or q3_engine_attach_nccl");
     Recorder r{e, true};
     cudaGraph_t g = nullptr;
     Q3_CUDA(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
@@ -361,6 +373,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     *out = nullptr;
     const q3_model_config& c = *cfg;
     Q3_CHECK(tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size, "q3_engine_create: bad tensor-parallel rank");
+    Q3_CHECK(tp_size <= kMaxRanks, "q3_engine_create: at most 8 tensor-parallel ranks");
     if (c.head_dim != 128) return fail(Q3_ERR_UNSUPPORTED, "q3_engine_create: head_dim must be 128");
     Q3_CHECK(c.layers > 0 && c.hidden > 0 && c.vocab > 0 && c.capacity > 1, "q3_engine_create: empty config");
     Q3_CHECK(c.kv_heads > 0 && c.q_heads % c.kv_heads == 0, "q3_engine_create: q_heads % kv_heads != 0");
@@ -453,6 +466,20 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->logits, e->vl)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->vsum, H)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->partial, H)) != Q3_OK) return bail(rc);
+    if (tp_size > 1) {
+        // exchange buffer: recv [2][world][H] fp32 | flags [2][world] u32 | keys [2][world] u64
+        e->xbuf_bytes = (2 * static_cast<size_t>(tp_size) * H * 4 + 2 * tp_size * 4 + 15) / 16 * 16 + 2 * tp_size * 8;
+        if ((rc = dalloc(e, &e->xbuf, e->xbuf_bytes)) != Q3_OK) return bail(rc);
+        cudaMemset(e->xbuf, 0, e->xbuf_bytes);
+        unsigned long long* seq = nullptr;
+        if ((rc = dalloc_t(e, &seq, 2)) != Q3_OK) return bail(rc);
+        cudaMemset(seq, 0, 16);
+        e->links.seq = seq;
+        e->links.counter = reinterpret_cast<uint32_t*>(seq + 1);
+        e->links.rank = tp_rank;
+        e->links.world = tp_size;
+        e->links.H = H;
+    }
     if ((rc = dalloc_t(e, &e->pos, 4)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->n_forced, 4)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->tokens, c.capacity + 1)) != Q3_OK) return bail(rc);
@@ -577,6 +604,8 @@ int q3_engine_destroy(q3_engine* e) {
     if (e->stream) cudaStreamSynchronize(e->stream);
     if (e->graph) cudaGraphExecDestroy(e->graph);
     if (e->comm) nccl().CommDestroy(e->comm);
+    for (void* p : e->xpeer)
+        if (p) cudaIpcCloseMemHandle(p);
     for (void* p : e->allocs) cudaFree(p);
     if (e->stream) cudaStreamDestroy(e->stream);
     delete e;
@@ -854,6 +883,8 @@ int q3_engine_sync(q3_engine* e) {
 }
 
 static int finish_last(q3_engine* e) {
+    if (e->peer_mode)
+        Q3_CUDA(launch_peer_keys(e->links, reinterpret_cast<unsigned long long*>(e->keys), e->err, e->stream));
     Q3_CUDA(launch_resolve_tokens(e->keys, e->world, e->tokens, e->argmax_hist, e->pos, e->n_forced,
                                   static_cast<int>(e->cfg.vocab), e->err, e->stream));
     return Q3_OK;
@@ -1059,7 +1090,8 @@ int q3_engine_profile_step(q3_engine* e, int klass, double* ms, size_t* launches
     Q3_CHECK(e && ms && launches && bytes, "null argument");
     Q3_CHECK(e->host_pos < e->cfg.capacity, "q3_engine_profile_step: KV cache full");
     Q3_CHECK(e->host_forced >= 1 || e->host_pos >= 1, "q3_engine_profile_step: no input token");
-    if (e->world > 1 && !e->comm) return fail(Q3_ERR_INVALID, "tensor-parallel engine needs NCCL");
+    if (e->world > 1 && !e->comm && !e->peer_mode)
+        return fail(Q3_ERR_INVALID, "tensor-parallel engine needs q3_engine_attach_peers or q3_engine_attach_nccl");
     Q3_CUDA(cudaSetDevice(e->device));
     std::vector<cudaEvent_t> ev;
     double b = 0;
@@ -1098,6 +1130,48 @@ int q3_nccl_unique_id(void* id_out) {
     if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclGetUniqueId: ") + nccl().GetErrorString(nr));
     static_assert(sizeof(ncclUniqueId) == 128, "NCCL unique id size");
     std::memcpy(id_out, &id, sizeof(id));
+    return Q3_OK;
+}
+
+int q3_engine_peer_handle(q3_engine* e, void* handle_out) {
+    Q3_CHECK(e && handle_out, "null argument");
+    Q3_CHECK(e->xbuf, "q3_engine_peer_handle: not a tensor-parallel engine");
+    Q3_CUDA(cudaSetDevice(e->device));
+    cudaIpcMemHandle_t h;
+    Q3_CUDA(cudaIpcGetMemHandle(&h, e->xbuf));
+    static_assert(sizeof(h) == Q3_PEER_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof(h));
+    return Q3_OK;
+}
+
+int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n) {
+    Q3_CHECK(e && handles, "null argument");
+    Q3_CHECK(e->xbuf, "q3_engine_attach_peers: not a tensor-parallel engine");
+    Q3_CHECK(n == static_cast<size_t>(e->world), "q3_engine_attach_peers: one handle per rank expected");
+    Q3_CHECK(!e->peer_mode, "q3_engine_attach_peers: already attached");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const size_t H = static_cast<size_t>(e->H), W = static_cast<size_t>(e->world);
+    const size_t flags_off = 2 * W * H * 4, keys_off = (flags_off + 2 * W * 4 + 15) / 16 * 16;
+    for (int j = 0; j < e->world; ++j) {
+        void* base = nullptr;
+        if (j == e->rank) {
+            base = e->xbuf;
+        } else {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(j) * Q3_PEER_HANDLE_BYTES,
+                        sizeof(h));
+            Q3_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+            e->xpeer[j] = base;
+        }
+        e->links.recv[j] = static_cast<float*>(base);
+        e->links.flags[j] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(base) + flags_off);
+        e->links.keys[j] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(base) + keys_off);
+    }
+    e->peer_mode = true;
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;
+    }
     return Q3_OK;
 }
 

@@ -85,6 +85,56 @@ __device__ __forceinline__ float cta_sum(float v, float* scratch) {
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ---- tensor-parallel exchange through peer memory
+constexpr uint32_t kPeerPolls = 1u << 20;
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long peer_seq(const PeerLinks& x) {
+    return *reinterpret_cast<volatile unsigned long long*>(x.seq);
+}
+
+// Consumer side: every CTA waits (bounded) until all ranks filled the slot of
+// exchange s, the one the kernel before produced.
+__device__ __forceinline__ void peer_wait(const PeerLinks& x, unsigned long long s, uint32_t* err) {
+    const uint32_t* fl = x.flags[x.rank] + (s & 1) * x.world;
+    if (threadIdx.x < static_cast<unsigned>(x.world)) {
+        uint32_t polls = 0;
+        while (ld_acquire_sys(fl + threadIdx.x) != static_cast<uint32_t>(s)) {
+            // after any recorded failure stop waiting at once (the engine reports it)
+            if ((++polls & 1023) == 0 && *reinterpret_cast<volatile uint32_t*>(err)) break;
+            if (polls > kPeerPolls) {
+                record_error(err, DEV_PEER_WAIT_TIMEOUT);
+                break;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Producer side, after every CTA stored its part into each rank's slot of
+// exchange s1: the last CTA to arrive raises the flag of s1 on every rank.
+__device__ __forceinline__ void peer_signal(const PeerLinks& x, unsigned long long s1) {
+    __threadfence_system();  // this thread's stores to the peers before the CTA's arrival
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t old = atomicAdd(x.counter, 1u);
+        if (old == gridDim.x - 1) {
+            __threadfence_system();
+            const uint32_t slot = static_cast<uint32_t>(s1 & 1);
+            for (int j = 0; j < x.world; ++j) st_release_sys(x.flags[j] + slot * x.world + x.rank, static_cast<uint32_t>(s1));
+            *x.counter = 0u;
+            *x.seq = s1;
+        }
+    }
+}
+
 template <int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -156,7 +206,17 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         if constexpr (PRO == PRO_EMBED_NORM) {
             const int nf = *a.n_forced;
             uint64_t best = 0;
-            for (int r = 0; r < a.n_keys; ++r) best = max(best, static_cast<uint64_t>(a.keys[r]));
+            if (a.peer.world) {
+                // the previous step's lm_head exchanged every rank's key (none before the first step)
+                const unsigned long long s = peer_seq(a.peer);
+                if (s) {
+                    peer_wait(a.peer, s, a.err);
+                    const unsigned long long* k = a.peer.keys[a.peer.rank] + (s & 1) * a.peer.world;
+                    for (int r = 0; r < a.peer.world; ++r) best = max(best, static_cast<uint64_t>(__ldcg(k + r)));
+                }
+            } else {
+                for (int r = 0; r < a.n_keys; ++r) best = max(best, static_cast<uint64_t>(a.keys[r]));
+            }
             const uint32_t greedy = argmax_key_index(best);
             int token = (pos < nf) ? a.tokens[pos] : static_cast<int>(greedy);
             if (token < 0 || token >= a.vocab) {
@@ -169,6 +229,15 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             }
             src = a.embed + static_cast<size_t>(token) * a.K;
         }
+        // tensor parallel through peer memory: the partials every rank stored here
+        const float* parts = nullptr;
+        if constexpr (PRO == PRO_RESID_NORM) {
+            if (a.peer.world) {
+                const unsigned long long s = peer_seq(a.peer);
+                peer_wait(a.peer, s, a.err);
+                parts = a.peer.recv[a.peer.rank] + (s & 1) * static_cast<size_t>(a.peer.world) * a.peer.H;
+            }
+        }
         float ss = 0.f;
         for (int i = tid; i < kv8; i += kThreads) {
             uint4 h = reinterpret_cast<const uint4*>(src)[i];
@@ -178,8 +247,21 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
                 ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
             } else if constexpr (PRO == PRO_RESID_NORM) {
-                const float4 v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
-                const float4 v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
+                float4 v0, v1;
+                if (parts) {
+                    // sum of the ranks' partials in rank order: the same bits on every rank
+                    v0 = make_float4(0.f, 0.f, 0.f, 0.f);
+                    v1 = v0;
+                    for (int r = 0; r < a.peer.world; ++r) {
+                        const float4* pr = reinterpret_cast<const float4*>(parts + static_cast<size_t>(r) * a.peer.H) + 2 * i;
+                        const float4 w0 = __ldcg(pr), w1 = __ldcg(pr + 1);
+                        v0.x += w0.x; v0.y += w0.y; v0.z += w0.z; v0.w += w0.w;
+                        v1.x += w1.x; v1.y += w1.y; v1.z += w1.z; v1.w += w1.w;
+                    }
+                } else {
+                    v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
+                    v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
+                }
                 const float rs[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
                 uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
 #pragma unroll
@@ -275,13 +357,24 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             a.y[(r0 >> 1) + m] = f2bf(silu * uv);
         }
     } else {
+        // tensor parallel through peer memory: this kernel produces exchange s1
+        unsigned long long s1 = 0;
+        if constexpr (EPI == EPI_PARTIAL) {
+            if (a.peer.world) s1 = peer_seq(a.peer) + 1;
+        }
         for (int rl = tid; rl < nrows; rl += kThreads) {
             const float r = row_sum(rl);
             const int gr = r0 + rl;
             if constexpr (EPI == EPI_STORE) {
                 a.y[gr] = f2bf(r);
             } else if constexpr (EPI == EPI_PARTIAL) {
-                a.yf[gr] = r;
+                if (a.peer.world) {
+                    // this rank's partial row into every rank's slot (NVLink stores to peers)
+                    const size_t off = ((s1 & 1) * static_cast<size_t>(a.peer.world) + a.peer.rank) * a.peer.H + gr;
+                    for (int j = 0; j < a.peer.world; ++j) a.peer.recv[j][off] = r;
+                } else {
+                    a.yf[gr] = r;
+                }
             } else if constexpr (EPI == EPI_RESID) {
                 // qwen3.hpp:158-159: hidden = bf16(down); hs = bf16(hs + hidden)
                 a.hs[gr] = f2bf(bf2f(a.hs[gr]) + round_bf(r));
@@ -307,6 +400,10 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 best_key = max(best_key, argmax_key(bf2f(b), static_cast<uint32_t>(gr) + a.vocab_offset));
             }
         }
+    }
+
+    if constexpr (EPI == EPI_PARTIAL) {
+        if (a.peer.world) peer_signal(a.peer, peer_seq(a.peer) + 1);
     }
 
     // ---- post-loop finishers
@@ -361,12 +458,33 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             if (old == gridDim.x - 1) {
                 __threadfence();
                 const unsigned long long k = atomicExch(reinterpret_cast<unsigned long long*>(a.key_slot), 0ull);
-                *a.key_out = k;
+                if (a.peer.world) {
+                    // this rank's best key to every rank, then the exchange flag
+                    const unsigned long long s1 = peer_seq(a.peer) + 1;
+                    const size_t off = (s1 & 1) * static_cast<size_t>(a.peer.world) + a.peer.rank;
+                    for (int j = 0; j < a.peer.world; ++j) a.peer.keys[j][off] = k;
+                    __threadfence_system();
+                    for (int j = 0; j < a.peer.world; ++j)
+                        st_release_sys(a.peer.flags[j] + (s1 & 1) * a.peer.world + a.peer.rank, static_cast<uint32_t>(s1));
+                    *a.peer.seq = s1;
+                } else {
+                    *a.key_out = k;
+                }
                 *a.done_counter = 0u;
                 atomicAdd(a.pos_inc, 1);
             }
         }
     }
+}
+
+// The keys of the last exchange (lm_head of the last step) into out[world],
+// for the host-side readers of the greedy token.
+__global__ void peer_keys_kernel(const PeerLinks x, unsigned long long* out, uint32_t* err) {
+    const unsigned long long s = peer_seq(x);
+    if (s == 0) return;
+    peer_wait(x, s, err);
+    if (threadIdx.x < static_cast<unsigned>(x.world))
+        out[threadIdx.x] = __ldcg(x.keys[x.rank] + (s & 1) * x.world + threadIdx.x);
 }
 
 template <int PRO, int EPI>
@@ -386,6 +504,11 @@ cudaError_t launch_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
 }
 
 }  // namespace
+
+cudaError_t launch_peer_keys(const PeerLinks& x, unsigned long long* out, uint32_t* err, cudaStream_t s) {
+    peer_keys_kernel<<<1, 32, 0, s>>>(x, out, err);
+    return cudaGetLastError();
+}
 
 cudaError_t configure_gemv_kernels() {
     const void* fns[] = {

@@ -37,6 +37,20 @@ struct GemvPlan {
     size_t smem;   // dynamic shared memory bytes
 };
 
+// Tensor-parallel exchange through peer memory (CUDA IPC mappings over
+// NVLink): rank j's receive buffer holds, per slot (exchange parity), every
+// rank's fp32 partial vector [world][H], a flag per rank and an argmax key per
+// rank.  world == 0 selects the NCCL path.
+constexpr int kMaxRanks = 8;
+struct PeerLinks {
+    float* recv[kMaxRanks];               // rank j's [2][world][H], mapped into this process
+    uint32_t* flags[kMaxRanks];           // rank j's [2][world]: exchange number that filled the slot
+    unsigned long long* keys[kMaxRanks];  // rank j's [2][world] argmax keys
+    unsigned long long* seq;              // exchanges this rank has produced (never reset)
+    uint32_t* counter;                    // CTA arrivals of the producing kernel
+    int rank, world, H;
+};
+
 struct GemvArgs {
     const bf16* W;
     int N, K;
@@ -79,6 +93,9 @@ struct GemvArgs {
     uint64_t* key_out;
     int32_t* pos_inc;          // incremented once by the last CTA
     uint32_t vocab_offset;
+    // ---- tensor-parallel exchange (EPI_PARTIAL / EPI_ARGMAX produce, PRO_RESID_NORM /
+    // PRO_EMBED_NORM consume); peer.world == 0: NCCL path through yf / vsum / keys
+    PeerLinks peer;
     // ---- errors
     uint32_t* err;
 };
@@ -175,6 +192,7 @@ struct GemmArgs {
     int bn;         // output tile width 128 / 256, 0 = choose
     uint32_t* err;
 };
+cudaError_t launch_peer_keys(const PeerLinks& x, unsigned long long* out, uint32_t* err, cudaStream_t s);
 int gemm_tile_n(int M, int N, int sms);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
 

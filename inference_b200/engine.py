@@ -16,6 +16,7 @@ from ._lib import ModelConfig, check, lib
 from .config import Qwen3Config
 
 TRACE_WORDS = 10  # Q3_TRACE_WORDS in include/q3_sm100a.h
+PEER_HANDLE_BYTES = 64  # Q3_PEER_HANDLE_BYTES in include/q3_sm100a.h
 
 
 def _ptr(a: np.ndarray) -> int:
@@ -63,6 +64,18 @@ class Engine:
         buf = C.create_string_buffer(128)
         check(lib().q3_nccl_unique_id(buf))
         return buf.raw
+
+    def peer_handle(self) -> bytes:
+        """This rank's exchange-buffer IPC handle (q3_engine_peer_handle)."""
+        buf = (C.c_uint8 * PEER_HANDLE_BYTES)()
+        check(lib().q3_engine_peer_handle(self.h, buf))
+        return bytes(buf)
+
+    def attach_peers(self, handles):
+        """Every rank's handle in rank order (q3_engine_attach_peers)."""
+        blob = b"".join(handles)
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check(lib().q3_engine_attach_peers(self.h, buf, len(handles)))
 
     def attach_nccl(self, uid: bytes):
         buf = C.create_string_buffer(bytes(uid), 128)

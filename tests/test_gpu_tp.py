@@ -1,4 +1,6 @@
-"""Tensor-parallel engine on 2 GPUs (NCCL), teacher-forced against the oracle.
+"""Tensor-parallel engine on 2 GPUs, teacher-forced against the oracle, with
+the partial sums exchanged by NCCL or through peer memory (CUDA IPC over
+NVLink, fused into the GEMVs).
 
 Each rank holds its head / MLP / vocabulary shard; the full logits are the
 concatenation of the ranks' vocabulary shards and must match the oracle's
@@ -25,7 +27,21 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, name, out_dir):
+def _attach(e, dist, mode, rank):
+    from inference_b200 import Engine
+
+    if mode == "peer":
+        hs = [None] * dist.get_world_size()
+        dist.all_gather_object(hs, e.peer_handle())
+        dist.barrier()  # every rank's buffer exists and is zeroed before anyone writes
+        e.attach_peers(hs)
+    else:
+        obj = [Engine.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        e.attach_nccl(obj[0])
+
+
+def _rank_main(rank, world, port, name, out_dir, mode):
     import datetime
 
     import torch
@@ -44,9 +60,7 @@ def _rank_main(rank, world, port, name, out_dir):
     toks = g["tokens"].astype(np.uint32)
     e = Engine(qc, capacity=cap, device=rank, tp_rank=rank, tp_size=world)
     e.init_synthetic(0)
-    obj = [Engine.nccl_unique_id() if rank == 0 else None]
-    dist.broadcast_object_list(obj, src=0)
-    e.attach_nccl(obj[0])
+    _attach(e, dist, mode, rank)
     e.set_tokens(toks)
     shards = []
     for _ in toks:
@@ -61,8 +75,9 @@ def _rank_main(rank, world, port, name, out_dir):
 
 
 @pytest.mark.timeout(600)
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
 @pytest.mark.parametrize("name", ["qwen3_8b_l2", "qwen3_0p6b"])
-def test_engine_tensor_parallel_2gpu(tmp_path, oracle, name):
+def test_engine_tensor_parallel_2gpu(tmp_path, oracle, name, mode):
     import torch
     import torch.multiprocessing as mp
 
@@ -71,7 +86,7 @@ def test_engine_tensor_parallel_2gpu(tmp_path, oracle, name):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     world = 2
-    mp.start_processes(_rank_main, args=(world, _free_port(), name, str(tmp_path)), nprocs=world,
+    mp.start_processes(_rank_main, args=(world, _free_port(), name, str(tmp_path), mode), nprocs=world,
                        start_method="spawn")
     parts = [dict(np.load(tmp_path / f"tp{r}.npz")) for r in range(world)]
     np.testing.assert_array_equal(parts[0]["hist"], parts[1]["hist"])  # every rank resolves the same token
@@ -90,3 +105,53 @@ def test_engine_tensor_parallel_2gpu(tmp_path, oracle, name):
         agree += int(int(parts[0]["hist"][i]) == nxt)
     om.close()
     assert agree >= len(toks) - 1
+
+
+def _stall_main(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from inference_b200 import Engine, Q3Error, Qwen3Config, prompt_ids
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    qc = Qwen3Config("qwen3-0.6b-l2", hidden=1024, inter=3072, layers=2, q_heads=16, kv_heads=8, vocab=151936,
+                     tied=True)
+    e = Engine(qc, capacity=64, device=rank, tp_rank=rank, tp_size=world)
+    e.init_synthetic(0)
+    _attach(e, dist, "peer", rank)
+    msg = ""
+    if rank == 0:
+        # rank 1 never steps: its flags never arrive, every wait must run out
+        e.set_tokens(prompt_ids(4))
+        e.step(1)
+        try:
+            e.sync()
+        except Q3Error as exc:
+            msg = str(exc)
+        # the engine stays usable: its state reads back without error
+        e.logits()
+    dist.barrier()  # rank 1 keeps its buffer mapped until rank 0 is done
+    with open(os.path.join(out_dir, f"stall{rank}.txt"), "w") as f:
+        f.write(msg)
+    e.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_peer_wait_times_out_without_fault(tmp_path):
+    """Failure detection: a peer that never produces its partials makes the
+    bounded flag wait run out; the step reports Q3_ERR_DEVICE 'peer wait
+    timed out' instead of hanging, and the context stays usable."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_stall_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    msg = (tmp_path / "stall0.txt").read_text()
+    assert "peer wait timed out" in msg, msg
