@@ -46,6 +46,8 @@ def parse_args():
     ap.add_argument("--prompt", type=int, default=0, help="profiling only: override the prompt length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--nccl", action="store_true", help="tensor parallel: exchange partial sums with NCCL "
+                    "instead of peer-memory stores fused into the GEMVs")
     ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path instead of the "
                                                           "persistent kernel (the tensor-parallel path)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=3)
@@ -270,9 +272,15 @@ def main():
     if a.graph and eng.persistent:
         eng.persistent = False
     if world > 1:
-        obj = [ib.Engine.nccl_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        eng.attach_nccl(obj[0])
+        if a.nccl:
+            obj = [ib.Engine.nccl_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(obj, src=0)
+            eng.attach_nccl(obj[0])
+        else:
+            handles = [None] * world
+            dist.all_gather_object(handles, eng.peer_handle())
+            dist.barrier()  # every rank's exchange buffer exists and is zeroed before anyone writes
+            eng.attach_peers(handles)
 
     window = capacity - prompt_len if not a.window else min(a.window, capacity - prompt_len)
     prompt = ib.prompt_ids(prompt_len, seed=1, vocab=cfg.vocab)
@@ -459,7 +467,9 @@ def main():
             "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
                        "decode_tokens_per_step": window, "global_batch": 1,
                        "decode_path": "persistent kernel" if eng.persistent else "CUDA graph of fused kernels",
-                       "parallelism": f"tp{world}", "weights": "random N(0,0.02) seed 0, ids seed 1",
+                       "parallelism": f"tp{world}",
+                       "tp_exchange": (None if world == 1 else "NCCL allreduce/allgather" if a.nccl else
+                                       "peer-memory stores fused into the o/down/lm_head GEMVs (CUDA IPC, NVLink)"), "weights": "random N(0,0.02) seed 0, ids seed 1",
                        "l2_flush": f"not needed: {cfg.weight_bytes() / 1e9:.1f} GB of weights streamed per token "
                                    f">> 126 MB L2"},
             "clocks": clock, "e2e": e2e, "gpu_launches": int(launches),
