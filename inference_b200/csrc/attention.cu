@@ -16,9 +16,10 @@
 //     Pages older than the current position are fetched before
 //     griddepcontrol.wait -- only the page receiving this token's K/V waits
 //     for the QKV kernel;
-//   * each half-warp owns 8 of a page's 64 tokens (16 lanes x 8 dims), with an
-//     online softmax in fp32 (exp2 of log2e-scaled scores);
-//   * half-warp states merge in shared memory in a fixed order; the splits then
+//   * each consumer warp owns 16 of a page's 64 tokens and does its math on the
+//     tensor cores (mma.sync: S = Q K^T, online softmax in fp32 on the
+//     fragments, O += P V with P in BF16 hi + lo parts);
+//   * warp states merge in shared memory in a fixed order; the splits then
 //     merge across the cluster through distributed shared memory, each CTA
 //     producing a slice of the outputs -- deterministic, no global partials.
 #include <cooperative_groups.h>
@@ -55,6 +56,27 @@ struct AttnSmem {
     uint64_t full[kStages];
     uint64_t empty[kStages];
 };
+
+__device__ __forceinline__ void ldmatrix_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                                  uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+// D (16 x 8, fp32) += A (16 x 16, BF16, row) B (16 x 8, BF16, col)
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
 
 template <int HG>
 __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a) {
@@ -120,32 +142,34 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         }
     } else {
         // ------------------------------------------------------------ consumers
+        // Tensor cores (mma.sync m16n8k16, BF16 -> FP32): warp w owns tokens
+        // 16w .. 16w + 15 of each 64-token page.  S = Q K^T with Q as the A
+        // operand (rows = the CTA's HG query heads, padded to 16 with zeros),
+        // online softmax on the accumulator fragments, then O += P V with P
+        // reused as the A operand, split into BF16 hi + lo parts so the
+        // probabilities keep ~16 bits.  Each warp first XOR-swizzles its own
+        // 16 rows of the K and V tiles in place (16-byte chunk c of row r to
+        // c ^ (r & 7)), so every ldmatrix phase hits 8 distinct bank groups.
         pdl_wait();  // q comes from the QKV kernel
         pdl_trigger();
-        const int hw = tid >> 4;  // half-warp 0..7
-        const int hl = tid & 15;  // lane within half-warp: dims [8 hl, 8 hl + 8)
+        const int g = lane >> 2, t4 = lane & 3;  // fragment row (query head) and column pair
         const int qh0 = kvh * G + qb * HG;
         const float qscale = (1.0f / sqrtf(static_cast<float>(kHd))) * kLog2e;
 
-        float q[HG][8];
+        uint32_t qa[8][2];  // A fragments of q: rows g (dims 16kk + 2t4, +1) and (+8); rows 8-15 are zero
 #pragma unroll
-        for (int g = 0; g < HG; ++g) {
-            const uint4 v = reinterpret_cast<const uint4*>(qv + static_cast<size_t>(qh0 + g) * kHd)[hl];
-            const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                q[g][2 * j] = bf_lo(w[j]);
-                q[g][2 * j + 1] = bf_hi(w[j]);
+        for (int kk = 0; kk < 8; ++kk) {
+            qa[kk][0] = qa[kk][1] = 0u;
+            if (g < HG) {
+                const uint32_t* qr = reinterpret_cast<const uint32_t*>(qv + static_cast<size_t>(qh0 + g) * kHd);
+                qa[kk][0] = qr[kk * 8 + t4];
+                qa[kk][1] = qr[kk * 8 + 4 + t4];
             }
         }
-        float m[HG], l[HG], acc[HG][8];
+        float o[16][4];
 #pragma unroll
-        for (int g = 0; g < HG; ++g) {
-            m[g] = -INFINITY;
-            l[g] = 0.f;
-#pragma unroll
-            for (int d = 0; d < 8; ++d) acc[g][d] = 0.f;
-        }
+        for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
+        float m_run = -INFINITY, l_run = 0.f;  // row g: running max (log2 units), this lane's partial sum
 
         bool failed = false;
         for (int i = 0; i < np; ++i) {
@@ -155,102 +179,137 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
             if (ok) {
                 const int page = pb + i;
                 const int valid = min(kPage, pos + 1 - page * kPage);
-                const uint4* kt = reinterpret_cast<const uint4*>(S.kv[s][0]);
-                const uint4* vt = reinterpret_cast<const uint4*>(S.kv[s][1]);
-                float sc[8][HG];
+                uint8_t* kt = S.kv[s][0];
+                uint8_t* vt = S.kv[s][1];
+                // ---- swizzle this warp's rows in place; rows past the position become zeros in V
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int j = hw + 8 * t;
-                    const uint4 kv = kt[j * 16 + hl];
-                    const uint32_t* w = reinterpret_cast<const uint32_t*>(&kv);
+                for (int tile = 0; tile < 2; ++tile) {
+                    uint8_t* base = tile ? vt : kt;
+                    const int c = lane & 15;
+                    uint4 rr[8];
 #pragma unroll
-                    for (int g = 0; g < HG; ++g) {
-                        float d = 0.f;
+                    for (int j = 0; j < 8; ++j) {
+                        const int r = warp * 16 + (lane >> 4) + 2 * j;
+                        rr[j] = *reinterpret_cast<const uint4*>(base + r * 256 + c * 16);
+                    }
+                    __syncwarp();
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            d = fmaf(q[g][2 * e], bf_lo(w[e]), d);
-                            d = fmaf(q[g][2 * e + 1], bf_hi(w[e]), d);
+                    for (int j = 0; j < 8; ++j) {
+                        const int r = warp * 16 + (lane >> 4) + 2 * j;
+                        *reinterpret_cast<uint4*>(base + r * 256 + (c ^ (r & 7)) * 16) =
+                            (tile == 0 || r < valid) ? rr[j] : make_uint4(0u, 0u, 0u, 0u);
+                    }
+                    __syncwarp();
+                }
+                // ---- S = Q K^T for this warp's two 8-token n-tiles
+                float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                {
+                    const int q = lane >> 3, r8 = lane & 7;
+                    const int row = warp * 16 + (q >> 1) * 8 + r8;
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const int chunk = kk * 2 + (q & 1);
+                        uint32_t b0, b1, b2, b3;
+                        ldmatrix_x4(kt + row * 256 + ((chunk ^ (row & 7)) * 16), b0, b1, b2, b3);
+                        mma_bf16_16816(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
+                        mma_bf16_16816(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
+                    }
+                }
+                // ---- online softmax on row g (tokens 16w + 8jn + 2t4 + e)
+                float mx = -INFINITY;
+#pragma unroll
+                for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const int tok = warp * 16 + jn * 8 + 2 * t4 + e;
+                        sc[jn][e] = tok < valid ? sc[jn][e] * qscale : -INFINITY;
+                        mx = fmaxf(mx, sc[jn][e]);
+                    }
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float m_new = fmaxf(m_run, mx);
+                float p[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+                if (m_new != -INFINITY) {
+                    const float corr = exp2f(m_run - m_new);
+                    m_run = m_new;
+                    l_run *= corr;
+#pragma unroll
+                    for (int d = 0; d < 16; ++d) {
+                        o[d][0] *= corr;
+                        o[d][1] *= corr;
+                    }
+#pragma unroll
+                    for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            p[jn][e] = exp2f(sc[jn][e] - m_new);
+                            l_run += p[jn][e];
                         }
-                        d += __shfl_xor_sync(0xffffffffu, d, 8);
-                        d += __shfl_xor_sync(0xffffffffu, d, 4);
-                        d += __shfl_xor_sync(0xffffffffu, d, 2);
-                        d += __shfl_xor_sync(0xffffffffu, d, 1);
-                        sc[t][g] = (j < valid) ? d * qscale : -INFINITY;
-                    }
                 }
+                // ---- O += P V: P rows g, k = the warp's 16 tokens (hi + lo BF16 parts)
+                uint32_t ph[2], pl[2];
 #pragma unroll
-                for (int g = 0; g < HG; ++g) {
-                    float mx = sc[0][g];
-#pragma unroll
-                    for (int t = 1; t < 8; ++t) mx = fmaxf(mx, sc[t][g]);
-                    const float mn = fmaxf(m[g], mx);
-                    if (mn == -INFINITY) continue;
-                    const float corr = exp2f(m[g] - mn);
-                    m[g] = mn;
-                    l[g] *= corr;
-#pragma unroll
-                    for (int d = 0; d < 8; ++d) acc[g][d] *= corr;
-#pragma unroll
-                    for (int t = 0; t < 8; ++t) {
-                        const float pr = exp2f(sc[t][g] - mn);
-                        sc[t][g] = pr;
-                        l[g] += pr;
-                    }
+                for (int jn = 0; jn < 2; ++jn) {
+                    const bf16 h0 = f2bf(p[jn][0]), h1 = f2bf(p[jn][1]);
+                    const bf16 l0 = f2bf(p[jn][0] - bf2f(h0)), l1 = f2bf(p[jn][1] - bf2f(h1));
+                    ph[jn] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) |
+                             (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
+                    pl[jn] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) |
+                             (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
                 }
+                {
+                    const int q = lane >> 3, r8 = lane & 7;
+                    const int row = warp * 16 + (q & 1) * 8 + r8;
 #pragma unroll
-                for (int t = 0; t < 8; ++t) {
-                    const int j = hw + 8 * t;
-                    if (j >= valid) continue;  // rows past the position hold stale data
-                    const uint4 vv = vt[j * 16 + hl];
-                    const uint32_t* w = reinterpret_cast<const uint32_t*>(&vv);
-                    float vf[8];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        vf[2 * e] = bf_lo(w[e]);
-                        vf[2 * e + 1] = bf_hi(w[e]);
-                    }
-#pragma unroll
-                    for (int g = 0; g < HG; ++g) {
-                        const float pr = (m[g] == -INFINITY) ? 0.f : sc[t][g];
-#pragma unroll
-                        for (int d = 0; d < 8; ++d) acc[g][d] = fmaf(pr, vf[d], acc[g][d]);
+                    for (int e = 0; e < 8; ++e) {
+                        const int chunk = 2 * e + (q >> 1);
+                        uint32_t b0, b1, b2, b3;
+                        ldmatrix_x4_trans(vt + row * 256 + ((chunk ^ (row & 7)) * 16), b0, b1, b2, b3);
+                        mma_bf16_16816(o[2 * e], ph[0], 0u, ph[1], 0u, b0, b1);
+                        mma_bf16_16816(o[2 * e], pl[0], 0u, pl[1], 0u, b0, b1);
+                        mma_bf16_16816(o[2 * e + 1], ph[0], 0u, ph[1], 0u, b2, b3);
+                        mma_bf16_16816(o[2 * e + 1], pl[0], 0u, pl[1], 0u, b2, b3);
                     }
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s]);
         }
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+        l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
 
-        // ---- merge the 8 half-warp states (fixed order) into this CTA's state
-#pragma unroll
-        for (int g = 0; g < HG; ++g) {
-            if (hl == 0) {
-                S.m[hw][g] = m[g];
-                S.l[hw][g] = l[g];
+        // ---- merge the 4 warp states (fixed order) into this CTA's state
+        if (g < HG) {
+            if (t4 == 0) {
+                S.m[warp][g] = m_run;
+                S.l[warp][g] = l_run;
             }
 #pragma unroll
-            for (int d = 0; d < 8; ++d) S.acc[hw][g][8 * hl + d] = acc[g][d];
+            for (int d = 0; d < 16; ++d) {
+                S.acc[warp][g][8 * d + 2 * t4] = o[d][0];
+                S.acc[warp][g][8 * d + 2 * t4 + 1] = o[d][1];
+            }
         }
         named_bar(1, kConsumers);
-        for (int o = tid; o < HG * kHd; o += kConsumers) {
-            const int g = o / kHd, d = o % kHd;
+        for (int oi = tid; oi < HG * kHd; oi += kConsumers) {
+            const int gg = oi / kHd, d = oi % kHd;
             float M = -INFINITY;
-            for (int h = 0; h < 8; ++h) M = fmaxf(M, S.m[h][g]);
+            for (int h = 0; h < kWarps; ++h) M = fmaxf(M, S.m[h][gg]);
             float Lsum = 0.f, A = 0.f;
             if (M != -INFINITY) {
-                for (int h = 0; h < 8; ++h) {
-                    const float f = exp2f(S.m[h][g] - M);
-                    Lsum += S.l[h][g] * f;
-                    A += S.acc[h][g][d] * f;
+                for (int h = 0; h < kWarps; ++h) {
+                    const float f = exp2f(S.m[h][gg] - M);
+                    Lsum += S.l[h][gg] * f;
+                    A += S.acc[h][gg][d] * f;
                 }
             }
             if (a.splits == 1) {
-                out[static_cast<size_t>(qh0 + g) * kHd + d] = f2bf(A / Lsum);
+                out[static_cast<size_t>(qh0 + gg) * kHd + d] = f2bf(A / Lsum);
             } else {
-                S.cacc[g][d] = A;
+                S.cacc[gg][d] = A;
                 if (d == 0) {
-                    S.cm[g] = M;
-                    S.cl[g] = Lsum;
+                    S.cm[gg] = M;
+                    S.cl[gg] = Lsum;
                 }
             }
         }
