@@ -75,21 +75,22 @@ def _rank_main(rank, world, port, name, out_dir, mode):
 
 
 @pytest.mark.timeout(600)
-@pytest.mark.parametrize("mode", ["peer", "nccl"])
-@pytest.mark.parametrize("name", ["qwen3_8b_l2", "qwen3_0p6b"])
-def test_engine_tensor_parallel_2gpu(tmp_path, oracle, name, mode):
+@pytest.mark.parametrize("name,mode,world", [("qwen3_8b_l2", "peer", 2), ("qwen3_8b_l2", "nccl", 2),
+                                             ("qwen3_0p6b", "peer", 2), ("qwen3_0p6b", "nccl", 2),
+                                             ("qwen3_8b_l2", "peer", 4)])
+def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
     import torch
     import torch.multiprocessing as mp
 
     from oracle import ModelConfig
 
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     mp.start_processes(_rank_main, args=(world, _free_port(), name, str(tmp_path), mode), nprocs=world,
                        start_method="spawn")
     parts = [dict(np.load(tmp_path / f"tp{r}.npz")) for r in range(world)]
-    np.testing.assert_array_equal(parts[0]["hist"], parts[1]["hist"])  # every rank resolves the same token
+    for r in range(1, world):
+        np.testing.assert_array_equal(parts[0]["hist"], parts[r]["hist"])  # every rank resolves the same token
     g = dict(np.load(os.path.join(GOLD, f"model_{name}_ref_cpu.npz")))
     h, inter, layers, qh, kvh, hd, vocab, cap, tied = (int(v) for v in g["config"])
     om = oracle.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)), seed=0)
