@@ -261,6 +261,21 @@ Q3_API size_t q3_engine_kv_bytes_per_position(q3_engine* e);
  * launches and algorithmic bytes. */
 Q3_API int q3_engine_profile_step(q3_engine* e, int kernel_class, double* ms, size_t* launches, double* bytes);
 
+/* Checkpoints (SURVEY next-step 1; the reference reads one safetensors file
+ * whole, src/lib/model/safetensors.hpp:30-54): `path` is a .safetensors file,
+ * a model.safetensors.index.json of a sharded checkpoint, or a directory
+ * holding either.  Shards are memory-mapped and every BF16 tensor goes
+ * through q3_engine_set_weight (packing and tensor-parallel sharding); the call
+ * fails if a tensor is malformed, unknown or missing.  n_loaded (optional)
+ * receives the number of tensors loaded. */
+Q3_API int q3_engine_load_safetensors(q3_engine* e, const char* path, size_t* n_loaded);
+
+/* The tensors of a checkpoint (same `path` forms) without loading anything
+ * and without a GPU: one line per tensor, "name\tdtype\tshape\tfile\toffset\tbytes"
+ * (shape as d0xd1, offset absolute in the file).  *needed receives the text
+ * size including the terminating zero; out may be NULL to ask for it. */
+Q3_API int q3_safetensors_list(const char* path, char* out, size_t capacity, size_t* needed);
+
 /* Tensor parallelism through peer memory (the fast path): every rank exports
  * its exchange buffer as a CUDA IPC handle of Q3_PEER_HANDLE_BYTES bytes,
  * the handles are shared by any means (the tests use torch.distributed), and

@@ -17,6 +17,7 @@ STATUS = {0: "Q3_OK", 1: "Q3_ERR_INVALID", 2: "Q3_ERR_CUDA", 3: "Q3_ERR_UNSUPPOR
 
 # Every exported symbol declared in include/q3_sm100a.h, with ctypes signatures.
 _vp, _sz, _u16p, _u32p, _i32p = C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p
+_szp = C.POINTER(C.c_size_t)
 SIGNATURES = {
     "q3_last_error": (C.c_char_p, []),
     "q3_version": (C.c_int, []),
@@ -63,6 +64,8 @@ SIGNATURES = {
     "q3_engine_profile_step": (C.c_int, [_vp, C.c_int, C.POINTER(C.c_double), C.POINTER(C.c_size_t),
                                          C.POINTER(C.c_double)]),
     "q3_nccl_unique_id": (C.c_int, [_vp]),
+    "q3_engine_load_safetensors": (C.c_int, [_vp, C.c_char_p, _szp]),
+    "q3_safetensors_list": (C.c_int, [C.c_char_p, C.c_char_p, _sz, _szp]),
     "q3_engine_peer_handle": (C.c_int, [_vp, _vp]),
     "q3_engine_attach_peers": (C.c_int, [_vp, _vp, _sz]),
     "q3_engine_attach_nccl": (C.c_int, [_vp, _vp]),

@@ -92,6 +92,11 @@ struct q3_engine {
 };
 
 namespace q3 {
+bool engine_tied(const q3_engine* e) { return e->cfg.tied != 0; }
+size_t engine_layers(const q3_engine* e) { return e->layers.size(); }
+}  // namespace q3
+
+namespace q3 {
 namespace {
 
 int dalloc(q3_engine* e, void** p, size_t bytes) {

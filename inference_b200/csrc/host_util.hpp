@@ -31,6 +31,10 @@ inline int fail(int status, const std::string& msg) {
         }                                                                                                     \
     } while (0)
 
+// Engine facts for host code outside engine.cu.
+bool engine_tied(const q3_engine* e);
+size_t engine_layers(const q3_engine* e);
+
 #define Q3_CHECK(cond, msg)                                \
     do {                                                   \
         if (!(cond)) return ::q3::fail(Q3_ERR_INVALID, msg); \

@@ -9,6 +9,7 @@ is KVCache::reset.  ``step`` is the device-resident loop used for timing.
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -64,6 +65,12 @@ class Engine:
         buf = C.create_string_buffer(128)
         check(lib().q3_nccl_unique_id(buf))
         return buf.raw
+
+    def load_safetensors(self, path) -> int:
+        """Load a Hugging Face checkpoint (file, index json or directory); returns the tensor count."""
+        n = C.c_size_t()
+        check(lib().q3_engine_load_safetensors(self.h, os.fsencode(path), C.byref(n)))
+        return int(n.value)
 
     def peer_handle(self) -> bytes:
         """This rank's exchange-buffer IPC handle (q3_engine_peer_handle)."""
