@@ -234,6 +234,7 @@ int record_step(Recorder& r, size_t pos_now) {
             cur = 0;
         } else if (tp) {
             pro = PRO_RESID_NORM;
+            a.xtag = 2 * static_cast<int>(l);  // the previous layer's down_proj exchange
             a.hs = e->hs[cur];
             a.hs_out = e->hs[cur ^ 1];
             a.vsum = e->partial;
@@ -251,6 +252,7 @@ int record_step(Recorder& r, size_t pos_now) {
         o.x = e->attn;
         if (tp) {
             o.yf = e->partial;
+            o.xtag = 2 * static_cast<int>(l) + 1;
             Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, o, L.w_o, e->H, e->qd, 0));
             Q3_TRY(allreduce(e, e->partial, e->H));
         } else {
@@ -263,6 +265,7 @@ int record_step(Recorder& r, size_t pos_now) {
         gu.norm_w = L.post_norm;
         gu.y = e->g;
         if (tp) {
+            gu.xtag = 2 * static_cast<int>(l) + 1;
             gu.hs = e->hs[cur];
             gu.hs_out = e->hs[cur ^ 1];
             gu.vsum = e->partial;
@@ -279,6 +282,7 @@ int record_step(Recorder& r, size_t pos_now) {
         d.x = e->g;
         if (tp) {
             d.yf = e->partial;
+            d.xtag = 2 * static_cast<int>(l) + 2;
             Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, d, L.w_down, e->H, e->il, 0));
             Q3_TRY(allreduce(e, e->partial, e->H));
         } else {
@@ -296,6 +300,7 @@ int record_step(Recorder& r, size_t pos_now) {
     h.pos_inc = e->pos;
     h.vocab_offset = e->voff;
     if (tp) {
+        h.xtag = 2 * static_cast<int>(e->layers.size());
         h.hs = e->hs[cur];
         h.hs_out = e->hs[cur ^ 1];
         h.vsum = e->partial;
@@ -379,6 +384,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     const q3_model_config& c = *cfg;
     Q3_CHECK(tp_size >= 1 && tp_rank >= 0 && tp_rank < tp_size, "q3_engine_create: bad tensor-parallel rank");
     Q3_CHECK(tp_size <= kMaxRanks, "q3_engine_create: at most 8 tensor-parallel ranks");
+    // peer-exchange tags number the 2 L partial exchanges of a step in 8 bits
+    Q3_CHECK(tp_size == 1 || c.layers <= 127, "q3_engine_create: tensor parallelism supports up to 127 layers");
     if (c.head_dim != 128) return fail(Q3_ERR_UNSUPPORTED, "q3_engine_create: head_dim must be 128");
     Q3_CHECK(c.layers > 0 && c.hidden > 0 && c.vocab > 0 && c.capacity > 1, "q3_engine_create: empty config");
     Q3_CHECK(c.kv_heads > 0 && c.q_heads % c.kv_heads == 0, "q3_engine_create: q_heads % kv_heads != 0");
@@ -472,8 +479,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->vsum, H)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->partial, H)) != Q3_OK) return bail(rc);
     if (tp_size > 1) {
-        // exchange buffer: recv [2][world][H] fp32 | flags [2][world] u32 | keys [2][world] u64
-        e->xbuf_bytes = (2 * static_cast<size_t>(tp_size) * H * 4 + 2 * tp_size * 4 + 15) / 16 * 16 + 2 * tp_size * 8;
+        // exchange buffer: pairs [2][world][H] u64 | flags [2][world] u32 | keys [2][world] u64
+        e->xbuf_bytes = (2 * static_cast<size_t>(tp_size) * H * 8 + 2 * tp_size * 4 + 15) / 16 * 16 + 2 * tp_size * 8;
         if ((rc = dalloc(e, &e->xbuf, e->xbuf_bytes)) != Q3_OK) return bail(rc);
         cudaMemset(e->xbuf, 0, e->xbuf_bytes);
         unsigned long long* seq = nullptr;
@@ -1156,7 +1163,7 @@ int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n) {
     Q3_CHECK(!e->peer_mode, "q3_engine_attach_peers: already attached");
     Q3_CUDA(cudaSetDevice(e->device));
     const size_t H = static_cast<size_t>(e->H), W = static_cast<size_t>(e->world);
-    const size_t flags_off = 2 * W * H * 4, keys_off = (flags_off + 2 * W * 4 + 15) / 16 * 16;
+    const size_t flags_off = 2 * W * H * 8, keys_off = (flags_off + 2 * W * 4 + 15) / 16 * 16;
     for (int j = 0; j < e->world; ++j) {
         void* base = nullptr;
         if (j == e->rank) {
@@ -1168,7 +1175,7 @@ int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n) {
             Q3_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
             e->xpeer[j] = base;
         }
-        e->links.recv[j] = static_cast<float*>(base);
+        e->links.recv[j] = static_cast<unsigned long long*>(base);
         e->links.flags[j] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(base) + flags_off);
         e->links.keys[j] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(base) + keys_off);
     }

@@ -99,6 +99,13 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 __device__ __forceinline__ unsigned long long peer_seq(const PeerLinks& x) {
     return *reinterpret_cast<volatile unsigned long long*>(x.seq);
 }
+// Tag of partial exchange xtag in the current step (unique for 2^24 steps).
+__device__ __forceinline__ uint32_t pair_tag(const PeerLinks& x, int xtag) {
+    return static_cast<uint32_t>(peer_seq(x)) * 256u + static_cast<uint32_t>(xtag);
+}
+__device__ __forceinline__ void ld_pairs(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
 
 // Consumer side: every CTA waits (bounded) until all ranks filled the slot of
 // exchange s, the one the kernel before produced.
@@ -116,23 +123,6 @@ __device__ __forceinline__ void peer_wait(const PeerLinks& x, unsigned long long
         }
     }
     __syncthreads();
-}
-
-// Producer side, after every CTA stored its part into each rank's slot of
-// exchange s1: the last CTA to arrive raises the flag of s1 on every rank.
-__device__ __forceinline__ void peer_signal(const PeerLinks& x, unsigned long long s1) {
-    __threadfence_system();  // this thread's stores to the peers before the CTA's arrival
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t old = atomicAdd(x.counter, 1u);
-        if (old == gridDim.x - 1) {
-            __threadfence_system();
-            const uint32_t slot = static_cast<uint32_t>(s1 & 1);
-            for (int j = 0; j < x.world; ++j) st_release_sys(x.flags[j] + slot * x.world + x.rank, static_cast<uint32_t>(s1));
-            *x.counter = 0u;
-            *x.seq = s1;
-        }
-    }
 }
 
 template <int PRO, int EPI>
@@ -229,13 +219,13 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             }
             src = a.embed + static_cast<size_t>(token) * a.K;
         }
-        // tensor parallel through peer memory: the partials every rank stored here
-        const float* parts = nullptr;
+        // tensor parallel through peer memory: the (value, tag) pairs every rank stored here
+        const unsigned long long* parts = nullptr;
+        uint32_t tag = 0;
         if constexpr (PRO == PRO_RESID_NORM) {
             if (a.peer.world) {
-                const unsigned long long s = peer_seq(a.peer);
-                peer_wait(a.peer, s, a.err);
-                parts = a.peer.recv[a.peer.rank] + (s & 1) * static_cast<size_t>(a.peer.world) * a.peer.H;
+                tag = pair_tag(a.peer, a.xtag);
+                parts = a.peer.recv[a.peer.rank] + ((a.xtag - 1) & 1) * static_cast<size_t>(a.peer.world) * a.peer.H;
             }
         }
         float ss = 0.f;
@@ -249,15 +239,30 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             } else if constexpr (PRO == PRO_RESID_NORM) {
                 float4 v0, v1;
                 if (parts) {
-                    // sum of the ranks' partials in rank order: the same bits on every rank
-                    v0 = make_float4(0.f, 0.f, 0.f, 0.f);
-                    v1 = v0;
+                    // sum of the ranks' partials in rank order (the same bits on every rank),
+                    // each pair read until it carries this exchange's tag (bounded)
+                    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                     for (int r = 0; r < a.peer.world; ++r) {
-                        const float4* pr = reinterpret_cast<const float4*>(parts + static_cast<size_t>(r) * a.peer.H) + 2 * i;
-                        const float4 w0 = __ldcg(pr), w1 = __ldcg(pr + 1);
-                        v0.x += w0.x; v0.y += w0.y; v0.z += w0.z; v0.w += w0.w;
-                        v1.x += w1.x; v1.y += w1.y; v1.z += w1.z; v1.w += w1.w;
+                        const unsigned long long* pr = parts + static_cast<size_t>(r) * a.peer.H + 8 * i;
+                        unsigned long long q[8];
+                        for (uint32_t polls = 0;; ++polls) {
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) ld_pairs(pr + 2 * e, q[2 * e], q[2 * e + 1]);
+                            bool all = true;
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) all = all && static_cast<uint32_t>(q[e] >> 32) == tag;
+                            if (all) break;
+                            if ((polls & 1023) == 1023 && *reinterpret_cast<volatile uint32_t*>(a.err)) break;
+                            if (polls > kPeerPolls) {
+                                record_error(a.err, DEV_PEER_WAIT_TIMEOUT);
+                                break;
+                            }
+                        }
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[e] += __uint_as_float(static_cast<uint32_t>(q[e]));
                     }
+                    v0 = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                    v1 = make_float4(acc[4], acc[5], acc[6], acc[7]);
                 } else {
                     v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
                     v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
@@ -357,10 +362,10 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             a.y[(r0 >> 1) + m] = f2bf(silu * uv);
         }
     } else {
-        // tensor parallel through peer memory: this kernel produces exchange s1
-        unsigned long long s1 = 0;
+        // tensor parallel through peer memory: this kernel produces partial exchange xtag
+        uint32_t tag = 0;
         if constexpr (EPI == EPI_PARTIAL) {
-            if (a.peer.world) s1 = peer_seq(a.peer) + 1;
+            if (a.peer.world) tag = pair_tag(a.peer, a.xtag);
         }
         for (int rl = tid; rl < nrows; rl += kThreads) {
             const float r = row_sum(rl);
@@ -369,9 +374,13 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 a.y[gr] = f2bf(r);
             } else if constexpr (EPI == EPI_PARTIAL) {
                 if (a.peer.world) {
-                    // this rank's partial row into every rank's slot (NVLink stores to peers)
-                    const size_t off = ((s1 & 1) * static_cast<size_t>(a.peer.world) + a.peer.rank) * a.peer.H + gr;
-                    for (int j = 0; j < a.peer.world; ++j) a.peer.recv[j][off] = r;
+                    // this rank's partial row into every rank's slot: one 8-byte (value, tag)
+                    // store per rank (NVLink to peers); no fence or flag needed
+                    const size_t off =
+                        (((a.xtag - 1) & 1) * static_cast<size_t>(a.peer.world) + a.peer.rank) * a.peer.H + gr;
+                    const unsigned long long pair =
+                        (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(r);
+                    for (int j = 0; j < a.peer.world; ++j) a.peer.recv[j][off] = pair;
                 } else {
                     a.yf[gr] = r;
                 }
@@ -400,10 +409,6 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 best_key = max(best_key, argmax_key(bf2f(b), static_cast<uint32_t>(gr) + a.vocab_offset));
             }
         }
-    }
-
-    if constexpr (EPI == EPI_PARTIAL) {
-        if (a.peer.world) peer_signal(a.peer, peer_seq(a.peer) + 1);
     }
 
     // ---- post-loop finishers

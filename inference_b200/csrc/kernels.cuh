@@ -38,15 +38,17 @@ struct GemvPlan {
 };
 
 // Tensor-parallel exchange through peer memory (CUDA IPC mappings over
-// NVLink): rank j's receive buffer holds, per slot (exchange parity), every
-// rank's fp32 partial vector [world][H], a flag per rank and an argmax key per
-// rank.  world == 0 selects the NCCL path.
+// NVLink).  Rank j's buffer holds, per slot (exchange parity), every rank's
+// fp32 partial vector as [world][H] 8-byte (value, tag) pairs -- a pair is
+// one store, so a reader that sees the expected tag sees the value -- plus a
+// flag and an argmax key per rank for the lm_head exchange.  world == 0
+// selects the NCCL path.
 constexpr int kMaxRanks = 8;
 struct PeerLinks {
-    float* recv[kMaxRanks];               // rank j's [2][world][H], mapped into this process
+    unsigned long long* recv[kMaxRanks];  // rank j's [2][world][H] (value, tag) pairs, mapped into this process
     uint32_t* flags[kMaxRanks];           // rank j's [2][world]: exchange number that filled the slot
     unsigned long long* keys[kMaxRanks];  // rank j's [2][world] argmax keys
-    unsigned long long* seq;              // exchanges this rank has produced (never reset)
+    unsigned long long* seq;              // lm_head exchanges (= steps) this rank has run (never reset)
     uint32_t* counter;                    // CTA arrivals of the producing kernel
     int rank, world, H;
 };
@@ -94,8 +96,11 @@ struct GemvArgs {
     int32_t* pos_inc;          // incremented once by the last CTA
     uint32_t vocab_offset;
     // ---- tensor-parallel exchange (EPI_PARTIAL / EPI_ARGMAX produce, PRO_RESID_NORM /
-    // PRO_EMBED_NORM consume); peer.world == 0: NCCL path through yf / vsum / keys
+    // PRO_EMBED_NORM consume); peer.world == 0: NCCL path through yf / vsum / keys.
+    // xtag: the partial exchange produced (EPI_PARTIAL) or consumed (PRO_RESID_NORM),
+    // 1 .. 2 L within a step (o_proj of layer l: 2 l + 1, down_proj: 2 l + 2)
     PeerLinks peer;
+    int xtag;
     // ---- errors
     uint32_t* err;
 };
