@@ -50,6 +50,9 @@ def parse_args():
                     "instead of peer-memory stores fused into the GEMVs")
     ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path instead of the "
                                                           "persistent kernel (the tensor-parallel path)")
+    ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
+                    help="fp8: E4M3 GEMV matrices with per-row power-of-two scales (the FP8-weight model, "
+                         "not the reference's BF16 model; the CUDA graph path)")
     ap.add_argument("--cpu-sample-tokens", type=int, default=3)
     ap.add_argument("--reference-cuda-tokens", type=int, default=0,
                     help="also time the reference's own cuBLAS CUDA backend (oracle/_ref/libref_cuda.so) for this "
@@ -267,7 +270,9 @@ def main():
 
     import inference_b200 as ib
 
-    eng = ib.Engine(cfg, capacity=capacity, device=local, tp_rank=rank, tp_size=world)
+    eng = ib.Engine(cfg, capacity=capacity, device=local, tp_rank=rank, tp_size=world, weights=a.weights)
+    if a.weights == "fp8":
+        workload += "-fp8"
     eng.init_synthetic(0)
     if a.graph and eng.persistent:
         eng.persistent = False
@@ -369,7 +374,7 @@ def main():
     bf16_peak, bf16_kind = measured_bf16_peak()
     prefill = {"tokens": n_pre, "ms": round(pre_t, 3), "tok_s": round(n_pre / (pre_t / 1000.0), 1),
                "path": ("batched: tcgen05 GEMMs (TMEM accumulators, TMA), batched split-KV attention"
-                        if world == 1 else "tensor parallel: per-token decode steps"),
+                        if world == 1 and a.weights == "bf16" else "per-token decode steps"),
                "tflops": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world, 1),
                "gemm_tflop": round(gemm_flop / 1e12, 3), "attention_tflop": round(attn_flop / 1e12, 3),
                "peak_tflops": bf16_peak, "frac": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world /
@@ -379,7 +384,7 @@ def main():
     # ---- dominant kernel roofline
     peak, peak_kind = measured_peaks()
     avg_pos = start_pos + (window - 1) / 2.0
-    bytes_tok = cfg.weight_bytes() + cfg.kv_bytes_per_position() * (avg_pos + 1)
+    bytes_tok = cfg.weight_bytes(a.weights) + cfg.kv_bytes_per_position() * (avg_pos + 1)
     mid = start_pos + window // 2
     # the kernel-per-op path, one eager step with CUDA events around each launch (diagnostic)
     eng.set_position(mid)
@@ -467,10 +472,10 @@ def main():
             "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
                        "decode_tokens_per_step": window, "global_batch": 1,
                        "decode_path": "persistent kernel" if eng.persistent else "CUDA graph of fused kernels",
-                       "parallelism": f"tp{world}",
+                       "parallelism": f"tp{world}", "weight_format": a.weights,
                        "tp_exchange": (None if world == 1 else "NCCL allreduce/allgather" if a.nccl else
                                        "peer-memory stores fused into the o/down/lm_head GEMVs (CUDA IPC, NVLink)"), "weights": "random N(0,0.02) seed 0, ids seed 1",
-                       "l2_flush": f"not needed: {cfg.weight_bytes() / 1e9:.1f} GB of weights streamed per token "
+                       "l2_flush": f"not needed: {cfg.weight_bytes(a.weights) / 1e9:.1f} GB of weights streamed per token "
                                    f">> 126 MB L2"},
             "clocks": clock, "e2e": e2e, "gpu_launches": int(launches),
             "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu, "prefill": prefill,

@@ -58,6 +58,19 @@ Q3_API int q3_embedding(const uint16_t* table_dev, size_t vocab, size_t hidden, 
 Q3_API int q3_gemv(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* y_dev, size_t n_out, size_t n_in,
                    void* stream);
 
+/* FP8 weights (no reference counterpart; the reference stores BF16 only,
+ * README.md:13).  q3_quantize_e4m3: for each of `rows` rows of w (BF16,
+ * row-major [rows, full_cols]) the scale 2^e with e the smallest integer such
+ * that max|row| <= 448 * 2^e goes to scale[r]; columns [c0, c0 + cols) of the
+ * row go to q[r, 0..cols) as E4M3(w / 2^e), rounded to nearest even and
+ * saturated at +-448.  cols, c0 even.
+ * q3_gemv_e4m3: y[n_out] = (W8[n_out, n_in] . x[n_in]) * scale, fp32
+ * accumulation, BF16 out; n_in % 16 == 0, 16-byte aligned x and W8. */
+Q3_API int q3_quantize_e4m3(const uint16_t* w_dev, size_t rows, size_t full_cols, size_t c0, size_t cols,
+                            uint8_t* q_dev, float* scale_dev, void* stream);
+Q3_API int q3_gemv_e4m3(const uint16_t* x_dev, const uint8_t* w8_dev, const float* scale_dev, uint16_t* y_dev,
+                        size_t n_out, size_t n_in, void* stream);
+
 /* Batched matmul for the prefill (no Backend counterpart: the reference
  * prefills by calling matmul once per prompt token, qwen3.hpp:168-173):
  * y[m, n] = x[m, k] . W[n, k]^T with W as stored (row-major [out, in]),
@@ -163,7 +176,16 @@ typedef struct q3_model_config {
     float theta;          /* rope_theta */
     uint32_t capacity;    /* KV-cache capacity (context size) */
     uint32_t eos;         /* eos_token_id (used only when stop_at_eos) */
+    /* Storage of the GEMV matrices (q, k, v, o, gate, up, down, lm_head):
+     * Q3_WEIGHTS_BF16 (0, the reference's format) or Q3_WEIGHTS_FP8_E4M3 (1:
+     * E4M3 bytes with one power-of-two scale per row, quantized on the device
+     * from the BF16 tensors that init_synthetic / set_weight provide; no
+     * reference counterpart).  Embedding and norm weights stay BF16. */
+    uint32_t weight_format;
 } q3_model_config;
+
+#define Q3_WEIGHTS_BF16 0
+#define Q3_WEIGHTS_FP8_E4M3 1
 
 typedef struct q3_engine q3_engine;
 

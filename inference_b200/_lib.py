@@ -24,6 +24,8 @@ SIGNATURES = {
     "q3_embedding": (C.c_int, [_u16p, _sz, _sz, C.c_uint32, _u16p, _vp]),
     "q3_gemv": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _vp]),
     "q3_gemm": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _sz, _vp]),
+    "q3_quantize_e4m3": (C.c_int, [_u16p, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
+    "q3_gemv_e4m3": (C.c_int, [_u16p, _vp, _vp, _u16p, _sz, _sz, _vp]),
     "q3_rmsnorm": (C.c_int, [_u16p, _u16p, _u16p, _sz, C.c_float, _vp]),
     "q3_rmsnorm_add": (C.c_int, [_u16p, _u16p, _u16p, _u16p, _sz, C.c_float, _vp]),
     "q3_rope": (C.c_int, [_u16p, _vp, _vp, _sz, _sz, _sz, _vp]),
@@ -106,4 +108,8 @@ class ModelConfig(C.Structure):
 
     _fields_ = [("hidden", C.c_uint32), ("inter", C.c_uint32), ("layers", C.c_uint32), ("q_heads", C.c_uint32),
                 ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("vocab", C.c_uint32), ("tied", C.c_uint32),
-                ("eps", C.c_float), ("theta", C.c_float), ("capacity", C.c_uint32), ("eos", C.c_uint32)]
+                ("eps", C.c_float), ("theta", C.c_float), ("capacity", C.c_uint32), ("eos", C.c_uint32),
+                ("weight_format", C.c_uint32)]
+
+
+WEIGHT_FORMATS = {"bf16": 0, "fp8": 1}  # Q3_WEIGHTS_BF16, Q3_WEIGHTS_FP8_E4M3

@@ -64,6 +64,17 @@ class B200Backend:
         n = weights.shape[0]
         check(lib().q3_gemm(_p(x), _p(weights), _p(output), m, n, k, self._stream()))
 
+    def quantize_e4m3(self, weights, q, scale, c0: int = 0, cols: int | None = None):
+        """Row-wise E4M3 with power-of-two scales (q3_quantize_e4m3): q[r, :] = E4M3(weights[r, c0:c0+cols] / scale[r])."""
+        rows, full = weights.shape
+        cols = full - c0 if cols is None else cols
+        check(lib().q3_quantize_e4m3(_p(weights), rows, full, c0, cols, _p(q), _p(scale), self._stream()))
+
+    def gemv_e4m3(self, x, q, scale, output):
+        """output[n] = (q[n, k] . x[k]) * scale[n] with E4M3 weights q (q3_gemv_e4m3)."""
+        n, k = q.shape
+        check(lib().q3_gemv_e4m3(_p(x), _p(q), _p(scale), _p(output), n, k, self._stream()))
+
     # backend.hpp:28
     def rmsnorm(self, input, weight, output, epsilon: float):
         check(lib().q3_rmsnorm(_p(input), _p(weight), _p(output), input.numel(), epsilon, self._stream()))

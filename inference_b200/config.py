@@ -24,11 +24,17 @@ class Qwen3Config:
         return replace(self, layers=layers, name=f"{self.name}-L{layers}")
 
     # bytes of weights read per decode step on one GPU (all layers + lm_head + norms)
-    def weight_bytes(self) -> int:
+    def weight_bytes(self, weights: str = "bf16") -> int:
+        """Bytes one decode step streams: every matrix, the norms, one embedding row.
+        weights="fp8": one byte per GEMV weight plus a 4-byte scale per matrix row."""
         H, I = self.hidden, self.inter
         qd, kd = self.q_heads * self.head_dim, self.kv_heads * self.head_dim
-        per_layer = (qd + 2 * kd) * H + H * qd + 2 * I * H + H * I + 2 * H + 2 * self.head_dim
-        return 2 * (per_layer * self.layers + self.vocab * H + H + H)
+        mats = self.layer_matmul_params()
+        vec = 2 * H + 2 * self.head_dim
+        if weights == "fp8":
+            rows = (qd + 2 * kd) + H + 2 * I + H
+            return (mats + 4 * rows + 2 * vec) * self.layers + self.vocab * (H + 4) + 2 * (H + H)
+        return 2 * ((mats + vec) * self.layers + self.vocab * H + H + H)
 
     def layer_matmul_params(self) -> int:
         """Weights of the QKV, O, gate/up and down matrices of one layer (GEMM FLOPs = 2 x tokens x this)."""

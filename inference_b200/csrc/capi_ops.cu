@@ -96,6 +96,37 @@ int q3_gemv(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t n_out, siz
     return launch_status(launch_gemv(PRO_PLAIN, EPI_STORE, a, as_stream(stream), false), "q3_gemv");
 }
 
+int q3_quantize_e4m3(const uint16_t* w, size_t rows, size_t full_cols, size_t c0, size_t cols, uint8_t* q,
+                     float* scale, void* stream) {
+    Q3_CHECK(w && q && scale, "q3_quantize_e4m3: null pointer");
+    Q3_CHECK(rows < (1u << 30) && full_cols < (1u << 30), "q3_quantize_e4m3: shape too large");
+    Q3_CHECK(c0 + cols <= full_cols && (c0 % 2) == 0 && (cols % 2) == 0, "q3_quantize_e4m3: bad column range");
+    Q3_CHECK(reinterpret_cast<uintptr_t>(q) % 2 == 0, "q3_quantize_e4m3: q must be 2-byte aligned");
+    if (rows == 0) return Q3_OK;
+    return launch_status(launch_quantize_e4m3(cb(w), full_cols, static_cast<int>(rows), static_cast<int>(full_cols),
+                                              static_cast<int>(c0), static_cast<int>(cols), q, cols, scale, 1,
+                                              as_stream(stream)),
+                         "q3_quantize_e4m3");
+}
+
+int q3_gemv_e4m3(const uint16_t* x, const uint8_t* w8, const float* scale, uint16_t* y, size_t n_out, size_t n_in,
+                 void* stream) {
+    Q3_CHECK(x && w8 && scale && y, "q3_gemv_e4m3: null pointer");
+    Q3_CHECK(n_out > 0 && n_in > 0, "q3_gemv_e4m3: empty shape");
+    Q3_CHECK(n_in % 16 == 0, "q3_gemv_e4m3: n_in must be a multiple of 16 (16-byte rows)");
+    Q3_CHECK(n_in <= 32768 && n_out < (1u << 30), "q3_gemv_e4m3: shape too large");
+    Q3_CHECK(aligned16(x) && aligned16(w8), "q3_gemv_e4m3: x and W8 must be 16-byte aligned");
+    GemvArgs a{};
+    a.W8 = w8;
+    a.wscale = scale;
+    a.N = static_cast<int>(n_out);
+    a.K = static_cast<int>(n_in);
+    a.plan = plan_gemv(a.N, a.K, EPI_STORE, current_sms(), 1);
+    a.x = cb(x);
+    a.y = mb(y);
+    return launch_status(launch_gemv(PRO_PLAIN, EPI_STORE, a, as_stream(stream), false), "q3_gemv_e4m3");
+}
+
 int q3_gemm(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t m, size_t n, size_t k, void* stream) {
     Q3_CHECK(x && w && y, "q3_gemm: null pointer");
     Q3_CHECK(m > 0 && n > 0 && k > 0, "q3_gemm: empty shape");

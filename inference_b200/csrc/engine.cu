@@ -20,6 +20,7 @@
 //     into the next GEMV's prologue; lm_head is vocab-sharded and the per-rank
 //     (value, index) keys are all-gathered and resolved in the next step.
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <string>
@@ -36,7 +37,10 @@ namespace {
 constexpr int kPageSize = 64;
 
 struct LayerW {
-    bf16 *w_qkv, *w_o, *w_gu, *w_down;
+    bf16 *w_qkv, *w_o, *w_gu, *w_down;  // BF16 engines
+    // FP8 engines: E4M3 matrices of the same shapes and one scale per row
+    uint8_t *f_qkv, *f_o, *f_gu, *f_down;
+    float *s_qkv, *s_o, *s_gu, *s_down;
     bf16 *in_norm, *post_norm, *q_norm, *k_norm;
     bf16 *k_pages, *v_pages;
 };
@@ -53,6 +57,9 @@ struct q3_engine {
     uint32_t voff = 0;
     // weights
     q3::bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
+    bool fp8 = false;  // Q3_WEIGHTS_FP8_E4M3: GEMV matrices as E4M3 + row scales
+    uint8_t* f_lm = nullptr;
+    float* s_lm = nullptr;
     std::vector<q3::LayerW> layers;
     int n_pages = 0;
     int32_t* page_table = nullptr;
@@ -151,16 +158,26 @@ GemvArgs base_args(q3_engine* e) {
     return a;
 }
 
-int gemv(Recorder& r, int pro, int epi, GemvArgs a, const bf16* W, int N, int K, int pos_for_bytes) {
-    (void)pos_for_bytes;
-    a.W = W;
+// One GEMV matrix in either storage format.
+struct WMat {
+    const bf16* w;
+    const uint8_t* q;  // FP8 E4M3 (q and s set) or null
+    const float* s;
+};
+
+int gemv(Recorder& r, int pro, int epi, GemvArgs a, WMat W, int N, int K) {
+    a.W = W.w;
+    a.W8 = W.q;
+    a.wscale = W.s;
     a.N = N;
     a.K = K;
-    a.plan = plan_gemv(N, K, epi, r.e->sms);
+    a.plan = plan_gemv(N, K, epi, r.e->sms, W.q ? 1 : 2);
     r.mark(true, 0);
     cudaError_t st = launch_gemv(pro, epi, a, r.e->stream, r.pdl);
     r.mark(false, 0);
-    if (r.bytes && (r.klass == 0 || r.klass == 2)) *r.bytes += static_cast<double>(N) * K * 2 + K * 2.0 + N * 2.0;
+    if (r.bytes && (r.klass == 0 || r.klass == 2))
+        *r.bytes += W.q ? static_cast<double>(N) * K + N * 4.0 + K * 2.0 + N * 2.0
+                        : static_cast<double>(N) * K * 2 + K * 2.0 + N * 2.0;
     if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("gemv launch: ") + cudaGetErrorString(st));
     return Q3_OK;
 }
@@ -203,6 +220,8 @@ int record_step(Recorder& r, size_t pos_now) {
     int cur = 0;  // residual buffer holding hs (tensor-parallel ping-pong)
     for (size_t l = 0; l < e->layers.size(); ++l) {
         const LayerW& L = e->layers[l];
+        const WMat w_qkv{L.w_qkv, L.f_qkv, L.s_qkv}, w_o{L.w_o, L.f_o, L.s_o};
+        const WMat w_gu{L.w_gu, L.f_gu, L.s_gu}, w_down{L.w_down, L.f_down, L.s_down};
         // ---- QKV (+ embedding / residual / RMSNorm prologue, qk-norm + RoPE + KV write epilogue)
         GemvArgs a = base_args(e);
         a.norm_w = L.in_norm;
@@ -244,7 +263,7 @@ int record_step(Recorder& r, size_t pos_now) {
             pro = PRO_NORM;
             a.hs = e->hs[0];
         }
-        Q3_TRY(gemv(r, pro, EPI_QKV, a, L.w_qkv, e->qd + 2 * e->kd, e->H, 0));
+        Q3_TRY(gemv(r, pro, EPI_QKV, a, w_qkv, e->qd + 2 * e->kd, e->H));
         // ---- attention
         Q3_TRY(attention(r, L, pos_now));
         // ---- o_proj (+ residual add)
@@ -253,12 +272,12 @@ int record_step(Recorder& r, size_t pos_now) {
         if (tp) {
             o.yf = e->partial;
             o.xtag = 2 * static_cast<int>(l) + 1;
-            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, o, L.w_o, e->H, e->qd, 0));
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, o, w_o, e->H, e->qd));
             Q3_TRY(allreduce(e, e->partial, e->H));
         } else {
             o.hs = e->hs[0];
             o.vsum_out = e->vsum;
-            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID_F32, o, L.w_o, e->H, e->qd, 0));
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID_F32, o, w_o, e->H, e->qd));
         }
         // ---- gate/up (+ RMSNorm prologue, SwiGLU epilogue)
         GemvArgs gu = base_args(e);
@@ -271,11 +290,11 @@ int record_step(Recorder& r, size_t pos_now) {
             gu.vsum = e->partial;
             gu.ss_unrounded = 1;  // rmsnorm_add (rmsnorm.cuh:58-60) squares the unrounded sums
             cur ^= 1;
-            Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_SWIGLU, gu, L.w_gu, 2 * e->il, e->H, 0));
+            Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_SWIGLU, gu, w_gu, 2 * e->il, e->H));
         } else {
             gu.hs = e->hs[0];
             gu.vsum = e->vsum;
-            Q3_TRY(gemv(r, PRO_NORM_F32, EPI_SWIGLU, gu, L.w_gu, 2 * e->il, e->H, 0));
+            Q3_TRY(gemv(r, PRO_NORM_F32, EPI_SWIGLU, gu, w_gu, 2 * e->il, e->H));
         }
         // ---- down_proj (+ residual add)
         GemvArgs d = base_args(e);
@@ -283,14 +302,15 @@ int record_step(Recorder& r, size_t pos_now) {
         if (tp) {
             d.yf = e->partial;
             d.xtag = 2 * static_cast<int>(l) + 2;
-            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, d, L.w_down, e->H, e->il, 0));
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, d, w_down, e->H, e->il));
             Q3_TRY(allreduce(e, e->partial, e->H));
         } else {
             d.hs = e->hs[0];
-            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID, d, L.w_down, e->H, e->il, 0));
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID, d, w_down, e->H, e->il));
         }
     }
     // ---- final RMSNorm + lm_head + argmax (vocab shard)
+    const WMat w_lm{e->lm_head, e->f_lm, e->s_lm};
     GemvArgs h = base_args(e);
     h.norm_w = e->final_norm;
     h.y = e->logits;
@@ -305,14 +325,14 @@ int record_step(Recorder& r, size_t pos_now) {
         h.hs_out = e->hs[cur ^ 1];
         h.vsum = e->partial;
         h.ss_unrounded = 0;
-        Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
+        Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_ARGMAX, h, w_lm, e->vl, e->H));
         if (!e->peer_mode) {
             ncclResult_t nr = nccl().AllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
             if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + nccl().GetErrorString(nr));
         }
     } else {
         h.hs = e->hs[0];
-        Q3_TRY(gemv(r, PRO_NORM, EPI_ARGMAX, h, e->lm_head, e->vl, e->H, 0));
+        Q3_TRY(gemv(r, PRO_NORM, EPI_ARGMAX, h, w_lm, e->vl, e->H));
     }
     return Q3_OK;
 }
@@ -396,9 +416,14 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     Q3_CHECK(c.vocab % tp_size == 0, "vocab must divide by the tensor-parallel size");
     Q3_CHECK(c.hidden % 8 == 0 && c.hidden <= 32768, "hidden must be a multiple of 8 (<= 32768)");
     Q3_CHECK(c.capacity < (1u << 24), "capacity too large");
+    Q3_CHECK(c.weight_format == Q3_WEIGHTS_BF16 || c.weight_format == Q3_WEIGHTS_FP8_E4M3,
+             "q3_engine_create: unknown weight_format");
+    Q3_CHECK(c.weight_format != Q3_WEIGHTS_FP8_E4M3 || (c.hidden % 16 == 0 && (c.inter / tp_size) % 16 == 0),
+             "FP8 weights need hidden and intermediate/tp multiples of 16");
 
     auto* e = new q3_engine();
     e->cfg = c;
+    e->fp8 = c.weight_format == Q3_WEIGHTS_FP8_E4M3;
     e->device = device;
     e->rank = tp_rank;
     e->world = tp_size;
@@ -425,7 +450,11 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- weights
     if ((rc = dalloc_t(e, &e->embed, static_cast<size_t>(c.vocab) * H)) != Q3_OK) return bail(rc);
-    if (c.tied) {
+    if (e->fp8) {
+        // the embedding stays BF16 for the lookup; lm_head gets its own E4M3 copy
+        if ((rc = dalloc_t(e, &e->f_lm, static_cast<size_t>(e->vl) * H)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_t(e, &e->s_lm, static_cast<size_t>(e->vl))) != Q3_OK) return bail(rc);
+    } else if (c.tied) {
         e->lm_head = e->embed + static_cast<size_t>(e->voff) * H;
     } else if ((rc = dalloc_t(e, &e->lm_head, static_cast<size_t>(e->vl) * H)) != Q3_OK) {
         return bail(rc);
@@ -434,11 +463,24 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     e->n_pages = static_cast<int>((c.capacity + kPageSize - 1) / kPageSize);
     const size_t page_elems = static_cast<size_t>(e->n_pages) * e->kvh * kPageSize * 128;
     e->layers.resize(c.layers);
+    const size_t rows_qkv = static_cast<size_t>(e->qd + 2 * e->kd), rows_gu = 2 * static_cast<size_t>(e->il);
     for (auto& L : e->layers) {
-        if ((rc = dalloc_t(e, &L.w_qkv, static_cast<size_t>(e->qd + 2 * e->kd) * H)) != Q3_OK) return bail(rc);
-        if ((rc = dalloc_t(e, &L.w_o, H * e->qd)) != Q3_OK) return bail(rc);
-        if ((rc = dalloc_t(e, &L.w_gu, 2 * static_cast<size_t>(e->il) * H)) != Q3_OK) return bail(rc);
-        if ((rc = dalloc_t(e, &L.w_down, H * e->il)) != Q3_OK) return bail(rc);
+        L = LayerW{};
+        if (e->fp8) {
+            if ((rc = dalloc_t(e, &L.f_qkv, rows_qkv * H)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.f_o, H * e->qd)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.f_gu, rows_gu * H)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.f_down, H * e->il)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.s_qkv, rows_qkv)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.s_o, H)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.s_gu, rows_gu)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.s_down, H)) != Q3_OK) return bail(rc);
+        } else {
+            if ((rc = dalloc_t(e, &L.w_qkv, rows_qkv * H)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.w_o, H * e->qd)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.w_gu, rows_gu * H)) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_t(e, &L.w_down, H * e->il)) != Q3_OK) return bail(rc);
+        }
         if ((rc = dalloc_t(e, &L.in_norm, H)) != Q3_OK) return bail(rc);
         if ((rc = dalloc_t(e, &L.post_norm, H)) != Q3_OK) return bail(rc);
         if ((rc = dalloc_t(e, &L.q_norm, 128)) != Q3_OK) return bail(rc);
@@ -450,9 +492,12 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
             return bail(fail(Q3_ERR_CUDA, "KV cache memset failed"));
     }
     // bytes streamed per decode step by this rank (weights read by the GEMVs + norms + one embedding row)
-    const size_t per_layer = (static_cast<size_t>(e->qd + 2 * e->kd) * H + H * e->qd + 2 * static_cast<size_t>(e->il) * H +
-                              H * e->il + 2 * H + 256) * 2;
-    e->weight_bytes = per_layer * c.layers + static_cast<size_t>(e->vl) * H * 2 + H * 2 + H * 2;
+    // (FP8: one byte per weight plus a 4-byte scale per row)
+    const size_t mat_elems = rows_qkv * H + H * e->qd + rows_gu * H + H * e->il;
+    const size_t mat_rows = rows_qkv + H + rows_gu + H;
+    const size_t per_layer = e->fp8 ? mat_elems + mat_rows * 4 + (2 * H + 256) * 2 : (mat_elems + 2 * H + 256) * 2;
+    const size_t lm_bytes = e->fp8 ? static_cast<size_t>(e->vl) * (H + 4) : static_cast<size_t>(e->vl) * H * 2;
+    e->weight_bytes = per_layer * c.layers + lm_bytes + H * 2 + H * 2;
 
     // ---- page table (identity for a single sequence) and RoPE tables
     std::vector<int32_t> pt(e->n_pages);
@@ -516,8 +561,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
 
-    // ---- persistent decode kernel (single GPU)
-    if (tp_size == 1) {
+    // ---- persistent decode kernel (single GPU, BF16 weights)
+    if (tp_size == 1 && !e->fp8) {
         PersistentArgs& a = e->pargs;
         a.H = e->H;
         a.qd = e->qd;
@@ -624,9 +669,96 @@ int q3_engine_destroy(q3_engine* e) {
     return Q3_OK;
 }
 
+namespace {
+
+// A temporary device buffer of BF16 weights (FP8 engines quantize from it).
+struct Staging {
+    bf16* p = nullptr;
+    ~Staging() {
+        if (p) cudaFree(p);
+    }
+    int alloc(size_t elems) {
+        if (cudaMalloc(&p, elems * 2) != cudaSuccess) {
+            p = nullptr;
+            return fail(Q3_ERR_OOM, "weight staging buffer: cudaMalloc failed");
+        }
+        return Q3_OK;
+    }
+};
+
+int quant(q3_engine* e, const bf16* src, size_t ld_src, size_t rows, size_t full_cols, size_t c0, size_t cols,
+          uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride) {
+    Q3_CUDA(launch_quantize_e4m3(src, ld_src, static_cast<int>(rows), static_cast<int>(full_cols), static_cast<int>(c0),
+                                 static_cast<int>(cols), dst, ld_dst, scale, scale_stride, e->stream));
+    return Q3_OK;
+}
+
+// FP8 engines: each GEMV matrix generated at full row width in BF16 (so a
+// row-parallel shard is scaled by its full row's maximum), then quantized.
+int init_synthetic_fp8(q3_engine* e, uint64_t seed) {
+    const q3_model_config& c = e->cfg;
+    const size_t H = e->H, qd = e->qd, kd = e->kd, il = e->il, vl = e->vl;
+    const size_t qfull = static_cast<size_t>(c.q_heads) * 128, inter = c.inter;
+    cudaStream_t s = e->stream;
+    Staging st;
+    size_t need = std::max({qd * H, H * qfull, il * H, H * inter});
+    if (!c.tied) need = std::max(need, vl * H);
+    Q3_TRY(st.alloc(need));
+    Q3_CUDA(launch_fill_normal(e->embed, seed, 1, c.vocab, H, 0, 0, H, H, s));
+    if (c.tied) {
+        Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, vl, H, 0, H, e->f_lm, H, e->s_lm, 1));
+    } else {
+        Q3_CUDA(launch_fill_normal(st.p, seed, 2, vl, H, e->voff, 0, H, H, s));
+        Q3_TRY(quant(e, st.p, H, vl, H, 0, H, e->f_lm, H, e->s_lm, 1));
+    }
+    Q3_CUDA(launch_fill_const(e->final_norm, H, 1.0f, s));
+    for (size_t l = 0; l < e->layers.size(); ++l) {
+        const LayerW& L = e->layers[l];
+        const uint64_t b = 16 + 16 * l;
+        const size_t qr0 = static_cast<size_t>(e->rank) * qd, kr0 = static_cast<size_t>(e->rank) * kd;
+        const size_t ir0 = static_cast<size_t>(e->rank) * il;
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 0, qd, H, qr0, 0, H, H, s));
+        Q3_TRY(quant(e, st.p, H, qd, H, 0, H, L.f_qkv, H, L.s_qkv, 1));
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 1, kd, H, kr0, 0, H, H, s));
+        Q3_TRY(quant(e, st.p, H, kd, H, 0, H, L.f_qkv + qd * H, H, L.s_qkv + qd, 1));
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 2, kd, H, kr0, 0, H, H, s));
+        Q3_TRY(quant(e, st.p, H, kd, H, 0, H, L.f_qkv + (qd + kd) * H, H, L.s_qkv + qd + kd, 1));
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 3, H, qfull, 0, 0, qfull, qfull, s));
+        Q3_TRY(quant(e, st.p, qfull, H, qfull, qr0, qd, L.f_o, qd, L.s_o, 1));
+        // gate row j -> stored row 2 j, up row j -> 2 j + 1 (the SwiGLU epilogue's pairs)
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 4, il, H, ir0, 0, H, H, s));
+        Q3_TRY(quant(e, st.p, H, il, H, 0, H, L.f_gu, 2 * H, L.s_gu, 2));
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 5, il, H, ir0, 0, H, H, s));
+        Q3_TRY(quant(e, st.p, H, il, H, 0, H, L.f_gu + H, 2 * H, L.s_gu + 1, 2));
+        Q3_CUDA(launch_fill_normal(st.p, seed, b + 6, H, inter, 0, 0, inter, inter, s));
+        Q3_TRY(quant(e, st.p, inter, H, inter, ir0, il, L.f_down, il, L.s_down, 1));
+        Q3_CUDA(launch_fill_const(L.in_norm, H, 1.0f, s));
+        Q3_CUDA(launch_fill_const(L.post_norm, H, 1.0f, s));
+        Q3_CUDA(launch_fill_const(L.q_norm, 128, 1.0f, s));
+        Q3_CUDA(launch_fill_const(L.k_norm, 128, 1.0f, s));
+    }
+    Q3_CUDA(cudaStreamSynchronize(s));
+    return Q3_OK;
+}
+
+// FP8 engines: `rows` full host rows (full_cols wide) to the device, then
+// columns [c0, c0 + cols) of each quantized into dst.
+int set_matrix_fp8(q3_engine* e, const uint16_t* host, size_t rows, size_t full_cols, size_t c0, size_t cols,
+                   uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride) {
+    Staging st;
+    Q3_TRY(st.alloc(rows * full_cols));
+    Q3_CUDA(cudaMemcpy(st.p, host, rows * full_cols * 2, cudaMemcpyHostToDevice));
+    Q3_TRY(quant(e, st.p, full_cols, rows, full_cols, c0, cols, dst, ld_dst, scale, scale_stride));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    return Q3_OK;
+}
+
+}  // namespace
+
 int q3_engine_init_synthetic(q3_engine* e, uint64_t seed) {
     Q3_CHECK(e, "null engine");
     Q3_CUDA(cudaSetDevice(e->device));
+    if (e->fp8) return init_synthetic_fp8(e, seed);
     const q3_model_config& c = e->cfg;
     const size_t H = e->H;
     cudaStream_t s = e->stream;
@@ -673,11 +805,18 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
     };
     if (n == "model.embed_tokens.weight") {
         Q3_CHECK(expect(c.vocab, H), "embed_tokens shape");
-        return copy2d(e->embed, H, host, H, H, c.vocab);
+        Q3_TRY(copy2d(e->embed, H, host, H, H, c.vocab));
+        if (e->fp8 && c.tied) {
+            Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, e->vl, H, 0, H, e->f_lm, H, e->s_lm, 1));
+            Q3_CUDA(cudaStreamSynchronize(e->stream));
+        }
+        return Q3_OK;
     }
     if (n == "lm_head.weight") {
         Q3_CHECK(expect(c.vocab, H), "lm_head shape");
         if (c.tied) return fail(Q3_ERR_INVALID, "lm_head.weight given for a tied-embedding model");
+        if (e->fp8)
+            return set_matrix_fp8(e, host + static_cast<size_t>(e->voff) * H, e->vl, H, 0, H, e->f_lm, H, e->s_lm, 1);
         return copy2d(e->lm_head, H, host + static_cast<size_t>(e->voff) * H, H, H, e->vl);
     }
     if (n == "model.norm.weight") {
@@ -695,30 +834,38 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
     const size_t qfull = static_cast<size_t>(c.q_heads) * 128, kfull = static_cast<size_t>(c.kv_heads) * 128;
     const size_t qr0 = static_cast<size_t>(e->rank) * e->qd, kr0 = static_cast<size_t>(e->rank) * e->kd;
     const size_t ir0 = static_cast<size_t>(e->rank) * e->il;
+    const size_t qd = e->qd, kd = e->kd, il = e->il;
     if (leaf == "self_attn.q_proj.weight") {
         Q3_CHECK(expect(qfull, H), "q_proj shape");
-        return copy2d(L.w_qkv, H, host + qr0 * H, H, H, e->qd);
+        if (e->fp8) return set_matrix_fp8(e, host + qr0 * H, qd, H, 0, H, L.f_qkv, H, L.s_qkv, 1);
+        return copy2d(L.w_qkv, H, host + qr0 * H, H, H, qd);
     }
     if (leaf == "self_attn.k_proj.weight") {
         Q3_CHECK(expect(kfull, H), "k_proj shape");
-        return copy2d(L.w_qkv + e->qd * H, H, host + kr0 * H, H, H, e->kd);
+        if (e->fp8) return set_matrix_fp8(e, host + kr0 * H, kd, H, 0, H, L.f_qkv + qd * H, H, L.s_qkv + qd, 1);
+        return copy2d(L.w_qkv + qd * H, H, host + kr0 * H, H, H, kd);
     }
     if (leaf == "self_attn.v_proj.weight") {
         Q3_CHECK(expect(kfull, H), "v_proj shape");
-        return copy2d(L.w_qkv + (e->qd + e->kd) * H, H, host + kr0 * H, H, H, e->kd);
+        if (e->fp8)
+            return set_matrix_fp8(e, host + kr0 * H, kd, H, 0, H, L.f_qkv + (qd + kd) * H, H, L.s_qkv + qd + kd, 1);
+        return copy2d(L.w_qkv + (qd + kd) * H, H, host + kr0 * H, H, H, kd);
     }
     if (leaf == "self_attn.o_proj.weight") {
         Q3_CHECK(expect(H, qfull), "o_proj shape");
-        return copy2d(L.w_o, e->qd, host + qr0, qfull, e->qd, H);
+        if (e->fp8) return set_matrix_fp8(e, host, H, qfull, qr0, qd, L.f_o, qd, L.s_o, 1);
+        return copy2d(L.w_o, qd, host + qr0, qfull, qd, H);
     }
     if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight") {
         Q3_CHECK(expect(c.inter, H), "gate/up shape");
-        bf16* dst = L.w_gu + (leaf == "mlp.up_proj.weight" ? H : 0);
-        return copy2d(dst, 2 * H, host + ir0 * H, H, H, e->il);
+        const size_t up = leaf == "mlp.up_proj.weight" ? 1 : 0;
+        if (e->fp8) return set_matrix_fp8(e, host + ir0 * H, il, H, 0, H, L.f_gu + up * H, 2 * H, L.s_gu + up, 2);
+        return copy2d(L.w_gu + up * H, 2 * H, host + ir0 * H, H, H, il);
     }
     if (leaf == "mlp.down_proj.weight") {
         Q3_CHECK(expect(H, c.inter), "down_proj shape");
-        return copy2d(L.w_down, e->il, host + ir0, c.inter, e->il, H);
+        if (e->fp8) return set_matrix_fp8(e, host, H, c.inter, ir0, il, L.f_down, il, L.s_down, 1);
+        return copy2d(L.w_down, il, host + ir0, c.inter, il, H);
     }
     auto vec = [&](bf16* dst, size_t len) -> int {
         Q3_CHECK(rows * cols == len, "norm weight shape: " + n);
@@ -795,8 +942,8 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
     Q3_CHECK(p0 + n <= e->host_forced, "q3_engine_prefill: tokens not set (set_tokens first)");
     if (p0 + n >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "q3_engine_prefill: KV cache capacity exceeded");
     Q3_CUDA(cudaSetDevice(e->device));
-    if (e->world > 1) {
-        // tensor-parallel engines prefill through the per-token decode step
+    if (e->world > 1 || e->fp8) {
+        // tensor-parallel and FP8-weight engines prefill through the per-token decode step
         return q3_engine_step(e, n);
     }
     const int H = e->H, qd = e->qd, kd = e->kd, il = e->il;

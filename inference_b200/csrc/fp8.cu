@@ -1,0 +1,59 @@
+// fp8.cu -- FP8 E4M3 weight storage: row-wise quantization with power-of-two
+// scales.  The reference stores BF16 weights only (README.md:13); this is the
+// build's optional weight format, halving the bytes the decode GEMVs stream.
+// A power-of-two scale keeps every dequantized weight q * 2^e an exact BF16
+// value (at most four significant bits), so an FP8 engine computes exactly the
+// BF16 model whose weights are those round trips, and the GEMV applies the
+// scale to the fp32 row sum (an exact power-of-two multiply).
+#include "kernels.cuh"
+
+namespace q3 {
+
+namespace {
+
+constexpr int kQThreads = 256;
+
+__global__ void __launch_bounds__(kQThreads) quantize_e4m3_kernel(const bf16* __restrict__ src, size_t ld_src,
+                                                                 int full_cols, int c0, int cols,
+                                                                 uint8_t* __restrict__ dst, size_t ld_dst,
+                                                                 float* __restrict__ scale, size_t scale_stride) {
+    __shared__ float red[kQThreads / 32];
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const bf16* s = src + static_cast<size_t>(row) * ld_src;
+    float mx = 0.f;
+    for (int c = tid; c < full_cols; c += kQThreads) mx = fmaxf(mx, fabsf(bf2f(s[c])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = 0.f;
+    for (int i = 0; i < kQThreads / 32; ++i) mx = fmaxf(mx, red[i]);
+    // mx = f * 2^k, f in [0.5, 1); 448 = 0.875 * 2^9
+    int e = 0;
+    if (mx > 0.f) {
+        int k;
+        const float f = frexpf(mx, &k);
+        e = (f <= 0.875f) ? k - 9 : k - 8;
+    }
+    if (tid == 0) scale[static_cast<size_t>(row) * scale_stride] = ldexpf(1.0f, e);
+    uint8_t* d = dst + static_cast<size_t>(row) * ld_dst;
+    const bf16* sc = s + c0;
+    for (int c = 2 * tid; c < cols; c += 2 * kQThreads) {
+        const float2 v = make_float2(ldexpf(bf2f(sc[c]), -e), ldexpf(bf2f(sc[c + 1]), -e));
+        const __nv_fp8x2_storage_t q = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
+        *reinterpret_cast<uint16_t*>(d + c) = static_cast<uint16_t>(q);
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_quantize_e4m3(const bf16* src, size_t ld_src, int rows, int full_cols, int c0, int cols,
+                                 uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if ((cols & 1) || (c0 & 1) || (ld_dst & 1) || c0 + cols > full_cols) return cudaErrorInvalidValue;
+    quantize_e4m3_kernel<<<rows, kQThreads, 0, s>>>(src, ld_src, full_cols, c0, cols, dst, ld_dst, scale,
+                                                    scale_stride);
+    return cudaGetLastError();
+}
+
+}  // namespace q3

@@ -42,7 +42,7 @@ namespace {
 #endif
 constexpr int kWarps = Q3_GEMV_WARPS;
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunk = Q3_GEMV_CHUNK;   // columns per item: 4 KB of BF16 weights
+constexpr int kChunk = Q3_GEMV_CHUNK;   // BF16 columns per item (4 KB); FP8 items take twice the columns
 constexpr int kMaxItems = 4096;         // (row, chunk) partial sums per CTA
 // One CTA per SM with a ~192 KB ring: loaded HBM latency needs well over
 // 100 KB in flight per SM to sustain its share of the bandwidth (measured:
@@ -57,7 +57,7 @@ struct SmemLayout {
 __host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K, int max_rows) {
     SmemLayout L;
     L.stage_off = 0;
-    L.x_off = static_cast<size_t>(kWarps) * p.stages * p.kc * 2;
+    L.x_off = static_cast<size_t>(kWarps) * p.stages * p.kc * p.wb;
     L.part_off = L.x_off + (static_cast<size_t>(K) * 2 + 15) / 16 * 16;
     L.bar_off = L.part_off + (static_cast<size_t>(max_rows) * p.nch * 4 + 15) / 16 * 16;
     L.misc_off = L.bar_off + static_cast<size_t>(kWarps) * p.stages * 8;
@@ -125,8 +125,11 @@ __device__ __forceinline__ void peer_wait(const PeerLinks& x, unsigned long long
     __syncthreads();
 }
 
-template <int PRO, int EPI>
+// F8: weights are E4M3 bytes (a.W8) with a scale per row (a.wscale); the ring
+// slots hold the same 4 KB, twice the columns.
+template <int PRO, int EPI, bool F8>
 __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    constexpr int WB = F8 ? 1 : 2;  // bytes per weight
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& p = a.plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off) + warp * p.stages;
     float* misc = reinterpret_cast<float*>(smem + L.misc_off);
     unsigned long long* cta_key = reinterpret_cast<unsigned long long*>(misc + 16);
-    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * p.kc * 2;
+    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * p.kc * WB;
 
     const int n_items = nrows * p.nch;
     const int i0 = static_cast<int>(static_cast<long long>(warp) * n_items / kWarps);
@@ -161,9 +164,10 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     auto issue = [&](int item, int slot) {
         const int row = r0 + item / p.nch, c = item % p.nch;
         const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
-        const uint32_t bytes = static_cast<uint32_t>(cols) * 2;
+        const uint32_t bytes = static_cast<uint32_t>(cols) * WB;
+        const uint8_t* wsrc = F8 ? a.W8 : reinterpret_cast<const uint8_t*>(a.W);
         mbar_arrive_expect_tx(&bars[slot], bytes);
-        bulk_g2s(ring + static_cast<size_t>(slot) * p.kc * 2, a.W + static_cast<size_t>(row) * a.K + c * p.kc,
+        bulk_g2s(ring + static_cast<size_t>(slot) * p.kc * WB, wsrc + (static_cast<size_t>(row) * a.K + c * p.kc) * WB,
                  bytes, &bars[slot], pol);
     };
     // Weights never depend on earlier kernels: start streaming before the wait.
@@ -323,15 +327,23 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         const int rl = item / p.nch, c = item % p.nch;
         if (ok) {
             const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
-            const int nv = cols / 8;
-            const uint4* wv = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(slot) * p.kc * 2);
+            const int nv = cols * WB / 16;  // 16-byte weight vectors
+            const uint4* wv = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(slot) * p.kc * WB);
             const uint4* xv = reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c) * p.kc);
             int v = lane;
-            for (; v + 32 < nv; v += 64) {
-                acc0 = dot8(wv[v], xv[v], acc0);
-                acc1 = dot8(wv[v + 32], xv[v + 32], acc1);
+            if constexpr (F8) {
+                for (; v + 32 < nv; v += 64) {
+                    acc0 = dot16_e4m3(wv[v], xv[2 * v], xv[2 * v + 1], acc0);
+                    acc1 = dot16_e4m3(wv[v + 32], xv[2 * v + 64], xv[2 * v + 65], acc1);
+                }
+                if (v < nv) acc0 = dot16_e4m3(wv[v], xv[2 * v], xv[2 * v + 1], acc0);
+            } else {
+                for (; v + 32 < nv; v += 64) {
+                    acc0 = dot8(wv[v], xv[v], acc0);
+                    acc1 = dot8(wv[v + 32], xv[v + 32], acc1);
+                }
+                if (v < nv) acc0 = dot8(wv[v], xv[v], acc0);
             }
-            if (v < nv) acc0 = dot8(wv[v], xv[v], acc0);
         }
         // flush at the end of this warp's part of a row
         if (c == p.nch - 1 || j == cnt - 1) {
@@ -347,10 +359,11 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     }
     __syncthreads();
 
-    // ---- epilogue: row sums in fixed chunk order
+    // ---- epilogue: row sums in fixed chunk order (FP8: times the row's power-of-two scale)
     auto row_sum = [&](int rl) {
         float r = 0.f;
         for (int c = 0; c < p.nch; ++c) r += part[rl * p.nch + c];
+        if constexpr (F8) r *= a.wscale[r0 + rl];
         return r;
     };
     uint64_t best_key = 0;
@@ -494,7 +507,7 @@ __global__ void peer_keys_kernel(const PeerLinks x, unsigned long long* out, uin
 
 template <int PRO, int EPI>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
-    auto* fn = gemv_kernel<PRO, EPI>;
+    auto* fn = a.W8 ? gemv_kernel<PRO, EPI, true> : gemv_kernel<PRO, EPI, false>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.plan.grid);
     cfg.blockDim = dim3(kThreads);
@@ -515,32 +528,42 @@ cudaError_t launch_peer_keys(const PeerLinks& x, unsigned long long* out, uint32
     return cudaGetLastError();
 }
 
-cudaError_t configure_gemv_kernels() {
-    const void* fns[] = {
-        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_STORE>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_RESID>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_RESID_F32>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_PLAIN, EPI_PARTIAL>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM, EPI_STORE>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM, EPI_QKV>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_EMBED_NORM, EPI_QKV>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_RESID_NORM, EPI_QKV>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM_F32, EPI_SWIGLU>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_RESID_NORM, EPI_SWIGLU>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_NORM, EPI_ARGMAX>),
-        reinterpret_cast<const void*>(gemv_kernel<PRO_RESID_NORM, EPI_ARGMAX>),
-    };
-    for (const void* f : fns) {
+template <int PRO, int EPI>
+cudaError_t configure_pair() {
+    for (const void* f : {reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, false>),
+                          reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, true>)}) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
 }
 
-GemvPlan plan_gemv(int N, int K, int epi, int sms) {
+cudaError_t configure_gemv_kernels() {
+    cudaError_t e = cudaSuccess;
+#define Q3_CFG(P, E) \
+    if (e == cudaSuccess) e = configure_pair<P, E>();
+    Q3_CFG(PRO_PLAIN, EPI_STORE)
+    Q3_CFG(PRO_PLAIN, EPI_RESID)
+    Q3_CFG(PRO_PLAIN, EPI_RESID_F32)
+    Q3_CFG(PRO_PLAIN, EPI_PARTIAL)
+    Q3_CFG(PRO_NORM, EPI_STORE)
+    Q3_CFG(PRO_NORM, EPI_QKV)
+    Q3_CFG(PRO_EMBED_NORM, EPI_QKV)
+    Q3_CFG(PRO_RESID_NORM, EPI_QKV)
+    Q3_CFG(PRO_NORM_F32, EPI_SWIGLU)
+    Q3_CFG(PRO_RESID_NORM, EPI_SWIGLU)
+    Q3_CFG(PRO_NORM, EPI_ARGMAX)
+    Q3_CFG(PRO_RESID_NORM, EPI_ARGMAX)
+#undef Q3_CFG
+    return e;
+}
+
+GemvPlan plan_gemv(int N, int K, int epi, int sms, int wb) {
     GemvPlan p{};
     p.row_gran = (epi == EPI_SWIGLU) ? 2 : 1;
-    p.kc = K < kChunk ? K : kChunk;
+    p.wb = wb;
+    const int chunk = kChunk * 2 / wb;  // 4 KB of weights per item
+    p.kc = K < chunk ? K : chunk;
     p.nch = (K + p.kc - 1) / p.kc;
     const int units = N / p.row_gran;
     // one CTA per SM, more only if the per-CTA partial sums would not fit
@@ -557,6 +580,8 @@ GemvPlan plan_gemv(int N, int K, int epi, int sms) {
 }
 
 cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl) {
+    // the plan's item width must match the weight format; FP8 rows are whole 16-byte vectors
+    if (a.plan.wb != (a.W8 ? 1 : 2) || (a.W8 && (a.K % 16 != 0 || !a.wscale))) return cudaErrorInvalidValue;
 #define Q3_CASE(P, E) \
     if (pro == P && epi == E) return launch_t<P, E>(a, s, pdl);
     Q3_CASE(PRO_PLAIN, EPI_STORE)

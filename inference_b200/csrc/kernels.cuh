@@ -34,6 +34,7 @@ struct GemvPlan {
     int stages;    // per-warp shared-memory ring depth
     int grid;      // CTAs
     int row_gran;  // rows assigned to CTAs in units of this many (2 for SWIGLU)
+    int wb;        // bytes per weight: 2 = BF16, 1 = FP8 E4M3
     size_t smem;   // dynamic shared memory bytes
 };
 
@@ -55,6 +56,10 @@ struct PeerLinks {
 
 struct GemvArgs {
     const bf16* W;
+    // FP8 weights (used when W8 is set): E4M3 bytes, row-major [N, K], and a
+    // power-of-two scale per row; row r of the matrix is W8[r, :] * wscale[r]
+    const uint8_t* W8;
+    const float* wscale;
     int N, K;
     GemvPlan plan;
     // ---- prologue
@@ -105,7 +110,7 @@ struct GemvArgs {
     uint32_t* err;
 };
 
-GemvPlan plan_gemv(int N, int K, int epi, int num_sms);
+GemvPlan plan_gemv(int N, int K, int epi, int num_sms, int wb = 2);
 cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------- attention
@@ -241,6 +246,15 @@ uint64_t seed_key(uint64_t seed);
 // called once per device before any launch (and before graph capture).
 cudaError_t configure_kernels();
 cudaError_t configure_gemv_kernels();
+
+// ---------------------------------------------------------------- FP8 weights
+// Row-wise E4M3 quantization with power-of-two scales: for each of `rows`
+// rows of src (BF16, row pitch ld_src elements, full_cols columns) the scale
+// is 2^e, e the smallest integer with max|row| <= 448 * 2^e; columns
+// [c0, c0 + cols) are written as E4M3(x / 2^e) (round to nearest even,
+// saturating) to dst (row pitch ld_dst bytes) and 2^e to scale[r * scale_stride].
+cudaError_t launch_quantize_e4m3(const bf16* src, size_t ld_src, int rows, int full_cols, int c0, int cols,
+                                 uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride, cudaStream_t s);
 cudaError_t configure_attention_kernels();
 int num_sms(int device);
 

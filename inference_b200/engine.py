@@ -13,7 +13,7 @@ import os
 
 import numpy as np
 
-from ._lib import ModelConfig, check, lib
+from ._lib import WEIGHT_FORMATS, ModelConfig, check, lib
 from .config import Qwen3Config
 
 TRACE_WORDS = 10  # Q3_TRACE_WORDS in include/q3_sm100a.h
@@ -25,10 +25,16 @@ def _ptr(a: np.ndarray) -> int:
 
 
 class Engine:
-    def __init__(self, cfg: Qwen3Config, capacity: int, device: int = 0, tp_rank: int = 0, tp_size: int = 1):
+    def __init__(self, cfg: Qwen3Config, capacity: int, device: int = 0, tp_rank: int = 0, tp_size: int = 1,
+                 weights: str = "bf16"):
+        """weights: "bf16" (the reference's format) or "fp8" (E4M3 GEMV matrices with a
+        power-of-two scale per row, quantized on the device from the BF16 tensors)."""
+        if weights not in WEIGHT_FORMATS:
+            raise ValueError(f"weights must be one of {sorted(WEIGHT_FORMATS)}")
         self.cfg, self.capacity, self.tp_rank, self.tp_size = cfg, capacity, tp_rank, tp_size
+        self.weights = weights
         mc = ModelConfig(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, cfg.head_dim, cfg.vocab,
-                         int(cfg.tied), cfg.eps, cfg.theta, capacity, cfg.eos)
+                         int(cfg.tied), cfg.eps, cfg.theta, capacity, cfg.eos, WEIGHT_FORMATS[weights])
         h = C.c_void_p()
         check(lib().q3_engine_create(C.byref(mc), device, tp_rank, tp_size, C.byref(h)))
         self.h = h

@@ -2,12 +2,16 @@
 
     python -m inference_b200.probe            # GEMV then prefill GEMM
     python -m inference_b200.probe attention  # decode attention
+    python -m inference_b200.probe gemv8      # FP8-weight GEMV
 
 Default: three launches of the decode GEMV (q3_gemv, Qwen3-8B gate/up shape:
 24576 x 4096, 201 MB of weights) followed by three launches of the prefill
 GEMM (q3_gemm, 512 tokens x 4096 -> 24576) on cuda:0, random BF16 operands.
 `attention`: three launches of the paged decode attention (q3_attention_paged)
 for Qwen3-8B heads (32 q / 8 kv) at position 4095 with a 16-split cluster.
+`gemv8`: the same gate/up shape with E4M3 weights (q3_quantize_e4m3 once,
+then three q3_gemv_e4m3 launches), then the BF16 GEMV again; prints each
+launch's CUDA-event time and GB/s (not meaningful under a profiler).
 """
 import torch
 
@@ -29,6 +33,30 @@ def attention():
     print("ok")
 
 
+def gemv8():
+    be = B200Backend(0)
+    n, k = 24576, 4096
+    x = torch.randn(k, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
+    q = torch.empty(n, k, device="cuda", dtype=torch.uint8)
+    sc = torch.empty(n, device="cuda", dtype=torch.float32)
+    y = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    be.quantize_e4m3(w, q, sc)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for name, fn, nbytes in (("fp8", lambda: be.gemv_e4m3(x, q, sc, y), n * k + 4 * n),
+                             ("bf16", lambda: be.matmul(x, w, y), 2 * n * k)):
+        for _ in range(3):
+            flush.fill_(1)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b)
+            print(f"{name} {ms * 1000:.1f} us {nbytes / ms / 1e6:.0f} GB/s")
+    print("ok")
+
+
 def main():
     be = B200Backend(0)
     x = torch.randn(4096, device="cuda").to(torch.bfloat16)
@@ -47,4 +75,4 @@ def main():
 if __name__ == "__main__":
     import sys
 
-    attention() if sys.argv[1:] == ["attention"] else main()
+    {"attention": attention, "gemv8": gemv8}.get(sys.argv[1] if sys.argv[1:] else "", main)()

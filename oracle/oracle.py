@@ -10,6 +10,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 _u16p = np.ctypeslib.ndpointer(dtype=np.uint16, flags="C_CONTIGUOUS")
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(dtype=np.uint8, flags="C_CONTIGUOUS")
 _u32p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
 _sz = C.c_size_t
 
@@ -79,6 +80,12 @@ class Oracle:
         L.q3o_model_kv_slot.argtypes = [C.c_void_p, _sz, _sz, _u16p, _u16p]
         L.q3o_model_weight.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.q3o_model_weight.restype = C.POINTER(C.c_uint16)
+        L.q3o_e4m3.argtypes = [C.c_float]
+        L.q3o_e4m3.restype = C.c_uint8
+        L.q3o_e4m3_value.argtypes = [C.c_uint8]
+        L.q3o_e4m3_value.restype = C.c_float
+        L.q3o_quantize_e4m3.argtypes = [_u16p, _sz, _sz, _u8p, _f32p]
+        L.q3o_model_quantize_fp8.argtypes = [C.c_void_p]
 
     # -- synthetic inputs
     def normal(self, seed, tensor_id, rows, cols, row0=0, col0=0, full_cols=None):
@@ -149,6 +156,21 @@ class Oracle:
     def argmax(self, logits):
         return int(self.lib.q3o_argmax(np.ascontiguousarray(logits), logits.size))
 
+    # -- FP8 E4M3 weights (row-wise power-of-two scales)
+    def e4m3(self, x: float) -> int:
+        return int(self.lib.q3o_e4m3(x))
+
+    def e4m3_value(self, q: int) -> float:
+        return float(self.lib.q3o_e4m3_value(q))
+
+    def quantize_e4m3(self, w):
+        """w [rows, cols] BF16 bits -> (q [rows, cols] uint8, scale [rows] float32)."""
+        w = np.ascontiguousarray(w, np.uint16)
+        q = np.empty(w.shape, np.uint8)
+        sc = np.empty(w.shape[0], np.float32)
+        self.lib.q3o_quantize_e4m3(w, w.shape[0], w.shape[1], q, sc)
+        return q, sc
+
     # -- model
     def model(self, cfg: ModelConfig, seed: int = 0) -> "OracleModel":
         return OracleModel(self, cfg, seed)
@@ -168,6 +190,11 @@ class OracleModel:
 
     def forward(self, token: int) -> int:
         return int(self.o.lib.q3o_model_forward(self.h, token))
+
+    def quantize_fp8(self) -> "OracleModel":
+        """Replace every GEMV matrix by its E4M3 round trip (the FP8-weight engine's model)."""
+        self.o.lib.q3o_model_quantize_fp8(self.h)
+        return self
 
     def logits(self) -> np.ndarray:
         p = self.o.lib.q3o_model_logits(self.h)

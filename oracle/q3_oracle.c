@@ -262,6 +262,70 @@ Q3O_API uint32_t q3o_argmax(const uint16_t* logits, size_t n) {
     return (uint32_t)best;
 }
 
+/* ---------------------------------------------------------------- FP8 weights
+ * (the build's optional weight format; no reference counterpart: the
+ * reference runs BF16 weights only, README.md:13).  OCP FP8 E4M3: 1 sign,
+ * 4 exponent bits (bias 7), 3 mantissa bits, subnormals down to 2^-9, no
+ * infinities, largest finite 448.  Encoding rounds to nearest, ties to even,
+ * and saturates to +-448 (the PTX cvt.rn.satfinite.e4m3x2.f32 semantics).
+ * Each weight row r gets a power-of-two scale 2^e_r, e_r the smallest integer
+ * with max|w_r| <= 448 * 2^e_r, so every dequantized weight q * 2^e_r has at
+ * most four significant bits and is exactly a BF16 value. */
+Q3O_API uint8_t q3o_e4m3(float x) {
+    const uint8_t s = signbit(x) ? 0x80 : 0x00;
+    if (isnan(x)) return (uint8_t)(s | 0x7F);
+    const float a = fabsf(x);
+    if (a > 448.0f) return (uint8_t)(s | 0x7E);
+    if (a < 0.015625f) {                             /* below 2^-6: subnormal steps of 2^-9 */
+        const int q = (int)nearbyintf(ldexpf(a, 9));  /* 0..8; 8 is the smallest normal, code 0x08 */
+        return (uint8_t)(s | q);
+    }
+    int e2;
+    frexpf(a, &e2);
+    int E = e2 - 1;                                  /* a = 1.f * 2^E, E >= -6 */
+    int m = (int)nearbyintf((ldexpf(a, -E) - 1.0f) * 8.0f);
+    if (m == 8) {
+        m = 0;
+        ++E;
+    }
+    return (uint8_t)(s | ((E + 7) << 3) | m);
+}
+
+Q3O_API float q3o_e4m3_value(uint8_t q) {
+    const int E = (q >> 3) & 0xF, m = q & 7;
+    float v = E ? ldexpf(1.0f + m / 8.0f, E - 7) : ldexpf((float)m, -9);
+    if ((q & 0x7F) == 0x7F) v = NAN;
+    return (q & 0x80) ? -v : v;
+}
+
+/* Row-wise E4M3 with power-of-two scales: q[rows, cols], scale[rows]. */
+Q3O_API void q3o_quantize_e4m3(const uint16_t* w, size_t rows, size_t cols, uint8_t* q, float* scale) {
+    for (size_t r = 0; r < rows; ++r) {
+        const uint16_t* wr = w + r * cols;
+        float mx = 0.0f;
+        for (size_t c = 0; c < cols; ++c) mx = fmaxf(mx, fabsf(bf2f(wr[c])));
+        int e = 0;
+        if (mx > 0.0f) {
+            int k;
+            const float f = frexpf(mx, &k);          /* mx = f * 2^k, 448 = 0.875 * 2^9 */
+            e = (f <= 0.875f) ? k - 9 : k - 8;
+        }
+        scale[r] = ldexpf(1.0f, e);
+        for (size_t c = 0; c < cols; ++c) q[r * cols + c] = q3o_e4m3(ldexpf(bf2f(wr[c]), -e));
+    }
+}
+
+/* In place: w <- bf16(dequant(quant(w))) (exact, see above). */
+static void fp8_roundtrip(uint16_t* w, size_t rows, size_t cols) {
+    uint8_t* q = (uint8_t*)malloc(cols);
+    float sc;
+    for (size_t r = 0; r < rows; ++r) {
+        q3o_quantize_e4m3(w + r * cols, 1, cols, q, &sc);
+        for (size_t c = 0; c < cols; ++c) w[r * cols + c] = f2bf(q3o_e4m3_value(q[c]) * sc);
+    }
+    free(q);
+}
+
 /* ---------------------------------------------------------------- model */
 
 typedef struct {
@@ -342,6 +406,30 @@ Q3O_API q3o_model* q3o_model_create(const q3o_config* cfg, uint64_t seed) {
     m->up_buf = (uint16_t*)calloc(I, 2);
     m->logits = (uint16_t*)calloc(cfg->vocab, 2);
     return m;
+}
+
+/* The model an FP8-weight engine computes: every GEMV matrix (q, k, v, o,
+ * gate, up, down, lm_head) replaced by its E4M3 round trip; the embedding
+ * lookup keeps the BF16 table (a tied model gets its own lm_head copy). */
+Q3O_API void q3o_model_quantize_fp8(q3o_model* m) {
+    const q3o_config* c = &m->cfg;
+    size_t H = c->hidden, I = c->inter, hd = c->head_dim;
+    size_t qd = c->q_heads * hd, kd = c->kv_heads * hd;
+    if (m->lm_head == m->embed) {
+        m->lm_head = (uint16_t*)malloc(c->vocab * H * 2);
+        memcpy(m->lm_head, m->embed, c->vocab * H * 2);
+    }
+    fp8_roundtrip(m->lm_head, c->vocab, H);
+    for (size_t l = 0; l < c->layers; ++l) {
+        q3o_layer* L = &m->layer[l];
+        fp8_roundtrip(L->q_proj, qd, H);
+        fp8_roundtrip(L->k_proj, kd, H);
+        fp8_roundtrip(L->v_proj, kd, H);
+        fp8_roundtrip(L->o_proj, H, qd);
+        fp8_roundtrip(L->gate, I, H);
+        fp8_roundtrip(L->up, I, H);
+        fp8_roundtrip(L->down, H, I);
+    }
 }
 
 Q3O_API void q3o_model_destroy(q3o_model* m) {

@@ -45,6 +45,11 @@ def test_invalid_arguments_fail_before_the_gpu():
     assert L.q3_engine_create(C.byref(bad), 0, 0, 1, C.byref(h)) == 3
     odd = ModelConfig(1024, 3072, 28, 16, 8, 128, 151936, 1, 1e-6, 1e6, 64, 0)
     assert L.q3_engine_create(C.byref(odd), 0, 0, 3, C.byref(h)) == 1  # 8 kv heads over 3 ranks
+    assert L.q3_gemv_e4m3(x, x, x, x, 4, 24, None) == 1  # n_in % 16
+    assert L.q3_quantize_e4m3(x, 4, 64, 32, 48, x, x, None) == 1  # columns past the row
+    assert L.q3_quantize_e4m3(x, 4, 64, 1, 8, x, x, None) == 1  # odd first column
+    fmt = ModelConfig(1024, 3072, 28, 16, 8, 128, 151936, 1, 1e-6, 1e6, 64, 0, 7)
+    assert L.q3_engine_create(C.byref(fmt), 0, 0, 1, C.byref(h)) == 1  # unknown weight format
     with pytest.raises(Q3Error):
         check(1)
 

@@ -12,8 +12,10 @@ from st_util import hf_tensors, write_sharded
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("weights", ["bf16", "fp8"])
 @pytest.mark.parametrize("tied", [True, False])
-def test_loaded_checkpoint_matches_synthetic_weights(tmp_path, oracle, tied):
+def test_loaded_checkpoint_matches_synthetic_weights(tmp_path, oracle, tied, weights):
+    """FP8 engines quantize what they load exactly as what they generate."""
     from inference_b200 import Engine, Qwen3Config, prompt_ids
 
     H, I, L, QH, KVH, V = 1024, 3072, 2, 16, 8, 8192
@@ -22,7 +24,7 @@ def test_loaded_checkpoint_matches_synthetic_weights(tmp_path, oracle, tied):
     ids = prompt_ids(6, vocab=V)
     logits = []
     for load in (False, True):
-        with Engine(qc, capacity=64) as e:
+        with Engine(qc, capacity=64, weights=weights) as e:
             if load:
                 n = e.load_safetensors(tmp_path)
                 assert n == 2 + (0 if tied else 1) + 11 * L
