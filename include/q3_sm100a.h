@@ -253,15 +253,19 @@ Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
 Q3_API int q3_engine_set_persistent(q3_engine* e, int enable);
 Q3_API int q3_engine_is_persistent(q3_engine* e);
 
-/* Phase timeline of the persistent kernel (tracing): with enable = 1 the next
+/* Phase timeline (tracing).  Persistent kernel: with enable = 1 the next
  * launches record, for the first step of each launch, per CTA and phase
  * (5 per layer + lm_head) Q3_TRACE_WORDS uint64 words: [0] / [1] phase start
  * and end (%globaltimer ns), [2] / [3] the SM clock (clock64) at the same
  * points, [4..7] SM cycles of parts of the phase (GEMV: input ready, waiting
  * for items, issuing refills, dot products; attention: q/k norm, page loop,
- * waiting for pages, split merge and publish), [8] the SM id.  out_host (if
- * not NULL) receives the last record, [ctas][phases][Q3_TRACE_WORDS];
- * capacity counts uint64 words. */
+ * waiting for pages, split merge and publish), [8] the SM id.  CUDA-graph
+ * path: every step records, per launch (the same 5 per layer + lm_head) and
+ * CTA, [0] / [1] CTA start / end (%globaltimer), [2] / [3] clock64 there,
+ * SM cycles of [4] start -> dependency wait returned, [5] prologue, [6] main
+ * loop, [7] epilogue, [8] the SM id (toggling re-records the graph).
+ * out_host (if not NULL) receives the last record,
+ * [ctas][phases][Q3_TRACE_WORDS]; capacity counts uint64 words. */
 #define Q3_TRACE_WORDS 10
 Q3_API int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases,
                            size_t* n_ctas);

@@ -53,6 +53,8 @@ struct AttnSmem {
     float cm[HG];  // this CTA's merged state, read by the cluster
     float cl[HG];
     float cacc[HG][kHd];
+    bf16 qn[HG][kHd];  // normalised, rotated q heads (fused q/k norm)
+    bf16 kn[kHd];      // normalised, rotated key row of the position
     uint64_t full[kStages];
     uint64_t empty[kStages];
 };
@@ -68,6 +70,27 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* p, uint32_t& r0, u
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(smem_u32(p)));
 }
+// One 128-wide head: RMSNorm (weights nw) then RoPE at `pos`, rounded once
+// (qk_norm_rope.cuh:14-90); a warp, lane l holding dims l, l + 32, l + 64, l + 96.
+__device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* nw, const float* cs, const float* sn,
+                                               int pos, float eps, bf16* dst, int lane) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = bf2f(src[lane + 32 * j]);
+    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+    const float scale = 1.0f / sqrtf(ss / 128.0f + eps);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int i = lane + 32 * j;
+        const float c = cs[static_cast<size_t>(pos) * 64 + i];
+        const float s = sn[static_cast<size_t>(pos) * 64 + i];
+        const float x = v[j] * bf2f(nw[i]) * scale;
+        const float y = v[j + 2] * bf2f(nw[i + 64]) * scale;
+        dst[i] = f2bf(x * c - y * s);
+        dst[i + 64] = f2bf(y * c + x * s);
+    }
+}
+
 // D (16 x 8, fp32) += A (16 x 16, BF16, row) B (16 x 8, BF16, col)
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                uint32_t b0, uint32_t b1) {
@@ -84,6 +107,12 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
     AttnSmem<HG>& S = *reinterpret_cast<AttnSmem<HG>*>(smem_raw);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const bool tracing = a.trace.buf != nullptr;
+    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0;
+    if (tracing && tid == 0) {
+        tr_t0 = globaltimer_ns();
+        tr_c0 = clock64();
+    }
     const int G = a.q_heads / a.kv_heads;
     const int nqb = G / HG;
     const int split = blockIdx.x, kvh = blockIdx.y, qb = blockIdx.z % nqb, qi = blockIdx.z / nqb;
@@ -152,16 +181,39 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         // c ^ (r & 7)), so every ldmatrix phase hits 8 distinct bank groups.
         pdl_wait();  // q comes from the QKV kernel
         pdl_trigger();
+        if (tracing && tid == 0) tr_c1 = clock64();
         const int g = lane >> 2, t4 = lane & 3;  // fragment row (query head) and column pair
         const int qh0 = kvh * G + qb * HG;
         const float qscale = (1.0f / sqrtf(static_cast<float>(kHd))) * kLog2e;
+        const bool fused = a.k_raw != nullptr;
+        const bool has_live = fused && live_page >= pb && live_page < pe;
+        if (fused) {
+            // q/k norm + RoPE of this step: warp w < HG takes q head qh0 + w, the last
+            // warp (after its q head) the key row when this split holds the live page
+            if (warp < HG)
+                norm_rope_head(qv + static_cast<size_t>(qh0 + warp) * kHd, a.q_norm, a.rope_cos, a.rope_sin, pos,
+                               a.eps, S.qn[warp], lane);
+            if (warp == kWarps - 1 && has_live) {
+                norm_rope_head(a.k_raw + static_cast<size_t>(kvh) * kHd, a.k_norm, a.rope_cos, a.rope_sin, pos,
+                               a.eps, S.kn, lane);
+                if (qb == 0) {
+                    __syncwarp();
+                    bf16* slot = const_cast<bf16*>(a.k) +
+                                 ((static_cast<size_t>(a.page_table[live_page]) * a.kv_heads + kvh) * kPage +
+                                  pos % kPage) * kHd;
+                    if (lane < 16) reinterpret_cast<uint4*>(slot)[lane] = reinterpret_cast<const uint4*>(S.kn)[lane];
+                }
+            }
+            named_bar(1, kConsumers);
+        }
 
         uint32_t qa[8][2];  // A fragments of q: rows g (dims 16kk + 2t4, +1) and (+8); rows 8-15 are zero
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
             qa[kk][0] = qa[kk][1] = 0u;
             if (g < HG) {
-                const uint32_t* qr = reinterpret_cast<const uint32_t*>(qv + static_cast<size_t>(qh0 + g) * kHd);
+                const uint32_t* qr = fused ? reinterpret_cast<const uint32_t*>(S.qn[g])
+                                           : reinterpret_cast<const uint32_t*>(qv + static_cast<size_t>(qh0 + g) * kHd);
                 qa[kk][0] = qr[kk * 8 + t4];
                 qa[kk][1] = qr[kk * 8 + 4 + t4];
             }
@@ -181,6 +233,13 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
                 const int valid = min(kPage, pos + 1 - page * kPage);
                 uint8_t* kt = S.kv[s][0];
                 uint8_t* vt = S.kv[s][1];
+                if (has_live && page == live_page && warp == (pos % kPage) / 16) {
+                    // this step's key row: the cache slot still holds the raw row (or older data)
+                    if (lane < 16)
+                        reinterpret_cast<uint4*>(kt + (pos % kPage) * 256)[lane] =
+                            reinterpret_cast<const uint4*>(S.kn)[lane];
+                    __syncwarp();
+                }
                 // ---- swizzle this warp's rows in place; rows past the position become zeros in V
 #pragma unroll
                 for (int tile = 0; tile < 2; ++tile) {
@@ -354,6 +413,20 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         }
     }
     cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+    const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (tracing && tid == 0 && cta < a.trace.ctas) {
+        unsigned long long* t = a.trace.buf + (static_cast<size_t>(cta) * a.trace.phases + a.trace.phase) * kTraceWords;
+        const unsigned long long c4 = clock64();
+        t[0] = tr_t0;
+        t[1] = globaltimer_ns();
+        t[2] = tr_c0;
+        t[3] = c4;
+        t[4] = tr_c1 - tr_c0;
+        t[5] = 0;
+        t[6] = c4 - tr_c1;
+        t[7] = 0;
+        t[8] = sm_id();
+    }
 }
 
 int heads_per_cta(int G) { return G >= 4 ? 4 : G; }

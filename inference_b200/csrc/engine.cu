@@ -70,13 +70,17 @@ struct q3_engine {
     // control state
     int32_t *pos = nullptr, *n_forced = nullptr, *tokens = nullptr, *argmax_hist = nullptr;
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
-    uint32_t *done_counter = nullptr, *head_counters = nullptr, *err = nullptr;
+    uint32_t *done_counter = nullptr, *err = nullptr;
     int attn_splits = 1;
     // persistent decode kernel (one launch per run of steps)
     bool persistent = false;
     q3::PersistentArgs pargs{};
     uint32_t* d_layer_tab = nullptr;
     unsigned long long* d_trace = nullptr;
+    // CUDA-graph path timeline: per launch of a step and CTA (q3_engine_trace)
+    bool gtrace = false;
+    unsigned long long* d_gtrace = nullptr;
+    int gtrace_ctas = 0;
     unsigned long long* gsync = nullptr;
     uint32_t* abort_word = nullptr;
     // batched prefill: token-row buffers of prefill_rows rows (allocated on first use)
@@ -137,6 +141,14 @@ struct Recorder {
     std::vector<cudaEvent_t>* ev = nullptr;
     double* bytes = nullptr;
     size_t launches = 0;
+    int phase = 0;  // launches recorded so far in this step (the timeline's phase index)
+
+    LaunchTrace trace() {
+        LaunchTrace t{};
+        if (e->gtrace) t = LaunchTrace{e->d_gtrace, phase, static_cast<int>(e->layers.size()) * 5 + 1, e->gtrace_ctas};
+        ++phase;
+        return t;
+    }
 
     void mark(bool begin, int kind) {
         if (!ev || !(klass == 2 || klass == kind)) return;
@@ -172,6 +184,7 @@ int gemv(Recorder& r, int pro, int epi, GemvArgs a, WMat W, int N, int K) {
     a.N = N;
     a.K = K;
     a.plan = plan_gemv(N, K, epi, r.e->sms, W.q ? 1 : 2);
+    a.trace = r.trace();
     r.mark(true, 0);
     cudaError_t st = launch_gemv(pro, epi, a, r.e->stream, r.pdl);
     r.mark(false, 0);
@@ -197,6 +210,14 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.pos_ptr = e->pos;
     a.splits = e->attn_splits;
     a.err = e->err;
+    // q/k RMSNorm + RoPE of this step (the QKV GEMV leaves the raw k rows after q)
+    a.k_raw = e->q + e->qd;
+    a.q_norm = L.q_norm;
+    a.k_norm = L.k_norm;
+    a.rope_cos = e->rope_cos;
+    a.rope_sin = e->rope_sin;
+    a.eps = e->cfg.eps;
+    a.trace = r.trace();
     r.mark(true, 1);
     cudaError_t st = launch_attention(a, e->stream, r.pdl);
     r.mark(false, 1);
@@ -230,15 +251,9 @@ int record_step(Recorder& r, size_t pos_now) {
         a.head_dim = 128;
         a.kv_heads_local = e->kvh;
         a.page_size = kPageSize;
-        a.q_out = e->q;
-        a.k_pages = L.k_pages;
+        a.q_out = e->q;  // q rows, then the raw key rows (normalised by the attention kernel)
         a.v_pages = L.v_pages;
         a.page_table = e->page_table;
-        a.q_norm = L.q_norm;
-        a.k_norm = L.k_norm;
-        a.rope_cos = e->rope_cos;
-        a.rope_sin = e->rope_sin;
-        a.head_counters = e->head_counters;
         int pro;
         if (l == 0) {
             pro = PRO_EMBED_NORM;
@@ -545,7 +560,6 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->key_send, 2)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->keys, static_cast<size_t>(tp_size) + 1)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->done_counter, 4)) != Q3_OK) return bail(rc);
-    if ((rc = dalloc_t(e, &e->head_counters, static_cast<size_t>(e->qh + e->kvh) + 4)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->err, 4)) != Q3_OK) return bail(rc);
     cudaMemset(e->pos, 0, 16);
     cudaMemset(e->n_forced, 0, 16);
@@ -555,7 +569,6 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     cudaMemset(e->key_send, 0, 16);
     cudaMemset(e->keys, 0, (tp_size + 1) * 8);
     cudaMemset(e->done_counter, 0, 16);
-    cudaMemset(e->head_counters, 0, (e->qh + e->kvh + 4) * 4);
     cudaMemset(e->err, 0, 4);
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
@@ -747,7 +760,8 @@ int set_matrix_fp8(q3_engine* e, const uint16_t* host, size_t rows, size_t full_
                    uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride) {
     Staging st;
     Q3_TRY(st.alloc(rows * full_cols));
-    Q3_CUDA(cudaMemcpy(st.p, host, rows * full_cols * 2, cudaMemcpyHostToDevice));
+    // stream-ordered before the quantize kernel (a pageable cudaMemcpy may return before its DMA lands)
+    Q3_CUDA(cudaMemcpyAsync(st.p, host, rows * full_cols * 2, cudaMemcpyHostToDevice, e->stream));
     Q3_TRY(quant(e, st.p, full_cols, rows, full_cols, c0, cols, dst, ld_dst, scale, scale_stride));
     Q3_CUDA(cudaStreamSynchronize(e->stream));
     return Q3_OK;
@@ -799,8 +813,11 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
     auto expect = [&](size_t r, size_t cc) { return rows == r && cols == cc; };
     auto copy2d = [&](void* dst, size_t dpitch_elems, const uint16_t* src, size_t spitch_elems, size_t width_elems,
                       size_t height) -> int {
-        Q3_CUDA(cudaMemcpy2D(dst, dpitch_elems * 2, src, spitch_elems * 2, width_elems * 2, height,
-                             cudaMemcpyHostToDevice));
+        // on the engine's stream and complete before returning: a host-to-device copy from
+        // pageable memory may still be in flight when a plain cudaMemcpy2D returns
+        Q3_CUDA(cudaMemcpy2DAsync(dst, dpitch_elems * 2, src, spitch_elems * 2, width_elems * 2, height,
+                                  cudaMemcpyHostToDevice, e->stream));
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
         return Q3_OK;
     };
     if (n == "model.embed_tokens.weight") {
@@ -869,7 +886,8 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
     }
     auto vec = [&](bf16* dst, size_t len) -> int {
         Q3_CHECK(rows * cols == len, "norm weight shape: " + n);
-        Q3_CUDA(cudaMemcpy(dst, host, len * 2, cudaMemcpyHostToDevice));
+        Q3_CUDA(cudaMemcpyAsync(dst, host, len * 2, cudaMemcpyHostToDevice, e->stream));
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
         return Q3_OK;
     };
     if (leaf == "input_layernorm.weight") return vec(L.in_norm, H);
@@ -1148,10 +1166,45 @@ int q3_engine_set_persistent(q3_engine* e, int enable) {
 
 int q3_engine_is_persistent(q3_engine* e) { return (e && e->persistent) ? 1 : 0; }
 
+namespace {
+
+// The CUDA-graph path's timeline: every launch of the step records per CTA;
+// toggling it re-records the graph with or without the trace buffer.
+int graph_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases, size_t* n_ctas) {
+    const size_t phases = e->layers.size() * 5 + 1;
+    // attention launches splits x kv heads x query-head blocks CTAs (at most one per q head)
+    const int ctas = std::max(e->sms, e->attn_splits * e->qh);
+    const size_t n = static_cast<size_t>(ctas) * phases * kTraceWords;
+    *n_phases = phases;
+    *n_ctas = static_cast<size_t>(ctas);
+    if (enable && !e->d_gtrace) {
+        int rc = dalloc_t(e, &e->d_gtrace, n);
+        if (rc != Q3_OK) return rc;
+        Q3_CUDA(cudaMemset(e->d_gtrace, 0, n * 8));
+    }
+    e->gtrace_ctas = ctas;
+    if (static_cast<bool>(enable) != e->gtrace) {
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        if (e->graph) {
+            cudaGraphExecDestroy(e->graph);
+            e->graph = nullptr;
+        }
+        e->gtrace = enable != 0;
+    }
+    if (out_host && e->d_gtrace) {
+        Q3_CHECK(capacity >= n, "q3_engine_trace: output buffer too small");
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_CUDA(cudaMemcpy(out_host, e->d_gtrace, n * 8, cudaMemcpyDeviceToHost));
+    }
+    return Q3_OK;
+}
+
+}  // namespace
+
 int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases, size_t* n_ctas) {
     Q3_CHECK(e && n_phases && n_ctas, "null argument");
-    if (!e->persistent) return fail(Q3_ERR_UNSUPPORTED, "the phase timeline needs the persistent decode kernel");
     Q3_CUDA(cudaSetDevice(e->device));
+    if (!e->persistent) return graph_trace(e, enable, out_host, capacity, n_phases, n_ctas);
     const size_t phases = e->layers.size() * 5 + 1;
     const size_t n = static_cast<size_t>(e->pargs.grid) * phases * kTraceWords;
     *n_phases = phases;
@@ -1203,6 +1256,7 @@ int q3_engine_kv_slot(q3_engine* e, size_t layer, size_t pos, uint16_t* k_out, u
     Q3_CHECK(e && k_out && v_out, "null argument");
     Q3_CHECK(layer < e->layers.size() && pos < e->cfg.capacity, "kv slot out of range");
     Q3_CUDA(cudaSetDevice(e->device));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));  // the legacy-stream copies below do not wait for it
     int32_t page = 0;
     Q3_CUDA(cudaMemcpy(&page, e->page_table + pos / kPageSize, 4, cudaMemcpyDeviceToHost));
     const LayerW& L = e->layers[layer];

@@ -40,6 +40,9 @@ namespace {
 #ifndef Q3_GEMV_MIN_BLOCKS
 #define Q3_GEMV_MIN_BLOCKS 1
 #endif
+#ifndef Q3_GEMV_DYNAMIC
+#define Q3_GEMV_DYNAMIC 0
+#endif
 constexpr int kWarps = Q3_GEMV_WARPS;
 constexpr int kThreads = kWarps * 32;
 constexpr int kChunk = Q3_GEMV_CHUNK;   // BF16 columns per item (4 KB); FP8 items take twice the columns
@@ -133,6 +136,16 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& p = a.plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // PRO / EPI < 0: one kernel for every prologue and epilogue, chosen at run
+    // time by a.pro / a.epi (one code image for all the GEMVs of a step)
+    const int pro = PRO >= 0 ? PRO : a.pro;
+    const int epi = EPI >= 0 ? EPI : a.epi;
+    const bool tracing = a.trace.buf != nullptr;
+    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_c2 = 0, tr_c3 = 0;
+    if (tracing && tid == 0) {
+        tr_t0 = globaltimer_ns();
+        tr_c0 = clock64();
+    }
 
     // ---- this CTA's rows and this warp's contiguous run of (row, chunk) items
     const int units = a.N / p.row_gran;
@@ -180,8 +193,9 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
 
     pdl_wait();
     pdl_trigger();
+    if (tracing && tid == 0) tr_c1 = clock64();
     int pos = 0;
-    if (EPI == EPI_QKV || PRO == PRO_EMBED_NORM) {
+    if (epi == EPI_QKV || pro == PRO_EMBED_NORM) {
         pos = *a.pos_ptr;
         if (pos < 0 || pos >= a.capacity) {
             if (tid == 0) record_error(a.err, DEV_BAD_POSITION);
@@ -191,13 +205,13 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
 
     // ---- prologue: x in shared memory
     const int kv8 = a.K / 8;
-    if constexpr (PRO == PRO_PLAIN) {
+    if (pro == PRO_PLAIN) {
         const uint4* src = reinterpret_cast<const uint4*>(a.x);
         uint4* dst = reinterpret_cast<uint4*>(xs);
         for (int i = tid; i < kv8; i += kThreads) dst[i] = src[i];
     } else {
         const bf16* src = a.hs;
-        if constexpr (PRO == PRO_EMBED_NORM) {
+        if (pro == PRO_EMBED_NORM) {
             const int nf = *a.n_forced;
             uint64_t best = 0;
             if (a.peer.world) {
@@ -226,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         // tensor parallel through peer memory: the (value, tag) pairs every rank stored here
         const unsigned long long* parts = nullptr;
         uint32_t tag = 0;
-        if constexpr (PRO == PRO_RESID_NORM) {
+        if (pro == PRO_RESID_NORM) {
             if (a.peer.world) {
                 tag = pair_tag(a.peer, a.xtag);
                 parts = a.peer.recv[a.peer.rank] + ((a.xtag - 1) & 1) * static_cast<size_t>(a.peer.world) * a.peer.H;
@@ -235,12 +249,12 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         float ss = 0.f;
         for (int i = tid; i < kv8; i += kThreads) {
             uint4 h = reinterpret_cast<const uint4*>(src)[i];
-            if constexpr (PRO == PRO_NORM_F32) {
+            if (pro == PRO_NORM_F32) {
                 const float4 v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
                 const float4 v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
                 ss += v0.x * v0.x + v0.y * v0.y + v0.z * v0.z + v0.w * v0.w;
                 ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
-            } else if constexpr (PRO == PRO_RESID_NORM) {
+            } else if (pro == PRO_RESID_NORM) {
                 float4 v0, v1;
                 if (parts) {
                     // sum of the ranks' partials in rank order (the same bits on every rank),
@@ -293,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 }
             }
             reinterpret_cast<uint4*>(xs)[i] = h;
-            if constexpr (PRO == PRO_EMBED_NORM || PRO == PRO_RESID_NORM) {
+            if (pro == PRO_EMBED_NORM || pro == PRO_RESID_NORM) {
                 if (blockIdx.x == 0) reinterpret_cast<uint4*>(a.hs_out)[i] = h;
             }
         }
@@ -315,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         }
     }
     __syncthreads();
+    if (tracing && tid == 0) tr_c2 = clock64();
 
     // ---- main loop: each warp streams its own items; no CTA-wide barrier
     float acc0 = 0.f, acc1 = 0.f;
@@ -358,6 +373,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         }
     }
     __syncthreads();
+    if (tracing && tid == 0) tr_c3 = clock64();
 
     // ---- epilogue: row sums in fixed chunk order (FP8: times the row's power-of-two scale)
     auto row_sum = [&](int rl) {
@@ -367,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         return r;
     };
     uint64_t best_key = 0;
-    if constexpr (EPI == EPI_SWIGLU) {
+    if (epi == EPI_SWIGLU) {
         for (int m = tid; m < nrows / 2; m += kThreads) {
             // qwen3.hpp:154-156 -> silu.cuh:18-20 on the BF16-rounded matmul outputs
             const float gv = round_bf(row_sum(2 * m)), uv = round_bf(row_sum(2 * m + 1));
@@ -377,15 +393,15 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     } else {
         // tensor parallel through peer memory: this kernel produces partial exchange xtag
         uint32_t tag = 0;
-        if constexpr (EPI == EPI_PARTIAL) {
+        if (epi == EPI_PARTIAL) {
             if (a.peer.world) tag = pair_tag(a.peer, a.xtag);
         }
         for (int rl = tid; rl < nrows; rl += kThreads) {
             const float r = row_sum(rl);
             const int gr = r0 + rl;
-            if constexpr (EPI == EPI_STORE) {
+            if (epi == EPI_STORE) {
                 a.y[gr] = f2bf(r);
-            } else if constexpr (EPI == EPI_PARTIAL) {
+            } else if (epi == EPI_PARTIAL) {
                 if (a.peer.world) {
                     // this rank's partial row into every rank's slot: one 8-byte (value, tag)
                     // store per rank (NVLink to peers); no fence or flag needed
@@ -397,26 +413,24 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 } else {
                     a.yf[gr] = r;
                 }
-            } else if constexpr (EPI == EPI_RESID) {
+            } else if (epi == EPI_RESID) {
                 // qwen3.hpp:158-159: hidden = bf16(down); hs = bf16(hs + hidden)
                 a.hs[gr] = f2bf(bf2f(a.hs[gr]) + round_bf(r));
-            } else if constexpr (EPI == EPI_RESID_F32) {
+            } else if (epi == EPI_RESID_F32) {
                 // qwen3.hpp:151-152 -> rmsnorm.cuh:58-60
                 const float v = bf2f(a.hs[gr]) + round_bf(r);
                 a.hs[gr] = f2bf(v);
                 a.vsum_out[gr] = v;
-            } else if constexpr (EPI == EPI_QKV) {
+            } else if (epi == EPI_QKV) {
+                // q and k rows raw (the attention kernel normalises and rotates them), v to its slot
                 const bf16 b = f2bf(r);
-                if (gr < a.q_rows) {
+                if (gr < a.q_rows + a.kv_rows) {
                     a.q_out[gr] = b;
-                } else if (gr < a.q_rows + a.kv_rows) {
-                    const int k = gr - a.q_rows;
-                    a.k_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
                 } else {
                     const int k = gr - a.q_rows - a.kv_rows;
                     a.v_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
                 }
-            } else if constexpr (EPI == EPI_ARGMAX) {
+            } else if (epi == EPI_ARGMAX) {
                 const bf16 b = f2bf(r);
                 a.y[gr] = b;
                 best_key = max(best_key, argmax_key(bf2f(b), static_cast<uint32_t>(gr) + a.vocab_offset));
@@ -425,48 +439,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     }
 
     // ---- post-loop finishers
-    if constexpr (EPI == EPI_QKV) {
-        // qk_norm_rope (qk_norm_rope.cuh:14-90) for every q / k head whose last
-        // rows this CTA produced: the CTA that completes a head normalises it.
-        __threadfence();
-        __syncthreads();
-        if (warp == 0) {
-            const int nqk = a.q_rows + a.kv_rows;
-            const int hi_row = min(r1, nqk);
-            for (int h = r0 / 128; h * 128 < hi_row; ++h) {
-                const int lo = max(r0, h * 128), hi = min(hi_row, (h + 1) * 128);
-                if (hi <= lo) continue;
-                uint32_t old = 0;
-                if (lane == 0) old = atomicAdd(&a.head_counters[h], static_cast<uint32_t>(hi - lo));
-                old = __shfl_sync(0xffffffffu, old, 0);
-                if (old + static_cast<uint32_t>(hi - lo) != 128u) continue;
-                __threadfence();
-                const bool is_q = h * 128 < a.q_rows;
-                bf16* base = is_q ? a.q_out + h * 128 : a.k_pages + kv_slot(a, pos, h - a.q_rows / 128);
-                const bf16* nw = is_q ? a.q_norm : a.k_norm;
-                float v[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    v[j] = __uint_as_float(static_cast<uint32_t>(
-                                               __ldcg(reinterpret_cast<const unsigned short*>(base) + lane + 32 * j))
-                                           << 16);
-                const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-                const float scale = 1.0f / sqrtf(ss / 128.0f + a.eps);
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int i = lane + 32 * j;
-                    const float c = a.rope_cos[static_cast<size_t>(pos) * 64 + i];
-                    const float sn = a.rope_sin[static_cast<size_t>(pos) * 64 + i];
-                    const float x = v[j] * bf2f(nw[i]) * scale;
-                    const float y = v[j + 2] * bf2f(nw[i + 64]) * scale;
-                    base[i] = f2bf(x * c - y * sn);
-                    base[i + 64] = f2bf(y * c + x * sn);
-                }
-                if (lane == 0) a.head_counters[h] = 0u;
-            }
-        }
-    }
-    if constexpr (EPI == EPI_ARGMAX) {
+    if (epi == EPI_ARGMAX) {
         if (best_key) atomicMax(cta_key, static_cast<unsigned long long>(best_key));
         __syncthreads();
         if (tid == 0) {
@@ -493,6 +466,23 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             }
         }
     }
+    if (tracing) {
+        __syncthreads();
+        if (tid == 0 && static_cast<int>(blockIdx.x) < a.trace.ctas) {
+            unsigned long long* t =
+                a.trace.buf + (static_cast<size_t>(blockIdx.x) * a.trace.phases + a.trace.phase) * kTraceWords;
+            const unsigned long long c4 = clock64();
+            t[0] = tr_t0;
+            t[1] = globaltimer_ns();
+            t[2] = tr_c0;
+            t[3] = c4;
+            t[4] = tr_c1 - tr_c0;
+            t[5] = tr_c2 - tr_c1;
+            t[6] = tr_c3 - tr_c2;
+            t[7] = c4 - tr_c3;
+            t[8] = sm_id();
+        }
+    }
 }
 
 // The keys of the last exchange (lm_head of the last step) into out[world],
@@ -506,8 +496,16 @@ __global__ void peer_keys_kernel(const PeerLinks x, unsigned long long* out, uin
 }
 
 template <int PRO, int EPI>
-cudaError_t launch_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
+cudaError_t launch_t(const GemvArgs& a0, cudaStream_t s, bool pdl) {
+#if Q3_GEMV_DYNAMIC
+    GemvArgs a = a0;
+    a.pro = PRO;
+    a.epi = EPI;
+    auto* fn = a.W8 ? gemv_kernel<-1, -1, true> : gemv_kernel<-1, -1, false>;
+#else
+    const GemvArgs& a = a0;
     auto* fn = a.W8 ? gemv_kernel<PRO, EPI, true> : gemv_kernel<PRO, EPI, false>;
+#endif
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.plan.grid);
     cfg.blockDim = dim3(kThreads);
@@ -533,6 +531,9 @@ cudaError_t configure_pair() {
     for (const void* f : {reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, false>),
                           reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, true>)}) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
+        // the whole carve-out as shared memory, so a CTA of the next (PDL-launched) kernel fits beside
+        // this one where the two footprints allow
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -554,6 +555,9 @@ cudaError_t configure_gemv_kernels() {
     Q3_CFG(PRO_RESID_NORM, EPI_SWIGLU)
     Q3_CFG(PRO_NORM, EPI_ARGMAX)
     Q3_CFG(PRO_RESID_NORM, EPI_ARGMAX)
+#if Q3_GEMV_DYNAMIC
+    Q3_CFG(-1, -1)
+#endif
 #undef Q3_CFG
     return e;
 }

@@ -8,6 +8,17 @@
 
 namespace q3 {
 
+// ---------------------------------------------------------------- launch timeline
+// Graph-path tracing (q3_engine_trace): launch `phase` of a step writes, per
+// CTA (linear block index below `ctas`), Q3_TRACE_WORDS words at
+// buf[(cta * phases + phase) * Q3_TRACE_WORDS]: [0] / [1] %globaltimer at CTA
+// start / end, [2] / [3] clock64 there, SM cycles of [4] start -> dependency
+// wait returned, [5] prologue, [6] main loop, [7] epilogue, [8] SM id.
+struct LaunchTrace {
+    unsigned long long* buf;  // null: off
+    int phase, phases, ctas;
+};
+
 // ---------------------------------------------------------------- GEMV
 // y = W x for one token, W row-major [N, K] BF16, fp32 accumulation.
 // The prologue builds x in shared memory; the epilogue consumes each row sum.
@@ -23,7 +34,7 @@ enum GemvEpi : int {
     EPI_RESID = 1,      // hs[r] = bf16(hs[r] + bf16(acc))
     EPI_RESID_F32 = 2,  // v = hs[r] + bf16(acc); hs[r] = bf16(v); vsum[r] = v
     EPI_SWIGLU = 3,     // rows (2j, 2j+1) = (gate_j, up_j): y[j] = bf16(silu(bf16 g) * bf16 u)
-    EPI_QKV = 4,        // q / k / v rows to q_out and the paged KV slot; q,k heads then norm + RoPE
+    EPI_QKV = 4,        // q and k rows (raw) to q_out, v rows to the paged KV slot
     EPI_ARGMAX = 5,     // logits[r] = bf16(acc); running (max, first index) across the grid
     EPI_PARTIAL = 6,    // yf[r] = acc (fp32 partial for a tensor-parallel reduction)
 };
@@ -83,17 +94,11 @@ struct GemvArgs {
     bf16* y;
     float* yf;
     float* vsum_out;
-    // EPI_QKV
+    // EPI_QKV: q rows then k rows to q_out, v rows to the v page slot of pos
     int q_rows, kv_rows, head_dim, kv_heads_local, page_size;
     bf16* q_out;
-    bf16* k_pages;
     bf16* v_pages;
     const int32_t* page_table;
-    const bf16* q_norm;
-    const bf16* k_norm;
-    const float* rope_cos;
-    const float* rope_sin;
-    uint32_t* head_counters;
     // EPI_ARGMAX
     uint64_t* key_slot;
     uint32_t* done_counter;
@@ -108,6 +113,8 @@ struct GemvArgs {
     int xtag;
     // ---- errors
     uint32_t* err;
+    LaunchTrace trace;
+    int pro, epi;  // the prologue / epilogue of the runtime-dispatched kernel
 };
 
 GemvPlan plan_gemv(int N, int K, int epi, int num_sms, int wb = 2);
@@ -130,6 +137,18 @@ struct AttnArgs {
     // pos + i, reads q + i * q_stride and writes out + i * out_stride.  0 or 1 =
     // the single decode query.
     int n_queries, q_stride, out_stride;
+    // Decode step with q/k RMSNorm + RoPE fused in (qk_norm_rope.cuh:14-90), k_raw
+    // set: q holds the raw q heads, k_raw [kv_heads, 128] this position's raw key
+    // rows; every CTA normalises and rotates its q heads, the CTAs whose split
+    // holds the position's page put the normalised key row into their K tile,
+    // and those of the first query-head block store it to its cache slot.
+    const bf16* k_raw;
+    const bf16* q_norm;
+    const bf16* k_norm;
+    const float* rope_cos;
+    const float* rope_sin;
+    float eps;
+    LaunchTrace trace;
 };
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);

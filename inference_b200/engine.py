@@ -134,12 +134,12 @@ class Engine:
         check(lib().q3_engine_set_persistent(self.h, int(bool(on))))
 
     def trace(self, enable: bool = True):
-        """Turn the persistent kernel's phase timeline on/off."""
+        """Turn the phase timeline on/off (persistent kernel or CUDA-graph path)."""
         ph, ct = C.c_size_t(), C.c_size_t()
         check(lib().q3_engine_trace(self.h, int(enable), None, 0, C.byref(ph), C.byref(ct)))
 
     def read_trace(self) -> np.ndarray:
-        """[ctas, phases, TRACE_WORDS] record of the first step of the last launch: [..., 0:2] phase
+        """[ctas, phases, TRACE_WORDS] record of the last traced step: [..., 0:2] phase (or CTA)
         start/end (globaltimer ns), [..., 2:4] clock64 there, [..., 4:8] SM cycles of parts of the
         phase, [..., 8] SM id (include/q3_sm100a.h, q3_engine_trace)."""
         ph, ct = C.c_size_t(), C.c_size_t()

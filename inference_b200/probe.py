@@ -3,6 +3,7 @@
     python -m inference_b200.probe            # GEMV then prefill GEMM
     python -m inference_b200.probe attention  # decode attention
     python -m inference_b200.probe gemv8      # FP8-weight GEMV
+    python -m inference_b200.probe decode [workload] [position] [steps]
 
 Default: three launches of the decode GEMV (q3_gemv, Qwen3-8B gate/up shape:
 24576 x 4096, 201 MB of weights) followed by three launches of the prefill
@@ -12,6 +13,9 @@ for Qwen3-8B heads (32 q / 8 kv) at position 4095 with a 16-split cluster.
 `gemv8`: the same gate/up shape with E4M3 weights (q3_quantize_e4m3 once,
 then three q3_gemv_e4m3 launches), then the BF16 GEMV again; prints each
 launch's CUDA-event time and GB/s (not meaningful under a profiler).
+`decode`: decode steps of the CUDA-graph path (default qwen3-0.6b-ctx1024,
+3 steps from position 520 over a synthetic KV cache); the only gemv_kernel /
+attn_kernel launches of the process are those of the steps.
 """
 import torch
 
@@ -57,6 +61,25 @@ def gemv8():
     print("ok")
 
 
+def decode(workload="qwen3-0.6b-ctx1024", pos="520", steps="3"):
+    from .config import WORKLOADS
+    from .backend import prompt_ids
+    from .engine import Engine
+
+    cfg, _, cap = WORKLOADS[workload]
+    pos, steps = int(pos), int(steps)
+    with Engine(cfg, capacity=cap) as e:
+        e.init_synthetic(0)
+        e.persistent = False
+        e.set_tokens(prompt_ids(16, vocab=cfg.vocab))
+        e.fill_kv(pos)
+        e.set_tokens(prompt_ids(pos + steps + 2, vocab=cfg.vocab))
+        e.set_position(pos)
+        e.step(steps)
+        e.sync()
+    print("ok")
+
+
 def main():
     be = B200Backend(0)
     x = torch.randn(4096, device="cuda").to(torch.bfloat16)
@@ -75,4 +98,4 @@ def main():
 if __name__ == "__main__":
     import sys
 
-    {"attention": attention, "gemv8": gemv8}.get(sys.argv[1] if sys.argv[1:] else "", main)()
+    {"attention": attention, "gemv8": gemv8, "decode": decode}.get(sys.argv[1] if sys.argv[1:] else "", main)(*sys.argv[2:])
