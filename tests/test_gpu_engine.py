@@ -184,3 +184,38 @@ def test_persistent_and_graph_paths_agree_at_long_context():
     for a_, b_ in zip(logits["persistent"], logits["graph"]):
         assert_logits_close(a_, b_, atol=6e-2, n_ulp=1, min_cos=0.9999)
     assert (args["persistent"] == args["graph"]).mean() >= 0.97
+
+
+@pytest.mark.parametrize("mode", ["persistent", "graph"])
+def test_phase_timeline(mode):
+    """q3_engine_trace: one record per (CTA, phase) for the 5 launches (or
+    phases) of every layer and lm_head, in step order, and turning it off
+    leaves the decoded tokens unchanged."""
+    from inference_b200 import Engine, Qwen3Config, prompt_ids
+
+    qc = Qwen3Config("qwen3-tiny", hidden=1024, inter=3072, layers=3, q_heads=16, kv_heads=8, vocab=8192, tied=True)
+    ids = prompt_ids(24, vocab=qc.vocab)
+    hist = {}
+    for tracing in (False, True):
+        with Engine(qc, capacity=256) as e:
+            e.persistent = mode == "persistent"
+            e.init_synthetic(0)
+            e.set_tokens(ids[:8])
+            if tracing:
+                e.trace(True)
+            e.step(16)
+            e.sync()
+            hist[tracing] = e.argmax_history(16)
+            if tracing:
+                raw = e.read_trace()
+                e.trace(False)
+                assert raw.shape[1] == 5 * qc.layers + 1 and raw.shape[2] == 10
+                start, end = raw[..., 0].astype(np.int64), raw[..., 1].astype(np.int64)
+                seen = start > 0
+                assert seen.any(axis=0).all(), "every phase recorded"
+                assert (end[seen] >= start[seen]).all()
+                first = np.where(seen, start, np.iinfo(np.int64).max).min(axis=0)
+                last_end = np.where(seen, end, 0).max(axis=0)
+                assert (np.diff(first) >= 0).all(), "phases start in step order"
+                assert last_end[-1] - first[0] < 10**8  # one step, well under 0.1 s
+    np.testing.assert_array_equal(hist[False], hist[True])
