@@ -71,25 +71,37 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* p, uint32_t& r0, u
                  : "r"(smem_u32(p)));
 }
 // One 128-wide head: RMSNorm (weights nw) then RoPE at `pos`, rounded once
-// (qk_norm_rope.cuh:14-90); a warp, lane l holding dims l, l + 32, l + 64, l + 96.
-__device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* nw, const float* cs, const float* sn,
-                                               int pos, float eps, bf16* dst, int lane) {
-    float v[4];
+// (qk_norm_rope.cuh:14-90); a warp, lane l holding dims l, l + 32, l + 64,
+// l + 96.  The weights and the RoPE row do not depend on earlier kernels and
+// are loaded (load) before griddepcontrol.wait; apply runs on the head after.
+struct NormRope {
+    float w[4], c[2], s[2];
+    __device__ __forceinline__ void load(const bf16* nw, const float* cs, const float* sn, int pos, int lane) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = bf2f(src[lane + 32 * j]);
-    const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-    const float scale = 1.0f / sqrtf(ss / 128.0f + eps);
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int i = lane + 32 * j;
-        const float c = cs[static_cast<size_t>(pos) * 64 + i];
-        const float s = sn[static_cast<size_t>(pos) * 64 + i];
-        const float x = v[j] * bf2f(nw[i]) * scale;
-        const float y = v[j + 2] * bf2f(nw[i + 64]) * scale;
-        dst[i] = f2bf(x * c - y * s);
-        dst[i + 64] = f2bf(y * c + x * s);
+        for (int j = 0; j < 2; ++j) {
+            const int i = lane + 32 * j;
+            w[j] = bf2f(nw[i]);
+            w[j + 2] = bf2f(nw[i + 64]);
+            c[j] = cs[static_cast<size_t>(pos) * 64 + i];
+            s[j] = sn[static_cast<size_t>(pos) * 64 + i];
+        }
     }
-}
+    __device__ __forceinline__ void apply(const bf16* src, float eps, bf16* dst, int lane) const {
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = bf2f(src[lane + 32 * j]);
+        const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
+        const float scale = 1.0f / sqrtf(ss / 128.0f + eps);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int i = lane + 32 * j;
+            const float x = v[j] * w[j] * scale;
+            const float y = v[j + 2] * w[j + 2] * scale;
+            dst[i] = f2bf(x * c[j] - y * s[j]);
+            dst[i + 64] = f2bf(y * c[j] + x * s[j]);
+        }
+    }
+};
 
 // D (16 x 8, fp32) += A (16 x 16, BF16, row) B (16 x 8, BF16, col)
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -179,23 +191,25 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         // probabilities keep ~16 bits.  Each warp first XOR-swizzles its own
         // 16 rows of the K and V tiles in place (16-byte chunk c of row r to
         // c ^ (r & 7)), so every ldmatrix phase hits 8 distinct bank groups.
+        const bool fused = a.k_raw != nullptr;
+        const bool has_live = fused && live_page >= pb && live_page < pe;
+        NormRope nq, nk;
+        if (fused) {
+            nq.load(a.q_norm, a.rope_cos, a.rope_sin, pos, lane);
+            if (warp == kWarps - 1 && has_live) nk.load(a.k_norm, a.rope_cos, a.rope_sin, pos, lane);
+        }
         pdl_wait();  // q comes from the QKV kernel
         pdl_trigger();
         if (tracing && tid == 0) tr_c1 = clock64();
         const int g = lane >> 2, t4 = lane & 3;  // fragment row (query head) and column pair
         const int qh0 = kvh * G + qb * HG;
         const float qscale = (1.0f / sqrtf(static_cast<float>(kHd))) * kLog2e;
-        const bool fused = a.k_raw != nullptr;
-        const bool has_live = fused && live_page >= pb && live_page < pe;
         if (fused) {
             // q/k norm + RoPE of this step: warp w < HG takes q head qh0 + w, the last
             // warp (after its q head) the key row when this split holds the live page
-            if (warp < HG)
-                norm_rope_head(qv + static_cast<size_t>(qh0 + warp) * kHd, a.q_norm, a.rope_cos, a.rope_sin, pos,
-                               a.eps, S.qn[warp], lane);
+            if (warp < HG) nq.apply(qv + static_cast<size_t>(qh0 + warp) * kHd, a.eps, S.qn[warp], lane);
             if (warp == kWarps - 1 && has_live) {
-                norm_rope_head(a.k_raw + static_cast<size_t>(kvh) * kHd, a.k_norm, a.rope_cos, a.rope_sin, pos,
-                               a.eps, S.kn, lane);
+                nk.apply(a.k_raw + static_cast<size_t>(kvh) * kHd, a.eps, S.kn, lane);
                 if (qb == 0) {
                     __syncwarp();
                     bf16* slot = const_cast<bf16*>(a.k) +
