@@ -190,10 +190,22 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     }
     for (int i = tid; i < nrows * p.nch; i += kThreads) part[i] = 0.f;
     if (tid == 0) *cta_key = 0ull;
+    // RMSNorm weights never depend on earlier kernels: this thread's first two
+    // 16-byte vectors of them load before the wait (the rest in the norm pass)
+    const int kv8 = a.K / 8;
+    uint4 wpre[2];
+    if (pro != PRO_PLAIN) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            if (tid + k * kThreads < kv8) wpre[k] = reinterpret_cast<const uint4*>(a.norm_w)[tid + k * kThreads];
+    }
 
     pdl_wait();
     pdl_trigger();
     if (tracing && tid == 0) tr_c1 = clock64();
+    // the residual rows this thread updates in the epilogue (first pass), read now
+    bf16 hs_pre = __float2bfloat16(0.f);
+    if ((epi == EPI_RESID || epi == EPI_RESID_F32) && tid < nrows) hs_pre = a.hs[r0 + tid];
     int pos = 0;
     if (epi == EPI_QKV || pro == PRO_EMBED_NORM) {
         pos = *a.pos_ptr;
@@ -204,7 +216,6 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     }
 
     // ---- prologue: x in shared memory
-    const int kv8 = a.K / 8;
     if (pro == PRO_PLAIN) {
         const uint4* src = reinterpret_cast<const uint4*>(a.x);
         uint4* dst = reinterpret_cast<uint4*>(xs);
@@ -313,9 +324,9 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         }
         ss = cta_sum(ss, misc);
         const float scale = 1.0f / sqrtf(ss / static_cast<float>(a.K) + a.eps);
-        for (int i = tid; i < kv8; i += kThreads) {
+        for (int i = tid, k = 0; i < kv8; i += kThreads, ++k) {
             uint4 h = reinterpret_cast<uint4*>(xs)[i];
-            const uint4 w = reinterpret_cast<const uint4*>(a.norm_w)[i];
+            const uint4 w = k == 0 ? wpre[0] : k == 1 ? wpre[1] : reinterpret_cast<const uint4*>(a.norm_w)[i];
             uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
             const uint32_t* ww = reinterpret_cast<const uint32_t*>(&w);
 #pragma unroll
@@ -415,10 +426,11 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 }
             } else if (epi == EPI_RESID) {
                 // qwen3.hpp:158-159: hidden = bf16(down); hs = bf16(hs + hidden)
-                a.hs[gr] = f2bf(bf2f(a.hs[gr]) + round_bf(r));
+                const bf16 h = rl < kThreads ? hs_pre : a.hs[gr];
+                a.hs[gr] = f2bf(bf2f(h) + round_bf(r));
             } else if (epi == EPI_RESID_F32) {
                 // qwen3.hpp:151-152 -> rmsnorm.cuh:58-60
-                const float v = bf2f(a.hs[gr]) + round_bf(r);
+                const float v = bf2f(rl < kThreads ? hs_pre : a.hs[gr]) + round_bf(r);
                 a.hs[gr] = f2bf(v);
                 a.vsum_out[gr] = v;
             } else if (epi == EPI_QKV) {
