@@ -64,10 +64,19 @@ Q3_API int q3_gemv(const uint16_t* x_dev, const uint16_t* w_dev, uint16_t* y_dev
  * that max|row| <= 448 * 2^e goes to scale[r]; columns [c0, c0 + cols) of the
  * row go to q[r, 0..cols) as E4M3(w / 2^e), rounded to nearest even and
  * saturated at +-448.  cols, c0 even.
- * q3_gemv_e4m3: y[n_out] = (W8[n_out, n_in] . x[n_in]) * scale, fp32
- * accumulation, BF16 out; n_in % 16 == 0, 16-byte aligned x and W8. */
+ * q3_gemv_e4m3: y[n_out] = (W8[n_out, n_in] . x[n_in]) * scale, W8 packed, on the tensor
+ * cores (weights exact as f16, x as f16 scaled by a power of two so that
+ * max|x| falls in [2^14, 2^15)), fp32 accumulation, BF16 out; n_in % 64 == 0,
+ * 16-byte aligned x and W8. */
 Q3_API int q3_quantize_e4m3(const uint16_t* w_dev, size_t rows, size_t full_cols, size_t c0, size_t cols,
                             uint8_t* q_dev, float* scale_dev, void* stream);
+/* The FP8 GEMV reads its weights in a packed layout (16-row x 256-column
+ * tiles of each CTA's row band, contiguous and bank-swizzled; it depends on
+ * the device's SM count): q3_pack_e4m3 converts a row-major E4M3 matrix
+ * [n_out, n_in] into it (q3_e4m3_packed_bytes(n_out, n_in) bytes, zero
+ * padding included); n_in % 64 == 0. */
+Q3_API size_t q3_e4m3_packed_bytes(size_t n_out, size_t n_in);
+Q3_API int q3_pack_e4m3(const uint8_t* q_dev, size_t n_out, size_t n_in, uint8_t* packed_dev, void* stream);
 Q3_API int q3_gemv_e4m3(const uint16_t* x_dev, const uint8_t* w8_dev, const float* scale_dev, uint16_t* y_dev,
                         size_t n_out, size_t n_in, void* stream);
 

@@ -70,10 +70,18 @@ class B200Backend:
         cols = full - c0 if cols is None else cols
         check(lib().q3_quantize_e4m3(_p(weights), rows, full, c0, cols, _p(q), _p(scale), self._stream()))
 
-    def gemv_e4m3(self, x, q, scale, output):
-        """output[n] = (q[n, k] . x[k]) * scale[n] with E4M3 weights q (q3_gemv_e4m3)."""
+    def pack_e4m3(self, q):
+        """Row-major E4M3 [n, k] (uint8 tensor) -> the FP8 GEMV's packed layout (q3_pack_e4m3)."""
+        torch = _torch()
         n, k = q.shape
-        check(lib().q3_gemv_e4m3(_p(x), _p(q), _p(scale), _p(output), n, k, self._stream()))
+        packed = torch.empty(lib().q3_e4m3_packed_bytes(n, k), dtype=torch.uint8, device=q.device)
+        check(lib().q3_pack_e4m3(_p(q), n, k, _p(packed), self._stream()))
+        return packed
+
+    def gemv_e4m3(self, x, packed, scale, output):
+        """output[n] = (W[n, :] . x) * scale[n], W E4M3 in the packed layout of pack_e4m3 (q3_gemv_e4m3)."""
+        n, k = output.numel(), x.numel()
+        check(lib().q3_gemv_e4m3(_p(x), _p(packed), _p(scale), _p(output), n, k, self._stream()))
 
     # backend.hpp:28
     def rmsnorm(self, input, weight, output, epsilon: float):

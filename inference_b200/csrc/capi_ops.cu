@@ -103,17 +103,31 @@ int q3_quantize_e4m3(const uint16_t* w, size_t rows, size_t full_cols, size_t c0
     Q3_CHECK(c0 + cols <= full_cols && (c0 % 2) == 0 && (cols % 2) == 0, "q3_quantize_e4m3: bad column range");
     Q3_CHECK(reinterpret_cast<uintptr_t>(q) % 2 == 0, "q3_quantize_e4m3: q must be 2-byte aligned");
     if (rows == 0) return Q3_OK;
+    const F8Dst d{q, scale, F8Pack{0, static_cast<int>(cols), 0, 0, 0}, 0, 1};  // row-major, pitch cols
     return launch_status(launch_quantize_e4m3(cb(w), full_cols, static_cast<int>(rows), static_cast<int>(full_cols),
-                                              static_cast<int>(c0), static_cast<int>(cols), q, cols, scale, 1,
-                                              as_stream(stream)),
+                                              static_cast<int>(c0), static_cast<int>(cols), d, as_stream(stream)),
                          "q3_quantize_e4m3");
+}
+
+size_t q3_e4m3_packed_bytes(size_t n_out, size_t n_in) {
+    if (n_out == 0 || n_in == 0 || n_out >= (1u << 30) || n_in > 32768) return 0;
+    return f8_packed_bytes(static_cast<int>(n_out), static_cast<int>(n_in));
+}
+
+int q3_pack_e4m3(const uint8_t* q, size_t n_out, size_t n_in, uint8_t* packed, void* stream) {
+    Q3_CHECK(q && packed, "q3_pack_e4m3: null pointer");
+    Q3_CHECK(n_out > 0 && n_in > 0 && n_in % 64 == 0, "q3_pack_e4m3: n_in must be a positive multiple of 64");
+    Q3_CHECK(n_in <= 32768 && n_out < (1u << 30), "q3_pack_e4m3: shape too large");
+    Q3_CHECK(aligned16(q) && aligned16(packed), "q3_pack_e4m3: 16-byte aligned buffers required");
+    const F8Pack L = f8_pack_for(static_cast<int>(n_out), static_cast<int>(n_in), EPI_STORE, current_sms());
+    return launch_status(launch_pack_e4m3(q, L, packed, as_stream(stream)), "q3_pack_e4m3");
 }
 
 int q3_gemv_e4m3(const uint16_t* x, const uint8_t* w8, const float* scale, uint16_t* y, size_t n_out, size_t n_in,
                  void* stream) {
     Q3_CHECK(x && w8 && scale && y, "q3_gemv_e4m3: null pointer");
     Q3_CHECK(n_out > 0 && n_in > 0, "q3_gemv_e4m3: empty shape");
-    Q3_CHECK(n_in % 16 == 0, "q3_gemv_e4m3: n_in must be a multiple of 16 (16-byte rows)");
+    Q3_CHECK(n_in % 64 == 0, "q3_gemv_e4m3: n_in must be a multiple of 64");
     Q3_CHECK(n_in <= 32768 && n_out < (1u << 30), "q3_gemv_e4m3: shape too large");
     Q3_CHECK(aligned16(x) && aligned16(w8), "q3_gemv_e4m3: x and W8 must be 16-byte aligned");
     GemvArgs a{};

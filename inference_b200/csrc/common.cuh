@@ -57,25 +57,6 @@ __device__ __forceinline__ float dot8(const uint4& a, const uint4& b, float acc)
     return acc;
 }
 
-// 16 FP8 E4M3 weights (one 16-byte vector, column order) against 16 BF16 x
-// values (two 16-byte vectors).  Each weight pair converts exactly to f16x2
-// (every E4M3 value is an f16 value), then to fp32; fp32 FMA in column order.
-__device__ __forceinline__ float dot16_e4m3(const uint4& w, const uint4& x0, const uint4& x1, float acc) {
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    const uint32_t xx[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __half2 lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(ww[i] & 0xFFFFu), __NV_E4M3);
-        const __half2 hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(ww[i] >> 16), __NV_E4M3);
-        const float2 a = __half22float2(lo), b = __half22float2(hi);
-        acc = fmaf(a.x, bf_lo(xx[2 * i]), acc);
-        acc = fmaf(a.y, bf_hi(xx[2 * i]), acc);
-        acc = fmaf(b.x, bf_lo(xx[2 * i + 1]), acc);
-        acc = fmaf(b.y, bf_hi(xx[2 * i + 1]), acc);
-    }
-    return acc;
-}
-
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

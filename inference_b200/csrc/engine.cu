@@ -126,6 +126,13 @@ int dalloc_t(q3_engine* e, T** p, size_t count) {
     return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T));
 }
 
+// Device bytes, zeroed.
+int dalloc_zero(q3_engine* e, uint8_t** p, size_t bytes) {
+    int rc = dalloc(e, reinterpret_cast<void**>(p), bytes);
+    if (rc == Q3_OK && cudaMemset(*p, 0, bytes) != cudaSuccess) return fail(Q3_ERR_CUDA, "cudaMemset failed");
+    return rc;
+}
+
 #define Q3_TRY(x)                  \
     do {                           \
         int rc_ = (x);             \
@@ -433,8 +440,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     Q3_CHECK(c.capacity < (1u << 24), "capacity too large");
     Q3_CHECK(c.weight_format == Q3_WEIGHTS_BF16 || c.weight_format == Q3_WEIGHTS_FP8_E4M3,
              "q3_engine_create: unknown weight_format");
-    Q3_CHECK(c.weight_format != Q3_WEIGHTS_FP8_E4M3 || (c.hidden % 16 == 0 && (c.inter / tp_size) % 16 == 0),
-             "FP8 weights need hidden and intermediate/tp multiples of 16");
+    Q3_CHECK(c.weight_format != Q3_WEIGHTS_FP8_E4M3 || (c.hidden % 64 == 0 && (c.inter / tp_size) % 64 == 0),
+             "FP8 weights need hidden and intermediate/tp multiples of 64");
 
     auto* e = new q3_engine();
     e->cfg = c;
@@ -467,7 +474,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->embed, static_cast<size_t>(c.vocab) * H)) != Q3_OK) return bail(rc);
     if (e->fp8) {
         // the embedding stays BF16 for the lookup; lm_head gets its own E4M3 copy
-        if ((rc = dalloc_t(e, &e->f_lm, static_cast<size_t>(e->vl) * H)) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_zero(e, &e->f_lm, f8_packed_bytes(e->vl, e->H))) != Q3_OK) return bail(rc);
         if ((rc = dalloc_t(e, &e->s_lm, static_cast<size_t>(e->vl))) != Q3_OK) return bail(rc);
     } else if (c.tied) {
         e->lm_head = e->embed + static_cast<size_t>(e->voff) * H;
@@ -482,10 +489,11 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     for (auto& L : e->layers) {
         L = LayerW{};
         if (e->fp8) {
-            if ((rc = dalloc_t(e, &L.f_qkv, rows_qkv * H)) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_t(e, &L.f_o, H * e->qd)) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_t(e, &L.f_gu, rows_gu * H)) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_t(e, &L.f_down, H * e->il)) != Q3_OK) return bail(rc);
+            // packed layouts (f8_packed_bytes), zero so the column padding is zero
+            if ((rc = dalloc_zero(e, &L.f_qkv, f8_packed_bytes(static_cast<int>(rows_qkv), e->H))) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_zero(e, &L.f_o, f8_packed_bytes(e->H, e->qd))) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_zero(e, &L.f_gu, f8_packed_bytes(static_cast<int>(rows_gu), e->H))) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_zero(e, &L.f_down, f8_packed_bytes(e->H, e->il))) != Q3_OK) return bail(rc);
             if ((rc = dalloc_t(e, &L.s_qkv, rows_qkv)) != Q3_OK) return bail(rc);
             if ((rc = dalloc_t(e, &L.s_o, H)) != Q3_OK) return bail(rc);
             if ((rc = dalloc_t(e, &L.s_gu, rows_gu)) != Q3_OK) return bail(rc);
@@ -700,10 +708,28 @@ struct Staging {
 };
 
 int quant(q3_engine* e, const bf16* src, size_t ld_src, size_t rows, size_t full_cols, size_t c0, size_t cols,
-          uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride) {
+          const F8Dst& d) {
     Q3_CUDA(launch_quantize_e4m3(src, ld_src, static_cast<int>(rows), static_cast<int>(full_cols), static_cast<int>(c0),
-                                 static_cast<int>(cols), dst, ld_dst, scale, scale_stride, e->stream));
+                                 static_cast<int>(cols), d, e->stream));
     return Q3_OK;
+}
+
+// The FP8 matrices as quantize destinations, each in the packed layout of the
+// GEMV that reads it (record_step's shapes and epilogues).
+F8Dst dst_qkv(const q3_engine* e, const LayerW& L, int row0) {
+    return F8Dst{L.f_qkv, L.s_qkv, f8_pack_for(e->qd + 2 * e->kd, e->H, EPI_QKV, e->sms), row0, 1};
+}
+F8Dst dst_o(const q3_engine* e, const LayerW& L) {
+    return F8Dst{L.f_o, L.s_o, f8_pack_for(e->H, e->qd, e->world > 1 ? EPI_PARTIAL : EPI_RESID_F32, e->sms), 0, 1};
+}
+F8Dst dst_gu(const q3_engine* e, const LayerW& L, int up) {  // gate row j -> row 2 j, up row j -> 2 j + 1
+    return F8Dst{L.f_gu, L.s_gu, f8_pack_for(2 * e->il, e->H, EPI_SWIGLU, e->sms), up, 2};
+}
+F8Dst dst_down(const q3_engine* e, const LayerW& L) {
+    return F8Dst{L.f_down, L.s_down, f8_pack_for(e->H, e->il, e->world > 1 ? EPI_PARTIAL : EPI_RESID, e->sms), 0, 1};
+}
+F8Dst dst_lm(const q3_engine* e) {
+    return F8Dst{e->f_lm, e->s_lm, f8_pack_for(e->vl, e->H, EPI_ARGMAX, e->sms), 0, 1};
 }
 
 // FP8 engines: each GEMV matrix generated at full row width in BF16 (so a
@@ -719,10 +745,10 @@ int init_synthetic_fp8(q3_engine* e, uint64_t seed) {
     Q3_TRY(st.alloc(need));
     Q3_CUDA(launch_fill_normal(e->embed, seed, 1, c.vocab, H, 0, 0, H, H, s));
     if (c.tied) {
-        Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, vl, H, 0, H, e->f_lm, H, e->s_lm, 1));
+        Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, vl, H, 0, H, dst_lm(e)));
     } else {
         Q3_CUDA(launch_fill_normal(st.p, seed, 2, vl, H, e->voff, 0, H, H, s));
-        Q3_TRY(quant(e, st.p, H, vl, H, 0, H, e->f_lm, H, e->s_lm, 1));
+        Q3_TRY(quant(e, st.p, H, vl, H, 0, H, dst_lm(e)));
     }
     Q3_CUDA(launch_fill_const(e->final_norm, H, 1.0f, s));
     for (size_t l = 0; l < e->layers.size(); ++l) {
@@ -731,20 +757,19 @@ int init_synthetic_fp8(q3_engine* e, uint64_t seed) {
         const size_t qr0 = static_cast<size_t>(e->rank) * qd, kr0 = static_cast<size_t>(e->rank) * kd;
         const size_t ir0 = static_cast<size_t>(e->rank) * il;
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 0, qd, H, qr0, 0, H, H, s));
-        Q3_TRY(quant(e, st.p, H, qd, H, 0, H, L.f_qkv, H, L.s_qkv, 1));
+        Q3_TRY(quant(e, st.p, H, qd, H, 0, H, dst_qkv(e, L, 0)));
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 1, kd, H, kr0, 0, H, H, s));
-        Q3_TRY(quant(e, st.p, H, kd, H, 0, H, L.f_qkv + qd * H, H, L.s_qkv + qd, 1));
+        Q3_TRY(quant(e, st.p, H, kd, H, 0, H, dst_qkv(e, L, static_cast<int>(qd))));
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 2, kd, H, kr0, 0, H, H, s));
-        Q3_TRY(quant(e, st.p, H, kd, H, 0, H, L.f_qkv + (qd + kd) * H, H, L.s_qkv + qd + kd, 1));
+        Q3_TRY(quant(e, st.p, H, kd, H, 0, H, dst_qkv(e, L, static_cast<int>(qd + kd))));
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 3, H, qfull, 0, 0, qfull, qfull, s));
-        Q3_TRY(quant(e, st.p, qfull, H, qfull, qr0, qd, L.f_o, qd, L.s_o, 1));
-        // gate row j -> stored row 2 j, up row j -> 2 j + 1 (the SwiGLU epilogue's pairs)
+        Q3_TRY(quant(e, st.p, qfull, H, qfull, qr0, qd, dst_o(e, L)));
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 4, il, H, ir0, 0, H, H, s));
-        Q3_TRY(quant(e, st.p, H, il, H, 0, H, L.f_gu, 2 * H, L.s_gu, 2));
+        Q3_TRY(quant(e, st.p, H, il, H, 0, H, dst_gu(e, L, 0)));
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 5, il, H, ir0, 0, H, H, s));
-        Q3_TRY(quant(e, st.p, H, il, H, 0, H, L.f_gu + H, 2 * H, L.s_gu + 1, 2));
+        Q3_TRY(quant(e, st.p, H, il, H, 0, H, dst_gu(e, L, 1)));
         Q3_CUDA(launch_fill_normal(st.p, seed, b + 6, H, inter, 0, 0, inter, inter, s));
-        Q3_TRY(quant(e, st.p, inter, H, inter, ir0, il, L.f_down, il, L.s_down, 1));
+        Q3_TRY(quant(e, st.p, inter, H, inter, ir0, il, dst_down(e, L)));
         Q3_CUDA(launch_fill_const(L.in_norm, H, 1.0f, s));
         Q3_CUDA(launch_fill_const(L.post_norm, H, 1.0f, s));
         Q3_CUDA(launch_fill_const(L.q_norm, 128, 1.0f, s));
@@ -757,12 +782,12 @@ int init_synthetic_fp8(q3_engine* e, uint64_t seed) {
 // FP8 engines: `rows` full host rows (full_cols wide) to the device, then
 // columns [c0, c0 + cols) of each quantized into dst.
 int set_matrix_fp8(q3_engine* e, const uint16_t* host, size_t rows, size_t full_cols, size_t c0, size_t cols,
-                   uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride) {
+                   const F8Dst& d) {
     Staging st;
     Q3_TRY(st.alloc(rows * full_cols));
     // stream-ordered before the quantize kernel (a pageable cudaMemcpy may return before its DMA lands)
     Q3_CUDA(cudaMemcpyAsync(st.p, host, rows * full_cols * 2, cudaMemcpyHostToDevice, e->stream));
-    Q3_TRY(quant(e, st.p, full_cols, rows, full_cols, c0, cols, dst, ld_dst, scale, scale_stride));
+    Q3_TRY(quant(e, st.p, full_cols, rows, full_cols, c0, cols, d));
     Q3_CUDA(cudaStreamSynchronize(e->stream));
     return Q3_OK;
 }
@@ -824,7 +849,7 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
         Q3_CHECK(expect(c.vocab, H), "embed_tokens shape");
         Q3_TRY(copy2d(e->embed, H, host, H, H, c.vocab));
         if (e->fp8 && c.tied) {
-            Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, e->vl, H, 0, H, e->f_lm, H, e->s_lm, 1));
+            Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, e->vl, H, 0, H, dst_lm(e)));
             Q3_CUDA(cudaStreamSynchronize(e->stream));
         }
         return Q3_OK;
@@ -833,7 +858,7 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
         Q3_CHECK(expect(c.vocab, H), "lm_head shape");
         if (c.tied) return fail(Q3_ERR_INVALID, "lm_head.weight given for a tied-embedding model");
         if (e->fp8)
-            return set_matrix_fp8(e, host + static_cast<size_t>(e->voff) * H, e->vl, H, 0, H, e->f_lm, H, e->s_lm, 1);
+            return set_matrix_fp8(e, host + static_cast<size_t>(e->voff) * H, e->vl, H, 0, H, dst_lm(e));
         return copy2d(e->lm_head, H, host + static_cast<size_t>(e->voff) * H, H, H, e->vl);
     }
     if (n == "model.norm.weight") {
@@ -854,34 +879,33 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
     const size_t qd = e->qd, kd = e->kd, il = e->il;
     if (leaf == "self_attn.q_proj.weight") {
         Q3_CHECK(expect(qfull, H), "q_proj shape");
-        if (e->fp8) return set_matrix_fp8(e, host + qr0 * H, qd, H, 0, H, L.f_qkv, H, L.s_qkv, 1);
+        if (e->fp8) return set_matrix_fp8(e, host + qr0 * H, qd, H, 0, H, dst_qkv(e, L, 0));
         return copy2d(L.w_qkv, H, host + qr0 * H, H, H, qd);
     }
     if (leaf == "self_attn.k_proj.weight") {
         Q3_CHECK(expect(kfull, H), "k_proj shape");
-        if (e->fp8) return set_matrix_fp8(e, host + kr0 * H, kd, H, 0, H, L.f_qkv + qd * H, H, L.s_qkv + qd, 1);
+        if (e->fp8) return set_matrix_fp8(e, host + kr0 * H, kd, H, 0, H, dst_qkv(e, L, static_cast<int>(qd)));
         return copy2d(L.w_qkv + qd * H, H, host + kr0 * H, H, H, kd);
     }
     if (leaf == "self_attn.v_proj.weight") {
         Q3_CHECK(expect(kfull, H), "v_proj shape");
-        if (e->fp8)
-            return set_matrix_fp8(e, host + kr0 * H, kd, H, 0, H, L.f_qkv + (qd + kd) * H, H, L.s_qkv + qd + kd, 1);
+        if (e->fp8) return set_matrix_fp8(e, host + kr0 * H, kd, H, 0, H, dst_qkv(e, L, static_cast<int>(qd + kd)));
         return copy2d(L.w_qkv + (qd + kd) * H, H, host + kr0 * H, H, H, kd);
     }
     if (leaf == "self_attn.o_proj.weight") {
         Q3_CHECK(expect(H, qfull), "o_proj shape");
-        if (e->fp8) return set_matrix_fp8(e, host, H, qfull, qr0, qd, L.f_o, qd, L.s_o, 1);
+        if (e->fp8) return set_matrix_fp8(e, host, H, qfull, qr0, qd, dst_o(e, L));
         return copy2d(L.w_o, qd, host + qr0, qfull, qd, H);
     }
     if (leaf == "mlp.gate_proj.weight" || leaf == "mlp.up_proj.weight") {
         Q3_CHECK(expect(c.inter, H), "gate/up shape");
         const size_t up = leaf == "mlp.up_proj.weight" ? 1 : 0;
-        if (e->fp8) return set_matrix_fp8(e, host + ir0 * H, il, H, 0, H, L.f_gu + up * H, 2 * H, L.s_gu + up, 2);
+        if (e->fp8) return set_matrix_fp8(e, host + ir0 * H, il, H, 0, H, dst_gu(e, L, static_cast<int>(up)));
         return copy2d(L.w_gu + up * H, 2 * H, host + ir0 * H, H, H, il);
     }
     if (leaf == "mlp.down_proj.weight") {
         Q3_CHECK(expect(H, c.inter), "down_proj shape");
-        if (e->fp8) return set_matrix_fp8(e, host, H, c.inter, ir0, il, L.f_down, il, L.s_down, 1);
+        if (e->fp8) return set_matrix_fp8(e, host, H, c.inter, ir0, il, dst_down(e, L));
         return copy2d(L.w_down, il, host + ir0, c.inter, il, H);
     }
     auto vec = [&](bf16* dst, size_t len) -> int {

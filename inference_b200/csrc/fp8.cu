@@ -14,9 +14,7 @@ namespace {
 constexpr int kQThreads = 256;
 
 __global__ void __launch_bounds__(kQThreads) quantize_e4m3_kernel(const bf16* __restrict__ src, size_t ld_src,
-                                                                 int full_cols, int c0, int cols,
-                                                                 uint8_t* __restrict__ dst, size_t ld_dst,
-                                                                 float* __restrict__ scale, size_t scale_stride) {
+                                                                 int full_cols, int c0, int cols, const F8Dst d) {
     __shared__ float red[kQThreads / 32];
     const int row = blockIdx.x, tid = threadIdx.x;
     const bf16* s = src + static_cast<size_t>(row) * ld_src;
@@ -35,24 +33,43 @@ __global__ void __launch_bounds__(kQThreads) quantize_e4m3_kernel(const bf16* __
         const float f = frexpf(mx, &k);
         e = (f <= 0.875f) ? k - 9 : k - 8;
     }
-    if (tid == 0) scale[static_cast<size_t>(row) * scale_stride] = ldexpf(1.0f, e);
-    uint8_t* d = dst + static_cast<size_t>(row) * ld_dst;
+    const int drow = d.row0 + row * d.row_step;
+    if (tid == 0) d.scale[drow] = ldexpf(1.0f, e);
     const bf16* sc = s + c0;
     for (int c = 2 * tid; c < cols; c += 2 * kQThreads) {
         const float2 v = make_float2(ldexpf(bf2f(sc[c]), -e), ldexpf(bf2f(sc[c + 1]), -e));
         const __nv_fp8x2_storage_t q = __nv_cvt_float2_to_fp8x2(v, __NV_SATFINITE, __NV_E4M3);
-        *reinterpret_cast<uint16_t*>(d + c) = static_cast<uint16_t>(q);
+        // an even column and the next share a 16-byte group in either layout
+        *reinterpret_cast<uint16_t*>(d.base + f8_offset(d.pack, drow, c)) = static_cast<uint16_t>(q);
     }
+}
+
+// One thread per 16-byte group of the row-major matrix (groups past K: zeros).
+__global__ void pack_e4m3_kernel(const uint8_t* __restrict__ q, const F8Pack L, uint8_t* __restrict__ packed) {
+    const int groups = L.nch * (kF8TileCols / 16);
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<long long>(L.N) * groups) return;
+    const int row = static_cast<int>(i / groups), col = static_cast<int>(i % groups) * 16;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (col < L.K) v = *reinterpret_cast<const uint4*>(q + static_cast<size_t>(row) * L.K + col);
+    *reinterpret_cast<uint4*>(packed + f8_offset(L, row, col)) = v;
 }
 
 }  // namespace
 
 cudaError_t launch_quantize_e4m3(const bf16* src, size_t ld_src, int rows, int full_cols, int c0, int cols,
-                                 uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride, cudaStream_t s) {
+                                 const F8Dst& dst, cudaStream_t s) {
     if (rows <= 0) return cudaSuccess;
-    if ((cols & 1) || (c0 & 1) || (ld_dst & 1) || c0 + cols > full_cols) return cudaErrorInvalidValue;
-    quantize_e4m3_kernel<<<rows, kQThreads, 0, s>>>(src, ld_src, full_cols, c0, cols, dst, ld_dst, scale,
-                                                    scale_stride);
+    if ((cols & 1) || (c0 & 1) || (dst.pack.K & 1) || c0 + cols > full_cols || cols > dst.pack.K)
+        return cudaErrorInvalidValue;
+    quantize_e4m3_kernel<<<rows, kQThreads, 0, s>>>(src, ld_src, full_cols, c0, cols, dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_pack_e4m3(const uint8_t* q, const F8Pack& pack, uint8_t* packed, cudaStream_t s) {
+    if (pack.N <= 0 || pack.K % 16 != 0) return cudaErrorInvalidValue;
+    const long long n = static_cast<long long>(pack.N) * pack.nch * (kF8TileCols / 16);
+    pack_e4m3_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(q, pack, packed);
     return cudaGetLastError();
 }
 

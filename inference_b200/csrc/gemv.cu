@@ -17,6 +17,15 @@
 //     cross-warp sum, so results are deterministic.
 //   * Epilogues apply the reference's BF16 rounding points exactly: matmul
 //     output rounded to BF16, then the following op on the rounded value.
+//   * FP8 E4M3 weights (F8) take the tensor cores instead: an item is a tile
+//     of 16 rows x 256 columns, stored contiguously and bank-swizzled by the
+//     packed layout (F8Pack) so one bulk copy brings it, each weight pair converts exactly to
+//     f16x2 (cvt.rn.f16x2.e4m3x2) as the A operand of mma.sync m16n8k16, and
+//     x enters as the B operand in f16, scaled by a power of two 2^-s chosen
+//     per CTA so that max|x| 2^-s lies in [2^14, 2^15) (exact for every
+//     |x| >= max|x| 2^-29; the few smaller ones round as f16 subnormals).
+//     Row sums are multiplied back by 2^s and by the row's scale in the
+//     epilogue.
 #include <algorithm>
 
 #include "kernels.cuh"
@@ -51,16 +60,25 @@ constexpr int kMaxItems = 4096;         // (row, chunk) partial sums per CTA
 // 100 KB in flight per SM to sustain its share of the bandwidth (measured:
 // 8 warps x 3 x 4 KB reached 71% of peak on a 201 MB GEMV, 16 x 3 x 4 KB 85%).
 constexpr size_t kSmemBudget = Q3_GEMV_SMEM_KB * 1024;
-constexpr int kMaxDynSmem = 220 * 1024;
+constexpr int kMaxDynSmem = 227 * 1024;   // the opt-in maximum per block
+constexpr size_t kSmemBudgetF8 = 226 * 1024;
+
+constexpr int kF8Rows = kF8TileRows;          // rows per FP8 tile (the mma M dimension)
+constexpr int kF8Cols = kF8TileCols;          // columns per FP8 item
+constexpr int kF8Slot = kF8Rows * kF8Cols;    // bytes per FP8 ring slot (one packed item)
 
 struct SmemLayout {
     size_t stage_off, x_off, part_off, bar_off, misc_off, total;
 };
 
+__host__ __device__ inline size_t slot_bytes(const GemvPlan& p) {
+    return p.wb == 1 ? static_cast<size_t>(kF8Slot) : static_cast<size_t>(p.kc) * 2;
+}
+
 __host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K, int max_rows) {
     SmemLayout L;
     L.stage_off = 0;
-    L.x_off = static_cast<size_t>(kWarps) * p.stages * p.kc * p.wb;
+    L.x_off = static_cast<size_t>(kWarps) * p.stages * slot_bytes(p);
     L.part_off = L.x_off + (static_cast<size_t>(K) * 2 + 15) / 16 * 16;
     L.bar_off = L.part_off + (static_cast<size_t>(max_rows) * p.nch * 4 + 15) / 16 * 16;
     L.misc_off = L.bar_off + static_cast<size_t>(kWarps) * p.stages * 8;
@@ -84,6 +102,43 @@ __device__ __forceinline__ float cta_sum(float v, float* scratch) {
     for (int w = 0; w < kWarps; ++w) t += scratch[w];
     __syncthreads();
     return t;
+}
+
+// Maximum over the CTA's threads.
+__device__ __forceinline__ float cta_max(float v, float* scratch) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) scratch[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t = fmaxf(t, scratch[w]);
+    __syncthreads();
+    return t;
+}
+
+// Four E4M3 weights w (byte i = column i) as two f16x2 registers, exact values,
+// by the conversion unit: lo = bytes 0-1, hi = bytes 2-3.
+__device__ __forceinline__ void e4m3x4_f16x2_cvt(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tcvt.rn.f16x2.e4m3x2 %0, l;\n\tcvt.rn.f16x2.e4m3x2 %1, h;\n\t}"
+        : "=r"(lo), "=r"(hi)
+        : "r"(w));
+}
+
+// D (16 x 8, fp32) += A (16 x 16, f16, row) B (16 x 8, f16, col); A rows g / g + 8 of
+// lane (g, t) come as 4-byte E4M3 words: bytes 0-1 = k 2t, 2t+1, bytes 2-3 = k 2t+8,
+// 2t+9 (exact f16 values).
+__device__ __forceinline__ void mma_e4m3_f16(float (&d)[4], uint32_t wg, uint32_t wg8, uint32_t b0, uint32_t b1) {
+    uint32_t a0, a1, a2, a3;
+    e4m3x4_f16x2_cvt(wg, a0, a2);
+    e4m3x4_f16x2_cvt(wg8, a1, a3);
+    // not volatile: a pure function of its operands, free to be scheduled among the conversions
+    asm(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -160,9 +215,10 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off) + warp * p.stages;
     float* misc = reinterpret_cast<float*>(smem + L.misc_off);
     unsigned long long* cta_key = reinterpret_cast<unsigned long long*>(misc + 16);
-    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * p.kc * WB;
+    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * slot_bytes(p);
 
-    const int n_items = nrows * p.nch;
+    // items: (row, chunk) pairs; FP8: (16-row tile, 256-column chunk) pairs
+    const int n_items = (F8 ? (nrows + kF8Rows - 1) / kF8Rows : nrows) * p.nch;
     const int i0 = static_cast<int>(static_cast<long long>(warp) * n_items / kWarps);
     const int i1 = static_cast<int>(static_cast<long long>(warp + 1) * n_items / kWarps);
     const int cnt = i1 - i0;
@@ -174,17 +230,33 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     __syncwarp();
 
     uint64_t pol = 0;
+    // BF16: lane 0 copies one row segment.  FP8 (whole warp): lane r < 16 copies row r of the tile.
     auto issue = [&](int item, int slot) {
-        const int row = r0 + item / p.nch, c = item % p.nch;
+        const int c = item % p.nch;
         const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
-        const uint32_t bytes = static_cast<uint32_t>(cols) * WB;
-        const uint8_t* wsrc = F8 ? a.W8 : reinterpret_cast<const uint8_t*>(a.W);
-        mbar_arrive_expect_tx(&bars[slot], bytes);
-        bulk_g2s(ring + static_cast<size_t>(slot) * p.kc * WB, wsrc + (static_cast<size_t>(row) * a.K + c * p.kc) * WB,
-                 bytes, &bars[slot], pol);
+        if constexpr (F8) {
+            (void)cols;
+            const int tile = item / p.nch;
+            const int rows = min(kF8Rows, nrows - tile * kF8Rows);
+            if (lane == 0) {
+                const uint32_t bytes = static_cast<uint32_t>(rows * kF8Cols);
+                mbar_arrive_expect_tx(&bars[slot], bytes);
+                bulk_g2s(ring + static_cast<size_t>(slot) * kF8Slot,
+                         a.W8 + (static_cast<size_t>(r0) * p.nch + static_cast<size_t>(tile) * kF8Rows * p.nch +
+                                 static_cast<size_t>(c) * rows) * kF8Cols,
+                         bytes, &bars[slot], pol);
+            }
+        } else {
+            const int row = r0 + item / p.nch;
+            const uint32_t bytes = static_cast<uint32_t>(cols) * WB;
+            mbar_arrive_expect_tx(&bars[slot], bytes);
+            bulk_g2s(ring + static_cast<size_t>(slot) * p.kc * WB,
+                     reinterpret_cast<const uint8_t*>(a.W) + (static_cast<size_t>(row) * a.K + c * p.kc) * WB, bytes,
+                     &bars[slot], pol);
+        }
     };
     // Weights never depend on earlier kernels: start streaming before the wait.
-    if (lane == 0) {
+    if (F8 || lane == 0) {
         pol = policy_evict_first();
         for (int j = 0; j < p.stages && j < cnt; ++j) issue(i0 + j, j);
     }
@@ -340,12 +412,86 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         }
     }
     __syncthreads();
+    int xshift = 0;  // FP8: x in shared memory holds f16(x 2^-xshift)
+    if constexpr (F8) {
+        float mx = 0.f;
+        for (int i = tid; i < kv8; i += kThreads) {
+            const uint4 h = reinterpret_cast<const uint4*>(xs)[i];
+            const uint32_t* hw = reinterpret_cast<const uint32_t*>(&h);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mx = fmaxf(mx, fmaxf(fabsf(bf_lo(hw[j])), fabsf(bf_hi(hw[j]))));
+        }
+        mx = cta_max(mx, misc);
+        if (mx > 0.f) {
+            int k;
+            frexpf(mx, &k);  // mx < 2^k
+            xshift = k - 15;
+        }
+        for (int i = tid; i < kv8; i += kThreads) {
+            uint4 h = reinterpret_cast<const uint4*>(xs)[i];
+            uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const __half lo = __float2half_rn(ldexpf(bf_lo(hw[j]), -xshift));
+                const __half hi = __float2half_rn(ldexpf(bf_hi(hw[j]), -xshift));
+                hw[j] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+            }
+            reinterpret_cast<uint4*>(xs)[i] = h;
+        }
+        __syncthreads();
+    }
     if (tracing && tid == 0) tr_c2 = clock64();
 
     // ---- main loop: each warp streams its own items; no CTA-wide barrier
     float acc0 = 0.f, acc1 = 0.f;
     bool failed = false;
-    for (int j = 0; j < cnt; ++j) {
+    if constexpr (F8) {
+        const int g = lane >> 2, t = lane & 3;
+        float d[4] = {0.f, 0.f, 0.f, 0.f}, e[4] = {0.f, 0.f, 0.f, 0.f};  // two independent mma chains
+        for (int j = 0; j < cnt; ++j) {
+            const int slot = j % p.stages;
+            bool ok = !failed && mbar_wait(&bars[slot], (j / p.stages) & 1, a.err, DEV_TMA_WAIT_TIMEOUT);
+            ok = __all_sync(0xffffffffu, ok);  // the mma and the refill need the whole warp
+            failed = failed || !ok;
+            const int item = i0 + j;
+            const int tile = item / p.nch, c = item % p.nch;
+            if (ok) {
+                const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
+                const uint8_t* ws = ring + static_cast<size_t>(slot) * kF8Slot;
+                const uint4* xq = reinterpret_cast<const uint4*>(xs) + c * (kF8Cols / 8);
+#pragma unroll 4
+                for (int blk = 0; blk < cols / 64; ++blk) {
+                    // lane (g, t): bytes 16t .. 16t + 15 of the block in rows g and g + 8 (16-byte group
+                    // 4 blk + t, stored at group (4 blk + t) ^ g), and the matching x halves; 4-byte
+                    // step s feeds one mma
+                    const int grp = ((4 * blk + t) ^ g) * 16;
+                    const uint4 wa = *reinterpret_cast<const uint4*>(ws + g * kF8Cols + grp);
+                    const uint4 wb = *reinterpret_cast<const uint4*>(ws + (g + 8) * kF8Cols + grp);
+                    const uint4 x0 = xq[blk * 8 + 2 * t], x1 = xq[blk * 8 + 2 * t + 1];
+                    mma_e4m3_f16(d, wa.x, wb.x, x0.x, x0.y);
+                    mma_e4m3_f16(e, wa.y, wb.y, x0.z, x0.w);
+                    mma_e4m3_f16(d, wa.z, wb.z, x1.x, x1.y);
+                    mma_e4m3_f16(e, wa.w, wb.w, x1.z, x1.w);
+                }
+            }
+            // flush at the end of this warp's part of a tile: column 0 of D (lanes t == 0)
+            if (c == p.nch - 1 || j == cnt - 1) {
+                const int rl = tile * kF8Rows + g;
+                if (t == 0) {
+                    if (rl < nrows) part[rl * p.nch + c] = d[0] + e[0];
+                    if (rl + 8 < nrows) part[(rl + 8) * p.nch + c] = d[2] + e[2];
+                }
+                d[0] = d[1] = d[2] = d[3] = 0.f;
+                e[0] = e[1] = e[2] = e[3] = 0.f;
+            }
+            __syncwarp();
+            if (!failed && j + p.stages < cnt) {
+                fence_proxy_async();  // generic-proxy reads of this slot precede the async refill
+                issue(i0 + j + p.stages, slot);
+            }
+        }
+    }
+    for (int j = 0; j < (F8 ? 0 : cnt); ++j) {  // BF16 (FP8 took the loop above)
         const int slot = j % p.stages;
         const bool ok = !failed && mbar_wait(&bars[slot], (j / p.stages) & 1, a.err, DEV_TMA_WAIT_TIMEOUT);
         failed = failed || !ok;
@@ -357,19 +503,11 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             const uint4* wv = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(slot) * p.kc * WB);
             const uint4* xv = reinterpret_cast<const uint4*>(xs + static_cast<size_t>(c) * p.kc);
             int v = lane;
-            if constexpr (F8) {
-                for (; v + 32 < nv; v += 64) {
-                    acc0 = dot16_e4m3(wv[v], xv[2 * v], xv[2 * v + 1], acc0);
-                    acc1 = dot16_e4m3(wv[v + 32], xv[2 * v + 64], xv[2 * v + 65], acc1);
-                }
-                if (v < nv) acc0 = dot16_e4m3(wv[v], xv[2 * v], xv[2 * v + 1], acc0);
-            } else {
-                for (; v + 32 < nv; v += 64) {
-                    acc0 = dot8(wv[v], xv[v], acc0);
-                    acc1 = dot8(wv[v + 32], xv[v + 32], acc1);
-                }
-                if (v < nv) acc0 = dot8(wv[v], xv[v], acc0);
+            for (; v + 32 < nv; v += 64) {
+                acc0 = dot8(wv[v], xv[v], acc0);
+                acc1 = dot8(wv[v + 32], xv[v + 32], acc1);
             }
+            if (v < nv) acc0 = dot8(wv[v], xv[v], acc0);
         }
         // flush at the end of this warp's part of a row
         if (c == p.nch - 1 || j == cnt - 1) {
@@ -390,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     auto row_sum = [&](int rl) {
         float r = 0.f;
         for (int c = 0; c < p.nch; ++c) r += part[rl * p.nch + c];
-        if constexpr (F8) r *= a.wscale[r0 + rl];
+        if constexpr (F8) r = ldexpf(r, xshift) * a.wscale[r0 + rl];  // x carried 2^-xshift
         return r;
     };
     uint64_t best_key = 0;
@@ -574,11 +712,17 @@ cudaError_t configure_gemv_kernels() {
     return e;
 }
 
+F8Pack f8_pack_for(int N, int K, int epi, int sms) {
+    const GemvPlan p = plan_gemv(N, K, epi, sms, 1);
+    return F8Pack{N, K, (K + kF8TileCols - 1) / kF8TileCols, p.grid, p.row_gran};
+}
+
 GemvPlan plan_gemv(int N, int K, int epi, int sms, int wb) {
     GemvPlan p{};
     p.row_gran = (epi == EPI_SWIGLU) ? 2 : 1;
     p.wb = wb;
-    const int chunk = kChunk * 2 / wb;  // 4 KB of weights per item
+    // BF16: 4 KB row segments; FP8: 16-row tiles of 256 columns
+    const int chunk = wb == 1 ? kF8Cols : kChunk;
     p.kc = K < chunk ? K : chunk;
     p.nch = (K + p.kc - 1) / p.kc;
     const int units = N / p.row_gran;
@@ -589,15 +733,16 @@ GemvPlan plan_gemv(int N, int K, int epi, int sms, int wb) {
     if (grid < min_grid) grid = static_cast<int>(std::min<long long>(min_grid, units));
     p.grid = std::max(1, grid);
     const int max_rows = (units + p.grid - 1) / p.grid * p.row_gran;
+    const size_t budget = wb == 1 ? kSmemBudgetF8 : kSmemBudget;
     for (p.stages = Q3_GEMV_MAX_STAGES; p.stages > 2; --p.stages)
-        if (smem_layout(p, K, max_rows).total <= kSmemBudget) break;
+        if (smem_layout(p, K, max_rows).total <= budget) break;
     p.smem = smem_layout(p, K, max_rows).total;
     return p;
 }
 
 cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl) {
-    // the plan's item width must match the weight format; FP8 rows are whole 16-byte vectors
-    if (a.plan.wb != (a.W8 ? 1 : 2) || (a.W8 && (a.K % 16 != 0 || !a.wscale))) return cudaErrorInvalidValue;
+    // the plan's item width must match the weight format; FP8 rows are whole 64-column blocks
+    if (a.plan.wb != (a.W8 ? 1 : 2) || (a.W8 && (a.K % 64 != 0 || !a.wscale))) return cudaErrorInvalidValue;
 #define Q3_CASE(P, E) \
     if (pro == P && epi == E) return launch_t<P, E>(a, s, pdl);
     Q3_CASE(PRO_PLAIN, EPI_STORE)

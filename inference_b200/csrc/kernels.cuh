@@ -267,13 +267,55 @@ cudaError_t configure_kernels();
 cudaError_t configure_gemv_kernels();
 
 // ---------------------------------------------------------------- FP8 weights
+// The FP8 GEMV's weight layout ("packed"): the [N, K] E4M3 matrix cut into the
+// row bands of its CTAs (the GEMV plan: `grid` bands of whole row_gran units),
+// each band into 16-row tiles (the last one shorter) and each tile into
+// 256-column chunks; item (tile, chunk) of a band is rows_t x 256 contiguous
+// bytes (rows_t = the tile's rows; columns past K are zero), so one bulk copy
+// fetches it, and inside an item row r keeps its 16-byte column group j at
+// group j ^ (r & 7), so the tensor-core fragment loads hit distinct banks.
+struct F8Pack {
+    int N, K, nch, grid, row_gran;  // N == 0: plain row-major with pitch K
+};
+constexpr int kF8TileRows = 16;
+constexpr int kF8TileCols = 256;
+__host__ __device__ inline size_t f8_offset(const F8Pack& L, int row, int col) {
+    if (L.N == 0) return static_cast<size_t>(row) * L.K + col;
+    const int U = L.N / L.row_gran, u = row / L.row_gran;
+    int b = static_cast<int>(static_cast<long long>(u) * L.grid / U);
+    while (b + 1 < L.grid && static_cast<int>(static_cast<long long>(b + 1) * U / L.grid) <= u) ++b;
+    const int u0 = static_cast<int>(static_cast<long long>(b) * U / L.grid);
+    const int u1 = static_cast<int>(static_cast<long long>(b + 1) * U / L.grid);
+    const int r0 = u0 * L.row_gran, nrows = (u1 - u0) * L.row_gran;
+    const int rl = row - r0, t = rl / kF8TileRows, rr = rl % kF8TileRows;
+    const int rows_t = nrows - t * kF8TileRows < kF8TileRows ? nrows - t * kF8TileRows : kF8TileRows;
+    const int c = col / kF8TileCols, g = (col % kF8TileCols) / 16;
+    return (static_cast<size_t>(r0) * L.nch + static_cast<size_t>(t) * kF8TileRows * L.nch +
+            static_cast<size_t>(c) * rows_t + rr) * kF8TileCols + ((g ^ (rr & 7)) << 4) + (col & 15);
+}
+inline size_t f8_packed_bytes(int N, int K) {
+    return static_cast<size_t>(N) * ((K + kF8TileCols - 1) / kF8TileCols) * kF8TileCols;
+}
+// The packed layout the GEMV with this epilogue uses for an [N, K] matrix.
+F8Pack f8_pack_for(int N, int K, int epi, int num_sms);
+
+// Where quantized rows go: source row r to matrix row row0 + r * row_step of
+// `base` (laid out by `pack`), its scale to scale[row0 + r * row_step].
+struct F8Dst {
+    uint8_t* base;
+    float* scale;
+    F8Pack pack;
+    int row0, row_step;
+};
 // Row-wise E4M3 quantization with power-of-two scales: for each of `rows`
 // rows of src (BF16, row pitch ld_src elements, full_cols columns) the scale
 // is 2^e, e the smallest integer with max|row| <= 448 * 2^e; columns
 // [c0, c0 + cols) are written as E4M3(x / 2^e) (round to nearest even,
-// saturating) to dst (row pitch ld_dst bytes) and 2^e to scale[r * scale_stride].
+// saturating) to columns 0 .. cols - 1 of the destination rows.
 cudaError_t launch_quantize_e4m3(const bf16* src, size_t ld_src, int rows, int full_cols, int c0, int cols,
-                                 uint8_t* dst, size_t ld_dst, float* scale, size_t scale_stride, cudaStream_t s);
+                                 const F8Dst& dst, cudaStream_t s);
+// Row-major E4M3 [N, K] (pitch K) -> the packed layout `pack` (zero padding included).
+cudaError_t launch_pack_e4m3(const uint8_t* q, const F8Pack& pack, uint8_t* packed, cudaStream_t s);
 cudaError_t configure_attention_kernels();
 int num_sms(int device);
 

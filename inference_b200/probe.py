@@ -4,6 +4,7 @@
     python -m inference_b200.probe attention  # decode attention
     python -m inference_b200.probe gemv8      # FP8-weight GEMV
     python -m inference_b200.probe decode [workload] [position] [steps]
+    python -m inference_b200.probe timeline [workload] [position]
 
 Default: three launches of the decode GEMV (q3_gemv, Qwen3-8B gate/up shape:
 24576 x 4096, 201 MB of weights) followed by three launches of the prefill
@@ -16,6 +17,10 @@ launch's CUDA-event time and GB/s (not meaningful under a profiler).
 `decode`: decode steps of the CUDA-graph path (default qwen3-0.6b-ctx1024,
 3 steps from position 520 over a synthetic KV cache); the only gemv_kernel /
 attn_kernel launches of the process are those of the steps.
+`timeline`: the CUDA-graph path's launch timeline (q3_engine_trace) of one
+decode step at `position`, summarised per launch kind over layers 1..L-1:
+CTA start to dependency release, prologue, main loop, epilogue (medians over
+CTAs, microseconds) and each launch's span from the previous launch's end.
 """
 import torch
 
@@ -46,6 +51,7 @@ def gemv8():
     sc = torch.empty(n, device="cuda", dtype=torch.float32)
     y = torch.empty(n, device="cuda", dtype=torch.bfloat16)
     be.quantize_e4m3(w, q, sc)
+    q = be.pack_e4m3(q)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     for name, fn, nbytes in (("fp8", lambda: be.gemv_e4m3(x, q, sc, y), n * k + 4 * n),
                              ("bf16", lambda: be.matmul(x, w, y), 2 * n * k)):
@@ -80,6 +86,53 @@ def decode(workload="qwen3-0.6b-ctx1024", pos="520", steps="3"):
     print("ok")
 
 
+def timeline(workload="qwen3-0.6b-ctx1024", pos="520"):
+    import numpy as np
+
+    from .backend import prompt_ids
+    from .config import WORKLOADS
+    from .engine import Engine
+
+    cfg, _, cap = WORKLOADS[workload]
+    pos = int(pos)
+    with Engine(cfg, capacity=cap) as e:
+        e.init_synthetic(0)
+        e.persistent = False
+        e.set_tokens(prompt_ids(16, vocab=cfg.vocab))
+        e.fill_kv(pos)
+        e.set_tokens(prompt_ids(pos + 16, vocab=cfg.vocab))
+        e.set_position(pos)
+        e.step(4)
+        e.trace(True)
+        e.set_position(pos)
+        e.step(3)
+        e.sync()
+        raw = e.read_trace().astype(np.float64)  # [ctas, phases, words]
+        e.trace(False)
+    seen = raw[..., 0] > 0
+    t0, t1, c0, c1 = raw[..., 0], raw[..., 1], raw[..., 2], raw[..., 3]
+    ghz = float(np.median(((c1 - c0) / np.maximum(t1 - t0, 1))[seen]))
+    us = lambda cyc: cyc / ghz / 1e3
+    n = raw.shape[1]
+    ends = [t1[seen[:, k], k].max() for k in range(n)]
+    print(f"{workload} position {pos}: step {(max(ends) - t0[seen].min()) / 1e3:.1f} us, SM clock {ghz:.3f} GHz")
+    names = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv"]
+    rows = {}
+    for k in range(5, n - 1):
+        v = seen[:, k]
+        rows.setdefault(names[k % 5], []).append(
+            [(ends[k] - ends[k - 1]) / 1e3, us(np.median(raw[v, k, 4])), us(np.median(raw[v, k, 5])),
+             us(np.median(raw[v, k, 6])), us(np.median(raw[v, k, 7]))])
+    print(f"{'launch':14s} {'span':>7s} {'to_wait':>8s} {'prologue':>9s} {'loop':>7s} {'epilogue':>9s}  (us)")
+    for name in names:
+        m = np.mean(rows[name], axis=0)
+        print(f"{name:14s} {m[0]:7.2f} {m[1]:8.2f} {m[2]:9.2f} {m[3]:7.2f} {m[4]:9.2f}")
+    v = seen[:, n - 1]
+    print(f"{'lm_head':14s} {(ends[n - 1] - ends[n - 2]) / 1e3:7.2f} {us(np.median(raw[v, n - 1, 4])):8.2f} "
+          f"{us(np.median(raw[v, n - 1, 5])):9.2f} {us(np.median(raw[v, n - 1, 6])):7.2f} "
+          f"{us(np.median(raw[v, n - 1, 7])):9.2f}")
+
+
 def main():
     be = B200Backend(0)
     x = torch.randn(4096, device="cuda").to(torch.bfloat16)
@@ -98,4 +151,4 @@ def main():
 if __name__ == "__main__":
     import sys
 
-    {"attention": attention, "gemv8": gemv8, "decode": decode}.get(sys.argv[1] if sys.argv[1:] else "", main)(*sys.argv[2:])
+    {"attention": attention, "gemv8": gemv8, "decode": decode, "timeline": timeline}.get(sys.argv[1] if sys.argv[1:] else "", main)(*sys.argv[2:])

@@ -99,3 +99,4 @@ def test_oracle_fp8_model_is_close_to_bf16(oracle):
     assert agree >= len(toks) // 2
     a.close()
     b.close()
+

@@ -53,8 +53,10 @@ def test_quantize_matches_oracle_bit_exact(be, oracle, rows, full, c0, cols):
     np.testing.assert_array_equal(host(q), oq[:, c0:c0 + cols])
 
 
+# (in, out): Qwen3 shapes, tensor-parallel slices (3200 = 12.5 chunks of 256 columns), ragged
+# row counts (partial 16-row tiles)
 FP8_GEMV_SHAPES = [(1024, 151936), (4096, 6144), (4096, 24576), (12288, 4096), (25600, 5120), (2560, 19456),
-                   (5120, 10240), (16, 3), (48, 1000)]
+                   (5120, 10240), (3200, 777), (1536, 4096), (64, 3), (192, 1000)]
 
 
 @pytest.mark.parametrize("i,o", FP8_GEMV_SHAPES)
@@ -72,7 +74,7 @@ def test_gemv_e4m3(be, oracle, i, o):
     q.copy_(torch.from_numpy(oq))
     sc.copy_(torch.from_numpy(osc))
     y = empty_bf16(o)
-    be.gemv_e4m3(dev(x), q, sc, y)
+    be.gemv_e4m3(dev(x), be.pack_e4m3(q), sc, y)
     mine = host(y)
     ref = oracle.gemv(x, deq_bf)
     assert_bf16_close(mine, ref, rtol=1e-2, atol=1e-3 * np.sqrt(i), min_exact=0.9)
