@@ -76,6 +76,10 @@ Q3_API int q3_quantize_e4m3(const uint16_t* w_dev, size_t rows, size_t full_cols
  * [n_out, n_in] into it (q3_e4m3_packed_bytes(n_out, n_in) bytes, zero
  * padding included); n_in % 64 == 0. */
 Q3_API size_t q3_e4m3_packed_bytes(size_t n_out, size_t n_in);
+/* Byte offset of weight (row, col) in that layout for a device with num_sms
+ * SMs (what q3_pack_e4m3 does on the device, for hosts that pack
+ * pre-quantized weights themselves); SIZE_MAX for invalid arguments. */
+Q3_API size_t q3_e4m3_packed_offset(size_t n_out, size_t n_in, int num_sms, size_t row, size_t col);
 Q3_API int q3_pack_e4m3(const uint8_t* q_dev, size_t n_out, size_t n_in, uint8_t* packed_dev, void* stream);
 Q3_API int q3_gemv_e4m3(const uint16_t* x_dev, const uint8_t* w8_dev, const float* scale_dev, uint16_t* y_dev,
                         size_t n_out, size_t n_in, void* stream);

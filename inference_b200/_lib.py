@@ -27,6 +27,7 @@ SIGNATURES = {
     "q3_quantize_e4m3": (C.c_int, [_u16p, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
     "q3_gemv_e4m3": (C.c_int, [_u16p, _vp, _vp, _u16p, _sz, _sz, _vp]),
     "q3_e4m3_packed_bytes": (_sz, [_sz, _sz]),
+    "q3_e4m3_packed_offset": (_sz, [_sz, _sz, C.c_int, _sz, _sz]),
     "q3_pack_e4m3": (C.c_int, [_vp, _sz, _sz, _vp, _vp]),
     "q3_rmsnorm": (C.c_int, [_u16p, _u16p, _u16p, _sz, C.c_float, _vp]),
     "q3_rmsnorm_add": (C.c_int, [_u16p, _u16p, _u16p, _u16p, _sz, C.c_float, _vp]),

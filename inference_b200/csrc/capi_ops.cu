@@ -114,6 +114,14 @@ size_t q3_e4m3_packed_bytes(size_t n_out, size_t n_in) {
     return f8_packed_bytes(static_cast<int>(n_out), static_cast<int>(n_in));
 }
 
+size_t q3_e4m3_packed_offset(size_t n_out, size_t n_in, int num_sms, size_t row, size_t col) {
+    if (n_out == 0 || n_in == 0 || n_in % 64 != 0 || n_in > 32768 || n_out >= (1u << 30) || num_sms <= 0 ||
+        row >= n_out || col >= n_in)
+        return SIZE_MAX;
+    const F8Pack L = f8_pack_for(static_cast<int>(n_out), static_cast<int>(n_in), EPI_STORE, num_sms);
+    return f8_offset(L, static_cast<int>(row), static_cast<int>(col));
+}
+
 int q3_pack_e4m3(const uint8_t* q, size_t n_out, size_t n_in, uint8_t* packed, void* stream) {
     Q3_CHECK(q && packed, "q3_pack_e4m3: null pointer");
     Q3_CHECK(n_out > 0 && n_in > 0 && n_in % 64 == 0, "q3_pack_e4m3: n_in must be a positive multiple of 64");

@@ -49,9 +49,6 @@ namespace {
 #ifndef Q3_GEMV_MIN_BLOCKS
 #define Q3_GEMV_MIN_BLOCKS 1
 #endif
-#ifndef Q3_GEMV_DYNAMIC
-#define Q3_GEMV_DYNAMIC 0
-#endif
 constexpr int kWarps = Q3_GEMV_WARPS;
 constexpr int kThreads = kWarps * 32;
 constexpr int kChunk = Q3_GEMV_CHUNK;   // BF16 columns per item (4 KB); FP8 items take twice the columns
@@ -191,10 +188,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& p = a.plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // PRO / EPI < 0: one kernel for every prologue and epilogue, chosen at run
-    // time by a.pro / a.epi (one code image for all the GEMVs of a step)
-    const int pro = PRO >= 0 ? PRO : a.pro;
-    const int epi = EPI >= 0 ? EPI : a.epi;
+    constexpr int pro = PRO, epi = EPI;
     const bool tracing = a.trace.buf != nullptr;
     unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_c2 = 0, tr_c3 = 0;
     if (tracing && tid == 0) {
@@ -646,16 +640,8 @@ __global__ void peer_keys_kernel(const PeerLinks x, unsigned long long* out, uin
 }
 
 template <int PRO, int EPI>
-cudaError_t launch_t(const GemvArgs& a0, cudaStream_t s, bool pdl) {
-#if Q3_GEMV_DYNAMIC
-    GemvArgs a = a0;
-    a.pro = PRO;
-    a.epi = EPI;
-    auto* fn = a.W8 ? gemv_kernel<-1, -1, true> : gemv_kernel<-1, -1, false>;
-#else
-    const GemvArgs& a = a0;
+cudaError_t launch_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
     auto* fn = a.W8 ? gemv_kernel<PRO, EPI, true> : gemv_kernel<PRO, EPI, false>;
-#endif
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.plan.grid);
     cfg.blockDim = dim3(kThreads);
@@ -705,9 +691,6 @@ cudaError_t configure_gemv_kernels() {
     Q3_CFG(PRO_RESID_NORM, EPI_SWIGLU)
     Q3_CFG(PRO_NORM, EPI_ARGMAX)
     Q3_CFG(PRO_RESID_NORM, EPI_ARGMAX)
-#if Q3_GEMV_DYNAMIC
-    Q3_CFG(-1, -1)
-#endif
 #undef Q3_CFG
     return e;
 }

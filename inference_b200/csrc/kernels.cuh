@@ -114,7 +114,6 @@ struct GemvArgs {
     // ---- errors
     uint32_t* err;
     LaunchTrace trace;
-    int pro, epi;  // the prologue / epilogue of the runtime-dispatched kernel
 };
 
 GemvPlan plan_gemv(int N, int K, int epi, int num_sms, int wb = 2);

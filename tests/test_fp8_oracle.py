@@ -100,3 +100,27 @@ def test_oracle_fp8_model_is_close_to_bf16(oracle):
     a.close()
     b.close()
 
+
+
+@pytest.mark.parametrize("n,k,sms", [(300, 320, 148), (37, 64, 4), (4096, 192, 148), (66, 512, 7)])
+def test_packed_fp8_layout_is_a_tiled_bijection(n, k, sms):
+    """q3_e4m3_packed_offset (the FP8 GEMV's weight layout, the same function
+    the device packer and quantizer use): every weight has its own byte inside
+    q3_e4m3_packed_bytes, column pairs stay adjacent, and each 16-row x
+    256-column tile of a CTA's row band is one contiguous run of rows x 256
+    bytes (one bulk copy)."""
+    from inference_b200 import lib
+
+    L = lib()
+    size = L.q3_e4m3_packed_bytes(n, k)
+    off = np.array([[L.q3_e4m3_packed_offset(n, k, sms, r, c) for c in range(k)] for r in range(n)], np.int64)
+    assert off.max() < size and off.min() >= 0
+    assert len(np.unique(off)) == n * k
+    assert (off[:, 1::2] == off[:, ::2] + 1).all()
+    # tiles: the 16-byte groups of one row segment of 256 columns sit in one
+    # 256-byte row of the tile, each tile's rows back to back
+    base = off[:, ::16] & ~255
+    for c0 in range(0, k, 256):
+        blk = base[:, c0 // 16:(c0 + 256) // 16]
+        assert (blk == blk[:, :1]).all()
+    assert L.q3_e4m3_packed_offset(n, k, sms, n, 0) == 2**64 - 1  # out of range
