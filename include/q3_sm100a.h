@@ -300,7 +300,7 @@ Q3_API size_t q3_engine_kv_bytes_per_position(q3_engine* e);
  * launches and algorithmic bytes. */
 Q3_API int q3_engine_profile_step(q3_engine* e, int kernel_class, double* ms, size_t* launches, double* bytes);
 
-/* Checkpoints (SURVEY next-step 1; the reference reads one safetensors file
+/* Checkpoints (the reference reads one safetensors file
  * whole, src/lib/model/safetensors.hpp:30-54): `path` is a .safetensors file,
  * a model.safetensors.index.json of a sharded checkpoint, or a directory
  * holding either.  Shards are memory-mapped and every BF16 tensor goes

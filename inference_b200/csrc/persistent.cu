@@ -244,7 +244,7 @@ struct Smem {
     float* part;       // per-(row, item) partial sums
     uint8_t* att;      // attention scratch
     float* red;        // 32 floats
-    uint32_t* flags;   // [0] barrier verdict, [1] last split
+    uint32_t* flags;   // [0] barrier outcome, [1] last split
     unsigned long long* key;
     Geom* geo;         // [PH_LM + 1]
     AttUnit* ast;      // this CTA's attention unit (fixed part)
