@@ -1,6 +1,7 @@
 """Tensor-parallel engine on 2 GPUs, teacher-forced against the oracle, with
 the partial sums exchanged by NCCL or through peer memory (CUDA IPC over
-NVLink, fused into the GEMVs).
+NVLink, fused into the GEMVs); one case with FP8 weights (against the
+oracle's FP8 model: row-parallel shards keep their full rows' scales).
 
 Each rank holds its head / MLP / vocabulary shard; the full logits are the
 concatenation of the ranks' vocabulary shards and must match the oracle's
@@ -58,9 +59,10 @@ def _rank_main(rank, world, port, name, out_dir, mode):
     qc = Qwen3Config(name, hidden=h, inter=inter, layers=layers, q_heads=qh, kv_heads=kvh, vocab=vocab,
                      tied=bool(tied))
     toks = g["tokens"].astype(np.uint32)
-    e = Engine(qc, capacity=cap, device=rank, tp_rank=rank, tp_size=world)
+    exchange, _, weights = mode.partition("-")  # "peer-fp8": peer exchange, FP8 weights
+    e = Engine(qc, capacity=cap, device=rank, tp_rank=rank, tp_size=world, weights=weights or "bf16")
     e.init_synthetic(0)
-    _attach(e, dist, mode, rank)
+    _attach(e, dist, exchange, rank)
     e.set_tokens(toks)
     shards = []
     for _ in toks:
@@ -77,7 +79,7 @@ def _rank_main(rank, world, port, name, out_dir, mode):
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("name,mode,world", [("qwen3_8b_l2", "peer", 2), ("qwen3_8b_l2", "nccl", 2),
                                              ("qwen3_0p6b", "peer", 2), ("qwen3_0p6b", "nccl", 2),
-                                             ("qwen3_8b_l2", "peer", 4)])
+                                             ("qwen3_8b_l2", "peer", 4), ("qwen3_0p6b", "peer-fp8", 2)])
 def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
     import torch
     import torch.multiprocessing as mp
@@ -94,6 +96,8 @@ def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
     g = dict(np.load(os.path.join(GOLD, f"model_{name}_ref_cpu.npz")))
     h, inter, layers, qh, kvh, hd, vocab, cap, tied = (int(v) for v in g["config"])
     om = oracle.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)), seed=0)
+    if mode.endswith("-fp8"):
+        om.quantize_fp8()  # row scales over full rows: the same model as the 1-GPU FP8 engine
     atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
     min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
     agree = 0
