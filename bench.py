@@ -48,8 +48,10 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--nccl", action="store_true", help="tensor parallel: exchange partial sums with NCCL "
                     "instead of peer-memory stores fused into the GEMVs")
-    ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path instead of the "
-                                                          "persistent kernel (the tensor-parallel path)")
+    ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path (the default) even "
+                                                          "where the persistent kernel was selected")
+    ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
+                    "batched_poll, no_grid_wait, deep_ring, live_prefetch, tp_prefill, or all")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
                     help="fp8: E4M3 GEMV matrices with per-row power-of-two scales (the FP8-weight model, "
                          "not the reference's BF16 model; the CUDA graph path)")
@@ -276,6 +278,11 @@ def main():
     eng.init_synthetic(0)
     if a.graph and eng.persistent:
         eng.persistent = False
+    tune = [t for t in a.tune.split(",") if t]
+    if tune:
+        eng.tuning = tune
+        if "all" in tune:
+            tune = sorted(ib.Engine.TUNE_FLAGS)
     if world > 1:
         if a.nccl:
             obj = [ib.Engine.nccl_unique_id() if rank == 0 else None]
@@ -374,7 +381,8 @@ def main():
     bf16_peak, bf16_kind = measured_bf16_peak()
     prefill = {"tokens": n_pre, "ms": round(pre_t, 3), "tok_s": round(n_pre / (pre_t / 1000.0), 1),
                "path": ("batched: tcgen05 GEMMs (TMEM accumulators, TMA), batched split-KV attention"
-                        if world == 1 and a.weights == "bf16" else "per-token decode steps"),
+                        + ("; row-parallel fp32 partials exchanged between ranks" if world > 1 else "")
+                        if a.weights == "bf16" and (world == 1 or "tp_prefill" in tune) else "per-token decode steps"),
                "tflops": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world, 1),
                "gemm_tflop": round(gemm_flop / 1e12, 3), "attention_tflop": round(attn_flop / 1e12, 3),
                "peak_tflops": bf16_peak, "frac": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world /
@@ -472,7 +480,7 @@ def main():
             "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
                        "decode_tokens_per_step": window, "global_batch": 1,
                        "decode_path": "persistent kernel" if eng.persistent else "CUDA graph of fused kernels",
-                       "parallelism": f"tp{world}", "weight_format": a.weights,
+                       "parallelism": f"tp{world}", "weight_format": a.weights, "tuning": tune,
                        "tp_exchange": (None if world == 1 else "NCCL allreduce/allgather" if a.nccl else
                                        "peer-memory stores fused into the o/down/lm_head GEMVs (CUDA IPC, NVLink)"), "weights": "random N(0,0.02) seed 0, ids seed 1",
                        "l2_flush": f"not needed: {cfg.weight_bytes(a.weights) / 1e9:.1f} GB of weights streamed per token "

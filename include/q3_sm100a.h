@@ -234,7 +234,9 @@ Q3_API int q3_engine_step(q3_engine* e, size_t n);
  * 512 tokens at a time instead of n decode steps -- and advances the
  * position by n.  No logits (the reference discards the prefill's).  The
  * tokens must have been given with q3_engine_set_tokens.  Tensor-parallel
- * engines run the n decode steps instead.  Asynchronous like step. */
+ * engines run the n decode steps instead unless Q3_TUNE_TP_PREFILL is set
+ * (q3_engine_set_tuning); FP8-weight engines always do.  Asynchronous like
+ * step. */
 Q3_API int q3_engine_prefill(q3_engine* e, size_t n);
 
 /* Blocks until queued steps finish; returns Q3_ERR_DEVICE if a kernel
@@ -258,13 +260,44 @@ Q3_API int q3_engine_generate(q3_engine* e, const uint32_t* prompt_host, size_t 
  * after one prefill. */
 Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
 
-/* Decode-step implementation: 1 (default on a single GPU when the model's
+/* Decode-step implementation: 0 (the default) replays the per-step CUDA
+ * graph of fused kernels; 1 (single GPU, BF16 weights, when the model's
  * shared-memory plan fits) runs n steps as one persistent cooperative kernel
  * (one CTA per SM streaming all weights through a TMA ring, grid barriers
- * between phases); 0 replays the per-step CUDA graph of fused kernels (the
- * tensor-parallel path).  Both produce the same tokens. */
+ * between phases).  Both produce the same tokens. */
 Q3_API int q3_engine_set_persistent(q3_engine* e, int enable);
 Q3_API int q3_engine_is_persistent(q3_engine* e);
+
+/* Opt-in variants of the CUDA-graph decode path (no counterpart in the
+ * reference), as bit flags; 0, the default, selects the kernels described
+ * above.  Every flag keeps the step's arithmetic and its order, so tokens
+ * and logits are bit-identical with and without it.  Setting them
+ * re-records the step graph at the next step.
+ *   Q3_TUNE_PEER_BATCHED_POLL: tensor parallel through peer memory -- the
+ *     RMSNorm prologue that sums the ranks' partial rows issues the loads of
+ *     up to four ranks at once instead of one rank per round trip;
+ *   Q3_TUNE_PEER_NO_GRID_WAIT: those prologues start on the (value, tag)
+ *     pairs alone, without griddepcontrol.wait on the producing GEMV;
+ *   Q3_TUNE_ATTN_DEEP_RING: decode attention keeps four K/V pages per CTA in
+ *     flight instead of two, where its grid (splits x kv heads x head blocks)
+ *     can be resident at one CTA per SM;
+ *   Q3_TUNE_ATTN_LIVE_PREFETCH: decode attention also fetches the page of the
+ *     current position before the dependency wait and patches that
+ *     position's V row in shared memory after it;
+ *   Q3_TUNE_TP_PREFILL: tensor-parallel engines prefill with the batched
+ *     tcgen05 GEMMs on their shards (row-parallel outputs exchanged as fp32
+ *     partials) instead of one decode step per prompt token.  Unlike the
+ *     other flags this changes the fp32 order of the prefill's sums (GEMM
+ *     instead of GEMV), exactly as the single-GPU batched prefill does.
+ * Unknown bits return Q3_ERR_INVALID. */
+#define Q3_TUNE_PEER_BATCHED_POLL 0x1u
+#define Q3_TUNE_PEER_NO_GRID_WAIT 0x2u
+#define Q3_TUNE_ATTN_DEEP_RING 0x4u
+#define Q3_TUNE_ATTN_LIVE_PREFETCH 0x8u
+#define Q3_TUNE_TP_PREFILL 0x10u
+#define Q3_TUNE_ALL 0x1Fu
+Q3_API int q3_engine_set_tuning(q3_engine* e, uint32_t flags);
+Q3_API int q3_engine_tuning(q3_engine* e, uint32_t* flags);
 
 /* Phase timeline (tracing).  Persistent kernel: with enable = 1 the next
  * launches record, for the first step of each launch, per CTA and phase
@@ -320,10 +353,11 @@ Q3_API int q3_safetensors_list(const char* path, char* out, size_t capacity, siz
  * the handles are shared by any means (the tests use torch.distributed), and
  * every rank attaches all of them, its own included, in rank order.  The
  * o_proj / down_proj GEMVs then store their fp32 partial rows straight into
- * every rank's buffer over NVLink and raise a flag; the next GEMV waits for
- * all flags (bounded; Q3_ERR_DEVICE "peer wait timed out" otherwise) and sums
- * the partials in rank order, so every rank holds the same bits.  The argmax
- * keys of lm_head travel the same way.  Replaces the two allreduces and the
+ * every rank's buffer over NVLink, each row as one 8-byte (value, tag) store;
+ * the next GEMV reads every rank's rows until all carry the exchange's tag
+ * (bounded; Q3_ERR_DEVICE "peer wait timed out" otherwise) and sums the
+ * partials in rank order, so every rank holds the same bits.  The argmax keys
+ * of lm_head travel with a flag per rank.  Replaces the two allreduces and the
  * allgather per layer that the NCCL path issues.  Requires peer access between
  * the GPUs (NVLink). */
 #define Q3_PEER_HANDLE_BYTES 64

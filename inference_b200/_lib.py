@@ -57,6 +57,8 @@ SIGNATURES = {
     "q3_engine_set_position": (C.c_int, [_vp, _sz]),
     "q3_engine_set_persistent": (C.c_int, [_vp, C.c_int]),
     "q3_engine_is_persistent": (C.c_int, [_vp]),
+    "q3_engine_set_tuning": (C.c_int, [_vp, C.c_uint32]),
+    "q3_engine_tuning": (C.c_int, [_vp, C.POINTER(C.c_uint32)]),
     "q3_engine_trace": (C.c_int, [_vp, C.c_int, _vp, _sz, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "q3_engine_position": (C.c_int, [_vp, C.POINTER(C.c_size_t)]),
     "q3_engine_logits": (C.c_int, [_vp, _u16p]),

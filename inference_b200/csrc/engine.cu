@@ -72,6 +72,10 @@ struct q3_engine {
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
     uint32_t *done_counter = nullptr, *err = nullptr;
     int attn_splits = 1;
+    // opt-in variants of the graph path (Q3_TUNE_*); attn_deep_fits: the decode
+    // attention grid is resident at one CTA per SM (Q3_TUNE_ATTN_DEEP_RING applies)
+    uint32_t tune = 0;
+    bool attn_deep_fits = false;
     // persistent decode kernel (one launch per run of steps)
     bool persistent = false;
     q3::PersistentArgs pargs{};
@@ -94,6 +98,10 @@ struct q3_engine {
     void* xpeer[q3::kMaxRanks] = {};
     q3::PeerLinks links{};
     bool peer_mode = false;
+    // tensor-parallel batched prefill (Q3_TUNE_TP_PREFILL): the partial-row slots
+    // and flags appended to xbuf, and the exchanges run so far (all ranks agree)
+    q3::TpExchange tpx{};
+    uint32_t tp_seq = 0;
     // graph / comms
     cudaGraphExec_t graph = nullptr;
     ncclComm_t comm = nullptr;
@@ -109,6 +117,24 @@ size_t engine_layers(const q3_engine* e) { return e->layers.size(); }
 
 namespace q3 {
 namespace {
+
+// Tensor-parallel exchange buffer, one per rank, shared by CUDA IPC:
+// decode pairs [2][world][H] u64 | flags [2][world] u32 | keys [2][world] u64 |
+// (256-aligned) prefill flags [2][kMaxRanks] u32 | (at +256) prefill partial
+// rows [2][rows][H] fp32.
+struct XbufLayout {
+    size_t flags_off, keys_off, pf_flags_off, pf_part_off, total;
+};
+XbufLayout xbuf_layout(size_t world, size_t H, size_t rows) {
+    XbufLayout L{};
+    L.flags_off = 2 * world * H * 8;
+    L.keys_off = (L.flags_off + 2 * world * 4 + 15) / 16 * 16;
+    L.pf_flags_off = (L.keys_off + 2 * world * 8 + 255) / 256 * 256;
+    L.pf_part_off = L.pf_flags_off + 256;
+    L.total = L.pf_part_off + 2 * rows * H * 4;
+    return L;
+}
+constexpr int kPrefillRows = 512;  // tokens per batched-prefill chunk
 
 int dalloc(q3_engine* e, void** p, size_t bytes) {
     if (bytes == 0) bytes = 16;
@@ -170,6 +196,7 @@ struct Recorder {
 GemvArgs base_args(q3_engine* e) {
     GemvArgs a{};
     if (e->peer_mode) a.peer = e->links;
+    a.tune = e->tune;
     a.eps = e->cfg.eps;
     a.err = e->err;
     a.capacity = static_cast<int>(e->cfg.capacity);
@@ -224,6 +251,8 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.rope_cos = e->rope_cos;
     a.rope_sin = e->rope_sin;
     a.eps = e->cfg.eps;
+    a.stages = ((e->tune & Q3_TUNE_ATTN_DEEP_RING) && e->attn_deep_fits) ? 4 : 2;
+    a.live_prefetch = (e->tune & Q3_TUNE_ATTN_LIVE_PREFETCH) ? 1 : 0;
     a.trace = r.trace();
     r.mark(true, 1);
     cudaError_t st = launch_attention(a, e->stream, r.pdl);
@@ -547,8 +576,13 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->vsum, H)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->partial, H)) != Q3_OK) return bail(rc);
     if (tp_size > 1) {
-        // exchange buffer: pairs [2][world][H] u64 | flags [2][world] u32 | keys [2][world] u64
-        e->xbuf_bytes = (2 * static_cast<size_t>(tp_size) * H * 8 + 2 * tp_size * 4 + 15) / 16 * 16 + 2 * tp_size * 8;
+        // exchange buffer (xbuf_layout): decode pairs, flags and keys, then the prefill slots
+        const size_t pf_rows = std::min<size_t>(kPrefillRows, c.capacity);
+        const XbufLayout xl = xbuf_layout(static_cast<size_t>(tp_size), static_cast<size_t>(H), pf_rows);
+        e->xbuf_bytes = xl.total;
+        e->tpx.slot_floats = pf_rows * static_cast<size_t>(H);
+        e->tpx.rank = tp_rank;
+        e->tpx.world = tp_size;
         if ((rc = dalloc(e, &e->xbuf, e->xbuf_bytes)) != Q3_OK) return bail(rc);
         cudaMemset(e->xbuf, 0, e->xbuf_bytes);
         unsigned long long* seq = nullptr;
@@ -581,6 +615,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
+    e->attn_deep_fits = attn_deep_ring_fits(e->qh, e->kvh, e->attn_splits, e->sms);
 
     // ---- persistent decode kernel (single GPU, BF16 weights)
     if (tp_size == 1 && !e->fp8) {
@@ -984,14 +1019,16 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
     Q3_CHECK(p0 + n <= e->host_forced, "q3_engine_prefill: tokens not set (set_tokens first)");
     if (p0 + n >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "q3_engine_prefill: KV cache capacity exceeded");
     Q3_CUDA(cudaSetDevice(e->device));
-    if (e->world > 1 || e->fp8) {
-        // tensor-parallel and FP8-weight engines prefill through the per-token decode step
+    const bool tp = e->world > 1;
+    if (e->fp8 || (tp && !((e->tune & Q3_TUNE_TP_PREFILL) && (e->peer_mode || e->comm)))) {
+        // FP8-weight engines, and tensor-parallel ones unless Q3_TUNE_TP_PREFILL is set,
+        // prefill through the per-token decode step
         return q3_engine_step(e, n);
     }
     const int H = e->H, qd = e->qd, kd = e->kd, il = e->il;
     const int ldqkv = qd + 2 * kd;
     if (!e->prefill_rows) {
-        const int rows = static_cast<int>(std::min<size_t>(512, e->cfg.capacity));
+        const int rows = static_cast<int>(std::min<size_t>(kPrefillRows, e->cfg.capacity));
         int rc;
         if ((rc = dalloc_t(e, &e->px, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
         if ((rc = dalloc_t(e, &e->pxn, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
@@ -1018,6 +1055,46 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
         g.bn = gemm_tile_n(m, nn, e->sms);
         g.err = e->err;
         return launch_gemm(g, s);
+    };
+    // Tensor parallel: the row-parallel GEMMs (o_proj, down_proj) write fp32 partial
+    // rows (GEMM_F32) into this rank's slot, and every rank adds the sum over all
+    // ranks' slots, in rank order, to its replicated residual rows (peer memory:
+    // flags + reads over NVLink; NCCL: an allreduce of the slot, then the same add).
+    float* pf_mine = nullptr;
+    TpExchange xnccl{};
+    if (tp) {
+        const XbufLayout xl = xbuf_layout(static_cast<size_t>(e->world), static_cast<size_t>(H),
+                                          e->tpx.slot_floats / static_cast<size_t>(H));
+        pf_mine = reinterpret_cast<float*>(static_cast<uint8_t*>(e->xbuf) + xl.pf_part_off);
+        xnccl.part[0] = pf_mine;
+        xnccl.slot_floats = e->tpx.slot_floats;
+        xnccl.rank = 0;
+        xnccl.world = 1;
+    }
+    auto tp_partial = [&](const bf16* x, const bf16* w, int m, int k, float* vs) -> int {
+        const uint32_t seq = ++e->tp_seq;
+        float* slot = pf_mine + (seq & 1u) * e->tpx.slot_floats;
+        GemmArgs g{};
+        g.x = x;
+        g.w = w;
+        g.yf = slot;
+        g.M = m;
+        g.N = H;
+        g.K = k;
+        g.ldy = H;
+        g.epi = GEMM_F32;
+        g.bn = gemm_tile_n(m, H, e->sms);
+        g.err = e->err;
+        Q3_CUDA(launch_gemm(g, s));
+        if (e->peer_mode) {
+            Q3_CUDA(launch_tp_signal(e->tpx, seq, s));
+            Q3_CUDA(launch_tp_resid_rows(e->tpx, seq, m, H, e->px, vs, e->err, e->sms, s));
+        } else {
+            ncclResult_t nr = nccl().AllReduce(slot, slot, static_cast<size_t>(m) * H, ncclFloat32, ncclSum, e->comm, s);
+            if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().GetErrorString(nr));
+            Q3_CUDA(launch_tp_resid_rows(xnccl, seq, m, H, e->px, vs, e->err, e->sms, s));
+        }
+        return Q3_OK;
     };
     for (size_t done = 0; done < n;) {
         const int t = static_cast<int>(std::min<size_t>(n - done, static_cast<size_t>(e->prefill_rows)));
@@ -1062,10 +1139,16 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
             aa.out_stride = qd;
             Q3_CUDA(launch_attention(aa, s, false));
             if (l == L - 1) break;
-            Q3_CUDA(gemm(e->pattn, W.w_o, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
+            if (tp)
+                Q3_TRY(tp_partial(e->pattn, W.w_o, t, qd, e->pvsum));
+            else
+                Q3_CUDA(gemm(e->pattn, W.w_o, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
             Q3_CUDA(launch_rmsnorm_rows(e->px, e->pvsum, W.post_norm, e->pxn, t, H, eps, s));
             Q3_CUDA(gemm(e->pxn, W.w_gu, e->pg, nullptr, t, 2 * il, H, il, GEMM_SWIGLU));
-            Q3_CUDA(gemm(e->pg, W.w_down, e->px, nullptr, t, H, il, H, GEMM_RESID));
+            if (tp)
+                Q3_TRY(tp_partial(e->pg, W.w_down, t, il, nullptr));
+            else
+                Q3_CUDA(gemm(e->pg, W.w_down, e->px, nullptr, t, H, il, H, GEMM_RESID));
         }
         done += static_cast<size_t>(t);
     }
@@ -1189,6 +1272,27 @@ int q3_engine_set_persistent(q3_engine* e, int enable) {
 }
 
 int q3_engine_is_persistent(q3_engine* e) { return (e && e->persistent) ? 1 : 0; }
+
+int q3_engine_set_tuning(q3_engine* e, uint32_t flags) {
+    Q3_CHECK(e, "null engine");
+    Q3_CHECK((flags & ~Q3_TUNE_ALL) == 0u, "q3_engine_set_tuning: unknown flag bits");
+    if (flags == e->tune) return Q3_OK;
+    Q3_CUDA(cudaSetDevice(e->device));
+    if (e->graph) {
+        // the step graph holds the launch arguments: record it again at the next step
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_CUDA(cudaGraphExecDestroy(e->graph));
+        e->graph = nullptr;
+    }
+    e->tune = flags;
+    return Q3_OK;
+}
+
+int q3_engine_tuning(q3_engine* e, uint32_t* flags) {
+    Q3_CHECK(e && flags, "q3_engine_tuning: null argument");
+    *flags = e->tune;
+    return Q3_OK;
+}
 
 namespace {
 
@@ -1388,7 +1492,8 @@ int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n) {
     Q3_CHECK(!e->peer_mode, "q3_engine_attach_peers: already attached");
     Q3_CUDA(cudaSetDevice(e->device));
     const size_t H = static_cast<size_t>(e->H), W = static_cast<size_t>(e->world);
-    const size_t flags_off = 2 * W * H * 8, keys_off = (flags_off + 2 * W * 4 + 15) / 16 * 16;
+    const XbufLayout xl = xbuf_layout(W, H, e->tpx.slot_floats / H);
+    const size_t flags_off = xl.flags_off, keys_off = xl.keys_off;
     for (int j = 0; j < e->world; ++j) {
         void* base = nullptr;
         if (j == e->rank) {
@@ -1403,6 +1508,8 @@ int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n) {
         e->links.recv[j] = static_cast<unsigned long long*>(base);
         e->links.flags[j] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(base) + flags_off);
         e->links.keys[j] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(base) + keys_off);
+        e->tpx.part[j] = reinterpret_cast<const float*>(static_cast<uint8_t*>(base) + xl.pf_part_off);
+        e->tpx.flags[j] = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(base) + xl.pf_flags_off);
     }
     e->peer_mode = true;
     if (e->graph) {

@@ -212,6 +212,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(r[1]))) << 16);
                     }
                     *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(row) * a.ldy + n / 2) = o;
+                } else if constexpr (EPI == GEMM_F32) {
+                    // a row-parallel shard's partial: summed over the ranks, then rounded once
+                    float4* dst = reinterpret_cast<float4*>(a.yf + static_cast<size_t>(row) * a.ldy + n);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 } else {
                     // residual: hs = bf16(hs + bf16(acc)) (qwen3.hpp:151-152, 158-159); the fp32
                     // sums feed the next rmsnorm_add (rmsnorm.cuh:58-60)
@@ -294,6 +299,7 @@ int gemm_tile_n(int M, int N, int sms) {
 
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     if (a.M <= 0 || a.N % 128 || a.K % kBK || a.K <= 0) return cudaErrorInvalidValue;
+    if (a.epi == GEMM_F32 && (!a.yf || a.ldy % 4 != 0 || a.ldy < a.N)) return cudaErrorInvalidValue;
     const int BN = a.bn ? a.bn : gemm_tile_n(a.M, a.N, 148);
     if (BN != 128 && BN != 256) return cudaErrorInvalidValue;
     if (a.N % BN) return cudaErrorInvalidValue;
@@ -306,6 +312,8 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
         case GEMM_SWIGLU * 2 + 1: return launch_bn<256, GEMM_SWIGLU>(a, tx, tw, s);
         case GEMM_RESID * 2: return launch_bn<128, GEMM_RESID>(a, tx, tw, s);
         case GEMM_RESID * 2 + 1: return launch_bn<256, GEMM_RESID>(a, tx, tw, s);
+        case GEMM_F32 * 2: return launch_bn<128, GEMM_F32>(a, tx, tw, s);
+        case GEMM_F32 * 2 + 1: return launch_bn<256, GEMM_F32>(a, tx, tw, s);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -111,6 +111,7 @@ struct GemvArgs {
     // 1 .. 2 L within a step (o_proj of layer l: 2 l + 1, down_proj: 2 l + 2)
     PeerLinks peer;
     int xtag;
+    uint32_t tune;             // Q3_TUNE_PEER_* bits (q3_engine_set_tuning)
     // ---- errors
     uint32_t* err;
     LaunchTrace trace;
@@ -147,8 +148,19 @@ struct AttnArgs {
     const float* rope_cos;
     const float* rope_sin;
     float eps;
+    // Opt-in variants (q3_engine_set_tuning): stages = K/V pages in flight per
+    // CTA, 2 (0 = 2) or 4 -- 4 only where attn_deep_ring_fits says the grid is
+    // resident at one CTA per SM; live_prefetch (fused single-query decode on
+    // the paged layout only): the page of the current position is fetched
+    // before griddepcontrol.wait like the older ones, and the position's V row
+    // (written by the QKV GEMV) is read after it and patched into the tile.
+    int stages;
+    int live_prefetch;
     LaunchTrace trace;
 };
+// Whether the decode grid (splits x kv_heads x query-head blocks, one cluster of
+// `splits` per kv head and block) can be resident with four pages per CTA.
+bool attn_deep_ring_fits(int q_heads, int kv_heads, int splits, int num_sms);
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
@@ -209,12 +221,13 @@ bool plan_persistent(PersistentArgs& a, int sms, size_t smem_limit);
 cudaError_t launch_persistent(const PersistentArgs& a, cudaStream_t s);
 
 // ---------------------------------------------------------------- prefill GEMM (tcgen05)
-enum GemmEpi : int { GEMM_STORE = 0, GEMM_SWIGLU = 1, GEMM_RESID = 2 };
+enum GemmEpi : int { GEMM_STORE = 0, GEMM_SWIGLU = 1, GEMM_RESID = 2, GEMM_F32 = 3 };
 struct GemmArgs {
     const bf16* x;  // [M, K] row-major (tokens)
     const bf16* w;  // [N, K] row-major (weights as stored)
     bf16* y;        // STORE: [M, ldy] <- XW^T; SWIGLU: [M, ldy] <- swiglu of column pairs; RESID: [M, ldy] += XW^T
     float* vsum;    // RESID only (optional): [M, ldy] fp32 sums before rounding
+    float* yf;      // F32 only: [M, ldy] <- XW^T unrounded (a tensor-parallel partial)
     int M, N, K, ldy;
     int epi;        // GemmEpi
     int bn;         // output tile width 128 / 256, 0 = choose
@@ -239,6 +252,25 @@ cudaError_t launch_embed_rows(const bf16* table, const int32_t* tokens, int p0, 
 cudaError_t launch_rmsnorm_rows(const bf16* x, const float* vsum, const bf16* w, bf16* xn, int n, int H, float eps,
                                 cudaStream_t s);
 cudaError_t launch_qkv_rows(const PrefillQkvArgs& a, int n, cudaStream_t s);
+
+// Tensor-parallel prefill exchange.  Every rank's GEMM (GEMM_F32) writes its
+// fp32 partial rows into slot (seq & 1) of its own buffer (part[rank], slots
+// slot_floats apart), raises flags[j][slot * kMaxRanks + rank] = seq in every
+// rank's buffer (launch_tp_signal), and every rank adds the sum over all ranks'
+// slots, in rank order, to its residual rows (launch_tp_resid_rows; part[j] of
+// a peer is its CUDA IPC mapping).  flags[rank] == null: no flags to wait for
+// (world 1: a buffer NCCL has already allreduced).  A rank overwrites a slot
+// two exchanges later, after every rank raised its flag for the exchange in
+// between, which it does only after reading the slot.
+struct TpExchange {
+    const float* part[kMaxRanks];
+    uint32_t* flags[kMaxRanks];
+    size_t slot_floats;
+    int rank, world;
+};
+cudaError_t launch_tp_signal(const TpExchange& x, uint32_t seq, cudaStream_t s);
+cudaError_t launch_tp_resid_rows(const TpExchange& x, uint32_t seq, int n, int H, bf16* xr, float* vsum, uint32_t* err,
+                                 int num_sms, cudaStream_t s);
 
 // ---------------------------------------------------------------- small ops
 cudaError_t launch_embedding(const bf16* table, int hidden, uint32_t token, bf16* out, cudaStream_t s);

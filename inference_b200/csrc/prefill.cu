@@ -115,7 +115,87 @@ __global__ void __launch_bounds__(kRowThreads) qkv_rows_kernel(PrefillQkvArgs a)
     }
 }
 
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// This rank's partial rows of exchange `seq` (written by the GEMM launched just
+// before on the same stream, so complete) are ready: raise the flag in every
+// rank's buffer after a system-scope fence.
+__global__ void tp_signal_kernel(TpExchange x, uint32_t seq) {
+    if (threadIdx.x != 0) return;
+    __threadfence_system();
+    const int slot = static_cast<int>(seq & 1u);
+    for (int j = 0; j < x.world; ++j)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(x.flags[j] + slot * kMaxRanks + x.rank), "r"(seq)
+                     : "memory");
+}
+
+// Residual update with the sum of every rank's partial rows, in rank order (the
+// same bits on every rank): v = x + bf16(sum); x = bf16(v); vsum = v (the
+// unrounded sums the next rmsnorm_add squares, rmsnorm.cuh:58-60).  With flags,
+// first waits (bounded) until every rank raised its flag for `seq`.
+__global__ void __launch_bounds__(kRowThreads) tp_resid_rows_kernel(TpExchange x, uint32_t seq, size_t n4, bf16* xr,
+                                                                  float* vsum, uint32_t* err) {
+    const int slot = static_cast<int>(seq & 1u);
+    if (x.flags[x.rank]) {
+        if (threadIdx.x < static_cast<unsigned>(x.world)) {
+            const uint32_t* f = x.flags[x.rank] + slot * kMaxRanks + threadIdx.x;
+            for (uint32_t polls = 0; ld_acquire_sys_u32(f) != seq; ++polls) {
+                if ((polls & 1023) == 1023 && *reinterpret_cast<volatile uint32_t*>(err)) break;
+                if (polls > (1u << 22)) {
+                    record_error(err, DEV_PEER_WAIT_TIMEOUT);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __syncthreads();
+    }
+    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        float4 p[kMaxRanks];
+#pragma unroll
+        for (int j = 0; j < kMaxRanks; ++j)
+            if (j < x.world) p[j] = __ldcg(reinterpret_cast<const float4*>(x.part[j] + slot * x.slot_floats) + i);
+        float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < kMaxRanks; ++j)
+            if (j < x.world) {
+                t.x += p[j].x;
+                t.y += p[j].y;
+                t.z += p[j].z;
+                t.w += p[j].w;
+            }
+        uint2 h = reinterpret_cast<const uint2*>(xr)[i];
+        const float v0 = bf_lo(h.x) + round_bf(t.x), v1 = bf_hi(h.x) + round_bf(t.y);
+        const float v2 = bf_lo(h.y) + round_bf(t.z), v3 = bf_hi(h.y) + round_bf(t.w);
+        h.x = static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(v0))) | (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(v1))) << 16);
+        h.y = static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(v2))) | (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(v3))) << 16);
+        reinterpret_cast<uint2*>(xr)[i] = h;
+        if (vsum) reinterpret_cast<float4*>(vsum)[i] = make_float4(v0, v1, v2, v3);
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_tp_signal(const TpExchange& x, uint32_t seq, cudaStream_t s) {
+    tp_signal_kernel<<<1, 32, 0, s>>>(x, seq);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_tp_resid_rows(const TpExchange& x, uint32_t seq, int n, int H, bf16* xr, float* vsum, uint32_t* err,
+                                 int num_sms, cudaStream_t s) {
+    if (x.world < 1 || x.world > kMaxRanks || H % 4 != 0 || n <= 0) return cudaErrorInvalidValue;
+    if (static_cast<size_t>(n) * H > x.slot_floats) return cudaErrorInvalidValue;
+    const size_t n4 = static_cast<size_t>(n) * H / 4;
+    const size_t want = (n4 + kRowThreads - 1) / kRowThreads;
+    const int grid = static_cast<int>(want < static_cast<size_t>(num_sms) * 8 ? want : static_cast<size_t>(num_sms) * 8);
+    tp_resid_rows_kernel<<<grid, kRowThreads, 0, s>>>(x, seq, n4, xr, vsum, err);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_embed_rows(const bf16* table, const int32_t* tokens, int p0, int n, int vocab, int H, bf16* x,
                               uint32_t* err, cudaStream_t s) {

@@ -133,6 +133,31 @@ class Engine:
     def persistent(self, on: bool):
         check(lib().q3_engine_set_persistent(self.h, int(bool(on))))
 
+    # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
+    TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2, "deep_ring": 0x4, "live_prefetch": 0x8,
+                  "tp_prefill": 0x10}
+
+    @property
+    def tuning(self) -> int:
+        f = C.c_uint32()
+        check(lib().q3_engine_tuning(self.h, C.byref(f)))
+        return int(f.value)
+
+    @tuning.setter
+    def tuning(self, flags):
+        """An int of Q3_TUNE_* bits, or an iterable of TUNE_FLAGS names ("all" = every flag)."""
+        if not isinstance(flags, int):
+            names = list(flags)
+            if "all" in names:
+                names = list(self.TUNE_FLAGS)
+            bad = [n for n in names if n not in self.TUNE_FLAGS]
+            if bad:
+                raise ValueError(f"unknown tuning flag(s) {bad}; choose from {sorted(self.TUNE_FLAGS)} or 'all'")
+            flags = 0
+            for n in names:
+                flags |= self.TUNE_FLAGS[n]
+        check(lib().q3_engine_set_tuning(self.h, int(flags)))
+
     def trace(self, enable: bool = True):
         """Turn the phase timeline on/off (persistent kernel or CUDA-graph path)."""
         ph, ct = C.c_size_t(), C.c_size_t()

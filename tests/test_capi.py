@@ -46,6 +46,9 @@ def test_invalid_arguments_fail_before_the_gpu():
     odd = ModelConfig(1024, 3072, 28, 16, 8, 128, 151936, 1, 1e-6, 1e6, 64, 0)
     assert L.q3_engine_create(C.byref(odd), 0, 0, 3, C.byref(h)) == 1  # 8 kv heads over 3 ranks
     assert L.q3_gemv_e4m3(x, x, x, x, 4, 24, None) == 1  # n_in % 16
+    assert L.q3_engine_set_tuning(None, 0) == 1  # null engine
+    flags = C.c_uint32(7)
+    assert L.q3_engine_tuning(None, C.byref(flags)) == 1 and flags.value == 7
     assert L.q3_quantize_e4m3(x, 4, 64, 32, 48, x, x, None) == 1  # columns past the row
     assert L.q3_quantize_e4m3(x, 4, 64, 1, 8, x, x, None) == 1  # odd first column
     fmt = ModelConfig(1024, 3072, 28, 16, 8, 128, 151936, 1, 1e-6, 1e6, 64, 0, 7)

@@ -1,0 +1,206 @@
+"""Opt-in variants of the decode path (q3_engine_set_tuning).
+
+The decode variants reorder no arithmetic, so every logit, argmax and KV slot
+must be bit-identical to the default kernels:
+  * attention with a four-page ring and the live page fetched before the
+    dependency wait, at positions from 0 to the end of an 8192-slot cache
+    (every page boundary the windows cross, up to 8 pages per split);
+  * on 2 GPUs, the peer-exchange prologue with batched rank reads and without
+    the grid-dependency wait, together with the attention variants.
+The tensor-parallel batched prefill changes the fp32 order of the prefill's
+sums (GEMMs instead of GEMVs, as the single-GPU prefill does), so it is held to
+the oracle like test_gpu_prefill.py: KV slots of the prefilled positions and
+the teacher-forced logits of the decode steps after it.
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from gpu_util import assert_logits_close, bf
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+DECODE_FLAGS = 0x1 | 0x2 | 0x4 | 0x8  # batched_poll | no_grid_wait | deep_ring | live_prefetch
+TP_PREFILL = 0x10
+
+
+def _cos(a, b):
+    a = bf(a).astype(np.float64).ravel()
+    b = bf(b).astype(np.float64).ravel()
+    return a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30)
+
+
+@pytest.mark.parametrize("kv_heads,q_heads", [(2, 8), (8, 16)])
+def test_attention_variants_bit_identical(kv_heads, q_heads):
+    from inference_b200 import Engine, Qwen3Config, prompt_ids
+
+    cfg = Qwen3Config(f"gqa{q_heads // kv_heads}-kv{kv_heads}-l2", hidden=1024, inter=3072, layers=2,
+                      q_heads=q_heads, kv_heads=kv_heads, vocab=151936, tied=True)
+    cap = 8192
+    ids = prompt_ids(cap, seed=1)
+    runs = {}
+    for flags in (0, DECODE_FLAGS):
+        logits, kv = [], []
+        with Engine(cfg, capacity=cap) as e:
+            e.init_synthetic(0)
+            e.tuning = flags
+            assert e.tuning == flags
+            e.set_tokens(ids)
+
+            def window(n):
+                for _ in range(n):
+                    p = e.position
+                    e.step(1)
+                    e.sync()
+                    logits.append(e.logits())
+                    kv.append(e.kv_slot(1, p))
+
+            window(70)         # positions 0..69: the first two pages, the live page the only one
+            e.fill_kv(4090)    # synthetic cache: 64 pages, 4 per split
+            window(10)         # 4090..4099 crosses the page boundary at 4096
+            e.fill_kv(8180)
+            window(11)         # 8180..8190: 128 pages, 8 per split (ring refills in both depths)
+            hist = e.argmax_history(8191)
+        runs[flags] = (logits, kv, hist)
+    base, tuned = runs[0], runs[DECODE_FLAGS]
+    for i, (a, b) in enumerate(zip(base[0], tuned[0])):
+        assert np.array_equal(a, b), f"step {i}: logits differ"
+    for i, ((k0, v0), (k1, v1)) in enumerate(zip(base[1], tuned[1])):
+        assert np.array_equal(k0, k1) and np.array_equal(v0, v1), f"step {i}: KV slot differs"
+    assert np.array_equal(base[2], tuned[2])
+
+
+def test_tuning_rejects_unknown_bits():
+    from inference_b200 import Engine, Q3Error, Qwen3Config
+
+    cfg = Qwen3Config("qwen3-0.6b-l1", hidden=1024, inter=3072, layers=1, q_heads=16, kv_heads=8, vocab=151936,
+                      tied=True)
+    with Engine(cfg, capacity=64) as e:
+        with pytest.raises(Q3Error):
+            e.tuning = 0x100
+        with pytest.raises(ValueError):
+            e.tuning = ["no_such_flag"]
+        e.tuning = ["all"]
+        assert e.tuning == 0x1F
+        e.tuning = 0
+        assert e.tuning == 0
+
+
+# ---------------------------------------------------------------- 2 GPUs
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _tp_main(rank, world, port, name, out_dir, mode, flags, n_pre):
+    import torch
+    import torch.distributed as dist
+
+    from inference_b200 import Engine, Qwen3Config
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    g = dict(np.load(os.path.join(GOLD, f"model_{name}_ref_cpu.npz")))
+    h, inter, layers, qh, kvh, hd, vocab, cap, tied = (int(v) for v in g["config"])
+    qc = Qwen3Config(name, hidden=h, inter=inter, layers=layers, q_heads=qh, kv_heads=kvh, vocab=vocab,
+                     tied=bool(tied))
+    toks = g["tokens"].astype(np.uint32)
+    e = Engine(qc, capacity=cap, device=rank, tp_rank=rank, tp_size=world)
+    e.init_synthetic(0)
+    e.tuning = flags
+    if mode == "peer":
+        hs = [None] * world
+        dist.all_gather_object(hs, e.peer_handle())
+        dist.barrier()  # every rank's buffer exists and is zeroed before anyone writes
+        e.attach_peers(hs)
+    else:
+        obj = [Engine.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        e.attach_nccl(obj[0])
+    e.set_tokens(toks)
+    if n_pre:
+        e.prefill(n_pre)
+        e.sync()
+    logits = []
+    for _ in range(len(toks) - n_pre):
+        e.step(1)
+        e.sync()
+        logits.append(e.logits())
+    kv = {f"k{lay}_{p}": e.kv_slot(int(lay), p)[0] for lay in g["kv_layers"] for p in range(len(toks))}
+    kv.update({f"v{lay}_{p}": e.kv_slot(int(lay), p)[1] for lay in g["kv_layers"] for p in range(len(toks))})
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=np.stack(logits), hist=e.argmax_history(len(toks)),
+             **kv)
+    e.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _run_tp(tmp_path, tag, name, mode, flags, n_pre, world=2):
+    import torch.multiprocessing as mp
+
+    out = tmp_path / tag
+    out.mkdir()
+    mp.start_processes(_tp_main, args=(world, _free_port(), name, str(out), mode, flags, n_pre), nprocs=world,
+                       start_method="spawn")
+    return [dict(np.load(out / f"rank{r}.npz")) for r in range(world)]
+
+
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("name", ["qwen3_0p6b", "qwen3_8b_l2"])
+def test_tp_decode_variants_bit_identical(tmp_path, name):
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    base = _run_tp(tmp_path, "base", name, "peer", 0, 0)
+    tuned = _run_tp(tmp_path, "tuned", name, "peer", DECODE_FLAGS, 0)
+    for r in range(2):
+        for key in base[r]:
+            assert np.array_equal(base[r][key], tuned[r][key]), (r, key)
+
+
+@pytest.mark.timeout(600)
+@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("name", ["qwen3_0p6b", "qwen3_8b_l2"])
+def test_tp_prefill_matches_oracle(tmp_path, oracle, name, mode):
+    import torch
+
+    from oracle import ModelConfig
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    g = dict(np.load(os.path.join(GOLD, f"model_{name}_ref_cpu.npz")))
+    h, inter, layers, qh, kvh, hd, vocab, cap, tied = (int(v) for v in g["config"])
+    toks = g["tokens"]
+    n = len(toks)
+    n_pre = n - n // 3
+    parts = _run_tp(tmp_path, "pf", name, mode, TP_PREFILL, n_pre, world)
+    om = oracle.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)), seed=0)
+    kl = kvh // world
+    for i in range(n_pre):
+        om.forward(int(toks[i]))
+        for lay in g["kv_layers"]:
+            ok_, ov_ = om.kv_slot(int(lay), i)
+            for r in range(world):
+                k, v = parts[r][f"k{lay}_{i}"], parts[r][f"v{lay}_{i}"]
+                assert _cos(k, ok_[r * kl:(r + 1) * kl]) >= 0.9995, (i, int(lay), r)
+                assert _cos(v, ov_[r * kl:(r + 1) * kl]) >= 0.9995, (i, int(lay), r)
+    atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
+    min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
+    agree = 0
+    for j, i in enumerate(range(n_pre, n)):
+        nxt = om.forward(int(toks[i]))
+        full = np.concatenate([parts[r]["logits"][j] for r in range(world)])
+        assert_logits_close(full, om.logits(), atol=atol, n_ulp=1, min_cos=min_cos)
+        agree += int(int(np.argmax(bf(full))) == nxt)
+    om.close()
+    assert agree >= (n - n_pre) - 1
