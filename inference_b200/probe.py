@@ -4,7 +4,8 @@
     python -m inference_b200.probe attention  # decode attention
     python -m inference_b200.probe gemv8      # FP8-weight GEMV
     python -m inference_b200.probe decode [workload] [position] [steps]
-    python -m inference_b200.probe timeline [workload] [position]
+    python -m inference_b200.probe timeline [workload] [position] [tune=a,b] [nccl]
+    python -m torch.distributed.run --nproc-per-node N -m inference_b200.probe timeline ...
 
 Default: three launches of the decode GEMV (q3_gemv, Qwen3-8B gate/up shape:
 24576 x 4096, 201 MB of weights) followed by three launches of the prefill
@@ -21,6 +22,9 @@ attn_kernel launches of the process are those of the steps.
 decode step at `position`, summarised per launch kind over layers 1..L-1:
 CTA start to dependency release, prologue, main loop, epilogue (medians over
 CTAs, microseconds) and each launch's span from the previous launch's end.
+Under torchrun the engine is tensor-parallel over the ranks (peer-memory
+exchange, or NCCL with `nccl`) and every rank's summary is printed;
+`tune=` applies q3_engine_set_tuning flags by name.
 """
 import torch
 
@@ -86,7 +90,27 @@ def decode(workload="qwen3-0.6b-ctx1024", pos="520", steps="3"):
     print("ok")
 
 
-def timeline(workload="qwen3-0.6b-ctx1024", pos="520"):
+def _tp_setup():
+    """Under torchrun (WORLD_SIZE > 1): this rank's (rank, world, local device) and an
+    initialised NCCL process group; (0, 1, 0, None) otherwise."""
+    import datetime
+    import os
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1:
+        return 0, 1, 0, None
+    import torch.distributed as dist
+
+    rank, local = int(os.environ["RANK"]), int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return rank, world, local, dist
+
+
+def timeline(workload="qwen3-0.6b-ctx1024", pos="520", *opts):
+    """opts: tune=a,b (q3_engine_set_tuning names) and, under torchrun, nccl (the NCCL
+    exchange instead of peer memory).  Each rank traces its own GPU (%globaltimer is
+    per GPU); rank 0 prints every rank's summary in rank order."""
     import numpy as np
 
     from .backend import prompt_ids
@@ -95,9 +119,23 @@ def timeline(workload="qwen3-0.6b-ctx1024", pos="520"):
 
     cfg, _, cap = WORKLOADS[workload]
     pos = int(pos)
-    with Engine(cfg, capacity=cap) as e:
+    tune = [t for o in opts if o.startswith("tune=") for t in o[5:].split(",") if t]
+    rank, world, local, dist = _tp_setup()
+    with Engine(cfg, capacity=cap, device=local, tp_rank=rank, tp_size=world) as e:
         e.init_synthetic(0)
         e.persistent = False
+        if tune:
+            e.tuning = tune
+        if dist is not None:
+            if "nccl" in opts:
+                obj = [Engine.nccl_unique_id() if rank == 0 else None]
+                dist.broadcast_object_list(obj, src=0)
+                e.attach_nccl(obj[0])
+            else:
+                hs = [None] * world
+                dist.all_gather_object(hs, e.peer_handle())
+                dist.barrier()
+                e.attach_peers(hs)
         e.set_tokens(prompt_ids(16, vocab=cfg.vocab))
         e.fill_kv(pos)
         e.set_tokens(prompt_ids(pos + 16, vocab=cfg.vocab))
@@ -115,7 +153,8 @@ def timeline(workload="qwen3-0.6b-ctx1024", pos="520"):
     us = lambda cyc: cyc / ghz / 1e3
     n = raw.shape[1]
     ends = [t1[seen[:, k], k].max() for k in range(n)]
-    print(f"{workload} position {pos}: step {(max(ends) - t0[seen].min()) / 1e3:.1f} us, SM clock {ghz:.3f} GHz")
+    lines = [f"{workload} position {pos} rank {rank}/{world}{' tuning ' + ','.join(tune) if tune else ''}: "
+             f"step {(max(ends) - t0[seen].min()) / 1e3:.1f} us, SM clock {ghz:.3f} GHz"]
     names = ["qkv_gemv", "attention", "o_gemv", "gate_up_gemv", "down_gemv"]
     rows = {}
     for k in range(5, n - 1):
@@ -123,14 +162,24 @@ def timeline(workload="qwen3-0.6b-ctx1024", pos="520"):
         rows.setdefault(names[k % 5], []).append(
             [(ends[k] - ends[k - 1]) / 1e3, us(np.median(raw[v, k, 4])), us(np.median(raw[v, k, 5])),
              us(np.median(raw[v, k, 6])), us(np.median(raw[v, k, 7]))])
-    print(f"{'launch':14s} {'span':>7s} {'to_wait':>8s} {'prologue':>9s} {'loop':>7s} {'epilogue':>9s}  (us)")
+    lines.append(f"{'launch':14s} {'span':>7s} {'to_wait':>8s} {'prologue':>9s} {'loop':>7s} {'epilogue':>9s}  (us)")
     for name in names:
         m = np.mean(rows[name], axis=0)
-        print(f"{name:14s} {m[0]:7.2f} {m[1]:8.2f} {m[2]:9.2f} {m[3]:7.2f} {m[4]:9.2f}")
+        lines.append(f"{name:14s} {m[0]:7.2f} {m[1]:8.2f} {m[2]:9.2f} {m[3]:7.2f} {m[4]:9.2f}")
     v = seen[:, n - 1]
-    print(f"{'lm_head':14s} {(ends[n - 1] - ends[n - 2]) / 1e3:7.2f} {us(np.median(raw[v, n - 1, 4])):8.2f} "
-          f"{us(np.median(raw[v, n - 1, 5])):9.2f} {us(np.median(raw[v, n - 1, 6])):7.2f} "
-          f"{us(np.median(raw[v, n - 1, 7])):9.2f}")
+    lines.append(f"{'lm_head':14s} {(ends[n - 1] - ends[n - 2]) / 1e3:7.2f} {us(np.median(raw[v, n - 1, 4])):8.2f} "
+                 f"{us(np.median(raw[v, n - 1, 5])):9.2f} {us(np.median(raw[v, n - 1, 6])):7.2f} "
+                 f"{us(np.median(raw[v, n - 1, 7])):9.2f}")
+    text = "\n".join(lines)
+    if dist is None:
+        print(text)
+        return
+    texts = [None] * world
+    dist.all_gather_object(texts, text)
+    if rank == 0:
+        print("\n\n".join(texts))
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def main():
