@@ -51,7 +51,7 @@ def parse_args():
     ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path (the default) even "
                                                           "where the persistent kernel was selected")
     ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
-                    "batched_poll, no_grid_wait, deep_ring, live_prefetch, tp_prefill, or all")
+                    "batched_poll, no_grid_wait, deep_ring, live_prefetch, tp_prefill, fp8_prefill, or all")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
                     help="fp8: E4M3 GEMV matrices with per-row power-of-two scales (the FP8-weight model, "
                          "not the reference's BF16 model; the CUDA graph path)")
@@ -382,7 +382,9 @@ def main():
     prefill = {"tokens": n_pre, "ms": round(pre_t, 3), "tok_s": round(n_pre / (pre_t / 1000.0), 1),
                "path": ("batched: tcgen05 GEMMs (TMEM accumulators, TMA), batched split-KV attention"
                         + ("; row-parallel fp32 partials exchanged between ranks" if world > 1 else "")
-                        if a.weights == "bf16" and (world == 1 or "tp_prefill" in tune) else "per-token decode steps"),
+                        + ("; E4M3 matrices expanded to their BF16 values first" if a.weights == "fp8" else "")
+                        if (a.weights == "bf16" or "fp8_prefill" in tune) and (world == 1 or "tp_prefill" in tune)
+                        else "per-token decode steps"),
                "tflops": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world, 1),
                "gemm_tflop": round(gemm_flop / 1e12, 3), "attention_tflop": round(attn_flop / 1e12, 3),
                "peak_tflops": bf16_peak, "frac": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world /

@@ -235,8 +235,8 @@ Q3_API int q3_engine_step(q3_engine* e, size_t n);
  * position by n.  No logits (the reference discards the prefill's).  The
  * tokens must have been given with q3_engine_set_tokens.  Tensor-parallel
  * engines run the n decode steps instead unless Q3_TUNE_TP_PREFILL is set
- * (q3_engine_set_tuning); FP8-weight engines always do.  Asynchronous like
- * step. */
+ * (q3_engine_set_tuning), FP8-weight engines unless Q3_TUNE_FP8_PREFILL is.
+ * Asynchronous like step. */
 Q3_API int q3_engine_prefill(q3_engine* e, size_t n);
 
 /* Blocks until queued steps finish; returns Q3_ERR_DEVICE if a kernel
@@ -288,14 +288,20 @@ Q3_API int q3_engine_is_persistent(q3_engine* e);
  *     tcgen05 GEMMs on their shards (row-parallel outputs exchanged as fp32
  *     partials) instead of one decode step per prompt token.  Unlike the
  *     other flags this changes the fp32 order of the prefill's sums (GEMM
- *     instead of GEMV), exactly as the single-GPU batched prefill does.
+ *     instead of GEMV), exactly as the single-GPU batched prefill does;
+ *   Q3_TUNE_FP8_PREFILL: FP8-weight engines prefill with the batched tcgen05
+ *     GEMMs too, each matrix first expanded into a BF16 scratch copy (E4M3
+ *     times a power-of-two row scale is an exact BF16 value, so the GEMMs
+ *     see exactly the FP8 model's weights), instead of one decode step per
+ *     prompt token.  The same change of fp32 order as above.
  * Unknown bits return Q3_ERR_INVALID. */
 #define Q3_TUNE_PEER_BATCHED_POLL 0x1u
 #define Q3_TUNE_PEER_NO_GRID_WAIT 0x2u
 #define Q3_TUNE_ATTN_DEEP_RING 0x4u
 #define Q3_TUNE_ATTN_LIVE_PREFETCH 0x8u
 #define Q3_TUNE_TP_PREFILL 0x10u
-#define Q3_TUNE_ALL 0x1Fu
+#define Q3_TUNE_FP8_PREFILL 0x20u
+#define Q3_TUNE_ALL 0x3Fu
 Q3_API int q3_engine_set_tuning(q3_engine* e, uint32_t flags);
 Q3_API int q3_engine_tuning(q3_engine* e, uint32_t* flags);
 

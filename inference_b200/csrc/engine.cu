@@ -90,6 +90,7 @@ struct q3_engine {
     // batched prefill: token-row buffers of prefill_rows rows (allocated on first use)
     int prefill_rows = 0;
     q3::bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pg = nullptr;
+    q3::bf16* pw = nullptr;  // FP8 engines (Q3_TUNE_FP8_PREFILL): one layer matrix expanded to BF16
     float* pvsum = nullptr;
     // tensor-parallel exchange through peer memory: this rank's buffer (shared
     // with the peers by CUDA IPC), the peers' mappings, local counters
@@ -1020,9 +1021,10 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
     if (p0 + n >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "q3_engine_prefill: KV cache capacity exceeded");
     Q3_CUDA(cudaSetDevice(e->device));
     const bool tp = e->world > 1;
-    if (e->fp8 || (tp && !((e->tune & Q3_TUNE_TP_PREFILL) && (e->peer_mode || e->comm)))) {
-        // FP8-weight engines, and tensor-parallel ones unless Q3_TUNE_TP_PREFILL is set,
-        // prefill through the per-token decode step
+    if ((e->fp8 && !(e->tune & Q3_TUNE_FP8_PREFILL)) ||
+        (tp && !((e->tune & Q3_TUNE_TP_PREFILL) && (e->peer_mode || e->comm)))) {
+        // FP8-weight engines unless Q3_TUNE_FP8_PREFILL is set, and tensor-parallel ones
+        // unless Q3_TUNE_TP_PREFILL is, prefill through the per-token decode step
         return q3_engine_step(e, n);
     }
     const int H = e->H, qd = e->qd, kd = e->kd, il = e->il;
@@ -1038,9 +1040,26 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
         if ((rc = dalloc_t(e, &e->pvsum, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
         e->prefill_rows = rows;
     }
+    if (e->fp8 && !e->pw) {
+        const size_t most = std::max({static_cast<size_t>(ldqkv) * H, static_cast<size_t>(H) * qd,
+                                      static_cast<size_t>(2 * il) * H, static_cast<size_t>(H) * il});
+        int rc;
+        if ((rc = dalloc_t(e, &e->pw, most)) != Q3_OK) return rc;
+    }
     const float eps = e->cfg.eps;
     cudaStream_t s = e->stream;
     const int L = static_cast<int>(e->layers.size());
+    // The BF16 matrix a prefill GEMM reads: the engine's own, or (FP8 engines) the
+    // packed E4M3 matrix expanded into pw -- exactly the FP8 model's weights.  One
+    // buffer serves every GEMM: stream order keeps an expansion after the GEMM
+    // that read the previous one.
+    auto weight = [&](const bf16* w, const F8Dst& d, const bf16** out) -> int {
+        *out = w;
+        if (!e->fp8) return Q3_OK;
+        Q3_CUDA(launch_dequant_e4m3(d.base, d.scale, d.pack, e->pw, s));
+        *out = e->pw;
+        return Q3_OK;
+    };
     auto gemm = [&](const bf16* x, const bf16* w, bf16* y, float* vs, int m, int nn, int k, int ldy, int epi) {
         GemmArgs g{};
         g.x = x;
@@ -1103,7 +1122,9 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
         for (int l = 0; l < L; ++l) {
             const LayerW& W = e->layers[l];
             Q3_CUDA(launch_rmsnorm_rows(e->px, nullptr, W.in_norm, e->pxn, t, H, eps, s));
-            Q3_CUDA(gemm(e->pxn, W.w_qkv, e->pqkv, nullptr, t, ldqkv, H, ldqkv, GEMM_STORE));
+            const bf16* wm = nullptr;
+            Q3_TRY(weight(W.w_qkv, dst_qkv(e, W, 0), &wm));
+            Q3_CUDA(gemm(e->pxn, wm, e->pqkv, nullptr, t, ldqkv, H, ldqkv, GEMM_STORE));
             PrefillQkvArgs qa{};
             qa.qkv = e->pqkv;
             qa.ld = ldqkv;
@@ -1139,16 +1160,19 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
             aa.out_stride = qd;
             Q3_CUDA(launch_attention(aa, s, false));
             if (l == L - 1) break;
+            Q3_TRY(weight(W.w_o, dst_o(e, W), &wm));
             if (tp)
-                Q3_TRY(tp_partial(e->pattn, W.w_o, t, qd, e->pvsum));
+                Q3_TRY(tp_partial(e->pattn, wm, t, qd, e->pvsum));
             else
-                Q3_CUDA(gemm(e->pattn, W.w_o, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
+                Q3_CUDA(gemm(e->pattn, wm, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
             Q3_CUDA(launch_rmsnorm_rows(e->px, e->pvsum, W.post_norm, e->pxn, t, H, eps, s));
-            Q3_CUDA(gemm(e->pxn, W.w_gu, e->pg, nullptr, t, 2 * il, H, il, GEMM_SWIGLU));
+            Q3_TRY(weight(W.w_gu, dst_gu(e, W, 0), &wm));
+            Q3_CUDA(gemm(e->pxn, wm, e->pg, nullptr, t, 2 * il, H, il, GEMM_SWIGLU));
+            Q3_TRY(weight(W.w_down, dst_down(e, W), &wm));
             if (tp)
-                Q3_TRY(tp_partial(e->pg, W.w_down, t, il, nullptr));
+                Q3_TRY(tp_partial(e->pg, wm, t, il, nullptr));
             else
-                Q3_CUDA(gemm(e->pg, W.w_down, e->px, nullptr, t, H, il, H, GEMM_RESID));
+                Q3_CUDA(gemm(e->pg, wm, e->px, nullptr, t, H, il, H, GEMM_RESID));
         }
         done += static_cast<size_t>(t);
     }

@@ -55,7 +55,44 @@ __global__ void pack_e4m3_kernel(const uint8_t* __restrict__ q, const F8Pack L, 
     *reinterpret_cast<uint4*>(packed + f8_offset(L, row, col)) = v;
 }
 
+// The exact BF16 values of a packed E4M3 matrix: out[row, col] =
+// E4M3(row, col) * scale[row], row-major [N, K] (K % 16 == 0).  Each product
+// has at most four significant bits and a power-of-two factor, so every step
+// (E4M3 -> f16 -> f32, the scaling, f32 -> BF16) is exact.  One thread per
+// 16-byte group: the group's bytes are contiguous in the packed layout too.
+__global__ void dequant_e4m3_kernel(const uint8_t* __restrict__ packed, const float* __restrict__ scale,
+                                    const F8Pack L, bf16* __restrict__ out) {
+    const int groups = L.K / 16;
+    const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<long long>(L.N) * groups) return;
+    const int row = static_cast<int>(i / groups), col = static_cast<int>(i % groups) * 16;
+    const uint4 v = *reinterpret_cast<const uint4*>(packed + f8_offset(L, row, col));
+    const float sc = scale[row];
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(&v);
+    uint4 o[2];
+    uint32_t* ow = reinterpret_cast<uint32_t*>(o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t word = w[j / 2] >> (16 * (j & 1));
+        const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(word & 0xFFFFu), __NV_E4M3);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h));
+        ow[j] = static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(f.x * sc))) |
+                (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(f.y * sc))) << 16);
+    }
+    uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * L.K + col);
+    dst[0] = o[0];
+    dst[1] = o[1];
+}
+
 }  // namespace
+
+cudaError_t launch_dequant_e4m3(const uint8_t* packed, const float* scale, const F8Pack& pack, bf16* out,
+                                cudaStream_t s) {
+    if (pack.N <= 0 || pack.K % 16 != 0) return cudaErrorInvalidValue;
+    const long long n = static_cast<long long>(pack.N) * (pack.K / 16);
+    dequant_e4m3_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(packed, scale, pack, out);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_quantize_e4m3(const bf16* src, size_t ld_src, int rows, int full_cols, int c0, int cols,
                                  const F8Dst& dst, cudaStream_t s) {

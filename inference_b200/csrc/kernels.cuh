@@ -347,6 +347,9 @@ cudaError_t launch_quantize_e4m3(const bf16* src, size_t ld_src, int rows, int f
                                  const F8Dst& dst, cudaStream_t s);
 // Row-major E4M3 [N, K] (pitch K) -> the packed layout `pack` (zero padding included).
 cudaError_t launch_pack_e4m3(const uint8_t* q, const F8Pack& pack, uint8_t* packed, cudaStream_t s);
+// The packed matrix's exact BF16 values times the row scales, row-major [N, K] (K % 16 == 0).
+cudaError_t launch_dequant_e4m3(const uint8_t* packed, const float* scale, const F8Pack& pack, bf16* out,
+                                cudaStream_t s);
 cudaError_t configure_attention_kernels();
 int num_sms(int device);
 

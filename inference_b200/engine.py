@@ -135,7 +135,7 @@ class Engine:
 
     # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
     TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2, "deep_ring": 0x4, "live_prefetch": 0x8,
-                  "tp_prefill": 0x10}
+                  "tp_prefill": 0x10, "fp8_prefill": 0x20}
 
     @property
     def tuning(self) -> int:

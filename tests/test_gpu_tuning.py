@@ -7,10 +7,11 @@ must be bit-identical to the default kernels:
     (every page boundary the windows cross, up to 8 pages per split);
   * on 2 GPUs, the peer-exchange prologue with batched rank reads and without
     the grid-dependency wait, together with the attention variants.
-The tensor-parallel batched prefill changes the fp32 order of the prefill's
-sums (GEMMs instead of GEMVs, as the single-GPU prefill does), so it is held to
-the oracle like test_gpu_prefill.py: KV slots of the prefilled positions and
-the teacher-forced logits of the decode steps after it.
+The batched prefills of tensor-parallel and of FP8-weight engines change the
+fp32 order of the prefill's sums (GEMMs instead of GEMVs, as the single-GPU
+prefill does), so they are held to the oracle like test_gpu_prefill.py: KV
+slots of the prefilled positions and the teacher-forced logits of the decode
+steps after it.
 """
 import datetime
 import os
@@ -73,6 +74,51 @@ def test_attention_variants_bit_identical(kv_heads, q_heads):
     assert np.array_equal(base[2], tuned[2])
 
 
+@pytest.mark.parametrize("name", ["qwen3_0p6b", "qwen3_8b_l2", "qwen3_32b_l1"])
+def test_fp8_prefill_matches_fp8_oracle(oracle, name):
+    """FP8 engine, batched prefill (each matrix expanded to its exact BF16 values,
+    then the tcgen05 GEMMs), against the oracle's FP8 model fed token by token:
+    the prefilled KV slots, then the teacher-forced logits of the decode steps."""
+    from inference_b200 import Engine, Qwen3Config
+    from oracle import ModelConfig
+
+    g = dict(np.load(os.path.join(GOLD, f"model_{name}_ref_cpu.npz")))
+    h, inter, layers, qh, kvh, hd, vocab, cap, tied = (int(v) for v in g["config"])
+    qc = Qwen3Config(name, hidden=h, inter=inter, layers=layers, q_heads=qh, kv_heads=kvh, vocab=vocab,
+                     tied=bool(tied))
+    toks = g["tokens"].astype(np.uint32)
+    n = len(toks)
+    n_pre = n - n // 3
+    om = oracle.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)),
+                      seed=0).quantize_fp8()
+    for t in toks[:n_pre]:
+        om.forward(int(t))
+    atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
+    min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
+    with Engine(qc, capacity=cap, weights="fp8") as e:
+        e.init_synthetic(0)
+        e.tuning = ["fp8_prefill"]
+        e.set_tokens(toks)
+        e.prefill(n_pre)
+        e.sync()
+        assert e.position == n_pre
+        for i in range(n_pre):
+            for lay in g["kv_layers"]:
+                k, v = e.kv_slot(int(lay), i)
+                ok_, ov_ = om.kv_slot(int(lay), i)
+                assert _cos(k, ok_) >= 0.9995 and _cos(v, ov_) >= 0.9995, (i, int(lay))
+        agree = 0
+        for i in range(n_pre, n):
+            e.step(1)
+            e.sync()
+            mine = e.logits()
+            nxt = om.forward(int(toks[i]))
+            assert_logits_close(mine, om.logits(), atol=atol, n_ulp=1, min_cos=min_cos)
+            agree += int(int(np.argmax(bf(mine))) == nxt)
+        assert agree >= (n - n_pre) - 1
+    om.close()
+
+
 def test_tuning_rejects_unknown_bits():
     from inference_b200 import Engine, Q3Error, Qwen3Config
 
@@ -80,11 +126,11 @@ def test_tuning_rejects_unknown_bits():
                       tied=True)
     with Engine(cfg, capacity=64) as e:
         with pytest.raises(Q3Error):
-            e.tuning = 0x100
+            e.tuning = 0x400
         with pytest.raises(ValueError):
             e.tuning = ["no_such_flag"]
         e.tuning = ["all"]
-        assert e.tuning == 0x1F
+        assert e.tuning == 0x3F
         e.tuning = 0
         assert e.tuning == 0
 
