@@ -10,6 +10,10 @@
   the same way for sm_100a.  It needs CCCL >= 3 headers (cuda::launch,
   cuda::device_memory_pool); CUDA 12.9 ships CCCL 2.8, so the CCCL 3.x tree
   bundled with flashinfer is used when present.
+* ``oracle/_ref/libref_b200.so`` -- the same harness and the reference's own
+  Qwen3 model, with this repository's drop-in Backend
+  (inference_b200/backend_b200/backend.cpp) linked in place of the reference's
+  CUDA backend: the reference's Model::forward running on libq3_sm100a.so.
 
 Run: ``python oracle/build_ref.py [--reference DIR] [--no-cuda]``.
 """
@@ -120,6 +124,37 @@ def build_ref_cuda(reference: str, force: bool = False) -> str | None:
     return out
 
 
+def build_ref_b200(reference: str, force: bool = False) -> str | None:
+    lib = os.path.join(reference, "src", "lib")
+    repo = os.path.dirname(HERE)
+    backend_cpp = os.path.join(repo, "inference_b200", "backend_b200", "backend.cpp")
+    q3_lib = os.path.join(repo, "inference_b200", "libq3_sm100a.so")
+    nl = _nlohmann_include()
+    nvcc = shutil.which("nvcc")
+    if not os.path.isdir(lib) or nl is None or nvcc is None or not os.path.isfile(q3_lib):
+        print("drop-in backend harness not buildable here (reference tree, nlohmann/json, nvcc or "
+              "libq3_sm100a.so missing)")
+        return None
+    os.makedirs(REF_OUT, exist_ok=True)
+    out = os.path.join(REF_OUT, "libref_b200.so")
+    harness = os.path.join(HERE, "ref_harness.cpp")
+    header = os.path.join(repo, "include", "q3_sm100a.h")
+    if force or not _newer(out, [harness, backend_cpp, header, q3_lib]):
+        obj_dir = os.path.join(REF_OUT, "obj")
+        os.makedirs(obj_dir, exist_ok=True)
+        cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc)), "include")
+        cuda_lib = os.path.join(os.path.dirname(cuda_inc), "lib64")
+        flags = ["g++", "-std=c++23", "-O2", "-fPIC", "-I", lib, "-I", nl, "-I", cuda_inc]
+        o1 = os.path.join(obj_dir, "backend_b200.o")
+        o2 = os.path.join(obj_dir, "harness_b200.o")
+        _run(flags + ["-I", os.path.join(repo, "include"), "-c", backend_cpp, "-o", o1])
+        _run(flags + ["-DREF_CUDA", "-c", harness, "-o", o2])
+        _run(["g++", "-shared", o1, o2, "-o", out, "-L", HERE, "-lq3_oracle",
+              "-L", os.path.dirname(q3_lib), "-lq3_sm100a",
+              "-Wl,-rpath,$ORIGIN/..:$ORIGIN/../../inference_b200", "-L", cuda_lib, "-lcudart"])
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=DEFAULT_REFERENCE)
@@ -134,6 +169,10 @@ def main(argv=None) -> int:
                 build_ref_cuda(a.reference, a.force)
             except subprocess.CalledProcessError as e:  # optional GPU oracle
                 print("reference CUDA backend build failed:", e)
+            try:
+                build_ref_b200(a.reference, a.force)
+            except subprocess.CalledProcessError as e:
+                print("drop-in backend harness build failed:", e)
     else:
         print("reference tree absent: using prebuilt oracle/_ref libraries if any")
     return 0

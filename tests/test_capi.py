@@ -74,3 +74,17 @@ def test_workspace_size_is_monotone():
     sizes = [L.q3_attention_workspace_bytes(32, 8, p) for p in (0, 63, 64, 1000, 8191, 100000)]
     assert all(a <= b for a, b in zip(sizes, sizes[1:]))
     assert L.q3_attention_workspace_bytes(12, 8, 100) == 0
+
+
+def test_drop_in_backend_harness_links_this_library():
+    """oracle/_ref/libref_b200.so (the reference's Model and ops with the drop-in
+    Backend of inference_b200/backend_b200/backend.cpp) loads without a GPU and
+    resolves the C ABI to the in-tree libq3_sm100a.so."""
+    path = os.path.join(ROOT, "oracle", "_ref", "libref_b200.so")
+    if not os.path.exists(path):
+        pytest.skip("drop-in backend harness not built (oracle/build_ref.py needs the reference tree)")
+    L = C.CDLL(path)
+    for s in ("ref_model_create", "ref_model_forward", "ref_model_logits", "ref_op_gemv", "ref_op_attention"):
+        assert hasattr(L, s), s
+    maps = open("/proc/self/maps").read()
+    assert os.path.realpath(os.path.join(ROOT, "inference_b200", "libq3_sm100a.so")) in maps
