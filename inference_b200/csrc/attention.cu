@@ -43,14 +43,15 @@ constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kTileBytes = kPage * kHd * 2;  // 16 KB
 constexpr float kLog2e = 1.4426950408889634f;
 
-// ST: K/V pages in flight per CTA (ring stages): 2 by default (two CTAs per
-// SM), 4 for decode grids resident at one CTA per SM (Q3_TUNE_ATTN_DEEP_RING).
+// ST: K/V pages in flight per CTA (ring stages): 2 by default; with
+// Q3_TUNE_ATTN_DEEP_RING 3 (still two CTAs per SM: <= 110 KB each) or, for
+// grids that fill at most half the SMs at one CTA per SM, 4.
 template <int HG, int ST>
 struct AttnSmem {
     uint8_t kv[ST][2][kTileBytes];
-    float m[8][HG];
-    float l[8][HG];
-    float acc[8][HG][kHd];
+    float m[kWarps][HG];  // per consumer warp: running max, sum, accumulators
+    float l[kWarps][HG];
+    float acc[kWarps][HG][kHd];
     float cm[HG];  // this CTA's merged state, read by the cluster
     float cl[HG];
     float cacc[HG][kHd];
@@ -117,7 +118,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 __device__ __forceinline__ void fence_proxy_async_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 template <int HG, int ST>
-__global__ void __launch_bounds__(kThreads, ST == 2 ? 2 : 1) attn_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const __grid_constant__ AttnArgs a) {
     constexpr int kStages = ST;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     AttnSmem<HG, ST>& S = *reinterpret_cast<AttnSmem<HG, ST>*>(smem_raw);
@@ -530,6 +531,9 @@ cudaError_t configure_attention_kernels() {
     cudaError_t e = configure_hg<1, 2>();
     if (e == cudaSuccess) e = configure_hg<2, 2>();
     if (e == cudaSuccess) e = configure_hg<4, 2>();
+    if (e == cudaSuccess) e = configure_hg<1, 3>();
+    if (e == cudaSuccess) e = configure_hg<2, 3>();
+    if (e == cudaSuccess) e = configure_hg<4, 3>();
     if (e == cudaSuccess) e = configure_hg<1, 4>();
     if (e == cudaSuccess) e = configure_hg<2, 4>();
     if (e == cudaSuccess) e = configure_hg<4, 4>();
@@ -539,14 +543,24 @@ cudaError_t configure_attention_kernels() {
     return cudaSuccess;
 }
 
-bool attn_deep_ring_fits(int q_heads, int kv_heads, int splits, int sms) {
-    if (kv_heads <= 0 || q_heads % kv_heads != 0) return false;
+template <int HG>
+int deep_stages(int clusters, int splits, int sms) {
+    // four stages at one CTA per SM only where the grid leaves at least half the
+    // SMs to the GEMV launched beside it (its weight prefetch overlaps attention)
+    if (2LL * clusters * splits <= sms && max_clusters<HG, 4>(splits) >= clusters) return 4;
+    // three stages keep two CTAs per SM: take them where they are as resident as two
+    const int two = max_clusters<HG, 2>(splits);
+    if (max_clusters<HG, 3>(splits) >= std::min(clusters, two)) return 3;
+    return 2;
+}
+
+int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int sms) {
+    if (kv_heads <= 0 || q_heads % kv_heads != 0) return 2;
     const int G = q_heads / kv_heads;
     const int HG = heads_per_cta(G);
     const int clusters = kv_heads * (G / HG);
-    if (static_cast<long long>(clusters) * splits > sms) return false;
-    const int fit = HG == 1 ? max_clusters<1, 4>(splits) : HG == 2 ? max_clusters<2, 4>(splits) : max_clusters<4, 4>(splits);
-    return fit >= clusters;
+    return HG == 1 ? deep_stages<1>(clusters, splits, sms)
+                   : HG == 2 ? deep_stages<2>(clusters, splits, sms) : deep_stages<4>(clusters, splits, sms);
 }
 
 // Splits per (kv head, block): a power of two forming one cluster, at most 16
@@ -576,7 +590,7 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.splits < 1 || a.splits > 16 || (a.splits & (a.splits - 1)) != 0) return cudaErrorInvalidValue;
     if (a.n_queries > 1 && static_cast<long long>(a.n_queries) * (G / heads_per_cta(G)) > 65535)
         return cudaErrorInvalidValue;
-    if (a.stages != 0 && a.stages != 2 && a.stages != 4) return cudaErrorInvalidValue;
+    if (a.stages != 0 && (a.stages < 2 || a.stages > 4)) return cudaErrorInvalidValue;
     const int HG = heads_per_cta(G);
     const int nqb = G / HG;
     if (a.stages == 4) {
@@ -584,6 +598,13 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
             case 1: return launch_hg<1, 4>(a, s, pdl, nqb);
             case 2: return launch_hg<2, 4>(a, s, pdl, nqb);
             default: return launch_hg<4, 4>(a, s, pdl, nqb);
+        }
+    }
+    if (a.stages == 3) {
+        switch (HG) {
+            case 1: return launch_hg<1, 3>(a, s, pdl, nqb);
+            case 2: return launch_hg<2, 3>(a, s, pdl, nqb);
+            default: return launch_hg<4, 3>(a, s, pdl, nqb);
         }
     }
     switch (HG) {

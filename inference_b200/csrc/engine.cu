@@ -72,10 +72,10 @@ struct q3_engine {
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
     uint32_t *done_counter = nullptr, *err = nullptr;
     int attn_splits = 1;
-    // opt-in variants of the graph path (Q3_TUNE_*); attn_deep_fits: the decode
-    // attention grid is resident at one CTA per SM (Q3_TUNE_ATTN_DEEP_RING applies)
+    // opt-in variants of the graph path (Q3_TUNE_*); attn_deep_stages: the decode
+    // attention's ring depth under Q3_TUNE_ATTN_DEEP_RING
     uint32_t tune = 0;
-    bool attn_deep_fits = false;
+    int attn_deep_stages = 2;
     // persistent decode kernel (one launch per run of steps)
     bool persistent = false;
     q3::PersistentArgs pargs{};
@@ -252,7 +252,7 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.rope_cos = e->rope_cos;
     a.rope_sin = e->rope_sin;
     a.eps = e->cfg.eps;
-    a.stages = ((e->tune & Q3_TUNE_ATTN_DEEP_RING) && e->attn_deep_fits) ? 4 : 2;
+    a.stages = (e->tune & Q3_TUNE_ATTN_DEEP_RING) ? e->attn_deep_stages : 2;
     a.live_prefetch = (e->tune & Q3_TUNE_ATTN_LIVE_PREFETCH) ? 1 : 0;
     a.trace = r.trace();
     r.mark(true, 1);
@@ -616,7 +616,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
-    e->attn_deep_fits = attn_deep_ring_fits(e->qh, e->kvh, e->attn_splits, e->sms);
+    e->attn_deep_stages = attn_deep_ring_stages(e->qh, e->kvh, e->attn_splits, e->sms);
 
     // ---- persistent decode kernel (single GPU, BF16 weights)
     if (tp_size == 1 && !e->fp8) {
