@@ -2,9 +2,11 @@
 
 The decode variants reorder no arithmetic, so every logit, argmax and KV slot
 must be bit-identical to the default kernels:
-  * attention with a four-page ring and the live page fetched before the
-    dependency wait, at positions from 0 to the end of an 8192-slot cache
-    (every page boundary the windows cross, up to 8 pages per split);
+  * attention with the deeper page ring (three pages at two CTAs per SM for
+    the 8-kv-head grid, four at one CTA per SM for the 2-kv-head one) and the
+    live page fetched before the dependency wait, at positions from 0 to the
+    end of an 8192-slot cache (every page boundary the windows cross, up to 8
+    pages per split, so both ring depths refill);
   * on 2 GPUs, the peer-exchange prologue with batched rank reads and without
     the grid-dependency wait, together with the attention variants.
 The batched prefills of tensor-parallel and of FP8-weight engines change the
@@ -63,7 +65,7 @@ def test_attention_variants_bit_identical(kv_heads, q_heads):
             e.fill_kv(4090)    # synthetic cache: 64 pages, 4 per split
             window(10)         # 4090..4099 crosses the page boundary at 4096
             e.fill_kv(8180)
-            window(11)         # 8180..8190: 128 pages, 8 per split (ring refills in both depths)
+            window(11)         # 8180..8190: 128 pages, 8 per split (every ring depth refills)
             hist = e.argmax_history(8191)
         runs[flags] = (logits, kv, hist)
     base, tuned = runs[0], runs[DECODE_FLAGS]
