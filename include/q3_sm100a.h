@@ -315,7 +315,10 @@ Q3_API int q3_engine_tuning(q3_engine* e, uint32_t* flags);
  * path: every step records, per launch (the same 5 per layer + lm_head) and
  * CTA, [0] / [1] CTA start / end (%globaltimer), [2] / [3] clock64 there,
  * SM cycles of [4] start -> dependency wait returned, [5] prologue, [6] main
- * loop, [7] epilogue, [8] the SM id (toggling re-records the graph).
+ * loop, [7] epilogue, [8] the SM id, and for a tensor-parallel GEMV that sums
+ * the ranks' partials in its prologue [9] the SM cycles from the dependency
+ * release until CTA thread 0 held every rank's partials of its first rows
+ * (toggling re-records the graph).
  * out_host (if not NULL) receives the last record,
  * [ctas][phases][Q3_TRACE_WORDS]; capacity counts uint64 words. */
 #define Q3_TRACE_WORDS 10

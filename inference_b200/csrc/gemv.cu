@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int pro = PRO, epi = EPI;
     const bool tracing = a.trace.buf != nullptr;
-    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_c2 = 0, tr_c3 = 0;
+    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_c2 = 0, tr_c3 = 0, tr_cx = 0;
     if (tracing && tid == 0) {
         tr_t0 = globaltimer_ns();
         tr_c0 = clock64();
@@ -424,6 +424,8 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                     v0 = reinterpret_cast<const float4*>(a.vsum)[2 * i];
                     v1 = reinterpret_cast<const float4*>(a.vsum)[2 * i + 1];
                 }
+                // timeline: when thread 0 holds every rank's partials of its first rows
+                if (tracing && parts && tid == 0 && tr_cx == 0) tr_cx = clock64();
                 const float rs[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
                 uint32_t* hw = reinterpret_cast<uint32_t*>(&h);
 #pragma unroll
@@ -687,6 +689,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             t[6] = tr_c3 - tr_c2;
             t[7] = c4 - tr_c3;
             t[8] = sm_id();
+            t[9] = tr_cx ? tr_cx - tr_c1 : 0;  // exchange-consuming prologue: thread 0's rows complete
         }
     }
 }

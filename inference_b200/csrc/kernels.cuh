@@ -13,7 +13,9 @@ namespace q3 {
 // CTA (linear block index below `ctas`), Q3_TRACE_WORDS words at
 // buf[(cta * phases + phase) * Q3_TRACE_WORDS]: [0] / [1] %globaltimer at CTA
 // start / end, [2] / [3] clock64 there, SM cycles of [4] start -> dependency
-// wait returned, [5] prologue, [6] main loop, [7] epilogue, [8] SM id.
+// wait returned, [5] prologue, [6] main loop, [7] epilogue, [8] SM id, [9] (a
+// prologue over the ranks' partials) cycles from [4]'s end until thread 0 held
+// every rank's partials of its first rows.
 struct LaunchTrace {
     unsigned long long* buf;  // null: off
     int phase, phases, ctas;

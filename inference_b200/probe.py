@@ -21,7 +21,9 @@ attn_kernel launches of the process are those of the steps.
 `timeline`: the CUDA-graph path's launch timeline (q3_engine_trace) of one
 decode step at `position`, summarised per launch kind over layers 1..L-1:
 CTA start to dependency release, prologue, main loop, epilogue (medians over
-CTAs, microseconds) and each launch's span from the previous launch's end.
+CTAs, microseconds), each launch's span from the previous launch's end, and
+for tensor-parallel GEMVs the part of the prologue until every rank's partial
+rows had arrived (`peers`).
 Under torchrun the engine is tensor-parallel over the ranks (peer-memory
 exchange, or NCCL with `nccl`) and every rank's summary is printed;
 `tune=` applies q3_engine_set_tuning flags by name.
@@ -161,15 +163,17 @@ def timeline(workload="qwen3-0.6b-ctx1024", pos="520", *opts):
         v = seen[:, k]
         rows.setdefault(names[k % 5], []).append(
             [(ends[k] - ends[k - 1]) / 1e3, us(np.median(raw[v, k, 4])), us(np.median(raw[v, k, 5])),
-             us(np.median(raw[v, k, 6])), us(np.median(raw[v, k, 7]))])
-    lines.append(f"{'launch':14s} {'span':>7s} {'to_wait':>8s} {'prologue':>9s} {'loop':>7s} {'epilogue':>9s}  (us)")
+             us(np.median(raw[v, k, 6])), us(np.median(raw[v, k, 7])), us(np.median(raw[v, k, 9]))])
+    # peers: part of the prologue until thread 0 held every rank's partials (tensor parallel)
+    lines.append(f"{'launch':14s} {'span':>7s} {'to_wait':>8s} {'prologue':>9s} {'loop':>7s} {'epilogue':>9s} "
+                 f"{'peers':>7s}  (us)")
     for name in names:
         m = np.mean(rows[name], axis=0)
-        lines.append(f"{name:14s} {m[0]:7.2f} {m[1]:8.2f} {m[2]:9.2f} {m[3]:7.2f} {m[4]:9.2f}")
+        lines.append(f"{name:14s} {m[0]:7.2f} {m[1]:8.2f} {m[2]:9.2f} {m[3]:7.2f} {m[4]:9.2f} {m[5]:7.2f}")
     v = seen[:, n - 1]
     lines.append(f"{'lm_head':14s} {(ends[n - 1] - ends[n - 2]) / 1e3:7.2f} {us(np.median(raw[v, n - 1, 4])):8.2f} "
                  f"{us(np.median(raw[v, n - 1, 5])):9.2f} {us(np.median(raw[v, n - 1, 6])):7.2f} "
-                 f"{us(np.median(raw[v, n - 1, 7])):9.2f}")
+                 f"{us(np.median(raw[v, n - 1, 7])):9.2f} {us(np.median(raw[v, n - 1, 9])):7.2f}")
     text = "\n".join(lines)
     if dist is None:
         print(text)
