@@ -186,6 +186,7 @@ def _tp_main(rank, world, port, name, out_dir, mode, flags, n_pre):
     kv.update({f"v{lay}_{p}": e.kv_slot(int(lay), p)[1] for lay in g["kv_layers"] for p in range(len(toks))})
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"), logits=np.stack(logits), hist=e.argmax_history(len(toks)),
              **kv)
+    dist.barrier()  # no rank frees its exchange buffer while a peer may still use it
     e.close()
     dist.barrier()
     dist.destroy_process_group()
