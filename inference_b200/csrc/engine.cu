@@ -576,6 +576,10 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->logits, e->vl)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->vsum, H)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->partial, H)) != Q3_OK) return bail(rc);
+    cudaError_t setup = cudaSuccess;  // the first failure of the set-up copies below
+    auto note = [&setup](cudaError_t st) {
+        if (setup == cudaSuccess) setup = st;
+    };
     if (tp_size > 1) {
         // exchange buffer (xbuf_layout): decode pairs, flags and keys, then the prefill slots
         const size_t pf_rows = std::min<size_t>(kPrefillRows, c.capacity);
@@ -585,10 +589,10 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
         e->tpx.rank = tp_rank;
         e->tpx.world = tp_size;
         if ((rc = dalloc(e, &e->xbuf, e->xbuf_bytes)) != Q3_OK) return bail(rc);
-        cudaMemset(e->xbuf, 0, e->xbuf_bytes);
+        note(cudaMemset(e->xbuf, 0, e->xbuf_bytes));
         unsigned long long* seq = nullptr;
         if ((rc = dalloc_t(e, &seq, 2)) != Q3_OK) return bail(rc);
-        cudaMemset(seq, 0, 16);
+        note(cudaMemset(seq, 0, 16));
         e->links.seq = seq;
         e->links.counter = reinterpret_cast<uint32_t*>(seq + 1);
         e->links.rank = tp_rank;
@@ -604,15 +608,15 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->keys, static_cast<size_t>(tp_size) + 1)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->done_counter, 4)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->err, 4)) != Q3_OK) return bail(rc);
-    cudaMemset(e->pos, 0, 16);
-    cudaMemset(e->n_forced, 0, 16);
-    cudaMemset(e->tokens, 0, (c.capacity + 1) * 4);
-    cudaMemset(e->argmax_hist, 0xFF, (c.capacity + 1) * 4);
-    cudaMemset(e->key_slot, 0, 16);
-    cudaMemset(e->key_send, 0, 16);
-    cudaMemset(e->keys, 0, (tp_size + 1) * 8);
-    cudaMemset(e->done_counter, 0, 16);
-    cudaMemset(e->err, 0, 4);
+    note(cudaMemset(e->pos, 0, 16));
+    note(cudaMemset(e->n_forced, 0, 16));
+    note(cudaMemset(e->tokens, 0, (c.capacity + 1) * 4));
+    note(cudaMemset(e->argmax_hist, 0xFF, (c.capacity + 1) * 4));
+    note(cudaMemset(e->key_slot, 0, 16));
+    note(cudaMemset(e->key_send, 0, 16));
+    note(cudaMemset(e->keys, 0, (tp_size + 1) * 8));
+    note(cudaMemset(e->done_counter, 0, 16));
+    note(cudaMemset(e->err, 0, 4));
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
@@ -668,7 +672,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
             const bool fits = aligned && ((top - base) >> 8) < (1ull << 32);
             if (fits) {
                 if ((rc = dalloc_t(e, &e->d_layer_tab, tab.size())) != Q3_OK) return bail(rc);
-                cudaMemcpy(e->d_layer_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
+                note(cudaMemcpy(e->d_layer_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
                 a.layer_tab = e->d_layer_tab;
                 a.layer_base = base;
                 if ((rc = dalloc_t(e, &att_part, static_cast<size_t>(e->kvh) * a.nqb * a.splits * HG * kAttRecord)) != Q3_OK)
@@ -676,9 +680,9 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
                 if ((rc = dalloc_t(e, &att_cnt, static_cast<size_t>(e->kvh) * a.nqb + 4)) != Q3_OK) return bail(rc);
                 if ((rc = dalloc_t(e, &e->gsync, 2)) != Q3_OK) return bail(rc);
                 if ((rc = dalloc_t(e, &e->abort_word, 4)) != Q3_OK) return bail(rc);
-                cudaMemset(att_cnt, 0, (static_cast<size_t>(e->kvh) * a.nqb + 4) * 4);
-                cudaMemset(e->gsync, 0, 16);
-                cudaMemset(e->abort_word, 0, 16);
+                note(cudaMemset(att_cnt, 0, (static_cast<size_t>(e->kvh) * a.nqb + 4) * 4));
+                note(cudaMemset(e->gsync, 0, 16));
+                note(cudaMemset(e->abort_word, 0, 16));
                 a.embed = e->embed;
                 a.lm_head = e->lm_head;
                 a.final_norm = e->final_norm;
@@ -707,6 +711,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
             }
         }
     }
+    if (setup != cudaSuccess)
+        return bail(fail(Q3_ERR_CUDA, std::string("engine setup copy: ") + cudaGetErrorString(setup)));
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "engine setup failed"));
     *out = e;
     return Q3_OK;
