@@ -59,6 +59,9 @@ def parse_args():
     ap.add_argument("--reference-cuda-tokens", type=int, default=0,
                     help="also time the reference's own cuBLAS CUDA backend (oracle/_ref/libref_cuda.so) for this "
                          "many Model::forward calls at mid-window context; reported as reference_cuda")
+    ap.add_argument("--drop-in-tokens", type=int, default=0,
+                    help="also time the reference's own Model::forward on this library's drop-in Backend "
+                         "(oracle/_ref/libref_b200.so) for this many calls at mid-window context; reported as drop_in")
     return ap.parse_args()
 
 
@@ -447,19 +450,26 @@ def main():
         except Exception as exc:  # report, never fail the GPU number
             cpu = {"value": None, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": f"failed: {exc}"}
 
-    # ---- the reference's own CUDA backend on the same GPU (optional, rank 0, N = 1)
-    ref_cuda = None
-    if rank == 0 and world == 1 and a.reference_cuda_tokens > 0:  # noqa: SIM102
+    # ---- the reference's own Model::forward on the same GPU (optional, rank 0, N = 1):
+    # with its cuBLAS CUDA backend, and with this library's drop-in Backend
+    timed_refs = {}
+    for key, kind, n_req, what in (("reference_cuda", "cuda", a.reference_cuda_tokens,
+                                    "reference cuBLAS CUDA backend built from its sources for sm_100a"),
+                                   ("drop_in", "b200", a.drop_in_tokens,
+                                    "the reference's Model::forward on this library's drop-in Backend "
+                                    "(inference_b200/backend_b200/backend.cpp)")):
+        if not (rank == 0 and world == 1 and n_req > 0):
+            continue
         try:
             from oracle import ModelConfig, RefLib
 
-            rl = RefLib("cuda")
-            n_tok = a.reference_cuda_tokens
+            rl = RefLib(kind)
+            n_tok = n_req
             mc = ModelConfig.make(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, 128, cfg.vocab,
                                   mid + n_tok + 2, tied=cfg.tied)
             rm = rl.model(mc, seed=0)
             rm.fill_kv(mid, seed=7)
-            rm.forward(1000)  # first call allocates the reference's flash scratch
+            rm.forward(1000)  # the first call allocates the backend's scratch (the reference's flash scratch)
             rm.token_count = mid
             torch.cuda.synchronize()
             t0 = time.perf_counter()
@@ -468,11 +478,10 @@ def main():
                 tok = rm.forward(tok)  # Model::forward: host sync per token, as the reference generator runs
             dt = time.perf_counter() - t0
             rm.close()
-            ref_cuda = {"value": round(n_tok / dt, 3), "unit": "tok/s",
-                        "sample": f"{n_tok} Model::forward calls at context {mid}, reference cuBLAS CUDA backend "
-                                  f"built from its sources for sm_100a"}
+            timed_refs[key] = {"value": round(n_tok / dt, 3), "unit": "tok/s",
+                               "sample": f"{n_tok} Model::forward calls at context {mid}, {what}"}
         except Exception as exc:
-            ref_cuda = {"value": None, "unit": "tok/s", "sample": f"failed: {exc}"}
+            timed_refs[key] = {"value": None, "unit": "tok/s", "sample": f"failed: {exc}"}
 
     if rank == 0:
         line = {
@@ -490,8 +499,7 @@ def main():
             "clocks": clock, "e2e": e2e, "gpu_launches": int(launches),
             "roofline": roofline, "step_roofline": step_roof, "cpu_baseline": cpu, "prefill": prefill,
         }
-        if ref_cuda is not None:
-            line["reference_cuda"] = ref_cuda
+        line.update(timed_refs)
         print(json.dumps(line), flush=True)
     eng.close()
     if dist:
