@@ -80,7 +80,7 @@ def _rank_main(rank, world, port, name, out_dir, mode):
 @pytest.mark.parametrize("name,mode,world", [("qwen3_8b_l2", "peer", 2), ("qwen3_8b_l2", "nccl", 2),
                                              ("qwen3_0p6b", "peer", 2), ("qwen3_0p6b", "nccl", 2),
                                              ("qwen3_8b_l2", "peer", 4), ("qwen3_0p6b", "peer-fp8", 2),
-                                             ("qwen3_32b_l1", "peer", 2)])
+                                             ("qwen3_32b_l1", "peer", 2), ("qwen3_8b_l2", "peer", 8)])
 def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
     import torch
     import torch.multiprocessing as mp
