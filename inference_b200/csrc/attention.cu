@@ -544,23 +544,26 @@ cudaError_t configure_attention_kernels() {
 }
 
 template <int HG>
-int deep_stages(int clusters, int splits, int sms) {
-    // four stages at one CTA per SM only where the grid leaves at least half the
-    // SMs to the GEMV launched beside it (its weight prefetch overlaps attention)
-    if (2LL * clusters * splits <= sms && max_clusters<HG, 4>(splits) >= clusters) return 4;
+int deep_stages(int clusters, int splits, int sms, bool kv_heavy) {
+    // four stages at one CTA per SM where the grid leaves at least half the SMs
+    // to the GEMV launched beside it (its weight prefetch overlaps attention), or
+    // where the KV pages outweigh that GEMV's weights and want every SM
+    const long long ctas = 1LL * clusters * splits;
+    if ((2 * ctas <= sms || (kv_heavy && ctas <= sms)) && max_clusters<HG, 4>(splits) >= clusters) return 4;
     // three stages keep two CTAs per SM: take them where they are as resident as two
     const int two = max_clusters<HG, 2>(splits);
     if (max_clusters<HG, 3>(splits) >= std::min(clusters, two)) return 3;
     return 2;
 }
 
-int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int sms) {
+int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int sms, bool kv_heavy) {
     if (kv_heads <= 0 || q_heads % kv_heads != 0) return 2;
     const int G = q_heads / kv_heads;
     const int HG = heads_per_cta(G);
     const int clusters = kv_heads * (G / HG);
-    return HG == 1 ? deep_stages<1>(clusters, splits, sms)
-                   : HG == 2 ? deep_stages<2>(clusters, splits, sms) : deep_stages<4>(clusters, splits, sms);
+    return HG == 1   ? deep_stages<1>(clusters, splits, sms, kv_heavy)
+           : HG == 2 ? deep_stages<2>(clusters, splits, sms, kv_heavy)
+                     : deep_stages<4>(clusters, splits, sms, kv_heavy);
 }
 
 // Splits per (kv head, block): a power of two forming one cluster, at most 16

@@ -620,7 +620,12 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
-    e->attn_deep_stages = attn_deep_ring_stages(e->qh, e->kvh, e->attn_splits, e->sms);
+    {
+        // a layer's K/V reads at the middle of the context against the o_proj weights
+        const double kv_mid = static_cast<double>(c.capacity) / 2 * e->kvh * 128 * 2 * 2;
+        const double o_bytes = static_cast<double>(e->H) * e->qd * 2;
+        e->attn_deep_stages = attn_deep_ring_stages(e->qh, e->kvh, e->attn_splits, e->sms, kv_mid > o_bytes);
+    }
 
     // ---- persistent decode kernel (single GPU, BF16 weights)
     if (tp_size == 1 && !e->fp8) {

@@ -163,9 +163,10 @@ struct AttnArgs {
 // K/V pages in flight per CTA for the decode grid (splits x kv_heads x
 // query-head blocks, one cluster of `splits` per kv head and block) under
 // Q3_TUNE_ATTN_DEEP_RING: 4 (one CTA per SM) where the grid fills at most half
-// the SMs and stays resident, else 3 (two CTAs per SM) where that is as
-// resident as the default 2, else 2.
-int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int num_sms);
+// the SMs -- or, kv_heavy (a layer's KV reads outweigh the next GEMV's
+// weights), at most all of them -- and stays resident; else 3 (two CTAs per
+// SM) where that is as resident as the default 2; else 2.
+int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int num_sms, bool kv_heavy);
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
