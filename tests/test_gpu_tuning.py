@@ -2,8 +2,8 @@
 
 The decode variants reorder no arithmetic, so every logit, argmax and KV slot
 must be bit-identical to the default kernels:
-  * attention with the deeper page ring (three pages at two CTAs per SM for
-    the 8-kv-head grid, four at one CTA per SM for the 2-kv-head one) and the
+  * attention with the deeper page ring (four pages at one CTA per SM, three
+    at two CTAs per SM, per the shapes below) and the
     live page fetched before the dependency wait, at positions from 0 to the
     end of an 8192-slot cache (every page boundary the windows cross, up to 8
     pages per split, so both ring depths refill);
@@ -36,11 +36,14 @@ def _cos(a, b):
     return a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30)
 
 
-@pytest.mark.parametrize("kv_heads,q_heads", [(2, 8), (8, 16)])
-def test_attention_variants_bit_identical(kv_heads, q_heads):
+# ring depth the deep-ring variant picks: (2, 8) a small grid -> 4 pages at one CTA per SM;
+# (8, 16) K/V reads outweigh o_proj at this context -> 4; (8, 32) 8B shapes -> 3 at two per SM
+@pytest.mark.parametrize("kv_heads,q_heads,hidden,inter", [(2, 8, 1024, 3072), (8, 16, 1024, 3072),
+                                                           (8, 32, 4096, 12288)])
+def test_attention_variants_bit_identical(kv_heads, q_heads, hidden, inter):
     from inference_b200 import Engine, Qwen3Config, prompt_ids
 
-    cfg = Qwen3Config(f"gqa{q_heads // kv_heads}-kv{kv_heads}-l2", hidden=1024, inter=3072, layers=2,
+    cfg = Qwen3Config(f"gqa{q_heads // kv_heads}-kv{kv_heads}-h{hidden}-l2", hidden=hidden, inter=inter, layers=2,
                       q_heads=q_heads, kv_heads=kv_heads, vocab=151936, tied=True)
     cap = 8192
     ids = prompt_ids(cap, seed=1)
