@@ -501,6 +501,11 @@ def main():
         }
         line.update(timed_refs)
         print(json.dumps(line), flush=True)
+    if dist:
+        # a rank's last kernels store into its peers' exchange buffers: every rank's
+        # stream is idle before any rank frees its buffer
+        eng.sync()
+        dist.barrier()
     eng.close()
     if dist:
         dist.barrier()

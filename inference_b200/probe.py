@@ -149,6 +149,9 @@ def timeline(workload="qwen3-0.6b-ctx1024", pos="520", *opts):
         e.sync()
         raw = e.read_trace().astype(np.float64)  # [ctas, phases, words]
         e.trace(False)
+        if dist is not None:
+            e.sync()
+            dist.barrier()  # no rank frees its exchange buffer while a peer's last stores may target it
     seen = raw[..., 0] > 0
     t0, t1, c0, c1 = raw[..., 0], raw[..., 1], raw[..., 2], raw[..., 3]
     ghz = float(np.median(((c1 - c0) / np.maximum(t1 - t0, 1))[seen]))
