@@ -88,3 +88,22 @@ def test_drop_in_backend_harness_links_this_library():
         assert hasattr(L, s), s
     maps = open("/proc/self/maps").read()
     assert os.path.realpath(os.path.join(ROOT, "inference_b200", "libq3_sm100a.so")) in maps
+
+
+def test_tuning_flag_names_match_the_header():
+    """Engine.TUNE_FLAGS (names used by bench.py --tune) mirror the Q3_TUNE_* bits of
+    include/q3_sm100a.h, and Q3_TUNE_ALL is their union."""
+    from inference_b200 import Engine
+
+    src = open(os.path.join(ROOT, "include", "q3_sm100a.h")).read()
+    bits = {m.group(1).lower(): int(m.group(2), 16)
+            for m in re.finditer(r"#define Q3_TUNE_(\w+) 0x([0-9A-Fa-f]+)u", src)}
+    every = bits.pop("all")
+    by_value = {v: k for k, v in bits.items()}
+    assert sorted(Engine.TUNE_FLAGS.values()) == sorted(bits.values())
+    for name, v in Engine.TUNE_FLAGS.items():
+        assert name.replace("_", "") in by_value[v].replace("_", ""), (name, by_value[v])
+    total = 0
+    for v in bits.values():
+        total |= v
+    assert total == every
