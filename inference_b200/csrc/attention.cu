@@ -44,8 +44,8 @@ constexpr int kTileBytes = kPage * kHd * 2;  // 16 KB
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ST: K/V pages in flight per CTA (ring stages): 2 by default; with
-// Q3_TUNE_ATTN_DEEP_RING 3 (still two CTAs per SM: <= 110 KB each) or, for
-// grids that fill at most half the SMs at one CTA per SM, 4.
+// Q3_TUNE_ATTN_DEEP_RING 3 (still two CTAs per SM: <= 110 KB each) or 4 (one
+// CTA per SM), as attn_deep_ring_stages picks for the grid.
 template <int HG, int ST>
 struct AttnSmem {
     uint8_t kv[ST][2][kTileBytes];
