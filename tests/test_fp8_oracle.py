@@ -105,8 +105,9 @@ def test_oracle_fp8_model_is_close_to_bf16(oracle):
 @pytest.mark.parametrize("n,k,sms", [(300, 320, 148), (37, 64, 4), (4096, 192, 148), (66, 512, 7)])
 def test_packed_fp8_layout_is_a_tiled_bijection(n, k, sms):
     """q3_e4m3_packed_offset (the FP8 GEMV's weight layout, the same function
-    the device packer and quantizer use): every weight has its own byte inside
-    q3_e4m3_packed_bytes, column pairs stay adjacent, and each 16-row x
+    the device packer, quantizer and BF16 expansion use): every weight has its
+    own byte inside q3_e4m3_packed_bytes, each 16-column group is 16 contiguous
+    bytes, and each 16-row x
     256-column tile of a CTA's row band is one contiguous run of rows x 256
     bytes (one bulk copy)."""
     from inference_b200 import lib
@@ -117,6 +118,10 @@ def test_packed_fp8_layout_is_a_tiled_bijection(n, k, sms):
     assert off.max() < size and off.min() >= 0
     assert len(np.unique(off)) == n * k
     assert (off[:, 1::2] == off[:, ::2] + 1).all()
+    # each 16-column group is 16 contiguous bytes (the packer and the BF16 expansion
+    # of the FP8 prefill move whole groups)
+    for j in range(1, 16):
+        assert (off[:, j::16] == off[:, 0::16][:, :off[:, j::16].shape[1]] + j).all()
     # tiles: the 16-byte groups of one row segment of 256 columns sit in one
     # 256-byte row of the tile, each tile's rows back to back
     base = off[:, ::16] & ~255
