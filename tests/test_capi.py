@@ -107,3 +107,22 @@ def test_tuning_flag_names_match_the_header():
     for v in bits.values():
         total |= v
     assert total == every
+
+
+def test_tp_prefill_shard_shapes_fit_the_gemm():
+    """Every Qwen3 configuration at every tensor-parallel size the engine accepts
+    (kv heads, intermediate and vocabulary divisible by the ranks) gives shard
+    GEMMs within the tcgen05 GEMM's shape rule (N % 128 == 0, K % 64 == 0;
+    launch_gemm in gemm.cu), so Q3_TUNE_TP_PREFILL never meets a rejected shape."""
+    from inference_b200.config import MODELS
+
+    checked = 0
+    for c in MODELS.values():
+        for tp in (1, 2, 4, 8):
+            if c.kv_heads % tp or c.inter % tp or (c.inter // tp) % 8 or c.vocab % tp:
+                continue
+            qd, kd, il, H = c.q_heads // tp * 128, c.kv_heads // tp * 128, c.inter // tp, c.hidden
+            for n, k in ((qd + 2 * kd, H), (H, qd), (2 * il, H), (H, il)):
+                assert n % 128 == 0 and k % 64 == 0, (c.name, tp, n, k)
+            checked += 1
+    assert checked == 16
