@@ -147,14 +147,15 @@ Q3_API int q3_argmax(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, 
 
 /* q3_argmax without any device allocation (no counterpart in the reference).
  * For callers that must not let the library allocate: serving runtimes that
- * plan all device memory themselves, code recording into a CUDA graph under
- * global stream capture (where cudaMalloc is not allowed), latency-critical
- * loops that cannot take cudaMalloc's implicit synchronisation.  Its scratch
- * is a 32 KB array compiled into the library (kept by every GPU that loads
- * it until the process exits), so n is limited to 16,777,216 logits; larger
- * inputs return Q3_ERR_INVALID.  The first call on a device looks up the
- * array's device address: make it before any stream capture.  Calls share
- * the array, so calls that overlap on the GPU (unordered streams) race. */
+ * plan all device memory themselves and hand libraries only buffers they own,
+ * latency-critical loops that cannot take cudaMalloc's implicit
+ * synchronisation.  Its scratch is a 32 KB array compiled into the library
+ * (kept by every GPU that loads it until the process exits), so n is limited
+ * to 16,777,216 logits; larger inputs return Q3_ERR_INVALID.  The first call
+ * on a device looks up the array's device address and caches it: make that
+ * call before any stream capture, and do not use the library across a
+ * cudaDeviceReset of the device.  Calls share the array, so calls that
+ * overlap on the GPU (unordered streams) race. */
 Q3_API int q3_argmax_noalloc(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, void* stream);
 
 /* make_rope_cache (src/lib/backend/util/rope_cache.hpp:23-45) on the host:
@@ -205,6 +206,10 @@ typedef struct q3_engine q3_engine;
 /* Tensor-parallel placement: rank `tp_rank` of `tp_size` on CUDA device
  * `device`.  tp_size 1 needs no communicator. */
 Q3_API int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp_size, q3_engine** out);
+/* Tensor-parallel engines: peers store into and read from this rank's
+ * exchange buffer over NVLink (decode partials, and the batched prefill's
+ * partial rows), so every rank calls q3_engine_sync, then the ranks meet at a
+ * host barrier, before any rank destroys its engine. */
 Q3_API int q3_engine_destroy(q3_engine* e);
 
 /* Weights: synthetic N(0, 0.02) BF16 from `seed` (norm weights 1.0), each
@@ -267,6 +272,16 @@ Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
  * between phases).  Both produce the same tokens. */
 Q3_API int q3_engine_set_persistent(q3_engine* e, int enable);
 Q3_API int q3_engine_is_persistent(q3_engine* e);
+
+/* L2 lookahead of the decode step's weight streams (no counterpart in the
+ * reference; changes no arithmetic): every GEMV warp prefetches into L2, before
+ * its dependency wait, the `items` work items (4 KB each) of its run that
+ * follow the ones its shared-memory ring holds, so HBM keeps streaming through
+ * the wait and the prologue; with attention_prefetch the decode attention
+ * kernel, which reads little from HBM, prefetches the o_proj weights into L2
+ * for the GEMV after it.  items in [0, 64]. */
+Q3_API int q3_engine_set_lookahead(q3_engine* e, int items, int attention_prefetch);
+Q3_API int q3_engine_lookahead(q3_engine* e, int* items, int* attention_prefetch);
 
 /* Opt-in variants of the CUDA-graph decode path (no counterpart in the
  * reference), as bit flags; 0, the default, selects the kernels described
@@ -331,6 +346,15 @@ Q3_API int q3_engine_logits(q3_engine* e, uint16_t* out_host);  /* this rank's v
 Q3_API int q3_engine_argmax_history(q3_engine* e, uint32_t* out_host, size_t n);
 Q3_API int q3_engine_kv_slot(q3_engine* e, size_t layer, size_t pos, uint16_t* k_host, uint16_t* v_host);
 Q3_API int q3_engine_fill_kv(q3_engine* e, size_t upto, uint64_t seed); /* synthetic KV for timing windows */
+/* KVCache contents (kv_cache.hpp:6-29: per layer key / value [capacity,
+ * kv_heads, head_dim], slot p = key.select(p)) for slots [pos0, pos0 + n) of
+ * one layer, as host arrays in that layout [n][kv_heads][128] (this rank's kv
+ * heads).  kv_write makes the written slots count as computed, so
+ * q3_engine_set_position may move the cursor to pos0 + n: a decode can resume
+ * from a KV history produced elsewhere (another engine, the reference). */
+Q3_API int q3_engine_kv_read(q3_engine* e, size_t layer, size_t pos0, size_t n, uint16_t* k_host, uint16_t* v_host);
+Q3_API int q3_engine_kv_write(q3_engine* e, size_t layer, size_t pos0, size_t n, const uint16_t* k_host,
+                              const uint16_t* v_host);
 
 /* Device pointers / sizes for instrumentation and tests. */
 Q3_API int q3_engine_stream(q3_engine* e, void** stream);

@@ -57,6 +57,8 @@ SIGNATURES = {
     "q3_engine_set_position": (C.c_int, [_vp, _sz]),
     "q3_engine_set_persistent": (C.c_int, [_vp, C.c_int]),
     "q3_engine_is_persistent": (C.c_int, [_vp]),
+    "q3_engine_set_lookahead": (C.c_int, [_vp, C.c_int, C.c_int]),
+    "q3_engine_lookahead": (C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "q3_engine_set_tuning": (C.c_int, [_vp, C.c_uint32]),
     "q3_engine_tuning": (C.c_int, [_vp, C.POINTER(C.c_uint32)]),
     "q3_engine_trace": (C.c_int, [_vp, C.c_int, _vp, _sz, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
@@ -65,6 +67,8 @@ SIGNATURES = {
     "q3_engine_argmax_history": (C.c_int, [_vp, _u32p, _sz]),
     "q3_engine_kv_slot": (C.c_int, [_vp, _sz, _sz, _u16p, _u16p]),
     "q3_engine_fill_kv": (C.c_int, [_vp, _sz, C.c_uint64]),
+    "q3_engine_kv_read": (C.c_int, [_vp, _sz, _sz, _sz, _u16p, _u16p]),
+    "q3_engine_kv_write": (C.c_int, [_vp, _sz, _sz, _sz, _u16p, _u16p]),
     "q3_engine_stream": (C.c_int, [_vp, C.POINTER(C.c_void_p)]),
     "q3_engine_weight_bytes": (_sz, [_vp]),
     "q3_engine_kv_bytes_per_position": (_sz, [_vp]),

@@ -161,6 +161,14 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
 
     if (warp == kWarps) {
         // ------------------------------------------------------------ producer
+        if (lane == 1 && a.pf) {
+            // the next weight stream into L2 while this kernel's page math runs
+            const size_t ctas = static_cast<size_t>(gridDim.x) * gridDim.y * gridDim.z;
+            const size_t me = blockIdx.x + static_cast<size_t>(gridDim.x) * (blockIdx.y + gridDim.y * blockIdx.z);
+            const size_t units = a.pf_bytes / 16;
+            const size_t u0 = me * units / ctas, u1 = (me + 1) * units / ctas;
+            if (u1 > u0) prefetch_l2(static_cast<const uint8_t*>(a.pf) + u0 * 16, (u1 - u0) * 16);
+        }
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             bool waited = false;

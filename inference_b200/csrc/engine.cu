@@ -76,6 +76,10 @@ struct q3_engine {
     // attention's ring depth under Q3_TUNE_ATTN_DEEP_RING
     uint32_t tune = 0;
     int attn_deep_stages = 2;
+    // L2 lookahead of the weight streams (q3_engine_set_lookahead): items per GEMV warp
+    // prefetched before the dependency wait, and whether attention prefetches W_o
+    int lookahead = 0;
+    int attn_pf = 0;
     // persistent decode kernel (one launch per run of steps)
     bool persistent = false;
     q3::PersistentArgs pargs{};
@@ -198,6 +202,7 @@ GemvArgs base_args(q3_engine* e) {
     GemvArgs a{};
     if (e->peer_mode) a.peer = e->links;
     a.tune = e->tune;
+    a.lookahead = e->lookahead;
     a.eps = e->cfg.eps;
     a.err = e->err;
     a.capacity = static_cast<int>(e->cfg.capacity);
@@ -254,6 +259,11 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.eps = e->cfg.eps;
     a.stages = (e->tune & Q3_TUNE_ATTN_DEEP_RING) ? e->attn_deep_stages : 2;
     a.live_prefetch = (e->tune & Q3_TUNE_ATTN_LIVE_PREFETCH) ? 1 : 0;
+    if (e->attn_pf) {
+        // the o_proj weights that the GEMV after this kernel streams
+        a.pf = e->fp8 ? static_cast<const void*>(L.f_o) : static_cast<const void*>(L.w_o);
+        a.pf_bytes = e->fp8 ? f8_packed_bytes(e->H, e->qd) : static_cast<size_t>(e->H) * e->qd * 2;
+    }
     a.trace = r.trace();
     r.mark(true, 1);
     cudaError_t st = launch_attention(a, e->stream, r.pdl);
@@ -1308,6 +1318,29 @@ int q3_engine_set_persistent(q3_engine* e, int enable) {
 
 int q3_engine_is_persistent(q3_engine* e) { return (e && e->persistent) ? 1 : 0; }
 
+int q3_engine_lookahead(q3_engine* e, int* items, int* attention_prefetch) {
+    Q3_CHECK(e && items && attention_prefetch, "null argument");
+    *items = e->lookahead;
+    *attention_prefetch = e->attn_pf;
+    return Q3_OK;
+}
+
+int q3_engine_set_lookahead(q3_engine* e, int items, int attention_prefetch) {
+    Q3_CHECK(e, "null engine");
+    Q3_CHECK(items >= 0 && items <= 64, "q3_engine_set_lookahead: items must be in [0, 64]");
+    if (items == e->lookahead && (attention_prefetch != 0) == (e->attn_pf != 0)) return Q3_OK;
+    Q3_CUDA(cudaSetDevice(e->device));
+    if (e->graph) {
+        // the step graph holds the launch arguments: record it again at the next step
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_CUDA(cudaGraphExecDestroy(e->graph));
+        e->graph = nullptr;
+    }
+    e->lookahead = items;
+    e->attn_pf = attention_prefetch != 0;
+    return Q3_OK;
+}
+
 int q3_engine_set_tuning(q3_engine* e, uint32_t flags) {
     Q3_CHECK(e, "null engine");
     Q3_CHECK((flags & ~Q3_TUNE_ALL) == 0u, "q3_engine_set_tuning: unknown flag bits");
@@ -1428,6 +1461,52 @@ int q3_engine_kv_slot(q3_engine* e, size_t layer, size_t pos, uint16_t* k_out, u
         Q3_CUDA(cudaMemcpy(k_out + h * 128, L.k_pages + off, 256, cudaMemcpyDeviceToHost));
         Q3_CUDA(cudaMemcpy(v_out + h * 128, L.v_pages + off, 256, cudaMemcpyDeviceToHost));
     }
+    return Q3_OK;
+}
+
+// Slots [pos0, pos0 + n) of one layer between the paged cache and host arrays
+// in the reference layout [n][kv_heads][128]: one strided copy per (page, head).
+static int kv_range_copy(q3_engine* e, size_t layer, size_t pos0, size_t n, uint16_t* k_host, uint16_t* v_host,
+                         bool to_device) {
+    Q3_CHECK(e && k_host && v_host, "null argument");
+    Q3_CHECK(layer < e->layers.size() && pos0 <= e->cfg.capacity && n <= e->cfg.capacity - pos0,
+             "kv range out of range");
+    Q3_CUDA(cudaSetDevice(e->device));
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    std::vector<int32_t> table((e->cfg.capacity + kPageSize - 1) / kPageSize);
+    Q3_CUDA(cudaMemcpy(table.data(), e->page_table, table.size() * 4, cudaMemcpyDeviceToHost));
+    const q3::LayerW& L = e->layers[layer];
+    const size_t row = 128 * sizeof(uint16_t), host_pitch = static_cast<size_t>(e->kvh) * row;
+    for (size_t p = pos0; p < pos0 + n;) {
+        const size_t in_page = std::min<size_t>(kPageSize - p % kPageSize, pos0 + n - p);
+        const int32_t page = table[p / kPageSize];
+        for (int h = 0; h < e->kvh; ++h) {
+            const size_t off = ((static_cast<size_t>(page) * e->kvh + h) * kPageSize + p % kPageSize) * 128;
+            const size_t hoff = ((p - pos0) * e->kvh + h) * 128;
+            for (int which = 0; which < 2; ++which) {
+                q3::bf16* d = (which ? L.v_pages : L.k_pages) + off;
+                uint16_t* hp = (which ? v_host : k_host) + hoff;
+                if (to_device)
+                    Q3_CUDA(cudaMemcpy2DAsync(d, row, hp, host_pitch, row, in_page, cudaMemcpyHostToDevice, e->stream));
+                else
+                    Q3_CUDA(cudaMemcpy2DAsync(hp, host_pitch, d, row, row, in_page, cudaMemcpyDeviceToHost, e->stream));
+            }
+        }
+        p += in_page;
+    }
+    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    return Q3_OK;
+}
+
+int q3_engine_kv_read(q3_engine* e, size_t layer, size_t pos0, size_t n, uint16_t* k_host, uint16_t* v_host) {
+    return kv_range_copy(e, layer, pos0, n, k_host, v_host, false);
+}
+
+int q3_engine_kv_write(q3_engine* e, size_t layer, size_t pos0, size_t n, const uint16_t* k_host,
+                       const uint16_t* v_host) {
+    Q3_TRY(kv_range_copy(e, layer, pos0, n, const_cast<uint16_t*>(k_host), const_cast<uint16_t*>(v_host), true));
+    // the written slots count as computed: set_position may move the cursor up to them
+    if (pos0 + n > e->host_max_pos) e->host_max_pos = pos0 + n;
     return Q3_OK;
 }
 

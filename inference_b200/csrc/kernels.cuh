@@ -114,6 +114,10 @@ struct GemvArgs {
     PeerLinks peer;
     int xtag;
     uint32_t tune;             // Q3_TUNE_PEER_* bits (q3_engine_set_tuning)
+    // ---- L2 lookahead: each warp prefetches into L2, before the dependency wait, the
+    // `lookahead` items of its run that follow the ones its shared-memory ring holds, so
+    // the weight stream keeps HBM busy through the wait and the prologue (0 = off)
+    int lookahead;
     // ---- errors
     uint32_t* err;
     LaunchTrace trace;
@@ -158,6 +162,10 @@ struct AttnArgs {
     // (written by the QKV GEMV) is read after it and patched into the tile.
     int stages;
     int live_prefetch;
+    // L2 prefetch of the next weight stream while the page math runs: each CTA of the
+    // grid prefetches its even share of [pf, pf + pf_bytes) at its start (null = off)
+    const void* pf;
+    size_t pf_bytes;
     LaunchTrace trace;
 };
 // K/V pages in flight per CTA for the decode grid (splits x kv_heads x

@@ -2,11 +2,10 @@
 //
 // q3_argmax keeps its reduction word in device memory it allocates on first
 // use.  Some callers cannot let a library allocate: serving runtimes that plan
-// every byte of device memory up front, code that records work while a stream
-// is being captured into a CUDA graph in global capture mode (cudaMalloc is
-// not permitted then), and latency-critical loops that cannot absorb
-// cudaMalloc's implicit device synchronisation.  This variant keeps its
-// scratch in a fixed array compiled into the library instead.
+// every byte of device memory up front and hand libraries only buffers they
+// own, and latency-critical loops that cannot absorb cudaMalloc's implicit
+// device synchronisation.  This variant keeps its scratch in a fixed array
+// compiled into the library instead.
 //
 // Scratch: kSegments keys of 8 bytes (32 KB), one per 4096-logit segment, so
 // the largest input is kSegments * kSegment = 16,777,216 logits; larger inputs
@@ -18,7 +17,10 @@
 //
 // The array's host-side name is not a device address.  The first call on each
 // device, with that device current, resolves the address once with
-// cudaGetSymbolAddress; make that first call before any stream capture.
+// cudaGetSymbolAddress; make that first call before any stream capture.  The
+// address is cached for the life of the process: the library must not be used
+// across a cudaDeviceReset of that device (the reset frees the module's
+// memory, and later calls would launch with the stale address).
 #include <mutex>
 #include <string>
 

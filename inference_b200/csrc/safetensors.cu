@@ -11,6 +11,7 @@
 // File format: 8-byte little-endian header length N, N bytes of JSON
 // {"name": {"dtype": "BF16", "shape": [r, c], "data_offsets": [b, e]}, ...,
 // "__metadata__": {...}}, then the data; offsets are relative to the data.
+#include <cmath>
 #include <fcntl.h>
 #include <sys/mman.h>
 #include <sys/stat.h>
@@ -235,6 +236,16 @@ size_t dtype_size(const std::string& d) {
     return 0;
 }
 
+// A JSON number that is an exact non-negative integer below 2^53 (every such
+// integer is a double exactly; larger or fractional values, negative numbers,
+// NaN and non-numbers are rejected before any conversion to uint64_t).
+bool json_index(const Json& j, uint64_t& out) {
+    if (j.kind != Json::Num || !(j.num >= 0.0) || !(j.num < 9007199254740992.0) || j.num != std::floor(j.num))
+        return false;
+    out = static_cast<uint64_t>(j.num);
+    return true;
+}
+
 // The tensors of one safetensors file, validated against its size.
 bool scan_file(const std::string& path, std::vector<Tensor>& out, std::string& err) {
     const int fd = open(path.c_str(), O_RDONLY);
@@ -280,17 +291,28 @@ bool scan_file(const std::string& path, std::vector<Tensor>& out, std::string& e
         t.dtype = dt->str;
         t.file = path;
         uint64_t elems = 1;
+        bool overflow = false;
         for (const Json& d : sh->arr) {
-            if (d.kind != Json::Num || d.num < 0) {
+            uint64_t dim = 0;
+            if (!json_index(d, dim)) {
                 err = path + ": bad shape of " + kv.first;
                 return false;
             }
-            t.shape.push_back(static_cast<uint64_t>(d.num));
-            elems *= t.shape.back();
+            t.shape.push_back(dim);
+            overflow = overflow || __builtin_mul_overflow(elems, dim, &elems);
         }
-        const uint64_t b = static_cast<uint64_t>(of->arr[0].num), e = static_cast<uint64_t>(of->arr[1].num);
+        uint64_t b = 0, e = 0, nbytes = 0;
+        if (!json_index(of->arr[0], b) || !json_index(of->arr[1], e)) {
+            err = path + ": data offsets of " + kv.first + " are not non-negative integers below 2^53";
+            return false;
+        }
         const size_t es = dtype_size(t.dtype);
-        if (e < b || e > dsize || (es && e - b != elems * es)) {
+        overflow = overflow || __builtin_mul_overflow(elems, static_cast<uint64_t>(es ? es : 1), &nbytes);
+        if (overflow) {
+            err = path + ": shape of " + kv.first + " overflows 64 bits";
+            return false;
+        }
+        if (e < b || e > dsize || (es && e - b != nbytes)) {
             err = path + ": data offsets of " + kv.first + " out of range or inconsistent with its shape";
             return false;
         }

@@ -133,6 +133,16 @@ class Engine:
     def persistent(self, on: bool):
         check(lib().q3_engine_set_persistent(self.h, int(bool(on))))
 
+    def lookahead(self):
+        """(items per GEMV warp, attention prefetch) of q3_engine_set_lookahead."""
+        i, a = C.c_int(), C.c_int()
+        check(lib().q3_engine_lookahead(self.h, C.byref(i), C.byref(a)))
+        return int(i.value), bool(a.value)
+
+    def set_lookahead(self, items: int, attention_prefetch: bool):
+        """L2 lookahead of the weight streams (q3_engine_set_lookahead)."""
+        check(lib().q3_engine_set_lookahead(self.h, int(items), int(bool(attention_prefetch))))
+
     # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
     TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2, "deep_ring": 0x4, "live_prefetch": 0x8,
                   "tp_prefill": 0x10, "fp8_prefill": 0x20}
@@ -202,6 +212,23 @@ class Engine:
         v = np.empty((kvh, 128), np.uint16)
         check(lib().q3_engine_kv_slot(self.h, layer, pos, _ptr(k), _ptr(v)))
         return k, v
+
+    def kv_read(self, layer: int, pos0: int, n: int):
+        """K and V slots [pos0, pos0 + n) of a layer as [n, kv_heads, 128] BF16 bits
+        (the reference's KV layout; this rank's kv heads)."""
+        kvh = self.cfg.kv_heads // self.tp_size
+        k = np.empty((n, kvh, 128), np.uint16)
+        v = np.empty((n, kvh, 128), np.uint16)
+        check(lib().q3_engine_kv_read(self.h, layer, pos0, n, _ptr(k), _ptr(v)))
+        return k, v
+
+    def kv_write(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray):
+        """Overwrite K and V slots [pos0, pos0 + len(k)) of a layer (reference layout)."""
+        k = np.ascontiguousarray(k, dtype=np.uint16)
+        v = np.ascontiguousarray(v, dtype=np.uint16)
+        if k.shape != v.shape:
+            raise ValueError("k and v shapes differ")
+        check(lib().q3_engine_kv_write(self.h, layer, pos0, k.shape[0], _ptr(k), _ptr(v)))
 
     def stream(self) -> int:
         s = C.c_void_p()

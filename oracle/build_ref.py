@@ -30,6 +30,12 @@ REF_OUT = os.path.join(HERE, "_ref")
 DEFAULT_REFERENCE = "/root/reference"
 
 
+def reference_dir() -> str:
+    """Where the reference's sources are read from: $Q3_REFERENCE_DIR if set,
+    else this recipe's default location."""
+    return os.environ.get("Q3_REFERENCE_DIR") or DEFAULT_REFERENCE
+
+
 def _site_packages() -> str:
     import sysconfig
 
@@ -157,10 +163,12 @@ def build_ref_b200(reference: str, force: bool = False) -> str | None:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", default=None, help="reference source tree (default: $Q3_REFERENCE_DIR, "
+                    "else the recipe's default location)")
     ap.add_argument("--no-cuda", action="store_true")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args(argv)
+    a.reference = a.reference or reference_dir()
     build_oracle(a.force)
     if os.path.isdir(a.reference):
         build_ref_cpu(a.reference, a.force)

@@ -248,6 +248,7 @@ class RefLib:
         L.ref_model_token_count.argtypes = [C.c_void_p]
         L.ref_model_token_count.restype = _sz
         L.ref_model_fill_kv.argtypes = [C.c_void_p, _sz, C.c_uint64]
+        L.ref_model_kv_range.argtypes = [C.c_void_p, _sz, _sz, _sz, _u16p, _u16p, C.c_int]
 
     def _check(self, rc):
         if rc != 0:
@@ -357,3 +358,16 @@ class RefModel:
         v = np.empty(kd, np.uint16)
         self.r._check(self.r.lib.ref_model_kv_slot(self.h, layer, pos, k, v))
         return k.reshape(self.cfg.kv_heads, -1), v.reshape(self.cfg.kv_heads, -1)
+
+    def kv_read(self, layer, pos0, n):
+        """Key / value slots [pos0, pos0 + n) of a layer, [n, kv_heads, head_dim] BF16 bits."""
+        k = np.empty((n, self.cfg.kv_heads, self.cfg.head_dim), np.uint16)
+        v = np.empty_like(k)
+        self.r._check(self.r.lib.ref_model_kv_range(self.h, layer, pos0, n, k, v, 0))
+        return k, v
+
+    def kv_write(self, layer, pos0, k, v):
+        """Overwrite key / value slots [pos0, pos0 + len(k)) of a layer."""
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        self.r._check(self.r.lib.ref_model_kv_range(self.h, layer, pos0, k.shape[0], k, v, 1))

@@ -88,7 +88,8 @@ static inline uint64_t mix64(uint64_t z) {
  * Element (r, c) of a tensor with `full_cols` columns uses counter
  * (tensor_id << 40) | (r * full_cols + c), so any row/column slice (a
  * tensor-parallel shard) reproduces the matching part of the full tensor.
- * The GPU generator in inference_b200/csrc/init.cu computes the same bits. */
+ * The GPU generator (fill_normal_kernel, inference_b200/csrc/small_ops.cu)
+ * computes the same bits. */
 static inline uint16_t normal_bf16(uint64_t key, uint64_t tensor_id, uint64_t flat) {
     uint64_t h = mix64(key ^ ((tensor_id << 40) | flat));
     int32_t s = (int32_t)(h & 0xFFFF) + (int32_t)((h >> 16) & 0xFFFF) + (int32_t)((h >> 32) & 0xFFFF) +

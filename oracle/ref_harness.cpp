@@ -292,6 +292,38 @@ int ref_model_kv_slot(void* h, std::size_t layer, std::size_t pos, std::uint16_t
     });
 }
 
+// Slots [pos0, pos0 + n) of one layer's key / value caches (layout [capacity,
+// kv_heads, head_dim], kv_cache.hpp:6-24) to / from host arrays [n][kv_heads][hd].
+int ref_model_kv_range(void* h, std::size_t layer, std::size_t pos0, std::size_t n, std::uint16_t* k, std::uint16_t* v,
+                       int to_model) {
+    auto* r = static_cast<RefModel*>(h);
+    return guarded([&] {
+        auto& layer_kv = r->kv.layers.at(layer);
+        const auto per = layer_kv.key.size() / r->kv.capacity;  // kv_heads * head_dim
+        if (pos0 > r->kv.capacity || n > r->kv.capacity - pos0) throw std::out_of_range("kv range");
+        const auto off = pos0 * per * sizeof(std::uint16_t), bytes = n * per * sizeof(std::uint16_t);
+        auto* kd = layer_kv.key.data<std::byte>() + off;
+        auto* vd = layer_kv.value.data<std::byte>() + off;
+#ifdef REF_CUDA
+        const auto dir = to_model ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToHost;
+        if (cudaDeviceSynchronize() != cudaSuccess) throw std::runtime_error("cudaDeviceSynchronize failed");
+        if (cudaMemcpy(to_model ? static_cast<void*>(kd) : static_cast<void*>(k), to_model ? static_cast<const void*>(k)
+                       : static_cast<const void*>(kd), bytes, dir) != cudaSuccess ||
+            cudaMemcpy(to_model ? static_cast<void*>(vd) : static_cast<void*>(v), to_model ? static_cast<const void*>(v)
+                       : static_cast<const void*>(vd), bytes, dir) != cudaSuccess)
+            throw std::runtime_error("cudaMemcpy of the KV range failed");
+#else
+        if (to_model) {
+            std::memcpy(kd, k, bytes);
+            std::memcpy(vd, v, bytes);
+        } else {
+            std::memcpy(k, kd, bytes);
+            std::memcpy(v, vd, bytes);
+        }
+#endif
+    });
+}
+
 std::size_t ref_model_token_count(void* h) { return static_cast<RefModel*>(h)->kv.token_count; }
 void ref_model_set_token_count(void* h, std::size_t n) { static_cast<RefModel*>(h)->kv.token_count = n; }
 

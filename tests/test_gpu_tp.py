@@ -71,6 +71,9 @@ def _rank_main(rank, world, port, name, out_dir, mode):
         shards.append(e.logits())
     hist = e.argmax_history(len(toks))
     np.savez(os.path.join(out_dir, f"tp{rank}.npz"), logits=np.stack(shards), hist=hist)
+    # peers read and write this rank's exchange buffer: every rank idle before any rank frees it
+    e.sync()
+    dist.barrier()
     e.close()
     dist.barrier()
     dist.destroy_process_group()

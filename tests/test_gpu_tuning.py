@@ -48,12 +48,17 @@ def test_attention_variants_bit_identical(kv_heads, q_heads, hidden, inter):
     cap = 8192
     ids = prompt_ids(cap, seed=1)
     runs = {}
-    for flags in (0, DECODE_FLAGS):
+    # (tuning flags, L2 lookahead items, attention prefetch): prefetches change no arithmetic
+    variants = ((0, 0, False), (DECODE_FLAGS, 0, False), (0, 8, True), (DECODE_FLAGS, 3, True))
+    for var in variants:
+        flags, items, attn_pf = var
         logits, kv = [], []
         with Engine(cfg, capacity=cap) as e:
             e.init_synthetic(0)
             e.tuning = flags
             assert e.tuning == flags
+            e.set_lookahead(items, attn_pf)
+            assert e.lookahead() == (items, attn_pf)
             e.set_tokens(ids)
 
             def window(n):
@@ -70,13 +75,15 @@ def test_attention_variants_bit_identical(kv_heads, q_heads, hidden, inter):
             e.fill_kv(8180)
             window(11)         # 8180..8190: 128 pages, 8 per split (every ring depth refills)
             hist = e.argmax_history(8191)
-        runs[flags] = (logits, kv, hist)
-    base, tuned = runs[0], runs[DECODE_FLAGS]
-    for i, (a, b) in enumerate(zip(base[0], tuned[0])):
-        assert np.array_equal(a, b), f"step {i}: logits differ"
-    for i, ((k0, v0), (k1, v1)) in enumerate(zip(base[1], tuned[1])):
-        assert np.array_equal(k0, k1) and np.array_equal(v0, v1), f"step {i}: KV slot differs"
-    assert np.array_equal(base[2], tuned[2])
+        runs[var] = (logits, kv, hist)
+    base = runs[variants[0]]
+    for var in variants[1:]:
+        tuned = runs[var]
+        for i, (a, b) in enumerate(zip(base[0], tuned[0])):
+            assert np.array_equal(a, b), f"{var} step {i}: logits differ"
+        for i, ((k0, v0), (k1, v1)) in enumerate(zip(base[1], tuned[1])):
+            assert np.array_equal(k0, k1) and np.array_equal(v0, v1), f"{var} step {i}: KV slot differs"
+        assert np.array_equal(base[2], tuned[2])
 
 
 @pytest.mark.parametrize("name", ["qwen3_0p6b", "qwen3_8b_l2", "qwen3_32b_l1"])

@@ -101,3 +101,29 @@ def test_malformed_files_are_rejected(tmp_path):
     _expect_error(d, "ghost.weight")
     # nothing to load
     _expect_error(tmp_path / "nowhere", "cannot open")
+
+
+def test_hostile_header_numbers_are_rejected(tmp_path):
+    """Shapes whose element count wraps 64 bits, data offsets that are not
+    numbers, and fractional or >= 2^53 numbers are rejected, not converted."""
+    ts = _tensors()
+    # 2^33 x 2^31 BF16 elements: the element count wraps to 0 in uint64, matching empty offsets
+    p = tmp_path / "wrap.safetensors"
+    write_safetensors(p, ts, header_patch=lambda h: h["model.norm.weight"].update(shape=[2 ** 33, 2 ** 31],
+                                                                               data_offsets=[0, 0]))
+    _expect_error(p, "overflows")
+    # data offsets given as strings
+    p = tmp_path / "strings.safetensors"
+    write_safetensors(p, ts, header_patch=lambda h: h["model.norm.weight"].update(data_offsets=["0", "16"]))
+    _expect_error(p, "not non-negative integers")
+    # a fractional offset and one at 2^53 (no exact uint64 conversion is defined for them)
+    p = tmp_path / "frac.safetensors"
+    write_safetensors(p, ts, header_patch=lambda h: h["model.norm.weight"].update(data_offsets=[0.5, 16.5]))
+    _expect_error(p, "not non-negative integers")
+    p = tmp_path / "huge.safetensors"
+    write_safetensors(p, ts, header_patch=lambda h: h["model.norm.weight"].update(data_offsets=[2 ** 53, 2 ** 53 + 16]))
+    _expect_error(p, "not non-negative integers")
+    # a fractional or negative dimension
+    p = tmp_path / "dimfrac.safetensors"
+    write_safetensors(p, ts, header_patch=lambda h: h["model.norm.weight"].update(shape=[7.5]))
+    _expect_error(p, "bad shape")

@@ -1,6 +1,7 @@
 """q3_argmax_noalloc: the greedy argmax for callers that cannot let the
-library allocate device memory (pre-planned serving memory, global stream
-capture, allocation-free hot loops).  Its scratch is a fixed array inside
+library allocate device memory (serving runtimes that plan every byte of
+device memory themselves, hot loops that cannot take cudaMalloc's implicit
+synchronisation).  Its scratch is a fixed array inside
 the library; this checks it against q3_argmax, which allocates its own
 scratch, through the C ABI, on two calls in a row -- the second call must
 not be disturbed by what the first left in the shared array.
