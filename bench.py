@@ -60,7 +60,7 @@ def parse_args(argv=None):
     ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path (the default) even "
                                                           "where the persistent kernel was selected")
     ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
-                    "batched_poll, no_grid_wait, deep_ring, live_prefetch, tp_prefill, fp8_prefill, or all")
+                    "batched_poll, no_grid_wait, tp_prefill, fp8_prefill, or all")
     ap.add_argument("--lookahead", type=int, default=None,
                     help="L2 lookahead items per GEMV warp (q3_engine_set_lookahead; default: the engine's)")
     ap.add_argument("--attn-prefetch", type=int, default=None, choices=[0, 1],

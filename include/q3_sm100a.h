@@ -293,12 +293,6 @@ Q3_API int q3_engine_lookahead(q3_engine* e, int* items, int* attention_prefetch
  *     up to four ranks at once instead of one rank per round trip;
  *   Q3_TUNE_PEER_NO_GRID_WAIT: those prologues start on the (value, tag)
  *     pairs alone, without griddepcontrol.wait on the producing GEMV;
- *   Q3_TUNE_ATTN_DEEP_RING: decode attention keeps four K/V pages per CTA in
- *     flight instead of two, where its grid (splits x kv heads x head blocks)
- *     can be resident at one CTA per SM;
- *   Q3_TUNE_ATTN_LIVE_PREFETCH: decode attention also fetches the page of the
- *     current position before the dependency wait and patches that
- *     position's V row in shared memory after it;
  *   Q3_TUNE_TP_PREFILL: tensor-parallel engines prefill with the batched
  *     tcgen05 GEMMs on their shards (row-parallel outputs exchanged as fp32
  *     partials) instead of one decode step per prompt token.  Unlike the
@@ -312,11 +306,9 @@ Q3_API int q3_engine_lookahead(q3_engine* e, int* items, int* attention_prefetch
  * Unknown bits return Q3_ERR_INVALID. */
 #define Q3_TUNE_PEER_BATCHED_POLL 0x1u
 #define Q3_TUNE_PEER_NO_GRID_WAIT 0x2u
-#define Q3_TUNE_ATTN_DEEP_RING 0x4u
-#define Q3_TUNE_ATTN_LIVE_PREFETCH 0x8u
 #define Q3_TUNE_TP_PREFILL 0x10u
 #define Q3_TUNE_FP8_PREFILL 0x20u
-#define Q3_TUNE_ALL 0x3Fu
+#define Q3_TUNE_ALL 0x33u /* bits 0x4 and 0x8 are unused (invalid) */
 Q3_API int q3_engine_set_tuning(q3_engine* e, uint32_t flags);
 Q3_API int q3_engine_tuning(q3_engine* e, uint32_t* flags);
 
@@ -401,6 +393,17 @@ Q3_API int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n_ra
  * shared by the caller (e.g. torch.distributed), then every rank attaches. */
 Q3_API int q3_nccl_unique_id(void* id_out_128_bytes);
 Q3_API int q3_engine_attach_nccl(q3_engine* e, const void* id_128_bytes);
+
+/* Failure detection on the NCCL path (no counterpart in the reference, which
+ * has no multi-GPU path): the communicator is created non-blocking, and every
+ * host wait on the engine's stream (q3_engine_sync and the calls that read
+ * state back) gives up after `seconds` plus 0.25 s per decode step queued
+ * since the last wait.  A rank whose peer has gone -- exited, or never stepped
+ * -- then aborts its communicator (its NCCL kernels return), reports
+ * Q3_ERR_NCCL, and refuses further steps; the engine can still be destroyed.
+ * Default 60 s.  Peer-memory engines bound their waits on the device instead
+ * (Q3_ERR_DEVICE "peer wait timed out"). */
+Q3_API int q3_engine_set_comm_timeout(q3_engine* e, double seconds);
 
 #ifdef __cplusplus
 }

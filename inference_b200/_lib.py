@@ -80,6 +80,7 @@ SIGNATURES = {
     "q3_engine_peer_handle": (C.c_int, [_vp, _vp]),
     "q3_engine_attach_peers": (C.c_int, [_vp, _vp, _sz]),
     "q3_engine_attach_nccl": (C.c_int, [_vp, _vp]),
+    "q3_engine_set_comm_timeout": (C.c_int, [_vp, C.c_double]),
 }
 
 

@@ -43,12 +43,15 @@ constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kTileBytes = kPage * kHd * 2;  // 16 KB
 constexpr float kLog2e = 1.4426950408889634f;
 
-// ST: K/V pages in flight per CTA (ring stages): 2 by default; with
-// Q3_TUNE_ATTN_DEEP_RING 3 (still two CTAs per SM: <= 110 KB each) or 4 (one
-// CTA per SM), as attn_deep_ring_stages picks for the grid.
-template <int HG, int ST>
+// K/V pages in flight per CTA (ring stages).  Deeper rings (3 at two CTAs per
+// SM, 4 at one) were measured on B200 and gained nothing at Qwen3-8B context
+// 2300 or Qwen3-0.6B context 8192: the split count, not the ring, bounds the
+// pages a CTA streams.
+constexpr int kStages = 2;
+
+template <int HG>
 struct AttnSmem {
-    uint8_t kv[ST][2][kTileBytes];
+    uint8_t kv[kStages][2][kTileBytes];
     float m[kWarps][HG];  // per consumer warp: running max, sum, accumulators
     float l[kWarps][HG];
     float acc[kWarps][HG][kHd];
@@ -57,8 +60,8 @@ struct AttnSmem {
     float cacc[HG][kHd];
     bf16 qn[HG][kHd];  // normalised, rotated q heads (fused q/k norm)
     bf16 kn[kHd];      // normalised, rotated key row of the position
-    uint64_t full[ST];
-    uint64_t empty[ST];
+    uint64_t full[kStages];
+    uint64_t empty[kStages];
 };
 
 __device__ __forceinline__ void ldmatrix_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -117,11 +120,10 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 
 __device__ __forceinline__ void fence_proxy_async_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-template <int HG, int ST>
-__global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const __grid_constant__ AttnArgs a) {
-    constexpr int kStages = ST;
+template <int HG>
+__global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    AttnSmem<HG, ST>& S = *reinterpret_cast<AttnSmem<HG, ST>*>(smem_raw);
+    AttnSmem<HG>& S = *reinterpret_cast<AttnSmem<HG>*>(smem_raw);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool tracing = a.trace.buf != nullptr;
@@ -155,9 +157,6 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
     const int pe = static_cast<int>(static_cast<long long>(split + 1) * n_pages / a.splits);
     const int np = pe - pb;
     const int live_page = pos / kPage;  // receives this step's K/V from the QKV kernel
-    // Q3_TUNE_ATTN_LIVE_PREFETCH: the live page streams before the wait too; its
-    // one new V row is patched in after it (its K row always is, from S.kn)
-    const bool live_pf = a.live_prefetch && a.paged && a.k_raw != nullptr && a.n_queries <= 1;
 
     if (warp == kWarps) {
         // ------------------------------------------------------------ producer
@@ -177,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
                 if (i >= kStages && !mbar_wait(&S.empty[s], ((i / kStages) - 1) & 1, a.err, DEV_TMA_WAIT_TIMEOUT))
                     break;
                 const int page = pb + i;
-                if (page >= live_page && !waited && !live_pf) {
+                if (page >= live_page && !waited) {
                     pdl_wait();
                     waited = true;
                 }
@@ -217,15 +216,6 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
         pdl_wait();  // q comes from the QKV kernel
         pdl_trigger();
         if (tracing && tid == 0) tr_c1 = clock64();
-        // live_pf: the warp holding the position's row reads its V row (written by the
-        // QKV GEMV) now, while q/k norm runs, and patches it into the tile below
-        const bool v_patch = live_pf && has_live && warp == (pos % kPage) / 16;
-        uint4 vrow = make_uint4(0u, 0u, 0u, 0u);
-        if (v_patch && lane < 16) {
-            const bf16* vsrc =
-                a.v + ((static_cast<size_t>(a.page_table[live_page]) * a.kv_heads + kvh) * kPage + pos % kPage) * kHd;
-            vrow = __ldcg(reinterpret_cast<const uint4*>(vsrc) + lane);
-        }
         const int g = lane >> 2, t4 = lane & 3;  // fragment row (query head) and column pair
         const int qh0 = kvh * G + qb * HG;
         const float qscale = (1.0f / sqrtf(static_cast<float>(kHd))) * kLog2e;
@@ -274,12 +264,9 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
                 uint8_t* vt = S.kv[s][1];
                 if (has_live && page == live_page && warp == (pos % kPage) / 16) {
                     // this step's key row: the cache slot still holds the raw row (or older data)
-                    if (lane < 16) {
+                    if (lane < 16)
                         reinterpret_cast<uint4*>(kt + (pos % kPage) * 256)[lane] =
                             reinterpret_cast<const uint4*>(S.kn)[lane];
-                        // and, fetched before the wait, the V row may predate the QKV GEMV's store
-                        if (v_patch) reinterpret_cast<uint4*>(vt + (pos % kPage) * 256)[lane] = vrow;
-                    }
                     __syncwarp();
                 }
                 // ---- swizzle this warp's rows in place; rows past the position become zeros in V
@@ -434,12 +421,12 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
             const int g = o / kHd, d = o % kHd;
             float M = -INFINITY;
             for (int sp = 0; sp < a.splits; ++sp) {
-                const AttnSmem<HG, ST>* R = cluster.map_shared_rank(&S, sp);
+                const AttnSmem<HG>* R = cluster.map_shared_rank(&S, sp);
                 M = fmaxf(M, R->cm[g]);
             }
             float Lsum = 0.f, A = 0.f;
             for (int sp = sub; sp < a.splits; sp += tpo) {
-                const AttnSmem<HG, ST>* R = cluster.map_shared_rank(&S, sp);
+                const AttnSmem<HG>* R = cluster.map_shared_rank(&S, sp);
                 const float ms = R->cm[g];
                 if (ms == -INFINITY) continue;
                 const float f = exp2f(ms - M);
@@ -476,10 +463,10 @@ __global__ void __launch_bounds__(kThreads, ST <= 3 ? 2 : 1) attn_kernel(const _
 
 int heads_per_cta(int G) { return G >= 4 ? 4 : G; }
 
-template <int HG, int ST>
+template <int HG>
 cudaError_t launch_hg(const AttnArgs& a, cudaStream_t s, bool pdl, int nqb) {
-    auto* fn = attn_kernel<HG, ST>;
-    const size_t smem = sizeof(AttnSmem<HG, ST>);
+    auto* fn = attn_kernel<HG>;
+    const size_t smem = sizeof(AttnSmem<HG>);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, a.kv_heads, nqb * (a.n_queries > 1 ? a.n_queries : 1));
     cfg.blockDim = dim3(kThreads);
@@ -502,22 +489,22 @@ cudaError_t launch_hg(const AttnArgs& a, cudaStream_t s, bool pdl, int nqb) {
     return cudaLaunchKernelEx(&cfg, fn, a);
 }
 
-template <int HG, int ST>
+template <int HG>
 cudaError_t configure_hg() {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel<HG, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(sizeof(AttnSmem<HG, ST>)));
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(sizeof(AttnSmem<HG>)));
     if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(attn_kernel<HG, ST>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        e = cudaFuncSetAttribute(attn_kernel<HG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     return e;
 }
 
-// Clusters of `splits` CTAs of attn_kernel<HG, ST> that can be resident at once.
-template <int HG, int ST>
+// Clusters of `splits` CTAs of attn_kernel<HG> that can be resident at once.
+template <int HG>
 int max_clusters(int splits) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(splits, 1, 1);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = sizeof(AttnSmem<HG, ST>);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem<HG>);
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = splits;
@@ -526,7 +513,7 @@ int max_clusters(int splits) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, attn_kernel<HG, ST>, &cfg) != cudaSuccess) clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, attn_kernel<HG>, &cfg) != cudaSuccess) clusters = 0;
     cudaGetLastError();
     return clusters;
 }
@@ -536,42 +523,13 @@ int g_max_cluster = 0;  // largest split cluster that can be resident (16 or 8)
 }  // namespace
 
 cudaError_t configure_attention_kernels() {
-    cudaError_t e = configure_hg<1, 2>();
-    if (e == cudaSuccess) e = configure_hg<2, 2>();
-    if (e == cudaSuccess) e = configure_hg<4, 2>();
-    if (e == cudaSuccess) e = configure_hg<1, 3>();
-    if (e == cudaSuccess) e = configure_hg<2, 3>();
-    if (e == cudaSuccess) e = configure_hg<4, 3>();
-    if (e == cudaSuccess) e = configure_hg<1, 4>();
-    if (e == cudaSuccess) e = configure_hg<2, 4>();
-    if (e == cudaSuccess) e = configure_hg<4, 4>();
+    cudaError_t e = configure_hg<1>();
+    if (e == cudaSuccess) e = configure_hg<2>();
+    if (e == cudaSuccess) e = configure_hg<4>();
     if (e != cudaSuccess) return e;
     // Can a 16-CTA cluster of the largest variant be resident at all?
-    g_max_cluster = max_clusters<4, 2>(16) > 0 ? 16 : 8;
+    g_max_cluster = max_clusters<4>(16) > 0 ? 16 : 8;
     return cudaSuccess;
-}
-
-template <int HG>
-int deep_stages(int clusters, int splits, int sms, bool kv_heavy) {
-    // four stages at one CTA per SM where the grid leaves at least half the SMs
-    // to the GEMV launched beside it (its weight prefetch overlaps attention), or
-    // where the KV pages outweigh that GEMV's weights and want every SM
-    const long long ctas = 1LL * clusters * splits;
-    if ((2 * ctas <= sms || (kv_heavy && ctas <= sms)) && max_clusters<HG, 4>(splits) >= clusters) return 4;
-    // three stages keep two CTAs per SM: take them where they are as resident as two
-    const int two = max_clusters<HG, 2>(splits);
-    if (max_clusters<HG, 3>(splits) >= std::min(clusters, two)) return 3;
-    return 2;
-}
-
-int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int sms, bool kv_heavy) {
-    if (kv_heads <= 0 || q_heads % kv_heads != 0) return 2;
-    const int G = q_heads / kv_heads;
-    const int HG = heads_per_cta(G);
-    const int clusters = kv_heads * (G / HG);
-    return HG == 1   ? deep_stages<1>(clusters, splits, sms, kv_heavy)
-           : HG == 2 ? deep_stages<2>(clusters, splits, sms, kv_heavy)
-                     : deep_stages<4>(clusters, splits, sms, kv_heavy);
 }
 
 // Splits per (kv head, block): a power of two forming one cluster, at most 16
@@ -601,27 +559,12 @@ cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
     if (a.splits < 1 || a.splits > 16 || (a.splits & (a.splits - 1)) != 0) return cudaErrorInvalidValue;
     if (a.n_queries > 1 && static_cast<long long>(a.n_queries) * (G / heads_per_cta(G)) > 65535)
         return cudaErrorInvalidValue;
-    if (a.stages != 0 && (a.stages < 2 || a.stages > 4)) return cudaErrorInvalidValue;
     const int HG = heads_per_cta(G);
     const int nqb = G / HG;
-    if (a.stages == 4) {
-        switch (HG) {
-            case 1: return launch_hg<1, 4>(a, s, pdl, nqb);
-            case 2: return launch_hg<2, 4>(a, s, pdl, nqb);
-            default: return launch_hg<4, 4>(a, s, pdl, nqb);
-        }
-    }
-    if (a.stages == 3) {
-        switch (HG) {
-            case 1: return launch_hg<1, 3>(a, s, pdl, nqb);
-            case 2: return launch_hg<2, 3>(a, s, pdl, nqb);
-            default: return launch_hg<4, 3>(a, s, pdl, nqb);
-        }
-    }
     switch (HG) {
-        case 1: return launch_hg<1, 2>(a, s, pdl, nqb);
-        case 2: return launch_hg<2, 2>(a, s, pdl, nqb);
-        default: return launch_hg<4, 2>(a, s, pdl, nqb);
+        case 1: return launch_hg<1>(a, s, pdl, nqb);
+        case 2: return launch_hg<2>(a, s, pdl, nqb);
+        default: return launch_hg<4>(a, s, pdl, nqb);
     }
 }
 

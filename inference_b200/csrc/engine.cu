@@ -21,9 +21,11 @@
 //     (value, index) keys are all-gathered and resolved in the next step.
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "host_util.hpp"
@@ -72,10 +74,8 @@ struct q3_engine {
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
     uint32_t *done_counter = nullptr, *err = nullptr;
     int attn_splits = 1;
-    // opt-in variants of the graph path (Q3_TUNE_*); attn_deep_stages: the decode
-    // attention's ring depth under Q3_TUNE_ATTN_DEEP_RING
+    // opt-in variants of the graph path (Q3_TUNE_*)
     uint32_t tune = 0;
-    int attn_deep_stages = 2;
     // L2 lookahead of the weight streams (q3_engine_set_lookahead): items per GEMV warp
     // prefetched before the dependency wait, and whether attention prefetches W_o
     int lookahead = 0;
@@ -110,6 +110,12 @@ struct q3_engine {
     // graph / comms
     cudaGraphExec_t graph = nullptr;
     ncclComm_t comm = nullptr;
+    // NCCL exchange bounds (q3_engine_set_comm_timeout): a host wait on this rank's stream
+    // gives up comm_timeout_s (plus a per-step allowance for the queued steps) after it
+    // starts, aborts the communicator and reports Q3_ERR_NCCL; comm_dead after that
+    double comm_timeout_s = 60.0;
+    size_t queued_steps = 0;
+    bool comm_dead = false;
     size_t host_pos = 0, host_forced = 0, host_max_pos = 0;
     size_t weight_bytes = 0;
     std::vector<void*> allocs;
@@ -169,6 +175,88 @@ int dalloc_zero(q3_engine* e, uint8_t** p, size_t bytes) {
         int rc_ = (x);             \
         if (rc_ != Q3_OK) return rc_; \
     } while (0)
+
+// ------------------------------------------------------------ NCCL, bounded
+// The communicator is non-blocking (ncclConfig_t.blocking = 0): every call
+// returns at once, and ncclCommGetAsyncError reports when it has settled.  A
+// peer that never arrives would otherwise hold this rank forever, so every
+// host-side wait is bounded and ends by aborting the communicator.
+void abort_comm(q3_engine* e) {
+    if (e->comm) nccl().CommAbort(e->comm);  // also stops this rank's NCCL kernels still waiting on peers
+    e->comm = nullptr;
+    e->comm_dead = true;
+}
+
+double seconds_since(const std::chrono::steady_clock::time_point& t0) {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// Waits (bounded) until the communicator's last non-blocking call has settled.
+int nccl_settle(q3_engine* e, const char* what) {
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t st = ncclSuccess;
+        const ncclResult_t r = nccl().CommGetAsyncError(e->comm, &st);
+        if (r != ncclSuccess) st = r;
+        if (st == ncclSuccess) return Q3_OK;
+        if (st != ncclInProgress) {
+            const std::string msg = std::string(what) + ": " + nccl().GetErrorString(st);
+            abort_comm(e);
+            return fail(Q3_ERR_NCCL, msg);
+        }
+        if (seconds_since(t0) > e->comm_timeout_s) {
+            abort_comm(e);
+            return fail(Q3_ERR_NCCL, std::string(what) + ": timed out; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
+// A NCCL call's immediate result: in progress means settle before going on.
+int nccl_check(q3_engine* e, ncclResult_t nr, const char* what) {
+    if (nr == ncclInProgress) return nccl_settle(e, what);
+    if (nr != ncclSuccess) {
+        const std::string msg = std::string(what) + ": " + nccl().GetErrorString(nr);
+        abort_comm(e);
+        return fail(Q3_ERR_NCCL, msg);
+    }
+    return Q3_OK;
+}
+
+// Host wait for the engine's stream.  NCCL engines poll it with a deadline of
+// comm_timeout_s plus 0.25 s per step queued since the last wait: a rank whose
+// peer has gone aborts the communicator (its NCCL kernels then return) and
+// reports Q3_ERR_NCCL instead of waiting without end.
+int stream_wait(q3_engine* e) {
+    if (!e->comm) {
+        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        e->queued_steps = 0;
+        return Q3_OK;
+    }
+    const double limit = e->comm_timeout_s + 0.25 * static_cast<double>(e->queued_steps);
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        const cudaError_t q = cudaStreamQuery(e->stream);
+        if (q == cudaSuccess) break;
+        if (q != cudaErrorNotReady) return fail(Q3_ERR_CUDA, std::string("stream: ") + cudaGetErrorString(q));
+        ncclResult_t st = ncclSuccess;
+        if (nccl().CommGetAsyncError(e->comm, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress) {
+            const std::string msg = std::string("NCCL exchange failed: ") + nccl().GetErrorString(st);
+            abort_comm(e);
+            cudaStreamSynchronize(e->stream);
+            return fail(Q3_ERR_NCCL, msg);
+        }
+        if (seconds_since(t0) > limit) {
+            abort_comm(e);
+            cudaStreamSynchronize(e->stream);  // the aborted NCCL kernels have returned
+            return fail(Q3_ERR_NCCL, "NCCL exchange: a peer did not arrive within " + std::to_string(limit) +
+                                         " s; communicator aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+    e->queued_steps = 0;
+    return Q3_OK;
+}
 
 // ------------------------------------------------------------ one decode step
 struct Recorder {
@@ -257,8 +345,6 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.rope_cos = e->rope_cos;
     a.rope_sin = e->rope_sin;
     a.eps = e->cfg.eps;
-    a.stages = (e->tune & Q3_TUNE_ATTN_DEEP_RING) ? e->attn_deep_stages : 2;
-    a.live_prefetch = (e->tune & Q3_TUNE_ATTN_LIVE_PREFETCH) ? 1 : 0;
     if (e->attn_pf) {
         // the o_proj weights that the GEMV after this kernel streams
         a.pf = e->fp8 ? static_cast<const void*>(L.f_o) : static_cast<const void*>(L.w_o);
@@ -276,9 +362,8 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
 
 int allreduce(q3_engine* e, float* buf, size_t n) {
     if (e->peer_mode) return Q3_OK;  // the producing GEMV exchanged its partials through peer memory
-    ncclResult_t nr = nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, e->stream);
-    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().GetErrorString(nr));
-    return Q3_OK;
+    if (!e->comm) return fail(Q3_ERR_NCCL, "NCCL communicator aborted");
+    return nccl_check(e, nccl().AllReduce(buf, buf, n, ncclFloat32, ncclSum, e->comm, e->stream), "ncclAllReduce");
 }
 
 int record_step(Recorder& r, size_t pos_now) {
@@ -389,8 +474,9 @@ int record_step(Recorder& r, size_t pos_now) {
         h.ss_unrounded = 0;
         Q3_TRY(gemv(r, PRO_RESID_NORM, EPI_ARGMAX, h, w_lm, e->vl, e->H));
         if (!e->peer_mode) {
-            ncclResult_t nr = nccl().AllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream);
-            if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllGather: ") + nccl().GetErrorString(nr));
+            if (!e->comm) return fail(Q3_ERR_NCCL, "NCCL communicator aborted");
+            Q3_TRY(nccl_check(e, nccl().AllGather(e->key_send, e->keys, 1, ncclUint64, e->comm, e->stream),
+                              "ncclAllGather"));
         }
     } else {
         h.hs = e->hs[0];
@@ -401,6 +487,7 @@ int record_step(Recorder& r, size_t pos_now) {
 
 int build_graph(q3_engine* e) {
     if (e->graph) return Q3_OK;
+    if (e->comm_dead) return fail(Q3_ERR_NCCL, "NCCL communicator aborted after a failed exchange");
     if (e->world > 1 && !e->comm && !e->peer_mode)
         return fail(Q3_ERR_INVALID, "tensor-parallel engine needs q3_engine_attach_peers or q3_engine_attach_nccl");
     Recorder r{e, true};
@@ -630,12 +717,6 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
-    {
-        // a layer's K/V reads at the middle of the context against the o_proj weights
-        const double kv_mid = static_cast<double>(c.capacity) / 2 * e->kvh * 128 * 2 * 2;
-        const double o_bytes = static_cast<double>(e->H) * e->qd * 2;
-        e->attn_deep_stages = attn_deep_ring_stages(e->qh, e->kvh, e->attn_splits, e->sms, kv_mid > o_bytes);
-    }
 
     // ---- persistent decode kernel (single GPU, BF16 weights)
     if (tp_size == 1 && !e->fp8) {
@@ -736,7 +817,11 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 int q3_engine_destroy(q3_engine* e) {
     if (!e) return Q3_OK;
     cudaSetDevice(e->device);
-    if (e->stream) cudaStreamSynchronize(e->stream);
+    if (e->comm && stream_wait(e) != Q3_OK) {
+        // a peer is gone: stream_wait aborted the communicator and the stream is idle
+    } else if (e->stream) {
+        cudaStreamSynchronize(e->stream);
+    }
     if (e->graph) cudaGraphExecDestroy(e->graph);
     if (e->comm) nccl().CommDestroy(e->comm);
     for (void* p : e->xpeer)
@@ -845,7 +930,7 @@ int set_matrix_fp8(q3_engine* e, const uint16_t* host, size_t rows, size_t full_
     // stream-ordered before the quantize kernel (a pageable cudaMemcpy may return before its DMA lands)
     Q3_CUDA(cudaMemcpyAsync(st.p, host, rows * full_cols * 2, cudaMemcpyHostToDevice, e->stream));
     Q3_TRY(quant(e, st.p, full_cols, rows, full_cols, c0, cols, d));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     return Q3_OK;
 }
 
@@ -899,7 +984,7 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
         // pageable memory may still be in flight when a plain cudaMemcpy2D returns
         Q3_CUDA(cudaMemcpy2DAsync(dst, dpitch_elems * 2, src, spitch_elems * 2, width_elems * 2, height,
                                   cudaMemcpyHostToDevice, e->stream));
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         return Q3_OK;
     };
     if (n == "model.embed_tokens.weight") {
@@ -907,7 +992,7 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
         Q3_TRY(copy2d(e->embed, H, host, H, H, c.vocab));
         if (e->fp8 && c.tied) {
             Q3_TRY(quant(e, e->embed + static_cast<size_t>(e->voff) * H, H, e->vl, H, 0, H, dst_lm(e)));
-            Q3_CUDA(cudaStreamSynchronize(e->stream));
+            Q3_TRY(stream_wait(e));
         }
         return Q3_OK;
     }
@@ -968,7 +1053,7 @@ int q3_engine_set_weight(q3_engine* e, const char* name, const uint16_t* host, s
     auto vec = [&](bf16* dst, size_t len) -> int {
         Q3_CHECK(rows * cols == len, "norm weight shape: " + n);
         Q3_CUDA(cudaMemcpyAsync(dst, host, len * 2, cudaMemcpyHostToDevice, e->stream));
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         return Q3_OK;
     };
     if (leaf == "input_layernorm.weight") return vec(L.in_norm, H);
@@ -998,7 +1083,7 @@ int q3_engine_set_tokens(q3_engine* e, const uint32_t* ids, size_t n) {
     if (n) Q3_CUDA(cudaMemcpyAsync(e->tokens, ids, n * 4, cudaMemcpyHostToDevice, e->stream));
     const int32_t nf = static_cast<int32_t>(n);
     Q3_CUDA(cudaMemcpyAsync(e->n_forced, &nf, 4, cudaMemcpyHostToDevice, e->stream));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     e->host_forced = n;
     return Q3_OK;
 }
@@ -1022,6 +1107,7 @@ int q3_engine_step(q3_engine* e, size_t n) {
         Q3_TRY(build_graph(e));
         for (size_t i = 0; i < n; ++i) Q3_CUDA(cudaGraphLaunch(e->graph, e->stream));
     }
+    e->queued_steps += n;
     e->host_pos += n;
     if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
     return Q3_OK;
@@ -1130,8 +1216,9 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
             Q3_CUDA(launch_tp_signal(e->tpx, seq, s));
             Q3_CUDA(launch_tp_resid_rows(e->tpx, seq, m, H, e->px, vs, e->err, e->sms, s));
         } else {
-            ncclResult_t nr = nccl().AllReduce(slot, slot, static_cast<size_t>(m) * H, ncclFloat32, ncclSum, e->comm, s);
-            if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclAllReduce: ") + nccl().GetErrorString(nr));
+            if (!e->comm) return fail(Q3_ERR_NCCL, "NCCL communicator aborted");
+            Q3_TRY(nccl_check(e, nccl().AllReduce(slot, slot, static_cast<size_t>(m) * H, ncclFloat32, ncclSum,
+                                                  e->comm, s), "ncclAllReduce"));
             Q3_CUDA(launch_tp_resid_rows(xnccl, seq, m, H, e->px, vs, e->err, e->sms, s));
         }
         return Q3_OK;
@@ -1207,7 +1294,7 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
 int q3_engine_sync(q3_engine* e) {
     Q3_CHECK(e, "null engine");
     Q3_CUDA(cudaSetDevice(e->device));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     return check_device_error(e);
 }
 
@@ -1303,7 +1390,7 @@ int q3_engine_set_position(q3_engine* e, size_t pos) {
     Q3_CUDA(cudaSetDevice(e->device));
     const int32_t p = static_cast<int32_t>(pos);
     Q3_CUDA(cudaMemcpyAsync(e->pos, &p, 4, cudaMemcpyHostToDevice, e->stream));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     e->host_max_pos = reached;
     e->host_pos = pos;
     return Q3_OK;
@@ -1332,7 +1419,7 @@ int q3_engine_set_lookahead(q3_engine* e, int items, int attention_prefetch) {
     Q3_CUDA(cudaSetDevice(e->device));
     if (e->graph) {
         // the step graph holds the launch arguments: record it again at the next step
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         Q3_CUDA(cudaGraphExecDestroy(e->graph));
         e->graph = nullptr;
     }
@@ -1348,7 +1435,7 @@ int q3_engine_set_tuning(q3_engine* e, uint32_t flags) {
     Q3_CUDA(cudaSetDevice(e->device));
     if (e->graph) {
         // the step graph holds the launch arguments: record it again at the next step
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         Q3_CUDA(cudaGraphExecDestroy(e->graph));
         e->graph = nullptr;
     }
@@ -1380,7 +1467,7 @@ int graph_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, s
     }
     e->gtrace_ctas = ctas;
     if (static_cast<bool>(enable) != e->gtrace) {
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         if (e->graph) {
             cudaGraphExecDestroy(e->graph);
             e->graph = nullptr;
@@ -1389,7 +1476,7 @@ int graph_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, s
     }
     if (out_host && e->d_gtrace) {
         Q3_CHECK(capacity >= n, "q3_engine_trace: output buffer too small");
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         Q3_CUDA(cudaMemcpy(out_host, e->d_gtrace, n * 8, cudaMemcpyDeviceToHost));
     }
     return Q3_OK;
@@ -1420,7 +1507,7 @@ int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacit
     }
     if (out_host && e->d_trace) {
         Q3_CHECK(capacity >= n, "q3_engine_trace: output buffer too small");
-        Q3_CUDA(cudaStreamSynchronize(e->stream));
+        Q3_TRY(stream_wait(e));
         Q3_CUDA(cudaMemcpy(out_host, e->d_trace, n * 8, cudaMemcpyDeviceToHost));
     }
     return Q3_OK;
@@ -1452,7 +1539,7 @@ int q3_engine_kv_slot(q3_engine* e, size_t layer, size_t pos, uint16_t* k_out, u
     Q3_CHECK(e && k_out && v_out, "null argument");
     Q3_CHECK(layer < e->layers.size() && pos < e->cfg.capacity, "kv slot out of range");
     Q3_CUDA(cudaSetDevice(e->device));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));  // the legacy-stream copies below do not wait for it
+    Q3_TRY(stream_wait(e));  // the legacy-stream copies below do not wait for it
     int32_t page = 0;
     Q3_CUDA(cudaMemcpy(&page, e->page_table + pos / kPageSize, 4, cudaMemcpyDeviceToHost));
     const LayerW& L = e->layers[layer];
@@ -1472,7 +1559,7 @@ static int kv_range_copy(q3_engine* e, size_t layer, size_t pos0, size_t n, uint
     Q3_CHECK(layer < e->layers.size() && pos0 <= e->cfg.capacity && n <= e->cfg.capacity - pos0,
              "kv range out of range");
     Q3_CUDA(cudaSetDevice(e->device));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     std::vector<int32_t> table((e->cfg.capacity + kPageSize - 1) / kPageSize);
     Q3_CUDA(cudaMemcpy(table.data(), e->page_table, table.size() * 4, cudaMemcpyDeviceToHost));
     const q3::LayerW& L = e->layers[layer];
@@ -1494,7 +1581,7 @@ static int kv_range_copy(q3_engine* e, size_t layer, size_t pos0, size_t n, uint
         }
         p += in_page;
     }
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     return Q3_OK;
 }
 
@@ -1523,7 +1610,7 @@ int q3_engine_fill_kv(q3_engine* e, size_t upto, uint64_t seed) {
     }
     const int32_t p = static_cast<int32_t>(upto);
     Q3_CUDA(cudaMemcpyAsync(e->pos, &p, 4, cudaMemcpyHostToDevice, e->stream));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     e->host_pos = upto;
     if (upto > e->host_max_pos) e->host_max_pos = upto;
     return Q3_OK;
@@ -1545,6 +1632,7 @@ int q3_engine_profile_step(q3_engine* e, int klass, double* ms, size_t* launches
     Q3_CHECK(e && ms && launches && bytes, "null argument");
     Q3_CHECK(e->host_pos < e->cfg.capacity, "q3_engine_profile_step: KV cache full");
     Q3_CHECK(e->host_forced >= 1 || e->host_pos >= 1, "q3_engine_profile_step: no input token");
+    if (e->comm_dead) return fail(Q3_ERR_NCCL, "NCCL communicator aborted after a failed exchange");
     if (e->world > 1 && !e->comm && !e->peer_mode)
         return fail(Q3_ERR_INVALID, "tensor-parallel engine needs q3_engine_attach_peers or q3_engine_attach_nccl");
     Q3_CUDA(cudaSetDevice(e->device));
@@ -1554,7 +1642,7 @@ int q3_engine_profile_step(q3_engine* e, int klass, double* ms, size_t* launches
     Q3_TRY(record_step(r, e->host_pos));
     e->host_pos += 1;
     if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    Q3_TRY(stream_wait(e));
     double total = 0;
     for (size_t i = 0; i + 1 < ev.size(); i += 2) {
         float t = 0;
@@ -1633,6 +1721,13 @@ int q3_engine_attach_peers(q3_engine* e, const void* handles, size_t n) {
     return Q3_OK;
 }
 
+int q3_engine_set_comm_timeout(q3_engine* e, double seconds) {
+    Q3_CHECK(e, "null engine");
+    Q3_CHECK(seconds > 0.0 && seconds <= 86400.0, "q3_engine_set_comm_timeout: seconds must be in (0, 86400]");
+    e->comm_timeout_s = seconds;
+    return Q3_OK;
+}
+
 int q3_engine_attach_nccl(q3_engine* e, const void* id_in) {
     Q3_CHECK(e && id_in, "null argument");
     if (e->world == 1) return Q3_OK;
@@ -1640,8 +1735,15 @@ int q3_engine_attach_nccl(q3_engine* e, const void* id_in) {
     ncclUniqueId id;
     std::memcpy(&id, id_in, sizeof(id));
     if (!nccl().ok) return fail(Q3_ERR_NCCL, nccl().error);
-    ncclResult_t nr = nccl().CommInitRank(&e->comm, e->world, id, e->rank);
-    if (nr != ncclSuccess) return fail(Q3_ERR_NCCL, std::string("ncclCommInitRank: ") + nccl().GetErrorString(nr));
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking = 0;  // every wait on peers is bounded by the engine (stream_wait, nccl_settle)
+    ncclResult_t nr = nccl().CommInitRankConfig(&e->comm, e->world, id, e->rank, &config);
+    if (nr != ncclSuccess && nr != ncclInProgress) {
+        e->comm = nullptr;
+        return fail(Q3_ERR_NCCL, std::string("ncclCommInitRankConfig: ") + nccl().GetErrorString(nr));
+    }
+    e->comm_dead = false;
+    Q3_TRY(nccl_settle(e, "ncclCommInitRankConfig"));
     if (e->graph) {
         cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;

@@ -154,27 +154,12 @@ struct AttnArgs {
     const float* rope_cos;
     const float* rope_sin;
     float eps;
-    // Opt-in variants (q3_engine_set_tuning): stages = K/V pages in flight per
-    // CTA, 2 (0 = 2), 3 or 4, as attn_deep_ring_stages picks for the decode
-    // grid; live_prefetch (fused single-query decode on
-    // the paged layout only): the page of the current position is fetched
-    // before griddepcontrol.wait like the older ones, and the position's V row
-    // (written by the QKV GEMV) is read after it and patched into the tile.
-    int stages;
-    int live_prefetch;
     // L2 prefetch of the next weight stream while the page math runs: each CTA of the
     // grid prefetches its even share of [pf, pf + pf_bytes) at its start (null = off)
     const void* pf;
     size_t pf_bytes;
     LaunchTrace trace;
 };
-// K/V pages in flight per CTA for the decode grid (splits x kv_heads x
-// query-head blocks, one cluster of `splits` per kv head and block) under
-// Q3_TUNE_ATTN_DEEP_RING: 4 (one CTA per SM) where the grid fills at most half
-// the SMs -- or, kv_heavy (a layer's KV reads outweigh the next GEMV's
-// weights), at most all of them -- and stays resident; else 3 (two CTAs per
-// SM) where that is as resident as the default 2; else 2.
-int attn_deep_ring_stages(int q_heads, int kv_heads, int splits, int num_sms, bool kv_heavy);
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);

@@ -94,6 +94,10 @@ class Engine:
         buf = C.create_string_buffer(bytes(uid), 128)
         check(lib().q3_engine_attach_nccl(self.h, buf))
 
+    def set_comm_timeout(self, seconds: float):
+        """Bound on host waits of the NCCL path (q3_engine_set_comm_timeout)."""
+        check(lib().q3_engine_set_comm_timeout(self.h, float(seconds)))
+
     # ---- decode
     def reset(self):
         check(lib().q3_engine_reset(self.h))
@@ -144,7 +148,7 @@ class Engine:
         check(lib().q3_engine_set_lookahead(self.h, int(items), int(bool(attention_prefetch))))
 
     # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
-    TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2, "deep_ring": 0x4, "live_prefetch": 0x8,
+    TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2,
                   "tp_prefill": 0x10, "fp8_prefill": 0x20}
 
     @property

@@ -64,31 +64,32 @@ def bf16_ulp(x: np.ndarray) -> np.ndarray:
 
 
 class Pair:
-    """Logit agreement of one implementation with the reference CUDA model."""
+    """Per-step logit agreement of one implementation with the reference CUDA model."""
 
     def __init__(self):
-        self.steps = 0
-        self.maxabs = 0.0
-        self.max_ulps = 0.0  # |d| in BF16 ulps of the reference logit
-        self.mincos = 1.0
-        self.agree = 0
-        self.worst_step = -1
+        self.rows = []  # per step: [position, max|d|, mean|d|, max(|d| - ulp(ref)), cosine, ref top-2 margin, agree]
 
     def add(self, mine_bits, ref_bits, next_token, step):
         m, r = bf(mine_bits).astype(np.float64), bf(ref_bits).astype(np.float64)
         d = np.abs(m - r)
-        mx = float(d.max())
-        if mx > self.maxabs:
-            self.maxabs, self.worst_step = mx, step
-        self.max_ulps = max(self.max_ulps, float((d / bf16_ulp(r)).max()))
         cos = float(m @ r / (np.linalg.norm(m) * np.linalg.norm(r) + 1e-30))
-        self.mincos = min(self.mincos, cos)
-        self.agree += int(int(np.argmax(m)) == int(next_token))  # first index of the maximum
-        self.steps += 1
+        top2 = np.partition(r, -2)[-2:]
+        agree = int(int(np.argmax(m)) == int(next_token))  # first index of the maximum
+        self.rows.append([step, float(d.max()), float(d.mean()), float((d - bf16_ulp(r)).max()), cos,
+                          float(top2[1] - top2[0]), agree])
 
     def summary(self):
-        return {"steps": self.steps, "maxabs": round(self.maxabs, 6), "max_ulps": round(self.max_ulps, 2),
-                "mincos": round(self.mincos, 8), "agree": self.agree, "worst_step": self.worst_step}
+        if not self.rows:
+            return None
+        a = np.array(self.rows)
+        return {"steps": len(a), "maxabs": round(float(a[:, 1].max()), 6), "meanabs": float(a[:, 2].mean()),
+                "excess_over_ulp": round(float(a[:, 3].max()), 6), "mincos": round(float(a[:, 4].min()), 8),
+                "agree": int(a[:, 6].sum()), "worst_step": int(a[int(a[:, 1].argmax()), 0])}
+
+    def table(self):
+        """The per-step rows, compact, for the test's paired statistics."""
+        return [[int(r[0]), round(r[1], 6), round(r[2], 8), round(r[3], 6), round(r[4], 9), round(r[5], 6),
+                 int(r[6])] for r in self.rows]
 
 
 def run(case: str) -> dict:
@@ -174,10 +175,13 @@ def run(case: str) -> dict:
         "decode_steps": C - P, "cpu_mode": "full" if cpu_mode == "full" else f"windows of {WINDOW} at {windows}",
         "engine_vs_ref_cuda": engine_pair.summary(),
         "ref_cpu_vs_ref_cuda": cpu_pair.summary(),
-        "engine_shared_history_vs_ref_cuda": eng2_pair.summary() if eng2 else None,
+        "engine_shared_history_vs_ref_cuda": eng2_pair.summary(),
         "windows": {str(k): {"ref_cpu": v[1].summary(), "engine_shared": v[2].summary(),
                              "engine": v[3].summary()}
                     for k, v in win_pairs.items()},
+        "rows": {"engine": engine_pair.table(), "ref_cpu": cpu_pair.table(),
+                 "engine_shared": eng2_pair.table() if eng2 else []},
+        "row_fields": ["position", "maxabs", "meanabs", "excess_over_ulp", "cosine", "ref_top2_margin", "agree"],
         "sequence_head": [int(x) for x in S[P:P + 8]],
         "engine_greedy_vs_sequence": int((hist[P - 1:C - 1] == S[P:C]).sum()),
         "seconds": {"prefill": round(t_pre - t_start, 1), "total": round(time.time() - t_start, 1)},

@@ -164,3 +164,61 @@ def test_peer_wait_times_out_without_fault(tmp_path):
     mp.start_processes(_stall_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
     msg = (tmp_path / "stall0.txt").read_text()
     assert "peer wait timed out" in msg, msg
+
+
+def _departed_main(rank, world, port, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from inference_b200 import Engine, Q3Error, Qwen3Config, prompt_ids
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    qc = Qwen3Config("qwen3-0.6b-l2", hidden=1024, inter=3072, layers=2, q_heads=16, kv_heads=8, vocab=151936,
+                     tied=True)
+    e = Engine(qc, capacity=64, device=rank, tp_rank=rank, tp_size=world)
+    e.init_synthetic(0)
+    _attach(e, dist, "nccl", rank)
+    e.set_comm_timeout(3.0)
+    e.set_tokens(prompt_ids(8))
+    e.step(2)  # both ranks: healthy exchanges
+    e.sync()
+    msg, after = "", ""
+    if rank == 0:
+        # rank 1 has left between steps: this step's exchange never completes
+        e.step(1)
+        try:
+            e.sync()
+        except Q3Error as exc:
+            msg = str(exc)
+        try:
+            e.step(1)
+        except Q3Error as exc:
+            after = str(exc)
+    dist.barrier()  # rank 1 waits here, idle, until rank 0 has given up
+    with open(os.path.join(out_dir, f"departed{rank}.txt"), "w") as f:
+        f.write(msg + "\n" + after)
+    e.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_nccl_departed_peer_aborts_without_hang(tmp_path):
+    """Failure detection on the NCCL path: after two healthy steps one rank stops
+    stepping (it leaves between steps, nothing in flight); the other rank's next
+    exchange never completes, its bounded host wait runs out, the communicator is
+    aborted (its NCCL kernels return) and the call reports Q3_ERR_NCCL; the engine
+    then refuses further steps instead of hanging.  NVLS is off."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    mp.start_processes(_departed_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
+    msg, after = (tmp_path / "departed0.txt").read_text().split("\n", 1)
+    assert "Q3_ERR_NCCL" in msg and "did not arrive" in msg, msg
+    assert "Q3_ERR_NCCL" in after and "aborted" in after, after

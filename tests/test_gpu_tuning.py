@@ -1,14 +1,13 @@
-"""Opt-in variants of the decode path (q3_engine_set_tuning).
+"""Opt-in variants of the decode path (q3_engine_set_tuning,
+q3_engine_set_lookahead).
 
 The decode variants reorder no arithmetic, so every logit, argmax and KV slot
 must be bit-identical to the default kernels:
-  * attention with the deeper page ring (four pages at one CTA per SM, three
-    at two CTAs per SM, per the shapes below) and the
-    live page fetched before the dependency wait, at positions from 0 to the
-    end of an 8192-slot cache (every page boundary the windows cross, up to 8
-    pages per split, so both ring depths refill);
+  * L2 lookahead (GEMV warps prefetching the items past their ring, attention
+    prefetching o_proj) at positions from 0 to the end of an 8192-slot cache
+    (every page boundary the windows cross, up to 8 pages per split);
   * on 2 GPUs, the peer-exchange prologue with batched rank reads and without
-    the grid-dependency wait, together with the attention variants.
+    the grid-dependency wait.
 The batched prefills of tensor-parallel and of FP8-weight engines change the
 fp32 order of the prefill's sums (GEMMs instead of GEMVs, as the single-GPU
 prefill does), so they are held to the oracle like test_gpu_prefill.py: KV
@@ -26,7 +25,7 @@ from gpu_util import assert_logits_close, bf
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-DECODE_FLAGS = 0x1 | 0x2 | 0x4 | 0x8  # batched_poll | no_grid_wait | deep_ring | live_prefetch
+DECODE_FLAGS = 0x1 | 0x2  # batched_poll | no_grid_wait
 TP_PREFILL = 0x10
 
 
@@ -36,11 +35,11 @@ def _cos(a, b):
     return a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-30)
 
 
-# ring depth the deep-ring variant picks: (2, 8) a small grid -> 4 pages at one CTA per SM;
-# (8, 16) K/V reads outweigh o_proj at this context -> 4; (8, 32) 8B shapes -> 3 at two per SM
+# GQA 4 with 2 kv heads (a small attention grid), Qwen3-0.6B and Qwen3-8B head and matrix shapes
 @pytest.mark.parametrize("kv_heads,q_heads,hidden,inter", [(2, 8, 1024, 3072), (8, 16, 1024, 3072),
                                                            (8, 32, 4096, 12288)])
-def test_attention_variants_bit_identical(kv_heads, q_heads, hidden, inter):
+@pytest.mark.parametrize("weights", ["bf16", "fp8"])
+def test_decode_prefetch_variants_bit_identical(kv_heads, q_heads, hidden, inter, weights):
     from inference_b200 import Engine, Qwen3Config, prompt_ids
 
     cfg = Qwen3Config(f"gqa{q_heads // kv_heads}-kv{kv_heads}-h{hidden}-l2", hidden=hidden, inter=inter, layers=2,
@@ -49,11 +48,11 @@ def test_attention_variants_bit_identical(kv_heads, q_heads, hidden, inter):
     ids = prompt_ids(cap, seed=1)
     runs = {}
     # (tuning flags, L2 lookahead items, attention prefetch): prefetches change no arithmetic
-    variants = ((0, 0, False), (DECODE_FLAGS, 0, False), (0, 8, True), (DECODE_FLAGS, 3, True))
+    variants = ((0, 0, False), (0, 8, True), (DECODE_FLAGS, 3, True), (0, 64, False))
     for var in variants:
         flags, items, attn_pf = var
         logits, kv = [], []
-        with Engine(cfg, capacity=cap) as e:
+        with Engine(cfg, capacity=cap, weights=weights) as e:
             e.init_synthetic(0)
             e.tuning = flags
             assert e.tuning == flags
@@ -141,8 +140,10 @@ def test_tuning_rejects_unknown_bits():
             e.tuning = 0x400
         with pytest.raises(ValueError):
             e.tuning = ["no_such_flag"]
+        with pytest.raises(Q3Error):
+            e.tuning = 0x4  # a retired bit
         e.tuning = ["all"]
-        assert e.tuning == 0x3F
+        assert e.tuning == 0x33
         e.tuning = 0
         assert e.tuning == 0
 
