@@ -61,10 +61,6 @@ def parse_args(argv=None):
                                                           "where the persistent kernel was selected")
     ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
                     "batched_poll, no_grid_wait, tp_prefill, fp8_prefill, or all")
-    ap.add_argument("--lookahead", type=int, default=None,
-                    help="L2 lookahead items per GEMV warp (q3_engine_set_lookahead; default: the engine's)")
-    ap.add_argument("--attn-prefetch", type=int, default=None, choices=[0, 1],
-                    help="attention prefetches the o_proj weights into L2 (default: the engine's)")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
                     help="fp8: E4M3 GEMV matrices with per-row power-of-two scales (the FP8-weight model, "
                          "not the reference's BF16 model; the CUDA graph path)")
@@ -456,16 +452,6 @@ def probe_gemv8(a):
     print("ok")
 
 
-def _apply_lookahead(eng, a):
-    """--lookahead / --attn-prefetch over the engine's defaults; returns what is set."""
-    items, attn = eng.lookahead()
-    if a.lookahead is not None or a.attn_prefetch is not None:
-        items = items if a.lookahead is None else a.lookahead
-        attn = attn if a.attn_prefetch is None else bool(a.attn_prefetch)
-        eng.set_lookahead(items, attn)
-    return {"items_per_warp": items, "attention_prefetch": attn}
-
-
 def _probe_engine(a, cfg, cap, rank=0, world=1, local=0, dist=None):
     import inference_b200 as ib
 
@@ -475,7 +461,6 @@ def _probe_engine(a, cfg, cap, rank=0, world=1, local=0, dist=None):
     tune = [t for t in a.tune.split(",") if t]
     if tune:
         e.tuning = tune
-    _apply_lookahead(e, a)
     if dist is not None:
         _attach(e, dist, a.nccl, rank, world)
     return e
@@ -648,7 +633,6 @@ def main(argv=None):
         eng.tuning = tune
         if "all" in tune:
             tune = sorted(ib.Engine.TUNE_FLAGS)
-    lookahead = _apply_lookahead(eng, a)
     if dist is not None:
         _attach(eng, dist, a.nccl, rank, world)
 
@@ -822,7 +806,6 @@ def main(argv=None):
                        "decode_tokens_per_step": window, "global_batch": 1,
                        "decode_path": "persistent kernel" if eng.persistent else "CUDA graph of fused kernels",
                        "parallelism": f"tp{world}", "weight_format": a.weights, "tuning": tune,
-                       "l2_lookahead": lookahead,
                        "tp_exchange": (None if world == 1 else "NCCL allreduce/allgather" if a.nccl else
                                        "peer-memory stores fused into the o/down/lm_head GEMVs (CUDA IPC, NVLink)"),
                        "weights": "random N(0,0.02) seed 0, ids seed 1",

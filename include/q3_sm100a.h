@@ -273,16 +273,6 @@ Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
 Q3_API int q3_engine_set_persistent(q3_engine* e, int enable);
 Q3_API int q3_engine_is_persistent(q3_engine* e);
 
-/* L2 lookahead of the decode step's weight streams (no counterpart in the
- * reference; changes no arithmetic): every GEMV warp prefetches into L2, before
- * its dependency wait, the `items` work items (4 KB each) of its run that
- * follow the ones its shared-memory ring holds, so HBM keeps streaming through
- * the wait and the prologue; with attention_prefetch the decode attention
- * kernel, which reads little from HBM, prefetches the o_proj weights into L2
- * for the GEMV after it.  items in [0, 64]. */
-Q3_API int q3_engine_set_lookahead(q3_engine* e, int items, int attention_prefetch);
-Q3_API int q3_engine_lookahead(q3_engine* e, int* items, int* attention_prefetch);
-
 /* Opt-in variants of the CUDA-graph decode path (no counterpart in the
  * reference), as bit flags; 0, the default, selects the kernels described
  * above.  Every flag keeps the step's arithmetic and its order, so tokens

@@ -57,8 +57,6 @@ SIGNATURES = {
     "q3_engine_set_position": (C.c_int, [_vp, _sz]),
     "q3_engine_set_persistent": (C.c_int, [_vp, C.c_int]),
     "q3_engine_is_persistent": (C.c_int, [_vp]),
-    "q3_engine_set_lookahead": (C.c_int, [_vp, C.c_int, C.c_int]),
-    "q3_engine_lookahead": (C.c_int, [_vp, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "q3_engine_set_tuning": (C.c_int, [_vp, C.c_uint32]),
     "q3_engine_tuning": (C.c_int, [_vp, C.POINTER(C.c_uint32)]),
     "q3_engine_trace": (C.c_int, [_vp, C.c_int, _vp, _sz, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),

@@ -127,7 +127,9 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool tracing = a.trace.buf != nullptr;
-    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0;
+    // trace marks (thread 0, a consumer): start, dependency released, q/k norm done,
+    // page loop done
+    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_cq = 0, tr_cp = 0;
     if (tracing && tid == 0) {
         tr_t0 = globaltimer_ns();
         tr_c0 = clock64();
@@ -160,14 +162,6 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
 
     if (warp == kWarps) {
         // ------------------------------------------------------------ producer
-        if (lane == 1 && a.pf) {
-            // the next weight stream into L2 while this kernel's page math runs
-            const size_t ctas = static_cast<size_t>(gridDim.x) * gridDim.y * gridDim.z;
-            const size_t me = blockIdx.x + static_cast<size_t>(gridDim.x) * (blockIdx.y + gridDim.y * blockIdx.z);
-            const size_t units = a.pf_bytes / 16;
-            const size_t u0 = me * units / ctas, u1 = (me + 1) * units / ctas;
-            if (u1 > u0) prefetch_l2(static_cast<const uint8_t*>(a.pf) + u0 * 16, (u1 - u0) * 16);
-        }
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();
             bool waited = false;
@@ -236,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
             named_bar(1, kConsumers);
         }
 
+        if (tracing && tid == 0) tr_cq = clock64();
         uint32_t qa[8][2];  // A fragments of q: rows g (dims 16kk + 2t4, +1) and (+8); rows 8-15 are zero
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
@@ -368,6 +363,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         }
         l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
         l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+        if (tracing && tid == 0) tr_cp = clock64();
 
         // ---- merge the 4 warp states (fixed order) into this CTA's state
         if (g < HG) {
@@ -454,9 +450,9 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         t[2] = tr_c0;
         t[3] = c4;
         t[4] = tr_c1 - tr_c0;
-        t[5] = 0;
-        t[6] = c4 - tr_c1;
-        t[7] = 0;
+        t[5] = tr_cq - tr_c1;  // q/k RMSNorm + RoPE (the "prologue")
+        t[6] = tr_cp - tr_cq;  // page loop
+        t[7] = c4 - tr_cp;     // warp merge, cluster merge (the "epilogue")
         t[8] = sm_id();
     }
 }

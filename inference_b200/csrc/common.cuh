@@ -149,19 +149,6 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
-// Prefetch [p, p + bytes) of global memory into L2 (no shared memory, no
-// completion to wait for): p 16-byte aligned, bytes a multiple of 16.  Issued
-// in pieces of at most 32 KB.
-__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
-    const char* c = static_cast<const char*>(p);
-    while (bytes > 0) {
-        const uint32_t n = bytes < (32u << 10) ? static_cast<uint32_t>(bytes) : (32u << 10);
-        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(c), "r"(n) : "memory");
-        c += n;
-        bytes -= n;
-    }
-}
-
 // ------------------------------------------------------------------ PDL
 // Programmatic dependent launch.  Without the launch attribute both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

@@ -76,10 +76,6 @@ struct q3_engine {
     int attn_splits = 1;
     // opt-in variants of the graph path (Q3_TUNE_*)
     uint32_t tune = 0;
-    // L2 lookahead of the weight streams (q3_engine_set_lookahead): items per GEMV warp
-    // prefetched before the dependency wait, and whether attention prefetches W_o
-    int lookahead = 0;
-    int attn_pf = 0;
     // persistent decode kernel (one launch per run of steps)
     bool persistent = false;
     q3::PersistentArgs pargs{};
@@ -290,7 +286,6 @@ GemvArgs base_args(q3_engine* e) {
     GemvArgs a{};
     if (e->peer_mode) a.peer = e->links;
     a.tune = e->tune;
-    a.lookahead = e->lookahead;
     a.eps = e->cfg.eps;
     a.err = e->err;
     a.capacity = static_cast<int>(e->cfg.capacity);
@@ -345,11 +340,6 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.rope_cos = e->rope_cos;
     a.rope_sin = e->rope_sin;
     a.eps = e->cfg.eps;
-    if (e->attn_pf) {
-        // the o_proj weights that the GEMV after this kernel streams
-        a.pf = e->fp8 ? static_cast<const void*>(L.f_o) : static_cast<const void*>(L.w_o);
-        a.pf_bytes = e->fp8 ? f8_packed_bytes(e->H, e->qd) : static_cast<size_t>(e->H) * e->qd * 2;
-    }
     a.trace = r.trace();
     r.mark(true, 1);
     cudaError_t st = launch_attention(a, e->stream, r.pdl);
@@ -1404,29 +1394,6 @@ int q3_engine_set_persistent(q3_engine* e, int enable) {
 }
 
 int q3_engine_is_persistent(q3_engine* e) { return (e && e->persistent) ? 1 : 0; }
-
-int q3_engine_lookahead(q3_engine* e, int* items, int* attention_prefetch) {
-    Q3_CHECK(e && items && attention_prefetch, "null argument");
-    *items = e->lookahead;
-    *attention_prefetch = e->attn_pf;
-    return Q3_OK;
-}
-
-int q3_engine_set_lookahead(q3_engine* e, int items, int attention_prefetch) {
-    Q3_CHECK(e, "null engine");
-    Q3_CHECK(items >= 0 && items <= 64, "q3_engine_set_lookahead: items must be in [0, 64]");
-    if (items == e->lookahead && (attention_prefetch != 0) == (e->attn_pf != 0)) return Q3_OK;
-    Q3_CUDA(cudaSetDevice(e->device));
-    if (e->graph) {
-        // the step graph holds the launch arguments: record it again at the next step
-        Q3_TRY(stream_wait(e));
-        Q3_CUDA(cudaGraphExecDestroy(e->graph));
-        e->graph = nullptr;
-    }
-    e->lookahead = items;
-    e->attn_pf = attention_prefetch != 0;
-    return Q3_OK;
-}
 
 int q3_engine_set_tuning(q3_engine* e, uint32_t flags) {
     Q3_CHECK(e, "null engine");

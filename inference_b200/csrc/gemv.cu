@@ -276,30 +276,6 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         pol = policy_evict_first();
         for (int j = 0; j < p.stages && j < cnt; ++j) issue(i0 + j, j);
     }
-    // L2 lookahead: the items after the ring's first fill (a warp's run is one contiguous
-    // byte range in both layouts) head for L2 now, so HBM keeps streaming this band
-    // through the dependency wait and the prologue
-    if (lane == 0 && a.lookahead > 0 && cnt > p.stages) {
-        auto item_ptr = [&](int item) -> const uint8_t* {
-            const int c = item % p.nch;
-            if constexpr (F8) {
-                const int tile = item / p.nch;
-                const int rows = min(kF8Rows, nrows - tile * kF8Rows);
-                return a.W8 + (static_cast<size_t>(r0) * p.nch + static_cast<size_t>(tile) * kF8Rows * p.nch +
-                               static_cast<size_t>(c) * rows) * kF8Cols;
-            } else {
-                return reinterpret_cast<const uint8_t*>(a.W) +
-                       (static_cast<size_t>(r0 + item / p.nch) * a.K + static_cast<size_t>(c) * p.kc) * WB;
-            }
-        };
-        const int first = i0 + p.stages, last = i0 + min(cnt, p.stages + a.lookahead);  // items [first, last)
-        const uint8_t* b = item_ptr(first);
-        // the band ends at row r1: F8 bands hold nrows x nch x 256 bytes from row r0's offset
-        const uint8_t* band_end = F8 ? a.W8 + static_cast<size_t>(r1) * p.nch * kF8Cols
-                                     : reinterpret_cast<const uint8_t*>(a.W) + static_cast<size_t>(r1) * a.K * WB;
-        const uint8_t* e = last < i1 ? item_ptr(last) : band_end;
-        if (e > b) prefetch_l2(b, static_cast<size_t>(e - b));
-    }
     for (int i = tid; i < nrows * p.nch; i += kThreads) part[i] = 0.f;
     if (tid == 0) *cta_key = 0ull;
     // RMSNorm weights never depend on earlier kernels: this thread's first two

@@ -114,10 +114,6 @@ struct GemvArgs {
     PeerLinks peer;
     int xtag;
     uint32_t tune;             // Q3_TUNE_PEER_* bits (q3_engine_set_tuning)
-    // ---- L2 lookahead: each warp prefetches into L2, before the dependency wait, the
-    // `lookahead` items of its run that follow the ones its shared-memory ring holds, so
-    // the weight stream keeps HBM busy through the wait and the prologue (0 = off)
-    int lookahead;
     // ---- errors
     uint32_t* err;
     LaunchTrace trace;
@@ -154,10 +150,6 @@ struct AttnArgs {
     const float* rope_cos;
     const float* rope_sin;
     float eps;
-    // L2 prefetch of the next weight stream while the page math runs: each CTA of the
-    // grid prefetches its even share of [pf, pf + pf_bytes) at its start (null = off)
-    const void* pf;
-    size_t pf_bytes;
     LaunchTrace trace;
 };
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);

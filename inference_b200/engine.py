@@ -137,16 +137,6 @@ class Engine:
     def persistent(self, on: bool):
         check(lib().q3_engine_set_persistent(self.h, int(bool(on))))
 
-    def lookahead(self):
-        """(items per GEMV warp, attention prefetch) of q3_engine_set_lookahead."""
-        i, a = C.c_int(), C.c_int()
-        check(lib().q3_engine_lookahead(self.h, C.byref(i), C.byref(a)))
-        return int(i.value), bool(a.value)
-
-    def set_lookahead(self, items: int, attention_prefetch: bool):
-        """L2 lookahead of the weight streams (q3_engine_set_lookahead)."""
-        check(lib().q3_engine_set_lookahead(self.h, int(items), int(bool(attention_prefetch))))
-
     # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
     TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2,
                   "tp_prefill": 0x10, "fp8_prefill": 0x20}
