@@ -57,8 +57,6 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--nccl", action="store_true", help="tensor parallel: exchange partial sums with NCCL "
                     "instead of peer-memory stores fused into the GEMVs")
-    ap.add_argument("--graph", action="store_true", help="use the per-step CUDA graph path (the default) even "
-                                                          "where the persistent kernel was selected")
     ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
                     "batched_poll, no_grid_wait, tp_prefill, fp8_prefill, or all")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
@@ -457,7 +455,6 @@ def _probe_engine(a, cfg, cap, rank=0, world=1, local=0, dist=None):
 
     e = ib.Engine(cfg, capacity=cap, device=local, tp_rank=rank, tp_size=world)
     e.init_synthetic(0)
-    e.persistent = False
     tune = [t for t in a.tune.split(",") if t]
     if tune:
         e.tuning = tune
@@ -626,8 +623,6 @@ def main(argv=None):
     if a.weights == "fp8":
         workload += "-fp8"
     eng.init_synthetic(0)
-    if a.graph and eng.persistent:
-        eng.persistent = False
     tune = [t for t in a.tune.split(",") if t]
     if tune:
         eng.tuning = tune
@@ -741,27 +736,15 @@ def main(argv=None):
     traffic_ratio = read_traffic_ratio(cfg.name)
     names = launch_names(cfg.layers)
     timeline_text = None
-    if eng.persistent:
-        # one cooperative launch per bench step: algorithmic bytes of the whole window / its device time
-        per_launch = bytes_tok * window / world
-        achieved = bytes_tok * tok_s / 1e9 / world
-        roofline = {"kernel": "persistent_decode_kernel (one cooperative launch = one decode window of "
-                              f"{window} tokens)",
-                    "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                    "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
-                    "traffic": round(traffic_ratio * per_launch) if traffic_ratio else None,
-                    "algorithmic_bytes_per_launch": round(per_launch), "launch_ms_avg": round(ms / a.steps, 3)}
-        launches = a.steps
-    else:
-        eng.set_position(mid)
-        eng.step(2)
-        summs = [summarize_trace(r) for r in traced_steps(eng, mid, 4)]
-        roofline = timeline_roofline(summs, names, cfg, world, mid, a.weights, ms / tokens, peak, peak_kind,
-                                     traffic_ratio)
-        timeline_text = trace_table(summs[-1], names, f"{workload} rank {rank}/{world}, one traced step at "
-                                                      f"position {mid}: {summs[-1]['spans'].sum():.1f} us traced, "
-                                                      f"{ms / tokens * 1000:.1f} us per token timed")
-        launches = len(names) * window * a.steps
+    eng.set_position(mid)
+    eng.step(2)
+    summs = [summarize_trace(r) for r in traced_steps(eng, mid, 4)]
+    roofline = timeline_roofline(summs, names, cfg, world, mid, a.weights, ms / tokens, peak, peak_kind,
+                                 traffic_ratio)
+    timeline_text = trace_table(summs[-1], names, f"{workload} rank {rank}/{world}, one traced step at "
+                                                  f"position {mid}: {summs[-1]['spans'].sum():.1f} us traced, "
+                                                  f"{ms / tokens * 1000:.1f} us per token timed")
+    launches = len(names) * window * a.steps
     # whole-step roofline: weights + average KV read per token over the window, all ranks
     step_roof = {"bytes_per_token": int(bytes_tok), "achieved_gbs": round(bytes_tok * tok_s / 1e9, 1),
                  "peak_gbs": peak * world, "frac": round(bytes_tok * tok_s / 1e9 / (peak * world), 4)}
@@ -804,7 +787,7 @@ def main(argv=None):
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": workload, "model": cfg.name, "prompt": prompt_len, "context": capacity,
                        "decode_tokens_per_step": window, "global_batch": 1,
-                       "decode_path": "persistent kernel" if eng.persistent else "CUDA graph of fused kernels",
+                       "decode_path": "CUDA graph of fused kernels",
                        "parallelism": f"tp{world}", "weight_format": a.weights, "tuning": tune,
                        "tp_exchange": (None if world == 1 else "NCCL allreduce/allgather" if a.nccl else
                                        "peer-memory stores fused into the o/down/lm_head GEMVs (CUDA IPC, NVLink)"),

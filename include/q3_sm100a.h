@@ -265,14 +265,6 @@ Q3_API int q3_engine_generate(q3_engine* e, const uint32_t* prompt_host, size_t 
  * after one prefill. */
 Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
 
-/* Decode-step implementation: 0 (the default) replays the per-step CUDA
- * graph of fused kernels; 1 (single GPU, BF16 weights, when the model's
- * shared-memory plan fits) runs n steps as one persistent cooperative kernel
- * (one CTA per SM streaming all weights through a TMA ring, grid barriers
- * between phases).  Both produce the same tokens. */
-Q3_API int q3_engine_set_persistent(q3_engine* e, int enable);
-Q3_API int q3_engine_is_persistent(q3_engine* e);
-
 /* Opt-in variants of the CUDA-graph decode path (no counterpart in the
  * reference), as bit flags; 0, the default, selects the kernels described
  * above.  Every flag keeps the step's arithmetic and its order, so tokens
@@ -302,22 +294,18 @@ Q3_API int q3_engine_is_persistent(q3_engine* e);
 Q3_API int q3_engine_set_tuning(q3_engine* e, uint32_t flags);
 Q3_API int q3_engine_tuning(q3_engine* e, uint32_t* flags);
 
-/* Phase timeline (tracing).  Persistent kernel: with enable = 1 the next
- * launches record, for the first step of each launch, per CTA and phase
- * (5 per layer + lm_head) Q3_TRACE_WORDS uint64 words: [0] / [1] phase start
- * and end (%globaltimer ns), [2] / [3] the SM clock (clock64) at the same
- * points, [4..7] SM cycles of parts of the phase (GEMV: input ready, waiting
- * for items, issuing refills, dot products; attention: q/k norm, page loop,
- * waiting for pages, split merge and publish), [8] the SM id.  CUDA-graph
- * path: every step records, per launch (the same 5 per layer + lm_head) and
- * CTA, [0] / [1] CTA start / end (%globaltimer), [2] / [3] clock64 there,
- * SM cycles of [4] start -> dependency wait returned, [5] prologue, [6] main
- * loop, [7] epilogue, [8] the SM id, and for a tensor-parallel GEMV that sums
- * the ranks' partials in its prologue [9] the SM cycles from the dependency
- * release until CTA thread 0 held every rank's partials of its first rows
- * (toggling re-records the graph).
- * out_host (if not NULL) receives the last record,
- * [ctas][phases][Q3_TRACE_WORDS]; capacity counts uint64 words. */
+/* Launch timeline (tracing) of the CUDA-graph decode path: with enable = 1
+ * every step records, per launch (5 per layer + lm_head) and CTA,
+ * Q3_TRACE_WORDS uint64 words: [0] / [1] CTA start / end (%globaltimer ns),
+ * [2] / [3] clock64 there, SM cycles of [4] start -> dependency wait
+ * returned, [5] prologue (attention: q/k RMSNorm + RoPE), [6] main loop
+ * (attention: the page loop), [7] epilogue (attention: warp and split merge),
+ * [8] the SM id, [9] for a tensor-parallel GEMV that sums the ranks' partials
+ * in its prologue the SM cycles from the dependency release until CTA thread
+ * 0 held every rank's partials of its first rows, for attention the cycles
+ * after its cluster barrier (toggling re-records the graph).  out_host (if
+ * not NULL) receives the last step's record, [ctas][launches][Q3_TRACE_WORDS];
+ * capacity counts uint64 words. */
 #define Q3_TRACE_WORDS 10
 Q3_API int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases,
                            size_t* n_ctas);
@@ -389,10 +377,12 @@ Q3_API int q3_engine_attach_nccl(q3_engine* e, const void* id_128_bytes);
  * host wait on the engine's stream (q3_engine_sync and the calls that read
  * state back) gives up after `seconds` plus 0.25 s per decode step queued
  * since the last wait.  A rank whose peer has gone -- exited, or never stepped
- * -- then aborts its communicator (its NCCL kernels return), reports
- * Q3_ERR_NCCL, and refuses further steps; the engine can still be destroyed.
- * Default 60 s.  Peer-memory engines bound their waits on the device instead
- * (Q3_ERR_DEVICE "peer wait timed out"). */
+ * -- then aborts its communicator, reports Q3_ERR_NCCL instead of blocking,
+ * and refuses further work; the engine can still be destroyed.  A collective
+ * captured in the step graph may keep its kernel waiting on the departed peer
+ * after the abort, so the process should then exit (tearing down its CUDA
+ * context).  Default 60 s.  Peer-memory engines bound every wait on the device
+ * instead (Q3_ERR_DEVICE "peer wait timed out", context usable). */
 Q3_API int q3_engine_set_comm_timeout(q3_engine* e, double seconds);
 
 #ifdef __cplusplus

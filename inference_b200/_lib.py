@@ -55,8 +55,6 @@ SIGNATURES = {
     "q3_engine_forward": (C.c_int, [_vp, C.c_uint32, C.POINTER(C.c_uint32)]),
     "q3_engine_generate": (C.c_int, [_vp, _u32p, _sz, _sz, C.c_int, _u32p, C.POINTER(C.c_size_t)]),
     "q3_engine_set_position": (C.c_int, [_vp, _sz]),
-    "q3_engine_set_persistent": (C.c_int, [_vp, C.c_int]),
-    "q3_engine_is_persistent": (C.c_int, [_vp]),
     "q3_engine_set_tuning": (C.c_int, [_vp, C.c_uint32]),
     "q3_engine_tuning": (C.c_int, [_vp, C.POINTER(C.c_uint32)]),
     "q3_engine_trace": (C.c_int, [_vp, C.c_int, _vp, _sz, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),

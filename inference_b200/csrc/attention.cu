@@ -19,17 +19,16 @@
 //   * each consumer warp owns 16 of a page's 64 tokens and does its math on the
 //     tensor cores (mma.sync: S = Q K^T, online softmax in fp32 on the
 //     fragments, O += P V with P in BF16 hi + lo parts);
-//   * warp states merge in shared memory in a fixed order; the splits then
-//     merge across the cluster through distributed shared memory, each CTA
-//     producing a slice of the outputs -- deterministic, no global partials.
-#include <cooperative_groups.h>
+//   * warp states merge in shared memory in a fixed order; each split then
+//     pushes its state of every output slice into the shared memory of the
+//     cluster CTA that owns the slice (distributed shared memory stores), and
+//     after one cluster barrier every CTA merges its slice locally in a fixed
+//     split order -- deterministic, no global partials.
 
 #include <algorithm>
 #include <cfloat>
 
 #include "kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace q3 {
 
@@ -55,9 +54,13 @@ struct AttnSmem {
     float m[kWarps][HG];  // per consumer warp: running max, sum, accumulators
     float l[kWarps][HG];
     float acc[kWarps][HG][kHd];
-    float cm[HG];  // this CTA's merged state, read by the cluster
-    float cl[HG];
-    float cacc[HG][kHd];
+    // split merge: CTA `o` of the cluster owns outputs [o * slice, (o + 1) * slice) of the
+    // HG x 128 (slice = HG * 128 / splits); every split pushes into the owner's shared
+    // memory its running max and sum per head, and its accumulators of those outputs,
+    // at [split][...] -- splits x slice = HG x 128 accumulators in all
+    float rx_m[16][HG];
+    float rx_l[16][HG];
+    float rx_acc[HG * kHd];
     bf16 qn[HG][kHd];  // normalised, rotated q heads (fused q/k norm)
     bf16 kn[kHd];      // normalised, rotated key row of the position
     uint64_t full[kStages];
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
     const bool tracing = a.trace.buf != nullptr;
     // trace marks (thread 0, a consumer): start, dependency released, q/k norm done,
     // page loop done
-    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_cq = 0, tr_cp = 0;
+    unsigned long long tr_t0 = 0, tr_c0 = 0, tr_c1 = 0, tr_cq = 0, tr_cp = 0, tr_cs = 0;
     if (tracing && tid == 0) {
         tr_t0 = globaltimer_ns();
         tr_c0 = clock64();
@@ -148,6 +151,9 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         fence_barrier_init();
     }
     __syncthreads();
+    // Every CTA of the cluster must be running before any pushes into its shared
+    // memory: arrive now, wait just before the first push (long after all started).
+    if (a.splits > 1) cluster_arrive_relaxed();
 
     // The position is final here: every kernel triggers its dependents only
     // after its own griddepcontrol.wait, so when this grid runs, the kernel
@@ -378,6 +384,8 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
             }
         }
         named_bar(1, kConsumers);
+        if (a.splits > 1) cluster_wait();  // phase 0: every CTA of the cluster has started
+        const int slice = HG * kHd / a.splits;  // outputs each CTA of the cluster finishes
         for (int oi = tid; oi < HG * kHd; oi += kConsumers) {
             const int gg = oi / kHd, d = oi % kHd;
             float M = -INFINITY;
@@ -393,54 +401,46 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
             if (a.splits == 1) {
                 out[static_cast<size_t>(qh0 + gg) * kHd + d] = f2bf(A / Lsum);
             } else {
-                S.cacc[gg][d] = A;
-                if (d == 0) {
-                    S.cm[gg] = M;
-                    S.cl[gg] = Lsum;
+                // push this split's state of output oi into its owner's shared memory
+                const int owner = oi / slice, j = oi % slice;
+                AttnSmem<HG>* R = static_cast<AttnSmem<HG>*>(map_cluster_rank(&S, owner));
+                R->rx_acc[split * slice + j] = A;
+                if (j == 0 || d == 0) {  // the first output of each (owner, head) pair carries m, l
+                    R->rx_m[split][gg] = M;
+                    R->rx_l[split][gg] = Lsum;
                 }
             }
         }
     }
     if (a.splits == 1) return;
 
-    // ---- merge the splits across the cluster through distributed shared memory
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
+    // ---- phase 1: every split's pushes are in (release / acquire), then each CTA
+    // finishes its own outputs from its shared memory; no CTA reads a peer's memory,
+    // so none has to outlive the barrier for the others
+    __syncwarp();  // the cluster barrier instructions below are warp-aligned
+    if (warp == kWarps) cluster_wait();  // the producer warp's phase-0 wait
+    cluster_arrive_release();
+    cluster_wait();
+    if (tracing && tid == 0) tr_cs = clock64();
     if (warp < kWarps) {
-        const int n_out = HG * kHd;
-        const int slice = n_out / a.splits;                   // outputs this CTA finishes
-        const int tpo = slice >= kConsumers ? 1 : kConsumers / slice;  // threads per output
-        const int per_pass = kConsumers / tpo;
-        const int sub = tid % tpo;
-        for (int base = 0; base < slice; base += per_pass) {
-            const int o = split * slice + base + tid / tpo;
+        const int slice = HG * kHd / a.splits;
+        for (int j = tid; j < slice; j += kConsumers) {
+            const int o = split * slice + j;
             const int g = o / kHd, d = o % kHd;
             float M = -INFINITY;
-            for (int sp = 0; sp < a.splits; ++sp) {
-                const AttnSmem<HG>* R = cluster.map_shared_rank(&S, sp);
-                M = fmaxf(M, R->cm[g]);
-            }
+            for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, S.rx_m[sp][g]);
             float Lsum = 0.f, A = 0.f;
-            for (int sp = sub; sp < a.splits; sp += tpo) {
-                const AttnSmem<HG>* R = cluster.map_shared_rank(&S, sp);
-                const float ms = R->cm[g];
+            for (int sp = 0; sp < a.splits; ++sp) {  // fixed split order
+                const float ms = S.rx_m[sp][g];
                 if (ms == -INFINITY) continue;
                 const float f = exp2f(ms - M);
-                Lsum += R->cl[g] * f;
-                A += R->cacc[g][d] * f;
+                Lsum += S.rx_l[sp][g] * f;
+                A += S.rx_acc[sp * slice + j] * f;
             }
-            // tpo consecutive lanes hold parts of one output: reduce in a fixed tree
-            for (int off = tpo >> 1; off > 0; off >>= 1) {
-                Lsum += __shfl_xor_sync(0xffffffffu, Lsum, off);
-                A += __shfl_xor_sync(0xffffffffu, A, off);
-            }
-            if (sub == 0) {
-                const int qh = kvh * G + qb * HG + g;
-                out[static_cast<size_t>(qh) * kHd + d] = f2bf(A / Lsum);
-            }
+            const int qh = kvh * G + qb * HG + g;
+            out[static_cast<size_t>(qh) * kHd + d] = f2bf(A / Lsum);
         }
     }
-    cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
     const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
     if (tracing && tid == 0 && cta < a.trace.ctas) {
         unsigned long long* t = a.trace.buf + (static_cast<size_t>(cta) * a.trace.phases + a.trace.phase) * kTraceWords;
@@ -453,6 +453,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         t[5] = tr_cq - tr_c1;  // q/k RMSNorm + RoPE (the "prologue")
         t[6] = tr_cp - tr_cq;  // page loop
         t[7] = c4 - tr_cp;     // warp merge, cluster merge (the "epilogue")
+        t[9] = tr_cs ? c4 - tr_cs : 0;  // of which: after the cluster barrier (the owner's merge)
         t[8] = sm_id();
     }
 }

@@ -149,6 +149,24 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, u
         : "memory");
 }
 
+// ------------------------------------------------------------------ clusters
+// The cluster barrier in split phases (every thread of every CTA of the cluster
+// takes part): arrive without memory ordering, arrive releasing this thread's
+// earlier writes (shared::cluster stores included), wait acquiring the others'.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// The generic address of `p` (this CTA's shared memory) in cluster CTA `rank`.
+__device__ __forceinline__ void* map_cluster_rank(void* p, uint32_t rank) {
+    uint64_t out;
+    asm volatile("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+    return reinterpret_cast<void*>(out);
+}
+
 // ------------------------------------------------------------------ PDL
 // Programmatic dependent launch.  Without the launch attribute both are no-ops.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

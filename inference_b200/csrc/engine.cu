@@ -76,17 +76,10 @@ struct q3_engine {
     int attn_splits = 1;
     // opt-in variants of the graph path (Q3_TUNE_*)
     uint32_t tune = 0;
-    // persistent decode kernel (one launch per run of steps)
-    bool persistent = false;
-    q3::PersistentArgs pargs{};
-    uint32_t* d_layer_tab = nullptr;
-    unsigned long long* d_trace = nullptr;
     // CUDA-graph path timeline: per launch of a step and CTA (q3_engine_trace)
     bool gtrace = false;
     unsigned long long* d_gtrace = nullptr;
     int gtrace_ctas = 0;
-    unsigned long long* gsync = nullptr;
-    uint32_t* abort_word = nullptr;
     // batched prefill: token-row buffers of prefill_rows rows (allocated on first use)
     int prefill_rows = 0;
     q3::bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pg = nullptr;
@@ -224,6 +217,7 @@ int nccl_check(q3_engine* e, ncclResult_t nr, const char* what) {
 // peer has gone aborts the communicator (its NCCL kernels then return) and
 // reports Q3_ERR_NCCL instead of waiting without end.
 int stream_wait(q3_engine* e) {
+    if (e->comm_dead) return fail(Q3_ERR_NCCL, "NCCL communicator aborted after a failed exchange");
     if (!e->comm) {
         Q3_CUDA(cudaStreamSynchronize(e->stream));
         e->queued_steps = 0;
@@ -239,12 +233,14 @@ int stream_wait(q3_engine* e) {
         if (nccl().CommGetAsyncError(e->comm, &st) == ncclSuccess && st != ncclSuccess && st != ncclInProgress) {
             const std::string msg = std::string("NCCL exchange failed: ") + nccl().GetErrorString(st);
             abort_comm(e);
-            cudaStreamSynchronize(e->stream);
             return fail(Q3_ERR_NCCL, msg);
         }
         if (seconds_since(t0) > limit) {
+            // No wait for the stream after the abort: a collective captured in the step
+            // graph may keep its kernel waiting on the departed peer, and the host must
+            // get control back.  The engine refuses further work; the process should
+            // tear down its CUDA context (exit) to reclaim that kernel.
             abort_comm(e);
-            cudaStreamSynchronize(e->stream);  // the aborted NCCL kernels have returned
             return fail(Q3_ERR_NCCL, "NCCL exchange: a peer did not arrive within " + std::to_string(limit) +
                                          " s; communicator aborted");
         }
@@ -502,10 +498,8 @@ int check_device_error(q3_engine* e) {
     if (err != 0) {
         static const char* names[] = {"ok", "TMA wait timed out", "peer wait timed out", "token id out of range",
                                       "position out of range", "grid barrier timed out"};
-        // clear the error and the persistent kernel's barrier state so the engine stays usable
+        // clear the error so the engine stays usable
         cudaMemset(e->err, 0, 4);
-        if (e->gsync) cudaMemset(e->gsync, 0, 16);
-        if (e->abort_word) cudaMemset(e->abort_word, 0, 4);
         return fail(Q3_ERR_DEVICE, std::string("device error: ") + (err < 6 ? names[err] : "unknown"));
     }
     return Q3_OK;
@@ -656,7 +650,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     // ---- activations and control
     if ((rc = dalloc_t(e, &e->hs[0], H)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->hs[1], H)) != Q3_OK) return bail(rc);
-    // q, then this step's raw key rows (the persistent kernel normalises them in its attention phase)
+    // q, then this step's raw key rows (the attention kernel normalises them)
     if ((rc = dalloc_t(e, &e->q, static_cast<size_t>(e->qd) + e->kd)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->attn, e->qd)) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->g, e->il)) != Q3_OK) return bail(rc);
@@ -708,95 +702,6 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
 
-    // ---- persistent decode kernel (single GPU, BF16 weights)
-    if (tp_size == 1 && !e->fp8) {
-        PersistentArgs& a = e->pargs;
-        a.H = e->H;
-        a.qd = e->qd;
-        a.kd = e->kd;
-        a.il = e->il;
-        a.vl = e->vl;
-        a.qh = e->qh;
-        a.kvh = e->kvh;
-        a.layers = static_cast<int>(c.layers);
-        a.vocab = static_cast<int>(c.vocab);
-        a.capacity = static_cast<int>(c.capacity);
-        a.voff = e->voff;
-        a.eps = c.eps;
-        int optin = 0;
-        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
-        if (optin > 0 && plan_persistent(a, e->sms, static_cast<size_t>(optin))) {
-            std::vector<PersistentLayer> hl(c.layers);
-            for (size_t l = 0; l < c.layers; ++l) {
-                const LayerW& L = e->layers[l];
-                hl[l] = PersistentLayer{L.w_qkv, L.w_o, L.w_gu, L.w_down, L.in_norm, L.post_norm,
-                                        L.q_norm, L.k_norm, L.k_pages, L.v_pages};
-            }
-            const int HG = attention_head_group(e->qh, e->kvh);
-            float* att_part = nullptr;
-            uint32_t* att_cnt = nullptr;
-            // pointer table: 32-bit offsets in 256-byte units from the lowest pointer
-            unsigned long long base = ~0ull, top = 0;
-            bool aligned = true;
-            for (const PersistentLayer& L : hl) {
-                const void* const* ptrs = reinterpret_cast<const void* const*>(&L);
-                for (int i = 0; i < kLayerPtrs; ++i) {
-                    const auto v = reinterpret_cast<unsigned long long>(ptrs[i]);
-                    base = std::min(base, v);
-                    top = std::max(top, v);
-                    aligned = aligned && (v % 256 == 0);
-                }
-            }
-            std::vector<uint32_t> tab(hl.size() * kLayerPtrs);
-            for (size_t l = 0; l < hl.size(); ++l) {
-                const void* const* ptrs = reinterpret_cast<const void* const*>(&hl[l]);
-                for (int i = 0; i < kLayerPtrs; ++i)
-                    tab[l * kLayerPtrs + i] =
-                        static_cast<uint32_t>((reinterpret_cast<unsigned long long>(ptrs[i]) - base) >> 8);
-            }
-            // otherwise the persistent kernel stays unavailable (layer_tab null)
-            const bool fits = aligned && ((top - base) >> 8) < (1ull << 32);
-            if (fits) {
-                if ((rc = dalloc_t(e, &e->d_layer_tab, tab.size())) != Q3_OK) return bail(rc);
-                note(cudaMemcpy(e->d_layer_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
-                a.layer_tab = e->d_layer_tab;
-                a.layer_base = base;
-                if ((rc = dalloc_t(e, &att_part, static_cast<size_t>(e->kvh) * a.nqb * a.splits * HG * kAttRecord)) != Q3_OK)
-                    return bail(rc);
-                if ((rc = dalloc_t(e, &att_cnt, static_cast<size_t>(e->kvh) * a.nqb + 4)) != Q3_OK) return bail(rc);
-                if ((rc = dalloc_t(e, &e->gsync, 2)) != Q3_OK) return bail(rc);
-                if ((rc = dalloc_t(e, &e->abort_word, 4)) != Q3_OK) return bail(rc);
-                note(cudaMemset(att_cnt, 0, (static_cast<size_t>(e->kvh) * a.nqb + 4) * 4));
-                note(cudaMemset(e->gsync, 0, 16));
-                note(cudaMemset(e->abort_word, 0, 16));
-                a.embed = e->embed;
-                a.lm_head = e->lm_head;
-                a.final_norm = e->final_norm;
-                a.page_table = e->page_table;
-                a.rope_cos = e->rope_cos;
-                a.rope_sin = e->rope_sin;
-                a.hs = e->hs[0];
-                a.q = e->q;
-                a.attn = e->attn;
-                a.g = e->g;
-                a.logits = e->logits;
-                a.vsum = e->vsum;
-                a.att_part = att_part;
-                a.att_counters = att_cnt;
-                a.pos = e->pos;
-                a.n_forced = e->n_forced;
-                a.tokens = e->tokens;
-                a.argmax_hist = e->argmax_hist;
-                a.key_slot = reinterpret_cast<unsigned long long*>(e->key_slot);
-                a.key_out = reinterpret_cast<unsigned long long*>(e->keys);
-                a.done_counter = e->done_counter;
-                a.gsync = e->gsync;
-                a.err = e->err;
-                a.abort = e->abort_word;
-                // available; q3_engine_set_persistent selects it (the graph path is the default)
-            }
-        }
-    }
     if (setup != cudaSuccess)
         return bail(fail(Q3_ERR_CUDA, std::string("engine setup copy: ") + cudaGetErrorString(setup)));
     if (cudaDeviceSynchronize() != cudaSuccess) return bail(fail(Q3_ERR_CUDA, "engine setup failed"));
@@ -808,8 +713,9 @@ int q3_engine_destroy(q3_engine* e) {
     if (!e) return Q3_OK;
     cudaSetDevice(e->device);
     if (e->comm && stream_wait(e) != Q3_OK) {
-        // a peer is gone: stream_wait aborted the communicator and the stream is idle
-    } else if (e->stream) {
+        // a peer is gone: stream_wait aborted the communicator; the stream may still hold
+        // a kernel waiting on that peer, so it is not waited for
+    } else if (e->stream && !e->comm_dead) {
         cudaStreamSynchronize(e->stream);
     }
     if (e->graph) cudaGraphExecDestroy(e->graph);
@@ -1085,18 +991,8 @@ int q3_engine_step(q3_engine* e, size_t n) {
     if (e->host_pos + n > e->cfg.capacity)
         return fail(Q3_ERR_INVALID, "q3_engine_step: KV cache capacity exceeded");
     Q3_CUDA(cudaSetDevice(e->device));
-    if (e->persistent) {
-        // one cooperative launch runs all n steps; bound a launch to 1 << 20 steps
-        for (size_t done = 0; done < n;) {
-            const size_t k = (n - done) < (1u << 20) ? (n - done) : (1u << 20);
-            e->pargs.n_steps = static_cast<int>(k);
-            Q3_CUDA(launch_persistent(e->pargs, e->stream));
-            done += k;
-        }
-    } else {
-        Q3_TRY(build_graph(e));
-        for (size_t i = 0; i < n; ++i) Q3_CUDA(cudaGraphLaunch(e->graph, e->stream));
-    }
+    Q3_TRY(build_graph(e));
+    for (size_t i = 0; i < n; ++i) Q3_CUDA(cudaGraphLaunch(e->graph, e->stream));
     e->queued_steps += n;
     e->host_pos += n;
     if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
@@ -1386,15 +1282,6 @@ int q3_engine_set_position(q3_engine* e, size_t pos) {
     return Q3_OK;
 }
 
-int q3_engine_set_persistent(q3_engine* e, int enable) {
-    Q3_CHECK(e, "null engine");
-    if (enable && !e->pargs.layer_tab) return fail(Q3_ERR_UNSUPPORTED, "persistent decode kernel unavailable for this engine");
-    e->persistent = enable != 0;
-    return Q3_OK;
-}
-
-int q3_engine_is_persistent(q3_engine* e) { return (e && e->persistent) ? 1 : 0; }
-
 int q3_engine_set_tuning(q3_engine* e, uint32_t flags) {
     Q3_CHECK(e, "null engine");
     Q3_CHECK((flags & ~Q3_TUNE_ALL) == 0u, "q3_engine_set_tuning: unknown flag bits");
@@ -1454,30 +1341,7 @@ int graph_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, s
 int q3_engine_trace(q3_engine* e, int enable, uint64_t* out_host, size_t capacity, size_t* n_phases, size_t* n_ctas) {
     Q3_CHECK(e && n_phases && n_ctas, "null argument");
     Q3_CUDA(cudaSetDevice(e->device));
-    if (!e->persistent) return graph_trace(e, enable, out_host, capacity, n_phases, n_ctas);
-    const size_t phases = e->layers.size() * 5 + 1;
-    const size_t n = static_cast<size_t>(e->pargs.grid) * phases * kTraceWords;
-    *n_phases = phases;
-    *n_ctas = static_cast<size_t>(e->pargs.grid);
-    if (enable) {
-        if (!e->pargs.trace) {
-            if (!e->d_trace) {
-                int rc = dalloc_t(e, &e->d_trace, n);
-                if (rc != Q3_OK) return rc;
-            }
-            Q3_CUDA(cudaMemset(e->d_trace, 0, n * 8));
-        }
-        e->pargs.trace = e->d_trace;
-        e->pargs.trace_phases = static_cast<int>(phases);
-    } else {
-        e->pargs.trace = nullptr;
-    }
-    if (out_host && e->d_trace) {
-        Q3_CHECK(capacity >= n, "q3_engine_trace: output buffer too small");
-        Q3_TRY(stream_wait(e));
-        Q3_CUDA(cudaMemcpy(out_host, e->d_trace, n * 8, cudaMemcpyDeviceToHost));
-    }
-    return Q3_OK;
+    return graph_trace(e, enable, out_host, capacity, n_phases, n_ctas);
 }
 
 int q3_engine_position(q3_engine* e, size_t* pos) {

@@ -309,14 +309,18 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     // the residual rows this thread updates in the epilogue (first pass), read now
     bf16 hs_pre = __float2bfloat16(0.f);
     if ((epi == EPI_RESID || epi == EPI_RESID_F32) && tid < nrows) hs_pre = a.hs[r0 + tid];
+    // The position: the embedding prologue needs it at once; the QKV epilogue only at the
+    // end, so there its load is issued now and checked after the prologue (a branch on it
+    // here would hold the whole prologue for the load's round trip)
     int pos = 0;
-    if (epi == EPI_QKV || pro == PRO_EMBED_NORM) {
-        pos = *a.pos_ptr;
+    if (epi == EPI_QKV || pro == PRO_EMBED_NORM) pos = *a.pos_ptr;
+    auto check_pos = [&]() {
         if (pos < 0 || pos >= a.capacity) {
             if (tid == 0) record_error(a.err, DEV_BAD_POSITION);
             pos = 0;
         }
-    }
+    };
+    if (pro == PRO_EMBED_NORM) check_pos();
 
     // ---- prologue: x in shared memory
     if (pro == PRO_PLAIN) {
@@ -499,6 +503,12 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
         __syncthreads();
     }
     if (tracing && tid == 0) tr_c2 = clock64();
+    // EPI_QKV: the V page slot of this position, looked up now for the epilogue
+    size_t v_slot = 0;
+    if (epi == EPI_QKV) {
+        if (pro != PRO_EMBED_NORM) check_pos();
+        v_slot = kv_slot(a, pos, 0);
+    }
 
     // ---- main loop: each warp streams its own items; no CTA-wide barrier
     float acc0 = 0.f, acc1 = 0.f;
@@ -636,7 +646,8 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                     a.q_out[gr] = b;
                 } else {
                     const int k = gr - a.q_rows - a.kv_rows;
-                    a.v_pages[kv_slot(a, pos, k >> 7) + (k & 127)] = b;
+                    // head h of the page sits h * page_size rows after head 0
+                    a.v_pages[v_slot + static_cast<size_t>(k >> 7) * a.page_size * 128 + (k & 127)] = b;
                 }
             } else if (epi == EPI_ARGMAX) {
                 const bf16 b = f2bf(r);

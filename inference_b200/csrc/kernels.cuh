@@ -20,6 +20,7 @@ struct LaunchTrace {
     unsigned long long* buf;  // null: off
     int phase, phases, ctas;
 };
+constexpr int kTraceWords = Q3_TRACE_WORDS;
 
 // ---------------------------------------------------------------- GEMV
 // y = W x for one token, W row-major [N, K] BF16, fp32 accumulation.
@@ -155,61 +156,6 @@ struct AttnArgs {
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
-
-// ---------------------------------------------------------------- persistent decode
-struct PersistentLayer {
-    const bf16 *w_qkv, *w_o, *w_gu, *w_down;
-    const bf16 *in_norm, *post_norm, *q_norm, *k_norm;
-    bf16 *k_pages, *v_pages;
-};
-// The ten pointers of a layer, in PersistentLayer order, as 32-bit offsets in
-// 256-byte units from layer_base (every tensor is a 256-byte aligned cudaMalloc).
-constexpr int kLayerPtrs = 10;
-
-// One attention split's state per query head in att_part: m, l, two pad
-// words (so the 128 fp32 accumulators start 16-byte aligned), acc[128].
-constexpr int kAttRecord = 132;
-// Query heads per attention unit: the largest of 4, 2, 1 dividing the group.
-inline int attention_head_group(int q_heads, int kv_heads) {
-    const int g = q_heads / kv_heads;
-    return g % 4 == 0 ? 4 : (g % 2 == 0 ? 2 : 1);
-}
-
-constexpr int kTraceWords = Q3_TRACE_WORDS;
-
-struct PersistentArgs {
-    // shapes (this rank)
-    int H, qd, kd, il, vl, qh, kvh, nqb, splits, layers, vocab, capacity, n_steps, n_pages;
-    uint32_t voff;
-    float eps;
-    // weights and tables
-    const uint32_t* layer_tab;  // device array [layers][kLayerPtrs]
-    unsigned long long layer_base;
-    const bf16 *embed, *lm_head, *final_norm;
-    const int32_t* page_table;
-    const float *rope_cos, *rope_sin;
-    // activations
-    bf16 *hs, *q, *attn, *g, *logits;
-    float* vsum;
-    float* att_part;          // [kvh * nqb][splits][HG][kAttRecord]
-    uint32_t* att_counters;   // [kvh * nqb]
-    // control
-    int32_t *pos, *n_forced, *tokens, *argmax_hist;
-    unsigned long long *key_slot, *key_out;
-    uint32_t* done_counter;
-    unsigned long long* gsync;  // grid-barrier arrivals of the running launch (zeroed before each launch)
-    uint32_t *err, *abort;
-    // optional phase timeline of the first step: [grid][phases][kTraceWords]
-    // globaltimer marks (persistent.cu lists them)
-    unsigned long long* trace;
-    int trace_phases;
-    // launch / shared-memory plan (plan_persistent)
-    int grid;
-    uint32_t ring_slots;
-    size_t off_bars, off_x, off_part, off_att, off_misc, off_tab, smem;
-};
-bool plan_persistent(PersistentArgs& a, int sms, size_t smem_limit);
-cudaError_t launch_persistent(const PersistentArgs& a, cudaStream_t s);
 
 // ---------------------------------------------------------------- prefill GEMM (tcgen05)
 enum GemmEpi : int { GEMM_STORE = 0, GEMM_SWIGLU = 1, GEMM_RESID = 2, GEMM_F32 = 3 };

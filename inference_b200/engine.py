@@ -129,14 +129,6 @@ class Engine:
                                        C.byref(n)))
         return out[: n.value].copy()
 
-    @property
-    def persistent(self) -> bool:
-        return bool(lib().q3_engine_is_persistent(self.h))
-
-    @persistent.setter
-    def persistent(self, on: bool):
-        check(lib().q3_engine_set_persistent(self.h, int(bool(on))))
-
     # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
     TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2,
                   "tp_prefill": 0x10, "fp8_prefill": 0x20}
@@ -163,7 +155,7 @@ class Engine:
         check(lib().q3_engine_set_tuning(self.h, int(flags)))
 
     def trace(self, enable: bool = True):
-        """Turn the phase timeline on/off (persistent kernel or CUDA-graph path)."""
+        """Turn the launch timeline of the CUDA-graph decode path on/off."""
         ph, ct = C.c_size_t(), C.c_size_t()
         check(lib().q3_engine_trace(self.h, int(enable), None, 0, C.byref(ph), C.byref(ct)))
 

@@ -73,3 +73,36 @@ def assert_logits_close(mine, gold, atol=3e-2, n_ulp=2, min_cos=0.9999):
     cos = m @ g / (np.linalg.norm(m) * np.linalg.norm(g) + 1e-30)
     assert cos >= min_cos, f"cosine {cos}"
     return float(np.abs(m - g).max()), float(cos)
+
+
+def spread_of(g):
+    """The reference's own implementation spread recorded with a golden model
+    fixture: max |logit difference| and min cosine between the reference's CPU
+    backend and the oracle over the fixture's steps (two fp32 orders of the
+    same arithmetic)."""
+    return float(np.asarray(g["env_maxabs"]).max()), float(np.asarray(g["env_cos"]).min())
+
+
+def assert_within_spread(mine, gold, spread):
+    """Model-level logits held to a measured implementation spread, no scale
+    factor: every |d| <= max(3e-2, spread) + one BF16 ulp of the gold logit (two
+    results that differ by d in fp32 can round to BF16 values d + 1 ulp apart).
+    Returns (max |d|, cosine) for the per-step comparison of paired_no_worse."""
+    m, g = bf(mine).astype(np.float64), bf(gold).astype(np.float64)
+    bound = max(3e-2, spread) + bf16_ulp(g)
+    bad = np.abs(m - g) > bound
+    assert not bad.any(), f"{bad.sum()} logits off, e.g. {m[bad][:4]} vs {g[bad][:4]} (spread {spread:.4f})"
+    cos = m @ g / (np.linalg.norm(m) * np.linalg.norm(g) + 1e-30)
+    return float(np.abs(m - g).max()), float(cos)
+
+
+def paired_no_worse(mine, ref, what="1 - cosine"):
+    """Per-step statistic of this implementation (e.g. 1 - cosine against the
+    oracle) against the same statistic of the reference's own pair on the same
+    steps: a paired one-sided test -- the mean difference stays within three
+    standard errors of zero (it may be negative: closer than the reference)."""
+    d = np.asarray(mine, np.float64) - np.asarray(ref, np.float64)
+    se = d.std(ddof=1) / np.sqrt(len(d)) if len(d) > 1 else 0.0
+    assert d.mean() <= 3.0 * se + 1e-12, (f"{what}: mean {np.mean(mine):.4g} vs the reference's {np.mean(ref):.4g} "
+                                          f"(paired difference {d.mean():.3g}, 3 SE {3 * se:.3g})")
+    return float(np.mean(mine)), float(np.mean(ref))

@@ -17,12 +17,12 @@ context:
   every decode step's logits are compared with the reference's, on
   independently computed KV histories.
 * The reference's CPU backend (libref_cpu.so) measures the reference's own
-  implementation spread: over the whole window where the CPU can afford it
-  (Qwen3-0.6B to context 1024, independent history like the engine), and
-  elsewhere over windows of WINDOW steps that start from the reference CUDA
-  model's KV cache copied in (shared history).  A second engine starts each
-  window from the same copied cache, so its spread is measured exactly like
-  the CPU's.
+  implementation spread: on its own history (like the engine) from the start
+  for as many decode steps as the CPU can afford (the whole window for
+  Qwen3-0.6B to context 1024), then over windows of WINDOW steps that start
+  from the reference CUDA model's KV cache copied in (shared history).  A
+  second engine starts each window from the same copied cache, so its spread
+  is measured exactly like the CPU's.
 
 The reference CUDA backend sizes its attention scratch once per process, from
 its first call's query heads and cache length
@@ -43,13 +43,13 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 
-# name -> (model, prompt tokens, context, CPU mode): "full" runs the reference CPU model over
-# the whole history; a list gives the window starts of shared-history CPU windows.
+# name -> (model, prompt tokens, context, decode steps the reference CPU model runs on its own
+# history from the start (all of them for the smallest model), shared-history window starts)
 CASES = {
-    "qwen3-0.6b-ctx1024": ("qwen3-0.6b", 16, 1024, "full"),
-    "qwen3-0.6b-ctx8192": ("qwen3-0.6b", 4096, 8192, [4095, 8158]),
-    "qwen3-4b-ctx4096": ("qwen3-4b", 128, 4096, [127, 2100, 4062]),
-    "qwen3-8b-ctx4096": ("qwen3-8b", 512, 4096, [511, 2300, 4062]),
+    "qwen3-0.6b-ctx1024": ("qwen3-0.6b", 16, 1024, 1008, []),
+    "qwen3-0.6b-ctx8192": ("qwen3-0.6b", 4096, 8192, 0, [4095, 8158]),
+    "qwen3-4b-ctx4096": ("qwen3-4b", 128, 4096, 160, [2100, 4062]),
+    "qwen3-8b-ctx4096": ("qwen3-8b", 512, 4096, 128, [2300, 4062]),
 }
 WINDOW = 32
 
@@ -93,18 +93,16 @@ class Pair:
 
 
 def run(case: str) -> dict:
-    from inference_b200 import MODELS, Engine
+    from inference_b200 import MODELS, Engine, prompt_ids
     from oracle import ModelConfig, RefLib
 
-    model, P, C, cpu_mode = CASES[case]
+    model, P, C, cpu_indep, windows = CASES[case]
     cfg = MODELS[model]
     t_start = time.time()
     mc = ModelConfig.make(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, 128, cfg.vocab, C,
                           tied=cfg.tied)
     ref = RefLib("cuda").model(mc, seed=0)
     cpu = RefLib("cpu").model(mc, seed=0)
-    from inference_b200 import prompt_ids
-
     prompt = prompt_ids(P, seed=1, vocab=cfg.vocab).astype(np.uint32)
     S = np.zeros(C, np.uint32)
     S[:P] = prompt
@@ -113,19 +111,20 @@ def run(case: str) -> dict:
     eng.init_synthetic(0)
     eng.set_tokens(prompt)
     eng.prefill(P - 1)
-    windows = [] if cpu_mode == "full" else list(cpu_mode)
-    eng2 = Engine(cfg, capacity=C) if windows else None
-    if eng2:
+    eng2 = None
+    if windows:
+        eng2 = Engine(cfg, capacity=C)
         eng2.init_synthetic(0)
 
-    # the reference prefills one forward per prompt token (the CPU model too when it runs in full)
+    # the reference prefills one forward per prompt token (the CPU model too when it starts
+    # on its own history)
     for p in range(P - 1):
         ref.forward(int(S[p]))
-        if cpu_mode == "full":
+        if cpu_indep:
             cpu.forward(int(S[p]))
     t_pre = time.time()
 
-    engine_pair, cpu_pair, eng2_pair = Pair(), Pair(), Pair()
+    engine_pair, cpu_indep_pair, cpu_shared_pair, eng2_pair = Pair(), Pair(), Pair(), Pair()
     win_pairs = {}
     active = None  # (start, cpu, engine 2, engine) Pairs of the running window
     for p in range(P - 1, C - 1):
@@ -147,23 +146,24 @@ def run(case: str) -> dict:
         eng.sync()
         e1 = eng.logits()
         engine_pair.add(e1, r_logits, nxt, p)
+        if p < P - 1 + cpu_indep:
+            cpu.forward(int(S[p]))
+            cpu_indep_pair.add(cpu.logits(), r_logits, nxt, p)
         if active:
-            active[3].add(e1, r_logits, nxt, p)
-        if cpu_mode == "full" or active:
             cpu.forward(int(S[p]))
             c_logits = cpu.logits()
-            cpu_pair.add(c_logits, r_logits, nxt, p)
-            if active:
-                active[1].add(c_logits, r_logits, nxt, p)
-                eng2.set_tokens(S[: p + 1])
-                eng2.step(1)
-                eng2.sync()
-                e2 = eng2.logits()
-                eng2_pair.add(e2, r_logits, nxt, p)
-                active[2].add(e2, r_logits, nxt, p)
-                if p + 1 - active[0] >= WINDOW:
-                    active = None
-    # the engine's own greedy history must repeat S where it was free to choose (bit-exact argmax)
+            cpu_shared_pair.add(c_logits, r_logits, nxt, p)
+            active[1].add(c_logits, r_logits, nxt, p)
+            active[3].add(e1, r_logits, nxt, p)
+            eng2.set_tokens(S[: p + 1])
+            eng2.step(1)
+            eng2.sync()
+            e2 = eng2.logits()
+            eng2_pair.add(e2, r_logits, nxt, p)
+            active[2].add(e2, r_logits, nxt, p)
+            if p + 1 - active[0] >= WINDOW:
+                active = None
+    # the engine's fused greedy argmax by position (bit-exact against the argmax of its logits)
     hist = eng.argmax_history(C - 1)
     ref.close()
     cpu.close()
@@ -171,16 +171,18 @@ def run(case: str) -> dict:
     if eng2:
         eng2.close()
     return {
-        "case": case, "model": model, "layers": cfg.layers, "prompt": P, "context": C,
-        "decode_steps": C - P, "cpu_mode": "full" if cpu_mode == "full" else f"windows of {WINDOW} at {windows}",
+        "case": case, "model": model, "layers": cfg.layers, "prompt": P, "context": C, "decode_steps": C - P,
+        "cpu": f"own history for the first {cpu_indep} decode steps; shared-history windows of {WINDOW} at "
+               f"{windows}",
         "engine_vs_ref_cuda": engine_pair.summary(),
-        "ref_cpu_vs_ref_cuda": cpu_pair.summary(),
+        "ref_cpu_vs_ref_cuda_own_history": cpu_indep_pair.summary(),
+        "ref_cpu_vs_ref_cuda_shared_history": cpu_shared_pair.summary(),
         "engine_shared_history_vs_ref_cuda": eng2_pair.summary(),
         "windows": {str(k): {"ref_cpu": v[1].summary(), "engine_shared": v[2].summary(),
                              "engine": v[3].summary()}
                     for k, v in win_pairs.items()},
-        "rows": {"engine": engine_pair.table(), "ref_cpu": cpu_pair.table(),
-                 "engine_shared": eng2_pair.table() if eng2 else []},
+        "rows": {"engine": engine_pair.table(), "ref_cpu_own": cpu_indep_pair.table(),
+                 "ref_cpu_shared": cpu_shared_pair.table(), "engine_shared": eng2_pair.table()},
         "row_fields": ["position", "maxabs", "meanabs", "excess_over_ulp", "cosine", "ref_top2_margin", "agree"],
         "sequence_head": [int(x) for x in S[P:P + 8]],
         "engine_greedy_vs_sequence": int((hist[P - 1:C - 1] == S[P:C]).sum()),

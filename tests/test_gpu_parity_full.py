@@ -21,10 +21,13 @@ the engine to it:
   implementation can flip such a step); the overall agreement is reported
   beside the reference CPU's own.
 
-Shared history: the CPU reference and a second engine start windows from the
-reference CUDA model's KV cache; independent history: the engine computes its
-own cache over the whole context (and, for Qwen3-0.6B to context 1024, the
-reference CPU backend does too).
+Own history: the engine computes its own KV cache over the whole context; the
+reference CPU backend does the same for the first decode steps (all of them
+for Qwen3-0.6B to context 1024).  Shared history: the CPU reference and a
+second engine start windows of 32 steps from the reference CUDA model's KV
+cache.  The reference CUDA backend itself is not run-to-run deterministic
+(two identical instances drift apart by BF16 ulps once their caches differ),
+so every comparison is against the one instance both sides follow.
 """
 import json
 import os
@@ -90,23 +93,25 @@ def _run_case(case, tmp_path):
 def test_engine_vs_reference_cuda_full_depth(case, tmp_path):
     d = _run_case(case, tmp_path)
     rows = d["rows"]
-    cpu = rows["ref_cpu"]
-    spread = max(3e-2, max(r[FIELDS["maxabs"]] for r in cpu))
-    report = {"case": case, "reference_cpu_vs_cuda": d["ref_cpu_vs_ref_cuda"],
-              "engine_vs_cuda": d["engine_vs_ref_cuda"],
-              "engine_shared_history_vs_cuda": d["engine_shared_history_vs_ref_cuda"], "bound": spread}
-    if d["cpu_mode"] == "full":
-        # independent histories on both sides, every decode step
-        eng = rows["engine"]
-        assert max(r[FIELDS["excess_over_ulp"]] for r in eng) <= spread, report
-        report["paired"] = _paired_no_worse(eng, cpu, "independent history")
-        report["decisive_steps"] = _decisive(eng, spread, "independent history")
-    else:
-        # shared history: the engine from the reference CUDA model's cache, like the CPU
-        eng = rows["engine_shared"]
-        assert max(r[FIELDS["excess_over_ulp"]] for r in eng) <= spread, report
-        report["paired"] = _paired_no_worse(eng, cpu, "shared history")
-        report["decisive_steps"] = _decisive(eng, spread, "shared history")
-    # the engine's own greedy history repeats the argmax of its own logits
+    report = {k: d[k] for k in ("case", "engine_vs_ref_cuda", "ref_cpu_vs_ref_cuda_own_history",
+                                "ref_cpu_vs_ref_cuda_shared_history", "engine_shared_history_vs_ref_cuda")}
+    checked = 0
+    # own histories on both sides (the engine's KV cache is its own; so is the CPU's)
+    for eng, cpu, what in ((rows["engine"], rows["ref_cpu_own"], "own history"),
+                           (rows["engine_shared"], rows["ref_cpu_shared"], "shared history")):
+        if not cpu:
+            continue
+        steps = {int(r[0]) for r in cpu}
+        eng = [r for r in eng if int(r[0]) in steps]
+        bound = max(3e-2, max(r[FIELDS["maxabs"]] for r in cpu))
+        excess = max(r[FIELDS["excess_over_ulp"]] for r in eng)
+        assert excess <= bound, f"{what}: |engine - reference CUDA| exceeds {bound:.4f} + 1 ulp by {excess - bound:.4f}"
+        report[what] = {"bound": bound, "paired_means": _paired_no_worse(eng, cpu, what),
+                        "decisive_steps": _decisive(eng, bound, what),
+                        "agree_engine": int(sum(r[FIELDS["agree"]] for r in eng)),
+                        "agree_ref_cpu": int(sum(r[FIELDS["agree"]] for r in cpu)), "steps": len(eng)}
+        checked += len(eng)
+    assert checked >= 64, report
+    # the engine's fused argmax (lm_head epilogue) is the argmax of its own logits, bit-exact
     assert d["engine_greedy_vs_sequence"] == d["engine_vs_ref_cuda"]["agree"], report
     print(json.dumps(report))

@@ -14,7 +14,7 @@ import socket
 import numpy as np
 import pytest
 
-from gpu_util import assert_logits_close, bf
+from gpu_util import assert_logits_close, assert_within_spread, bf, paired_no_worse, spread_of
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
@@ -102,17 +102,17 @@ def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
     om = oracle.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)), seed=0)
     if mode.endswith("-fp8"):
         om.quantize_fp8()  # row scales over full rows: the same model as the 1-GPU FP8 engine
-    atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
-    min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
-    agree = 0
+    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    agree, coss = 0, []
     toks = g["tokens"]
     for i, t in enumerate(toks):
         nxt = om.forward(int(t))
         full = np.concatenate([parts[r]["logits"][i] for r in range(world)])
-        assert_logits_close(full, om.logits(), atol=atol, n_ulp=1, min_cos=min_cos)
+        coss.append(assert_within_spread(full, om.logits(), spread)[1])
         assert int(parts[0]["hist"][i]) == int(np.argmax(bf(full)))
         agree += int(int(parts[0]["hist"][i]) == nxt)
     om.close()
+    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][:len(coss)])
     assert agree >= len(toks) - 1
 
 
@@ -165,60 +165,3 @@ def test_peer_wait_times_out_without_fault(tmp_path):
     msg = (tmp_path / "stall0.txt").read_text()
     assert "peer wait timed out" in msg, msg
 
-
-def _departed_main(rank, world, port, out_dir):
-    import datetime
-
-    import torch
-    import torch.distributed as dist
-
-    from inference_b200 import Engine, Q3Error, Qwen3Config, prompt_ids
-
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
-    qc = Qwen3Config("qwen3-0.6b-l2", hidden=1024, inter=3072, layers=2, q_heads=16, kv_heads=8, vocab=151936,
-                     tied=True)
-    e = Engine(qc, capacity=64, device=rank, tp_rank=rank, tp_size=world)
-    e.init_synthetic(0)
-    _attach(e, dist, "nccl", rank)
-    e.set_comm_timeout(3.0)
-    e.set_tokens(prompt_ids(8))
-    e.step(2)  # both ranks: healthy exchanges
-    e.sync()
-    msg, after = "", ""
-    if rank == 0:
-        # rank 1 has left between steps: this step's exchange never completes
-        e.step(1)
-        try:
-            e.sync()
-        except Q3Error as exc:
-            msg = str(exc)
-        try:
-            e.step(1)
-        except Q3Error as exc:
-            after = str(exc)
-    dist.barrier()  # rank 1 waits here, idle, until rank 0 has given up
-    with open(os.path.join(out_dir, f"departed{rank}.txt"), "w") as f:
-        f.write(msg + "\n" + after)
-    e.close()
-    dist.destroy_process_group()
-
-
-@pytest.mark.timeout(300)
-def test_nccl_departed_peer_aborts_without_hang(tmp_path):
-    """Failure detection on the NCCL path: after two healthy steps one rank stops
-    stepping (it leaves between steps, nothing in flight); the other rank's next
-    exchange never completes, its bounded host wait runs out, the communicator is
-    aborted (its NCCL kernels return) and the call reports Q3_ERR_NCCL; the engine
-    then refuses further steps instead of hanging.  NVLS is off."""
-    import torch
-    import torch.multiprocessing as mp
-
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    mp.start_processes(_departed_main, args=(2, _free_port(), str(tmp_path)), nprocs=2, start_method="spawn")
-    msg, after = (tmp_path / "departed0.txt").read_text().split("\n", 1)
-    assert "Q3_ERR_NCCL" in msg and "did not arrive" in msg, msg
-    assert "Q3_ERR_NCCL" in after and "aborted" in after, after

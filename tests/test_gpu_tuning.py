@@ -16,7 +16,7 @@ import socket
 import numpy as np
 import pytest
 
-from gpu_util import assert_logits_close, bf
+from gpu_util import assert_logits_close, assert_within_spread, bf, paired_no_worse, spread_of
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
@@ -98,8 +98,8 @@ def test_fp8_prefill_matches_fp8_oracle(oracle, name):
                       seed=0).quantize_fp8()
     for t in toks[:n_pre]:
         om.forward(int(t))
-    atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
-    min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
+    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    coss = []
     with Engine(qc, capacity=cap, weights="fp8") as e:
         e.init_synthetic(0)
         e.tuning = ["fp8_prefill"]
@@ -118,10 +118,11 @@ def test_fp8_prefill_matches_fp8_oracle(oracle, name):
             e.sync()
             mine = e.logits()
             nxt = om.forward(int(toks[i]))
-            assert_logits_close(mine, om.logits(), atol=atol, n_ulp=1, min_cos=min_cos)
+            coss.append(assert_within_spread(mine, om.logits(), spread)[1])
             agree += int(int(np.argmax(bf(mine))) == nxt)
         assert agree >= (n - n_pre) - 1
     om.close()
+    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][n_pre:n])
 
 
 def test_tuning_rejects_unknown_bits():
@@ -248,13 +249,13 @@ def test_tp_prefill_matches_oracle(tmp_path, oracle, name, mode):
                 k, v = parts[r][f"k{lay}_{i}"], parts[r][f"v{lay}_{i}"]
                 assert _cos(k, ok_[r * kl:(r + 1) * kl]) >= 0.9995, (i, int(lay), r)
                 assert _cos(v, ov_[r * kl:(r + 1) * kl]) >= 0.9995, (i, int(lay), r)
-    atol = max(3e-2, 1.5 * float(g["env_maxabs"].max()))
-    min_cos = min(0.9999, 1.0 - 1.5 * (1.0 - float(g["env_cos"].min())))
-    agree = 0
+    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    agree, coss = 0, []
     for j, i in enumerate(range(n_pre, n)):
         nxt = om.forward(int(toks[i]))
         full = np.concatenate([parts[r]["logits"][j] for r in range(world)])
-        assert_logits_close(full, om.logits(), atol=atol, n_ulp=1, min_cos=min_cos)
+        coss.append(assert_within_spread(full, om.logits(), spread)[1])
         agree += int(int(np.argmax(bf(full))) == nxt)
     om.close()
+    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][n_pre:n])
     assert agree >= (n - n_pre) - 1
