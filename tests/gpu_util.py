@@ -75,12 +75,23 @@ def assert_logits_close(mine, gold, atol=3e-2, n_ulp=2, min_cos=0.9999):
     return float(np.abs(m - g).max()), float(cos)
 
 
-def spread_of(g):
-    """The reference's own implementation spread recorded with a golden model
-    fixture: max |logit difference| and min cosine between the reference's CPU
-    backend and the oracle over the fixture's steps (two fp32 orders of the
-    same arithmetic)."""
-    return float(np.asarray(g["env_maxabs"]).max()), float(np.asarray(g["env_cos"]).min())
+def spread_of(g, name):
+    """The reference's own implementation spread on a golden model record's
+    steps: (max |logit difference| among the reference's implementations --
+    its CPU backend vs the oracle, and, where tests/golden/make_golden_cuda.py
+    has recorded it, its CUDA backend vs the oracle --, and per step the
+    distance 1 - cosine of a GPU implementation of the reference from the
+    oracle: its CUDA backend's where recorded, else its CPU backend's)."""
+    import os
+
+    spread = float(np.asarray(g["env_maxabs"]).max())
+    dev = 1.0 - np.asarray(g["env_cos"], np.float64)
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", f"model_{name}_ref_cuda.npz")
+    if os.path.exists(p):
+        c = np.load(p)
+        spread = max(spread, float(np.asarray(c["cuda_maxabs"]).max()))
+        dev = 1.0 - np.asarray(c["cuda_cos"], np.float64)
+    return spread, dev
 
 
 def assert_within_spread(mine, gold, spread):

@@ -99,7 +99,7 @@ def test_fp8_engine_matches_fp8_oracle(oracle, name):
     g, qc, oc, cap = _cfgs(name)
     toks = g["tokens"].astype(np.uint32)
     om = oracle.model(oc, seed=0).quantize_fp8()
-    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    spread, ref_dev = spread_of(g, name)  # the reference's own implementations vs the oracle
     agree, coss = 0, []
     with Engine(qc, capacity=cap, weights="fp8") as e:
         e.init_synthetic(0)
@@ -116,7 +116,7 @@ def test_fp8_engine_matches_fp8_oracle(oracle, name):
         out = e.generate(toks[:8], 4, stop_at_eos=False)
         assert len(out) == 4
     om.close()
-    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][:len(coss)])
+    paired_no_worse(1.0 - np.array(coss), ref_dev[:len(coss)])
     assert agree >= len(toks) - 1
 
 

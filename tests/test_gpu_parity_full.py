@@ -95,23 +95,36 @@ def test_engine_vs_reference_cuda_full_depth(case, tmp_path):
     rows = d["rows"]
     report = {k: d[k] for k in ("case", "engine_vs_ref_cuda", "ref_cpu_vs_ref_cuda_own_history",
                                 "ref_cpu_vs_ref_cuda_shared_history", "engine_shared_history_vs_ref_cuda")}
-    checked = 0
-    # own histories on both sides (the engine's KV cache is its own; so is the CPU's)
+    # the reference's own CPU-vs-CUDA spread measured in this run (every step it ran)
+    cpu_all = rows["ref_cpu_own"] + rows["ref_cpu_shared"]
+    bound = max(3e-2, max(r[FIELDS["maxabs"]] for r in cpu_all))
+    report["bound"] = bound
+    failures, checked = [], 0
     for eng, cpu, what in ((rows["engine"], rows["ref_cpu_own"], "own history"),
                            (rows["engine_shared"], rows["ref_cpu_shared"], "shared history")):
         if not cpu:
             continue
         steps = {int(r[0]) for r in cpu}
         eng = [r for r in eng if int(r[0]) in steps]
-        bound = max(3e-2, max(r[FIELDS["maxabs"]] for r in cpu))
+        entry = {"steps": len(eng), "agree_engine": int(sum(r[FIELDS["agree"]] for r in eng)),
+                 "agree_ref_cpu": int(sum(r[FIELDS["agree"]] for r in cpu)),
+                 "max_engine": max(r[FIELDS["maxabs"]] for r in eng),
+                 "max_ref_cpu": max(r[FIELDS["maxabs"]] for r in cpu)}
+        for key, check in (("paired_means", lambda: _paired_no_worse(eng, cpu, what)),
+                           ("decisive_steps", lambda: _decisive(eng, bound, what))):
+            try:
+                entry[key] = check()
+            except AssertionError as exc:
+                failures.append(str(exc))
         excess = max(r[FIELDS["excess_over_ulp"]] for r in eng)
-        assert excess <= bound, f"{what}: |engine - reference CUDA| exceeds {bound:.4f} + 1 ulp by {excess - bound:.4f}"
-        report[what] = {"bound": bound, "paired_means": _paired_no_worse(eng, cpu, what),
-                        "decisive_steps": _decisive(eng, bound, what),
-                        "agree_engine": int(sum(r[FIELDS["agree"]] for r in eng)),
-                        "agree_ref_cpu": int(sum(r[FIELDS["agree"]] for r in cpu)), "steps": len(eng)}
+        if excess > bound:
+            failures.append(f"{what}: |engine - reference CUDA| exceeds {bound:.4f} + 1 ulp by {excess - bound:.4f}")
+        report[what] = entry
         checked += len(eng)
-    assert checked >= 64, report
+    if checked < 64:
+        failures.append(f"only {checked} compared steps")
     # the engine's fused argmax (lm_head epilogue) is the argmax of its own logits, bit-exact
-    assert d["engine_greedy_vs_sequence"] == d["engine_vs_ref_cuda"]["agree"], report
+    if d["engine_greedy_vs_sequence"] != d["engine_vs_ref_cuda"]["agree"]:
+        failures.append("fused argmax differs from the argmax of the engine's logits")
     print(json.dumps(report))
+    assert not failures, failures

@@ -48,7 +48,7 @@ def test_prefill_then_decode_matches_oracle(oracle, name):
     om = oracle.model(oc, seed=0)
     for t in toks[:n_pre]:
         om.forward(int(t))
-    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    spread, ref_dev = spread_of(g, name)  # the reference's own implementations vs the oracle
     coss = []
     with Engine(qc, capacity=cap) as e:
         e.init_synthetic(0)
@@ -72,7 +72,7 @@ def test_prefill_then_decode_matches_oracle(oracle, name):
             agree += int(int(np.argmax(bf(mine))) == nxt)
         assert agree >= (n - n_pre) - 1
     om.close()
-    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][n_pre:n])
+    paired_no_worse(1.0 - np.array(coss), ref_dev[n_pre:n])
 
 
 def test_prefill_chunks_match_decode_steps():

@@ -96,7 +96,7 @@ def test_reference_model_on_drop_in_backend(refb200, oracle, name):
     mc = ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied))
     rm = refb200.model(mc, seed=0)
     om = oracle.model(mc, seed=0)
-    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    spread, ref_dev = spread_of(g, name)  # the reference's own implementations vs the oracle
     agree, coss = 0, []
     toks = g["tokens"]
     for i, t in enumerate(toks):
@@ -112,5 +112,5 @@ def test_reference_model_on_drop_in_backend(refb200, oracle, name):
             assert _cos(k, ok_) >= 0.999 and _cos(v, ov_) >= 0.999, (i, int(lay))
     rm.close()
     om.close()
-    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][:len(coss)])
+    paired_no_worse(1.0 - np.array(coss), ref_dev[:len(coss)])
     assert agree >= len(toks) - 1

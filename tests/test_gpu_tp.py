@@ -102,7 +102,7 @@ def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
     om = oracle.model(ModelConfig.make(h, inter, layers, qh, kvh, hd, vocab, cap, tied=bool(tied)), seed=0)
     if mode.endswith("-fp8"):
         om.quantize_fp8()  # row scales over full rows: the same model as the 1-GPU FP8 engine
-    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    spread, ref_dev = spread_of(g, name)  # the reference's own implementations vs the oracle
     agree, coss = 0, []
     toks = g["tokens"]
     for i, t in enumerate(toks):
@@ -112,7 +112,7 @@ def test_engine_tensor_parallel(tmp_path, oracle, name, mode, world):
         assert int(parts[0]["hist"][i]) == int(np.argmax(bf(full)))
         agree += int(int(parts[0]["hist"][i]) == nxt)
     om.close()
-    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][:len(coss)])
+    paired_no_worse(1.0 - np.array(coss), ref_dev[:len(coss)])
     assert agree >= len(toks) - 1
 
 

@@ -98,7 +98,7 @@ def test_fp8_prefill_matches_fp8_oracle(oracle, name):
                       seed=0).quantize_fp8()
     for t in toks[:n_pre]:
         om.forward(int(t))
-    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    spread, ref_dev = spread_of(g, name)  # the reference's own implementations vs the oracle
     coss = []
     with Engine(qc, capacity=cap, weights="fp8") as e:
         e.init_synthetic(0)
@@ -122,7 +122,7 @@ def test_fp8_prefill_matches_fp8_oracle(oracle, name):
             agree += int(int(np.argmax(bf(mine))) == nxt)
         assert agree >= (n - n_pre) - 1
     om.close()
-    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][n_pre:n])
+    paired_no_worse(1.0 - np.array(coss), ref_dev[n_pre:n])
 
 
 def test_tuning_rejects_unknown_bits():
@@ -249,7 +249,7 @@ def test_tp_prefill_matches_oracle(tmp_path, oracle, name, mode):
                 k, v = parts[r][f"k{lay}_{i}"], parts[r][f"v{lay}_{i}"]
                 assert _cos(k, ok_[r * kl:(r + 1) * kl]) >= 0.9995, (i, int(lay), r)
                 assert _cos(v, ov_[r * kl:(r + 1) * kl]) >= 0.9995, (i, int(lay), r)
-    spread, _ = spread_of(g)  # the reference CPU vs the oracle on these steps
+    spread, ref_dev = spread_of(g, name)  # the reference's own implementations vs the oracle
     agree, coss = 0, []
     for j, i in enumerate(range(n_pre, n)):
         nxt = om.forward(int(toks[i]))
@@ -257,5 +257,5 @@ def test_tp_prefill_matches_oracle(tmp_path, oracle, name, mode):
         coss.append(assert_within_spread(full, om.logits(), spread)[1])
         agree += int(int(np.argmax(bf(full))) == nxt)
     om.close()
-    paired_no_worse(1.0 - np.array(coss), 1.0 - g["env_cos"][n_pre:n])
+    paired_no_worse(1.0 - np.array(coss), ref_dev[n_pre:n])
     assert agree >= (n - n_pre) - 1
