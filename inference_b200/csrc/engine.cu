@@ -74,6 +74,7 @@ struct q3_engine {
     uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
     uint32_t *done_counter = nullptr, *err = nullptr;
     int attn_splits = 1;
+    int o_early = 0;  // o_proj GEMV CTAs that start beside attention (plan_gemv_early)
     // opt-in variants of the graph path (Q3_TUNE_*)
     uint32_t tune = 0;
     // CUDA-graph path timeline: per launch of a step and CTA (q3_engine_trace)
@@ -296,13 +297,16 @@ struct WMat {
     const float* s;
 };
 
-int gemv(Recorder& r, int pro, int epi, GemvArgs a, WMat W, int N, int K) {
+// early_ctas > 0 (BF16 weights): the GEMV runs after a kernel that leaves that many
+// SMs free, so its first CTAs start beside it (plan_gemv_early)
+int gemv(Recorder& r, int pro, int epi, GemvArgs a, WMat W, int N, int K, int early_ctas = 0) {
     a.W = W.w;
     a.W8 = W.q;
     a.wscale = W.s;
     a.N = N;
     a.K = K;
-    a.plan = plan_gemv(N, K, epi, r.e->sms, W.q ? 1 : 2);
+    a.plan = (early_ctas > 0 && !W.q) ? plan_gemv_early(N, K, epi, r.e->sms, early_ctas)
+                                      : plan_gemv(N, K, epi, r.e->sms, W.q ? 1 : 2);
     a.trace = r.trace();
     r.mark(true, 0);
     cudaError_t st = launch_gemv(pro, epi, a, r.e->stream, r.pdl);
@@ -399,18 +403,18 @@ int record_step(Recorder& r, size_t pos_now) {
         Q3_TRY(gemv(r, pro, EPI_QKV, a, w_qkv, e->qd + 2 * e->kd, e->H));
         // ---- attention
         Q3_TRY(attention(r, L, pos_now));
-        // ---- o_proj (+ residual add)
+        // ---- o_proj (+ residual add); its first CTAs start on the SMs attention leaves free
         GemvArgs o = base_args(e);
         o.x = e->attn;
         if (tp) {
             o.yf = e->partial;
             o.xtag = 2 * static_cast<int>(l) + 1;
-            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, o, w_o, e->H, e->qd));
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_PARTIAL, o, w_o, e->H, e->qd, e->o_early));
             Q3_TRY(allreduce(e, e->partial, e->H));
         } else {
             o.hs = e->hs[0];
             o.vsum_out = e->vsum;
-            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID_F32, o, w_o, e->H, e->qd));
+            Q3_TRY(gemv(r, PRO_PLAIN, EPI_RESID_F32, o, w_o, e->H, e->qd, e->o_early));
         }
         // ---- gate/up (+ RMSNorm prologue, SwiGLU epilogue)
         GemvArgs gu = base_args(e);
@@ -701,6 +705,13 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
 
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
+    {
+        // decode attention: splits x kv heads x query-head blocks CTAs, two per SM; the SMs
+        // it leaves free start the o_proj GEMV's first CTAs while it runs
+        const int G = e->qh / e->kvh, HG = G >= 4 ? 4 : G;
+        const int attn_ctas = e->attn_splits * e->kvh * (G / HG);
+        e->o_early = std::max(0, e->sms - (attn_ctas + 1) / 2);
+    }
 
     if (setup != cudaSuccess)
         return bail(fail(Q3_ERR_CUDA, std::string("engine setup copy: ") + cudaGetErrorString(setup)));

@@ -27,6 +27,7 @@
 //     Row sums are multiplied back by 2^s and by the row's scale in the
 //     epilogue.
 #include <algorithm>
+#include <cmath>
 
 #include "kernels.cuh"
 
@@ -220,11 +221,11 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
 
     // ---- this CTA's rows and this warp's contiguous run of (row, chunk) items
     const int units = a.N / p.row_gran;
-    const int u0 = static_cast<int>(static_cast<long long>(blockIdx.x) * units / gridDim.x);
-    const int u1 = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * units / gridDim.x);
+    int u0, u1;
+    gemv_band(p, units, blockIdx.x, u0, u1);
     const int r0 = u0 * p.row_gran, r1 = u1 * p.row_gran;
     const int nrows = r1 - r0;
-    const int max_rows = (units + gridDim.x - 1) / gridDim.x * p.row_gran;
+    const int max_rows = p.max_units * p.row_gran;
     const SmemLayout L = smem_layout(p, a.K, max_rows);
     bf16* xs = reinterpret_cast<bf16*>(smem + L.x_off);
     float* part = reinterpret_cast<float*>(smem + L.part_off);
@@ -791,10 +792,36 @@ GemvPlan plan_gemv(int N, int K, int epi, int sms, int wb) {
     const long long min_grid = (items + kMaxItems - 1) / kMaxItems;
     if (grid < min_grid) grid = static_cast<int>(std::min<long long>(min_grid, units));
     p.grid = std::max(1, grid);
-    const int max_rows = (units + p.grid - 1) / p.grid * p.row_gran;
+    p.max_units = (units + p.grid - 1) / p.grid;
+    const int max_rows = p.max_units * p.row_gran;
     const size_t budget = wb == 1 ? kSmemBudgetF8 : kSmemBudget;
     for (p.stages = Q3_GEMV_MAX_STAGES; p.stages > 2; --p.stages)
         if (smem_layout(p, K, max_rows).total <= budget) break;
+    p.smem = smem_layout(p, K, max_rows).total;
+    return p;
+}
+
+GemvPlan plan_gemv_early(int N, int K, int epi, int sms, int early_ctas) {
+    GemvPlan p = plan_gemv(N, K, epi, sms, 2);
+    const int units = N / p.row_gran, E = early_ctas;
+    if (E <= 0 || E >= p.grid) return p;
+    // the ring an early CTA fills before the dependency release, in units of rows
+    const double ring_units = static_cast<double>(kWarps) * p.stages * slot_bytes(p) /
+                              (static_cast<double>(K) * 2 * p.row_gran);
+    // equal bytes left after the release: b_E - ring = b_L, E b_E + (grid - E) b_L = units
+    const double b_late = std::max(0.0, (units - E * ring_units) / p.grid);
+    long long early_units = std::llround(E * (b_late + ring_units));
+    early_units = std::min<long long>(std::max<long long>(early_units, (static_cast<long long>(units) * E) / p.grid),
+                                      units);
+    const int max_early = static_cast<int>((early_units + E - 1) / E);
+    // the per-CTA partial sums must still fit
+    if (static_cast<long long>(max_early) * p.row_gran * p.nch > kMaxItems) return p;
+    p.early = E;
+    p.early_units = static_cast<int>(early_units);
+    p.max_units = std::max(max_early, (units - p.early_units + (p.grid - E) - 1) / (p.grid - E));
+    const int max_rows = p.max_units * p.row_gran;
+    for (p.stages = Q3_GEMV_MAX_STAGES; p.stages > 2; --p.stages)
+        if (smem_layout(p, K, max_rows).total <= kSmemBudget) break;
     p.smem = smem_layout(p, K, max_rows).total;
     return p;
 }

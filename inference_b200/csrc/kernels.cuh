@@ -50,7 +50,30 @@ struct GemvPlan {
     int row_gran;  // rows assigned to CTAs in units of this many (2 for SWIGLU)
     int wb;        // bytes per weight: 2 = BF16, 1 = FP8 E4M3
     size_t smem;   // dynamic shared memory bytes
+    // Row bands: by default units (row_gran rows each) are spread evenly over the grid.
+    // early > 0: CTAs [0, early) share early_units units and the rest the remainder --
+    // for a GEMV launched beside a kernel that occupies some SMs, whose first CTAs start
+    // (and fill their rings) early while the others wait for SMs to free up.
+    int early, early_units;
+    int max_units;  // the largest band
 };
+// Units [u0, u1) of CTA b's band.
+__host__ __device__ inline void gemv_band(const GemvPlan& p, int units, int b, int& u0, int& u1) {
+    if (p.early > 0 && p.early < p.grid) {
+        const int late = p.grid - p.early;
+        if (b < p.early) {
+            u0 = static_cast<int>(static_cast<long long>(b) * p.early_units / p.early);
+            u1 = static_cast<int>(static_cast<long long>(b + 1) * p.early_units / p.early);
+        } else {
+            const int r = b - p.early, rest = units - p.early_units;
+            u0 = p.early_units + static_cast<int>(static_cast<long long>(r) * rest / late);
+            u1 = p.early_units + static_cast<int>(static_cast<long long>(r + 1) * rest / late);
+        }
+    } else {
+        u0 = static_cast<int>(static_cast<long long>(b) * units / p.grid);
+        u1 = static_cast<int>(static_cast<long long>(b + 1) * units / p.grid);
+    }
+}
 
 // Tensor-parallel exchange through peer memory (CUDA IPC mappings over
 // NVLink).  Rank j's buffer holds, per slot (exchange parity), every rank's
@@ -121,6 +144,10 @@ struct GemvArgs {
 };
 
 GemvPlan plan_gemv(int N, int K, int epi, int num_sms, int wb = 2);
+// plan_gemv for a BF16 GEMV whose first `early_ctas` CTAs start beside the kernel
+// before it: their bands grow by what their shared-memory rings prefetch there, so
+// that every CTA has the same bytes left to stream once the dependency is released.
+GemvPlan plan_gemv_early(int N, int K, int epi, int num_sms, int early_ctas);
 cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl);
 
 // ---------------------------------------------------------------- attention
