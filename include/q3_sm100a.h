@@ -385,6 +385,49 @@ Q3_API int q3_engine_attach_nccl(q3_engine* e, const void* id_128_bytes);
  * instead (Q3_ERR_DEVICE "peer wait timed out", context usable). */
 Q3_API int q3_engine_set_comm_timeout(q3_engine* e, double seconds);
 
+/* ------------------------------------------------------------------------
+ * Tokenizer and text generation (host code): tokenizer::Tokenizer
+ * (src/lib/tokenizer/tokenizer.hpp:35-66, tokenizer.cpp:205-265) and
+ * Generator::generate on text (src/lib/inference/generator.cpp:37-63).
+ * Byte-level BPE of a Qwen3 tokenizer.json: added tokens, NFC, the Qwen2
+ * pre-tokenizer pattern, BPE by merge rank.
+ * ---------------------------------------------------------------------- */
+typedef struct q3_tokenizer q3_tokenizer;
+
+/* Tokenizer(model_path) (tokenizer.cpp:205-215): `path` is a tokenizer.json
+ * or a directory holding one.  Q3_ERR_UNSUPPORTED for a model other than BPE
+ * or a pre-tokenizer pattern other than Qwen2's. */
+Q3_API int q3_tokenizer_load(const char* path, q3_tokenizer** out);
+Q3_API int q3_tokenizer_destroy(q3_tokenizer* t);
+
+/* Tokenizer::tokenize (tokenizer.cpp:217-235) of text[0..len) (UTF-8;
+ * ill-formed bytes become U+FFFD as in the reference's ICU conversion).
+ * Writes the ids to ids[0..capacity) and their count to *n_ids; ids NULL only
+ * counts.  Q3_ERR_INVALID if capacity is too small. */
+Q3_API int q3_tokenizer_encode(const q3_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t capacity,
+                               size_t* n_ids);
+
+/* Tokenizer::decode (tokenizer.cpp:237-265): the bytes of ids[0..n) as a
+ * NUL-terminated string in out[0..capacity); *needed = its size with the NUL.
+ * out NULL only sizes.  Q3_ERR_INVALID for an id outside the vocabulary. */
+Q3_API int q3_tokenizer_decode(const q3_tokenizer* t, const uint32_t* ids, size_t n, char* out, size_t capacity,
+                               size_t* needed);
+
+/* Model::apply_chat_template (src/lib/model/qwen3/qwen3.hpp:97-103) into
+ * out, sized like q3_tokenizer_decode. */
+Q3_API int q3_chat_template(const char* prompt, size_t len, char* out, size_t capacity, size_t* needed);
+
+/* Generator::generate (generator.cpp:37-63): chat template, tokenize, then
+ * q3_engine_generate with EOS stopping and no limit but the KV cache, and the
+ * response decoded.  *out receives a NUL-terminated string allocated by the
+ * library (free it with q3_string_free) and *out_len its length without the
+ * NUL.  Q3_ERR_INVALID ("prompt does not fit in the model context") if the
+ * templated prompt has >= capacity tokens, as the reference's
+ * std::length_error. */
+Q3_API int q3_engine_generate_text(q3_engine* e, const q3_tokenizer* t, const char* prompt, size_t len, char** out,
+                                   size_t* out_len);
+Q3_API void q3_string_free(char* s);
+
 #ifdef __cplusplus
 }
 #endif

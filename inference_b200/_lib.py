@@ -77,6 +77,13 @@ SIGNATURES = {
     "q3_engine_attach_peers": (C.c_int, [_vp, _vp, _sz]),
     "q3_engine_attach_nccl": (C.c_int, [_vp, _vp]),
     "q3_engine_set_comm_timeout": (C.c_int, [_vp, C.c_double]),
+    "q3_tokenizer_load": (C.c_int, [C.c_char_p, C.POINTER(C.c_void_p)]),
+    "q3_tokenizer_destroy": (C.c_int, [_vp]),
+    "q3_tokenizer_encode": (C.c_int, [_vp, C.c_char_p, _sz, _u32p, _sz, _szp]),
+    "q3_tokenizer_decode": (C.c_int, [_vp, _u32p, _sz, _vp, _sz, _szp]),
+    "q3_chat_template": (C.c_int, [C.c_char_p, _sz, _vp, _sz, _szp]),
+    "q3_engine_generate_text": (C.c_int, [_vp, _vp, C.c_char_p, _sz, C.POINTER(C.c_void_p), _szp]),
+    "q3_string_free": (None, [_vp]),
 }
 
 

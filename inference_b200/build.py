@@ -2,8 +2,9 @@
 
     python -m inference_b200.build [--force] [-j N]
 
-Each .cu under csrc/ compiles to an object under inference_b200/_build/, then
-all link into inference_b200/libq3_sm100a.so against the CUDA runtime (NCCL is
+Each .cu (device + host) and .cpp (host only: the tokenizer) under csrc/
+compiles to an object under inference_b200/_build/, then all link into
+inference_b200/libq3_sm100a.so against the CUDA runtime (NCCL is
 loaded at run time, only for tensor parallelism).
 """
 from __future__ import annotations
@@ -35,7 +36,7 @@ def nvcc() -> str:
 
 def _deps() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.hpp")) +
-                  glob.glob(os.path.join(ROOT, "include", "*.h")))
+                  glob.glob(os.path.join(CSRC, "*.inc")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
 
 
 def _stale(out: str, srcs: list[str]) -> bool:
@@ -47,12 +48,12 @@ def _stale(out: str, srcs: list[str]) -> bool:
 
 def build(force: bool = False, jobs: int = 8, verbose: bool = True, extra: list[str] | None = None) -> str:
     os.makedirs(BUILD, exist_ok=True)
-    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    sources = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     deps = _deps()
     objs = []
     todo = []
     for src in sources:
-        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(BUILD, os.path.splitext(os.path.basename(src))[0] + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + deps):
             todo.append((src, obj))

@@ -114,6 +114,7 @@ struct q3_engine {
 namespace q3 {
 bool engine_tied(const q3_engine* e) { return e->cfg.tied != 0; }
 size_t engine_layers(const q3_engine* e) { return e->layers.size(); }
+size_t engine_capacity(const q3_engine* e) { return e->cfg.capacity; }
 }  // namespace q3
 
 namespace q3 {

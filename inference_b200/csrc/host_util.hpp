@@ -34,10 +34,17 @@ inline int fail(int status, const std::string& msg) {
 // Engine facts for host code outside engine.cu.
 bool engine_tied(const q3_engine* e);
 size_t engine_layers(const q3_engine* e);
+size_t engine_capacity(const q3_engine* e);
 
 #define Q3_CHECK(cond, msg)                                \
     do {                                                   \
         if (!(cond)) return ::q3::fail(Q3_ERR_INVALID, msg); \
+    } while (0)
+
+#define Q3_TRY_STATUS(x)               \
+    do {                               \
+        const int rc_ = (x);           \
+        if (rc_ != Q3_OK) return rc_;  \
     } while (0)
 
 }  // namespace q3

@@ -129,6 +129,13 @@ class Engine:
                                        C.byref(n)))
         return out[: n.value].copy()
 
+    def generate_text(self, tokenizer, prompt) -> bytes:
+        """Generator::generate (generator.cpp:37-63) on text: the response to the
+        chat-templated prompt, greedy until EOS or a full KV cache, as bytes."""
+        from .tokenizer import generate_text
+
+        return generate_text(self, tokenizer, prompt)
+
     # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
     TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2,
                   "tp_prefill": 0x10, "fp8_prefill": 0x20}
