@@ -10,15 +10,19 @@
 //   * the context's pages are divided evenly over the splits from the device
 //     position at run time, so one launch shape (one CUDA graph) serves every
 //     position;
-//   * a producer warp streams 64-token K and V pages into a two-stage shared
-//     ring with 1-D TMA bulk copies (one 16 KB copy per page in the paged
-//     layout; 64 row copies in the reference's [capacity, kvh, 128] layout).
+//   * a producer warp streams 64-token K and V pages into a four-stage shared
+//     ring with 3-D TMA tensor copies (128-byte swizzle: two 64-column boxes
+//     per 64-row tile, from the paged pool or the reference's [capacity, kvh,
+//     128] layout alike), so ldmatrix reads conflict-free rows with no pass
+//     over the tile first;
 //     Pages older than the current position are fetched before
 //     griddepcontrol.wait -- only the page receiving this token's K/V waits
 //     for the QKV kernel;
 //   * each consumer warp owns 16 of a page's 64 tokens and does its math on the
-//     tensor cores (mma.sync: S = Q K^T, online softmax in fp32 on the
-//     fragments, O += P V with P in BF16 hi + lo parts);
+//     tensor cores with the tokens as the 16-row M dimension and the CTA's
+//     query heads (up to 8) as N: S^T = K Q^T, online softmax in fp32 on the
+//     fragments, O^T += V^T P^T with P in BF16 hi + lo parts, transposed from
+//     the accumulator layout into the B operand by movmatrix;
 //   * warp states merge in shared memory in a fixed order; each split then
 //     pushes its state of every output slice into the shared memory of the
 //     cluster CTA that owns the slice (distributed shared memory stores), and
@@ -27,6 +31,7 @@
 
 #include <algorithm>
 #include <cfloat>
+#include <cstddef>
 
 #include "kernels.cuh"
 
@@ -42,11 +47,11 @@ constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kTileBytes = kPage * kHd * 2;  // 16 KB
 constexpr float kLog2e = 1.4426950408889634f;
 
-// K/V pages in flight per CTA (ring stages).  Deeper rings (3 at two CTAs per
-// SM, 4 at one) were measured on B200 and gained nothing at Qwen3-8B context
-// 2300 or Qwen3-0.6B context 8192: the split count, not the ring, bounds the
-// pages a CTA streams.
-constexpr int kStages = 2;
+// K/V pages in flight per CTA (ring stages).  Four 32 KB stages also make the
+// CTA too large for two to share an SM: the 16-CTA clusters would otherwise be
+// packed two CTAs per SM onto half the SMs (measured on B200: 128 CTAs on 64
+// SMs), leaving the other half idle while attention runs.
+constexpr int kStages = 4;
 
 template <int HG>
 struct AttnSmem {
@@ -61,11 +66,25 @@ struct AttnSmem {
     float rx_m[16][HG];
     float rx_l[16][HG];
     float rx_acc[HG * kHd];
-    bf16 qn[HG][kHd];  // normalised, rotated q heads (fused q/k norm)
-    bf16 kn[kHd];      // normalised, rotated key row of the position
+    float fw[kWarps][HG];  // per head: each warp's weight in the CTA's merge, the max, the sum
+    float cm[HG];
+    float cl[HG];
+    float rf[16][HG];      // per head: each split's weight in the owner's merge, the sum
+    float rl[HG];
+    alignas(16) bf16 qn[HG][kHd];  // normalised, rotated q heads (fused q/k norm)
+    alignas(16) bf16 kn[kHd];      // normalised, rotated key row of the position (read as uint4)
     uint64_t full[kStages];
     uint64_t empty[kStages];
 };
+
+// The K/V ring and the key row are read and written as 16-byte vectors.
+template <int HG>
+constexpr bool smem_aligned() {
+    return offsetof(AttnSmem<HG>, kv) % 16 == 0 && offsetof(AttnSmem<HG>, qn) % 16 == 0 &&
+           offsetof(AttnSmem<HG>, kn) % 16 == 0 && offsetof(AttnSmem<HG>, full) % 8 == 0;
+}
+static_assert(smem_aligned<1>() && smem_aligned<2>() && smem_aligned<4>() && smem_aligned<8>(),
+              "attention shared-memory layout");
 
 __device__ __forceinline__ void ldmatrix_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
@@ -78,6 +97,18 @@ __device__ __forceinline__ void ldmatrix_x4_trans(const void* p, uint32_t& r0, u
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                  : "r"(smem_u32(p)));
 }
+// 8 x 8 BF16 matrix held in the fragment layout (lane 4r + c: row r, columns
+// 2c, 2c + 1) -> its transpose in the same layout.
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+    uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf2(bf16 lo, bf16 hi) {
+    return static_cast<uint32_t>(__bfloat16_as_ushort(lo)) | (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
+}
+
 // One 128-wide head: RMSNorm (weights nw) then RoPE at `pos`, rounded once
 // (qk_norm_rope.cuh:14-90); a warp, lane l holding dims l, l + 32, l + 64,
 // l + 96.  The weights and the RoPE row do not depend on earlier kernels and
@@ -123,10 +154,28 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 
 __device__ __forceinline__ void fence_proxy_async_cta() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// Byte offset of 16-byte column chunk `chunk` (0..15) of row `row` in a 64 x 128
+// BF16 tile as two 64-column boxes loaded with the 128-byte swizzle: box
+// chunk >> 3 at 8 KB steps, rows of 128 bytes, chunk c of row r at c ^ (r & 7).
+__device__ __forceinline__ int tile_off(int row, int chunk) {
+    return (chunk >> 3) * 8192 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 template <int HG>
-__global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    AttnSmem<HG>& S = *reinterpret_cast<AttnSmem<HG>*>(smem_raw);
+    // the swizzled TMA boxes want 1024-byte aligned destinations
+    uint8_t* smem_base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    AttnSmem<HG>& S = *reinterpret_cast<AttnSmem<HG>*>(smem_base);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool tracing = a.trace.buf != nullptr;
@@ -180,20 +229,14 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
                     pdl_wait();
                     waited = true;
                 }
-                if (a.paged) {
-                    const size_t base = (static_cast<size_t>(a.page_table[page]) * a.kv_heads + kvh) * kPage * kHd;
-                    mbar_arrive_expect_tx(&S.full[s], 2 * kTileBytes);
-                    bulk_g2s(S.kv[s][0], a.k + base, kTileBytes, &S.full[s], pol);
-                    bulk_g2s(S.kv[s][1], a.v + base, kTileBytes, &S.full[s], pol);
-                } else {
-                    const int rows = min(kPage, pos + 1 - page * kPage);
-                    mbar_arrive_expect_tx(&S.full[s], 2 * rows * kHd * 2);
-                    for (int r = 0; r < rows; ++r) {
-                        const size_t off = (static_cast<size_t>(page * kPage + r) * a.kv_heads + kvh) * kHd;
-                        bulk_g2s(S.kv[s][0] + r * kHd * 2, a.k + off, kHd * 2, &S.full[s], pol);
-                        bulk_g2s(S.kv[s][1] + r * kHd * 2, a.v + off, kHd * 2, &S.full[s], pol);
-                    }
-                }
+                // paged: (column, row, physical page x kv heads + head); flat: (column, head, position)
+                const int y = a.paged ? 0 : kvh;
+                const int z = a.paged ? a.page_table[page] * a.kv_heads + kvh : page * kPage;
+                mbar_arrive_expect_tx(&S.full[s], 2 * kTileBytes);
+                tma_load_3d(S.kv[s][0], &a.tk, 0, y, z, &S.full[s], pol);
+                tma_load_3d(S.kv[s][0] + kTileBytes / 2, &a.tk, 64, y, z, &S.full[s], pol);
+                tma_load_3d(S.kv[s][1], &a.tv, 0, y, z, &S.full[s], pol);
+                tma_load_3d(S.kv[s][1] + kTileBytes / 2, &a.tv, 64, y, z, &S.full[s], pol);
             }
         }
     } else {
@@ -222,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         if (fused) {
             // q/k norm + RoPE of this step: warp w < HG takes q head qh0 + w, the last
             // warp (after its q head) the key row when this split holds the live page
-            if (warp < HG) nq.apply(qv + static_cast<size_t>(qh0 + warp) * kHd, a.eps, S.qn[warp], lane);
+            for (int h = warp; h < HG; h += kWarps) nq.apply(qv + static_cast<size_t>(qh0 + h) * kHd, a.eps, S.qn[h], lane);
             if (warp == kWarps - 1 && has_live) {
                 nk.apply(a.k_raw + static_cast<size_t>(kvh) * kHd, a.eps, S.kn, lane);
                 if (qb == 0) {
@@ -237,21 +280,24 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
         }
 
         if (tracing && tid == 0) tr_cq = clock64();
-        uint32_t qa[8][2];  // A fragments of q: rows g (dims 16kk + 2t4, +1) and (+8); rows 8-15 are zero
+        // B fragments of Q^T (k = dims 16kk + 2t4, +1 and + 8, n = query head g; heads >= HG are zero)
+        uint32_t qb[8][2];
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-            qa[kk][0] = qa[kk][1] = 0u;
+            qb[kk][0] = qb[kk][1] = 0u;
             if (g < HG) {
                 const uint32_t* qr = fused ? reinterpret_cast<const uint32_t*>(S.qn[g])
                                            : reinterpret_cast<const uint32_t*>(qv + static_cast<size_t>(qh0 + g) * kHd);
-                qa[kk][0] = qr[kk * 8 + t4];
-                qa[kk][1] = qr[kk * 8 + 4 + t4];
+                qb[kk][0] = qr[kk * 8 + t4];
+                qb[kk][1] = qr[kk * 8 + 4 + t4];
             }
         }
-        float o[16][4];
+        // O^T accumulators: d-tile dt, rows (dims) 16dt + g and + 8, columns (heads) 2t4 and 2t4 + 1
+        float o[8][4];
 #pragma unroll
-        for (int d = 0; d < 16; ++d) o[d][0] = o[d][1] = o[d][2] = o[d][3] = 0.f;
-        float m_run = -INFINITY, l_run = 0.f;  // row g: running max (log2 units), this lane's partial sum
+        for (int dt = 0; dt < 8; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
+        // heads 2t4 and 2t4 + 1: running max (log2 units) and this lane's partial sum (tokens g, g + 8)
+        float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
         bool failed = false;
         for (int i = 0; i < np; ++i) {
@@ -265,139 +311,156 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
                 uint8_t* vt = S.kv[s][1];
                 if (has_live && page == live_page && warp == (pos % kPage) / 16) {
                     // this step's key row: the cache slot still holds the raw row (or older data)
+                    const int r = pos % kPage;
                     if (lane < 16)
-                        reinterpret_cast<uint4*>(kt + (pos % kPage) * 256)[lane] =
-                            reinterpret_cast<const uint4*>(S.kn)[lane];
+                        *reinterpret_cast<uint4*>(kt + tile_off(r, lane)) = reinterpret_cast<const uint4*>(S.kn)[lane];
                     __syncwarp();
                 }
-                // ---- swizzle this warp's rows in place; rows past the position become zeros in V
-#pragma unroll
-                for (int tile = 0; tile < 2; ++tile) {
-                    uint8_t* base = tile ? vt : kt;
-                    const int c = lane & 15;
-                    uint4 rr[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int r = warp * 16 + (lane >> 4) + 2 * j;
-                        rr[j] = *reinterpret_cast<const uint4*>(base + r * 256 + c * 16);
-                    }
-                    __syncwarp();
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int r = warp * 16 + (lane >> 4) + 2 * j;
-                        *reinterpret_cast<uint4*>(base + r * 256 + (c ^ (r & 7)) * 16) =
-                            (tile == 0 || r < valid) ? rr[j] : make_uint4(0u, 0u, 0u, 0u);
-                    }
+                if (valid < kPage) {
+                    // rows past the position become zeros in V (their P is 0; the slots may hold
+                    // anything, NaN included); each row is two 128-byte box rows
+                    for (int r = max(valid, warp * 16); r < warp * 16 + 16; ++r)
+                        reinterpret_cast<uint2*>(vt + (lane >> 4) * 8192 + r * 128)[lane & 15] = make_uint2(0u, 0u);
                     __syncwarp();
                 }
-                // ---- S = Q K^T for this warp's two 8-token n-tiles
-                float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-                {
-                    const int q = lane >> 3, r8 = lane & 7;
-                    const int row = warp * 16 + (q >> 1) * 8 + r8;
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const int chunk = kk * 2 + (q & 1);
-                        uint32_t b0, b1, b2, b3;
-                        ldmatrix_x4(kt + row * 256 + ((chunk ^ (row & 7)) * 16), b0, b1, b2, b3);
-                        mma_bf16_16816(sc[0], qa[kk][0], 0u, qa[kk][1], 0u, b0, b1);
-                        mma_bf16_16816(sc[1], qa[kk][0], 0u, qa[kk][1], 0u, b2, b3);
-                    }
-                }
-                // ---- online softmax on row g (tokens 16w + 8jn + 2t4 + e)
-                float mx = -INFINITY;
-#pragma unroll
-                for (int jn = 0; jn < 2; ++jn)
-#pragma unroll
-                    for (int e = 0; e < 2; ++e) {
-                        const int tok = warp * 16 + jn * 8 + 2 * t4 + e;
-                        sc[jn][e] = tok < valid ? sc[jn][e] * qscale : -INFINITY;
-                        mx = fmaxf(mx, sc[jn][e]);
-                    }
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const float m_new = fmaxf(m_run, mx);
-                float p[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
-                if (m_new != -INFINITY) {
-                    const float corr = exp2f(m_run - m_new);
-                    m_run = m_new;
-                    l_run *= corr;
-#pragma unroll
-                    for (int d = 0; d < 16; ++d) {
-                        o[d][0] *= corr;
-                        o[d][1] *= corr;
-                    }
-#pragma unroll
-                    for (int jn = 0; jn < 2; ++jn)
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            p[jn][e] = exp2f(sc[jn][e] - m_new);
-                            l_run += p[jn][e];
-                        }
-                }
-                // ---- O += P V: P rows g, k = the warp's 16 tokens (hi + lo BF16 parts)
-                uint32_t ph[2], pl[2];
-#pragma unroll
-                for (int jn = 0; jn < 2; ++jn) {
-                    const bf16 h0 = f2bf(p[jn][0]), h1 = f2bf(p[jn][1]);
-                    const bf16 l0 = f2bf(p[jn][0] - bf2f(h0)), l1 = f2bf(p[jn][1] - bf2f(h1));
-                    ph[jn] = static_cast<uint32_t>(__bfloat16_as_ushort(h0)) |
-                             (static_cast<uint32_t>(__bfloat16_as_ushort(h1)) << 16);
-                    pl[jn] = static_cast<uint32_t>(__bfloat16_as_ushort(l0)) |
-                             (static_cast<uint32_t>(__bfloat16_as_ushort(l1)) << 16);
-                }
+                // ---- S^T = K Q^T: A = this warp's 16 key rows, two accumulators (even / odd k-steps)
+                float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
                 {
                     const int q = lane >> 3, r8 = lane & 7;
                     const int row = warp * 16 + (q & 1) * 8 + r8;
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const int chunk = 2 * e + (q >> 1);
-                        uint32_t b0, b1, b2, b3;
-                        ldmatrix_x4_trans(vt + row * 256 + ((chunk ^ (row & 7)) * 16), b0, b1, b2, b3);
-                        mma_bf16_16816(o[2 * e], ph[0], 0u, ph[1], 0u, b0, b1);
-                        mma_bf16_16816(o[2 * e], pl[0], 0u, pl[1], 0u, b0, b1);
-                        mma_bf16_16816(o[2 * e + 1], ph[0], 0u, ph[1], 0u, b2, b3);
-                        mma_bf16_16816(o[2 * e + 1], pl[0], 0u, pl[1], 0u, b2, b3);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const int chunk = kk * 2 + (q >> 1);
+                        uint32_t a0, a1, a2, a3;
+                        ldmatrix_x4(kt + tile_off(row, chunk), a0, a1, a2, a3);
+                        if (kk & 1)
+                            mma_bf16_16816(sb, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+                        else
+                            mma_bf16_16816(sa, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+                    }
+                }
+                // ---- online softmax per head column: tokens g (elements 0, 1) and g + 8 (2, 3)
+                const int tok = warp * 16 + g;
+                float sc[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    sc[e] = (tok + (e >> 1) * 8) < valid ? (sa[e] + sb[e]) * qscale : -INFINITY;
+                float mx0 = fmaxf(sc[0], sc[2]), mx1 = fmaxf(sc[1], sc[3]);
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+                }
+                float p[4] = {0.f, 0.f, 0.f, 0.f};
+                float corr0 = 1.f, corr1 = 1.f;
+                const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+                if (mn0 != -INFINITY) {
+                    corr0 = exp2f(m_run[0] - mn0);
+                    m_run[0] = mn0;
+                    p[0] = exp2f(sc[0] - mn0);
+                    p[2] = exp2f(sc[2] - mn0);
+                }
+                if (mn1 != -INFINITY) {
+                    corr1 = exp2f(m_run[1] - mn1);
+                    m_run[1] = mn1;
+                    p[1] = exp2f(sc[1] - mn1);
+                    p[3] = exp2f(sc[3] - mn1);
+                }
+                l_run[0] = l_run[0] * corr0 + p[0] + p[2];
+                l_run[1] = l_run[1] * corr1 + p[1] + p[3];
+#pragma unroll
+                for (int dt = 0; dt < 8; ++dt) {
+                    o[dt][0] *= corr0;
+                    o[dt][1] *= corr1;
+                    o[dt][2] *= corr0;
+                    o[dt][3] *= corr1;
+                }
+                // ---- P^T as the B operand (k = tokens, n = heads): BF16 hi + lo parts, each
+                // 8 x 8 block (tokens g / g + 8 by heads) transposed by movmatrix
+                bf16 hb[4], lb[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    hb[e] = f2bf(p[e]);
+                    lb[e] = f2bf(p[e] - bf2f(hb[e]));
+                }
+                const uint32_t bh0 = movmatrix_trans(pack_bf2(hb[0], hb[1]));
+                const uint32_t bh1 = movmatrix_trans(pack_bf2(hb[2], hb[3]));
+                const uint32_t bl0 = movmatrix_trans(pack_bf2(lb[0], lb[1]));
+                const uint32_t bl1 = movmatrix_trans(pack_bf2(lb[2], lb[3]));
+                // ---- O^T += V^T P^T: A = V^T tiles (dims 16dt.., tokens of this warp) by ldmatrix.trans
+                {
+                    const int q = lane >> 3, r8 = lane & 7;
+                    const int row = warp * 16 + (q >> 1) * 8 + r8;
+#pragma unroll
+                    for (int dt = 0; dt < 8; ++dt) {
+                        const int chunk = 2 * dt + (q & 1);
+                        uint32_t a0, a1, a2, a3;
+                        ldmatrix_x4_trans(vt + tile_off(row, chunk), a0, a1, a2, a3);
+                        mma_bf16_16816(o[dt], a0, a1, a2, a3, bh0, bh1);
+                        mma_bf16_16816(o[dt], a0, a1, a2, a3, bl0, bl1);
                     }
                 }
             }
             // the slot is refilled by the async proxy after this warp's generic-proxy
-            // writes to it (the swizzle, the patched rows): order them first
+            // writes to it (the patched key row, the zeroed V rows): order them first
             if (i + kStages < np) fence_proxy_async_cta();
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[s]);
         }
-        l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-        l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
+            l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], off);
+        }
         if (tracing && tid == 0) tr_cp = clock64();
 
         // ---- merge the 4 warp states (fixed order) into this CTA's state
-        if (g < HG) {
-            if (t4 == 0) {
-                S.m[warp][g] = m_run;
-                S.l[warp][g] = l_run;
+        {
+            const int h0 = 2 * t4, h1 = 2 * t4 + 1;
+            if (g == 0) {
+                if (h0 < HG) {
+                    S.m[warp][h0] = m_run[0];
+                    S.l[warp][h0] = l_run[0];
+                }
+                if (h1 < HG) {
+                    S.m[warp][h1] = m_run[1];
+                    S.l[warp][h1] = l_run[1];
+                }
             }
 #pragma unroll
-            for (int d = 0; d < 16; ++d) {
-                S.acc[warp][g][8 * d + 2 * t4] = o[d][0];
-                S.acc[warp][g][8 * d + 2 * t4 + 1] = o[d][1];
+            for (int dt = 0; dt < 8; ++dt) {
+                if (h0 < HG) {
+                    S.acc[warp][h0][16 * dt + g] = o[dt][0];
+                    S.acc[warp][h0][16 * dt + g + 8] = o[dt][2];
+                }
+                if (h1 < HG) {
+                    S.acc[warp][h1][16 * dt + g] = o[dt][1];
+                    S.acc[warp][h1][16 * dt + g + 8] = o[dt][3];
+                }
             }
+        }
+        named_bar(1, kConsumers);
+        if (tid < HG) {  // per head: the CTA's max, each warp's weight, the weighted sum
+            float M = -INFINITY;
+            for (int h = 0; h < kWarps; ++h) M = fmaxf(M, S.m[h][tid]);
+            float Lsum = 0.f;
+            for (int h = 0; h < kWarps; ++h) {
+                const float f = M == -INFINITY ? 0.f : exp2f(S.m[h][tid] - M);
+                S.fw[h][tid] = f;
+                Lsum += S.l[h][tid] * f;
+            }
+            S.cm[tid] = M;
+            S.cl[tid] = Lsum;
         }
         named_bar(1, kConsumers);
         if (a.splits > 1) cluster_wait();  // phase 0: every CTA of the cluster has started
         const int slice = HG * kHd / a.splits;  // outputs each CTA of the cluster finishes
         for (int oi = tid; oi < HG * kHd; oi += kConsumers) {
             const int gg = oi / kHd, d = oi % kHd;
-            float M = -INFINITY;
-            for (int h = 0; h < kWarps; ++h) M = fmaxf(M, S.m[h][gg]);
-            float Lsum = 0.f, A = 0.f;
-            if (M != -INFINITY) {
-                for (int h = 0; h < kWarps; ++h) {
-                    const float f = exp2f(S.m[h][gg] - M);
-                    Lsum += S.l[h][gg] * f;
-                    A += S.acc[h][gg][d] * f;
-                }
-            }
+            const float M = S.cm[gg], Lsum = S.cl[gg];
+            float A = 0.f;
+#pragma unroll
+            for (int h = 0; h < kWarps; ++h) A += S.acc[h][gg][d] * S.fw[h][gg];
             if (a.splits == 1) {
                 out[static_cast<size_t>(qh0 + gg) * kHd + d] = f2bf(A / Lsum);
             } else {
@@ -423,22 +486,31 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
     cluster_wait();
     if (tracing && tid == 0) tr_cs = clock64();
     if (warp < kWarps) {
+        // per head (a warp each, lane = split): the max over splits, each split's weight
+        // and the weighted sum (fixed shuffle tree)
+        for (int h = warp; h < HG; h += kWarps) {
+            const float ms = lane < a.splits ? S.rx_m[lane][h] : -INFINITY;
+            float M = ms;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+            const float f = ms == -INFINITY ? 0.f : exp2f(ms - M);
+            float L = lane < a.splits ? S.rx_l[lane][h] * f : 0.f;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+            if (lane < 16) S.rf[lane][h] = f;
+            if (lane == 0) S.rl[h] = L;
+        }
+        named_bar(1, kConsumers);
         const int slice = HG * kHd / a.splits;
         for (int j = tid; j < slice; j += kConsumers) {
             const int o = split * slice + j;
             const int g = o / kHd, d = o % kHd;
-            float M = -INFINITY;
-            for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, S.rx_m[sp][g]);
-            float Lsum = 0.f, A = 0.f;
-            for (int sp = 0; sp < a.splits; ++sp) {  // fixed split order
-                const float ms = S.rx_m[sp][g];
-                if (ms == -INFINITY) continue;
-                const float f = exp2f(ms - M);
-                Lsum += S.rx_l[sp][g] * f;
-                A += S.rx_acc[sp * slice + j] * f;
-            }
+            float A = 0.f;
+#pragma unroll
+            for (int sp = 0; sp < 16; ++sp)  // fixed split order
+                if (sp < a.splits) A += S.rx_acc[sp * slice + j] * S.rf[sp][g];
             const int qh = kvh * G + qb * HG + g;
-            out[static_cast<size_t>(qh) * kHd + d] = f2bf(A / Lsum);
+            out[static_cast<size_t>(qh) * kHd + d] = f2bf(A / S.rl[g]);
         }
     }
     const int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
@@ -458,12 +530,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_kernel(const __grid_constant
     }
 }
 
-int heads_per_cta(int G) { return G >= 4 ? 4 : G; }
 
 template <int HG>
 cudaError_t launch_hg(const AttnArgs& a, cudaStream_t s, bool pdl, int nqb) {
     auto* fn = attn_kernel<HG>;
-    const size_t smem = sizeof(AttnSmem<HG>);
+    const size_t smem = sizeof(AttnSmem<HG>) + 1024;  // + alignment of the TMA boxes
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.splits, a.kv_heads, nqb * (a.n_queries > 1 ? a.n_queries : 1));
     cfg.blockDim = dim3(kThreads);
@@ -489,7 +560,7 @@ cudaError_t launch_hg(const AttnArgs& a, cudaStream_t s, bool pdl, int nqb) {
 template <int HG>
 cudaError_t configure_hg() {
     cudaError_t e = cudaFuncSetAttribute(attn_kernel<HG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(sizeof(AttnSmem<HG>)));
+                                         static_cast<int>(sizeof(AttnSmem<HG>) + 1024));
     if (e == cudaSuccess)
         e = cudaFuncSetAttribute(attn_kernel<HG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     return e;
@@ -501,7 +572,7 @@ int max_clusters(int splits) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(splits, 1, 1);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = sizeof(AttnSmem<HG>);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem<HG>) + 1024;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = splits;
@@ -516,27 +587,38 @@ int max_clusters(int splits) {
 }
 
 int g_max_cluster = 0;  // largest split cluster that can be resident (16 or 8)
+int g_clusters16 = 0;   // 16-CTA clusters of the largest variant resident at once
 
 }  // namespace
+
+int attn_heads_per_cta(int G) { return G >= 8 ? 8 : G; }
+
+int attn_sms_used(int q_heads, int kv_heads, int splits) {
+    const int G = q_heads / kv_heads;
+    return splits * kv_heads * (G / attn_heads_per_cta(G));  // one CTA per SM
+}
 
 cudaError_t configure_attention_kernels() {
     cudaError_t e = configure_hg<1>();
     if (e == cudaSuccess) e = configure_hg<2>();
     if (e == cudaSuccess) e = configure_hg<4>();
+    if (e == cudaSuccess) e = configure_hg<8>();
     if (e != cudaSuccess) return e;
-    // Can a 16-CTA cluster of the largest variant be resident at all?
-    g_max_cluster = max_clusters<4>(16) > 0 ? 16 : 8;
+    // How many 16-CTA clusters of the largest variant can be resident at once (one CTA
+    // per SM: a cluster needs 16 SMs of one GPC)?
+    g_clusters16 = max_clusters<8>(16);
+    g_max_cluster = g_clusters16 > 0 ? 16 : 8;
     return cudaSuccess;
 }
 
-// Splits per (kv head, block): a power of two forming one cluster, at most 16
-// (8 where a 16-CTA cluster cannot be resident), and no more than the pages.
+// Splits per (kv head, block): a power of two forming one cluster, no more than
+// the pages; 16 when the decode launch's kv_heads clusters of 16 are all resident
+// at once, else 8.
 int attn_splits(int kv_heads, int max_pos, int page_size, int sms) {
     (void)page_size;
-    (void)kv_heads;
     (void)sms;
     const int max_pages = max_pos / kPage + 1;
-    const int cap = g_max_cluster > 0 ? g_max_cluster : 8;
+    const int cap = (g_max_cluster == 16 && g_clusters16 >= kv_heads) ? 16 : 8;
     int s = 1;
     while (s * 2 <= cap && s * 2 <= max_pages) s *= 2;
     return s;
@@ -550,18 +632,53 @@ size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits) {
     return 256;
 }
 
-cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl) {
+// 3-D tensor map of a K or V cache for the page loads: paged [pages][kvh][64][128]
+// as (column, row, page x kvh + head), box 64 x 64 x 1; flat [positions][kvh][128]
+// as (column, head, position), box 64 x 1 x 64.  128-byte swizzle, zero fill past
+// the extent.
+bool make_cache_map(CUtensorMap* map, const bf16* base, int paged, int kv_heads, long long extent) {
+    auto fn = tensor_map_encoder();
+    if (!fn || !base || (reinterpret_cast<uintptr_t>(base) & 15) || extent <= 0) return false;
+    cuuint64_t dims[3];
+    cuuint64_t strides[2];
+    cuuint32_t box[3];
+    if (paged) {
+        dims[0] = kHd, dims[1] = kPage, dims[2] = static_cast<cuuint64_t>(extent) * kv_heads;
+        strides[0] = kHd * 2, strides[1] = static_cast<cuuint64_t>(kPage) * kHd * 2;
+        box[0] = 64, box[1] = kPage, box[2] = 1;
+    } else {
+        dims[0] = kHd, dims[1] = static_cast<cuuint64_t>(kv_heads), dims[2] = static_cast<cuuint64_t>(extent);
+        strides[0] = kHd * 2, strides[1] = static_cast<cuuint64_t>(kv_heads) * kHd * 2;
+        box[0] = 64, box[1] = 1, box[2] = kPage;
+    }
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<bf16*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_attention(const AttnArgs& args, cudaStream_t s, bool pdl) {
+    AttnArgs a = args;
+    if (!a.paged && a.pos_ptr && a.pool <= 0) return cudaErrorInvalidValue;  // the extent must be known
+    // paged pool of unknown size: the page table is trusted, as it is for the addresses
+    const long long extent = a.pool > 0 ? a.pool
+                             : a.paged ? (1ll << 20)
+                                       : static_cast<long long>(a.pos_host) + (a.n_queries > 1 ? a.n_queries : 1);
+    if (!make_cache_map(&a.tk, a.k, a.paged, a.kv_heads, extent) ||
+        !make_cache_map(&a.tv, a.v, a.paged, a.kv_heads, extent))
+        return cudaErrorInvalidValue;
     const int G = a.q_heads / a.kv_heads;
     if (a.q_heads % a.kv_heads != 0 || !(G == 1 || G == 2 || G == 4 || G == 8)) return cudaErrorInvalidValue;
     if (a.splits < 1 || a.splits > 16 || (a.splits & (a.splits - 1)) != 0) return cudaErrorInvalidValue;
-    if (a.n_queries > 1 && static_cast<long long>(a.n_queries) * (G / heads_per_cta(G)) > 65535)
+    if (a.n_queries > 1 && static_cast<long long>(a.n_queries) * (G / attn_heads_per_cta(G)) > 65535)
         return cudaErrorInvalidValue;
-    const int HG = heads_per_cta(G);
+    const int HG = attn_heads_per_cta(G);
     const int nqb = G / HG;
     switch (HG) {
         case 1: return launch_hg<1>(a, s, pdl, nqb);
         case 2: return launch_hg<2>(a, s, pdl, nqb);
-        default: return launch_hg<4>(a, s, pdl, nqb);
+        case 4: return launch_hg<4>(a, s, pdl, nqb);
+        default: return launch_hg<8>(a, s, pdl, nqb);
     }
 }
 

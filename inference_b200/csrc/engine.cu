@@ -331,6 +331,7 @@ int attention(Recorder& r, const LayerW& L, size_t pos_now) {
     a.kv_heads = e->kvh;
     a.page_size = kPageSize;
     a.paged = 1;
+    a.pool = e->n_pages;
     a.pos_ptr = e->pos;
     a.splits = e->attn_splits;
     a.err = e->err;
@@ -707,11 +708,9 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     // ---- attention: splits of the full context merge inside one thread-block cluster
     e->attn_splits = attn_splits(e->kvh, static_cast<int>(c.capacity) - 1, kPageSize, e->sms);
     {
-        // decode attention: splits x kv heads x query-head blocks CTAs, two per SM; the SMs
-        // it leaves free start the o_proj GEMV's first CTAs while it runs
-        const int G = e->qh / e->kvh, HG = G >= 4 ? 4 : G;
-        const int attn_ctas = e->attn_splits * e->kvh * (G / HG);
-        e->o_early = std::max(0, e->sms - (attn_ctas + 1) / 2);
+        // decode attention occupies attn_sms_used SMs; the SMs it leaves free start the
+        // o_proj GEMV's first CTAs while it runs
+        e->o_early = std::max(0, e->sms - attn_sms_used(e->qh, e->kvh, e->attn_splits));
     }
 
     if (setup != cudaSuccess)
@@ -1156,6 +1155,7 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
             aa.kv_heads = e->kvh;
             aa.page_size = kPageSize;
             aa.paged = 1;
+            aa.pool = e->n_pages;
             aa.pos_host = pc;
             // many queries already fill the GPU: a split gets at least 8 pages
             const int pages = (pc + t - 1) / kPageSize + 1;

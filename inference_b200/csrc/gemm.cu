@@ -252,23 +252,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
 }
 
-// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
 // Row-major [rows, K] BF16 matrix, box = box_rows x 64 columns, 128-byte swizzle.
 bool make_tmap(CUtensorMap* map, const bf16* base, int rows, int K, int box_rows) {
-    auto fn = encode_fn();
+    auto fn = tensor_map_encoder();
     if (!fn) return false;
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
@@ -290,6 +276,20 @@ cudaError_t launch_bn(const GemmArgs& a, const CUtensorMap& tx, const CUtensorMa
 }
 
 }  // namespace
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
 
 // BN = 256 when that still gives at least one wave of CTAs, else 128.
 int gemm_tile_n(int M, int N, int sms) {

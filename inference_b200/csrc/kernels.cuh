@@ -1,6 +1,8 @@
 // kernels.cuh -- argument blocks and host launchers of the sm_100a kernels.
 #pragma once
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -179,10 +181,23 @@ struct AttnArgs {
     const float* rope_sin;
     float eps;
     LaunchTrace trace;
+    // Extent of the cache the tensor maps cover: paged, physical pages in the pool
+    // (0 = not known: the page table is trusted); flat, positions (0 = pos + queries).
+    int pool;
+    // Filled by launch_attention: 3-D tensor maps of K and V (128-byte swizzle, boxes
+    // of 64 rows x 64 columns) for the page loads.
+    CUtensorMap tk, tv;
 };
 int attn_splits(int kv_heads, int max_pos, int page_size, int num_sms);
+// Query heads one attention CTA handles (of a GQA group of G), and the SMs a decode
+// launch occupies (one CTA per SM).
+int attn_heads_per_cta(int G);
+int attn_sms_used(int q_heads, int kv_heads, int splits);
 size_t attn_workspace_bytes(int q_heads, int kv_heads, int splits);
 cudaError_t launch_attention(const AttnArgs& a, cudaStream_t s, bool pdl);
+
+// cuTensorMapEncodeTiled, resolved once through the runtime (null if unavailable).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 // ---------------------------------------------------------------- prefill GEMM (tcgen05)
 enum GemmEpi : int { GEMM_STORE = 0, GEMM_SWIGLU = 1, GEMM_RESID = 2, GEMM_F32 = 3 };

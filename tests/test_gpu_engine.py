@@ -156,7 +156,8 @@ def test_batched_and_per_token_prefill_agree_at_long_context(oracle):
     splits with several pages each), then 64 teacher-forced decode steps, each
     against the oracle: the batched path's mean max |d| and mean 1 - cosine over
     the steps are within 25% of the per-token path's, and the greedy choices
-    agree but for near-ties.  The steps share one prompt's KV history, so they
+    agree but for near-ties (the two picks' logits closer than twice the
+    paths' largest logit difference at that step).  The steps share one prompt's KV history, so they
     are not independent samples and a per-step paired test would be decided by
     that one history's rounding; the ratio bound holds both paths to the same
     error level instead."""
@@ -200,7 +201,13 @@ def test_batched_and_per_token_prefill_agree_at_long_context(oracle):
     for col, what in ((0, "max |d|"), (1, "1 - cosine")):
         mb, mp = b[:, col].mean(), p[:, col].mean()
         assert mb <= 1.25 * mp, f"{what} vs the oracle: batched {mb:.4g}, per-token {mp:.4g}"
-    assert (args["batched"] == args["per_token"]).mean() >= 0.97
+    # greedy choices: where the two paths pick different tokens, the batched path's
+    # logits of the two picks lie within that step's batched-vs-per-token spread
+    for j in np.nonzero(args["batched"] != args["per_token"])[0]:
+        lb, lp = bf(logits["batched"][j]).astype(np.float64), bf(logits["per_token"][j]).astype(np.float64)
+        gap = lb[args["batched"][j]] - lb[args["per_token"][j]]
+        assert gap <= 2.0 * np.abs(lb - lp).max(), f"step {j}: a decisive greedy choice differs"
+    assert (args["batched"] == args["per_token"]).mean() >= 0.9
 
 
 def test_phase_timeline():
