@@ -386,6 +386,56 @@ Q3_API int q3_engine_attach_nccl(q3_engine* e, const void* id_128_bytes);
 Q3_API int q3_engine_set_comm_timeout(q3_engine* e, double seconds);
 
 /* ------------------------------------------------------------------------
+ * Batched decode (batch > 1; the reference decodes one sequence: README.md:14).
+ * Up to max_seqs sequences decode together on one engine's weights (a single-GPU
+ * BF16 engine): each step is one forward of all live sequences as rows through
+ * the batched tcgen05 GEMMs, with each row's own position and KV pages, then a
+ * greedy argmax per row (backend.cu:107-112).  KV memory is a pool of
+ * pool_pages pages of 64 positions per layer; a sequence takes
+ * ceil(max_len / 64) of them when added.  Steps are asynchronous like
+ * q3_engine_step; tokens / logits synchronise.
+ * ---------------------------------------------------------------------- */
+typedef struct q3_batch q3_batch;
+
+Q3_API int q3_batch_create(q3_engine* e, uint32_t max_seqs, uint32_t pool_pages, q3_batch** out);
+Q3_API int q3_batch_destroy(q3_batch* b);
+
+/* A new sequence: prompt[0..n) and room for max_len tokens in all (0 = the
+ * engine's capacity).  Prefills positions [0, n - 1) (Model::prefill,
+ * qwen3.hpp:168-173); the last prompt id is its first step's input.
+ * Q3_ERR_INVALID "prompt does not fit in the model context" if n >= max_len;
+ * Q3_ERR_OOM if the page pool is exhausted. */
+Q3_API int q3_batch_add(q3_batch* b, const uint32_t* prompt, size_t n, size_t max_len, uint32_t* seq);
+
+/* Paged-KV sharing: a new sequence continuing from `src` with the same tokens
+ * so far.  Its page table references src's full pages (read-only from then on
+ * for both) and holds a copy of src's partial page; its later tokens may
+ * differ (q3_batch_append). */
+Q3_API int q3_batch_fork(q3_batch* b, uint32_t src, uint32_t* seq);
+
+/* Forces ids[0..n) as the sequence's next tokens after every token already
+ * determined (teacher forcing); steps consume them instead of greedy picks. */
+Q3_API int q3_batch_append(q3_batch* b, uint32_t seq, const uint32_t* ids, size_t n);
+
+/* Releases the sequence's slot and its references to pages. */
+Q3_API int q3_batch_release(q3_batch* b, uint32_t seq);
+
+/* n steps of every live sequence with room for another token (a sequence stops
+ * at max_len). */
+Q3_API int q3_batch_step(q3_batch* b, size_t n);
+
+/* The sequence's tokens (prompt, generated and appended); *n = their count;
+ * out NULL only counts. */
+Q3_API int q3_batch_tokens(q3_batch* b, uint32_t seq, uint32_t* out, size_t capacity, size_t* n);
+
+/* The BF16 logits [vocab] of the sequence's row in the last step. */
+Q3_API int q3_batch_logits(q3_batch* b, uint32_t seq, uint16_t* out);
+
+/* The sequence's position (the index of its next input token) and the pool's
+ * free pages (either pointer may be NULL; seq is ignored without position). */
+Q3_API int q3_batch_info(q3_batch* b, uint32_t seq, size_t* position, size_t* free_pages);
+
+/* ------------------------------------------------------------------------
  * Tokenizer and text generation (host code): tokenizer::Tokenizer
  * (src/lib/tokenizer/tokenizer.hpp:35-66, tokenizer.cpp:205-265) and
  * Generator::generate on text (src/lib/inference/generator.cpp:37-63).

@@ -84,6 +84,16 @@ SIGNATURES = {
     "q3_chat_template": (C.c_int, [C.c_char_p, _sz, _vp, _sz, _szp]),
     "q3_engine_generate_text": (C.c_int, [_vp, _vp, C.c_char_p, _sz, C.POINTER(C.c_void_p), _szp]),
     "q3_string_free": (None, [_vp]),
+    "q3_batch_create": (C.c_int, [_vp, C.c_uint32, C.c_uint32, C.POINTER(C.c_void_p)]),
+    "q3_batch_destroy": (C.c_int, [_vp]),
+    "q3_batch_add": (C.c_int, [_vp, _u32p, _sz, _sz, C.POINTER(C.c_uint32)]),
+    "q3_batch_fork": (C.c_int, [_vp, C.c_uint32, C.POINTER(C.c_uint32)]),
+    "q3_batch_append": (C.c_int, [_vp, C.c_uint32, _u32p, _sz]),
+    "q3_batch_release": (C.c_int, [_vp, C.c_uint32]),
+    "q3_batch_step": (C.c_int, [_vp, _sz]),
+    "q3_batch_tokens": (C.c_int, [_vp, C.c_uint32, _u32p, _sz, _szp]),
+    "q3_batch_logits": (C.c_int, [_vp, C.c_uint32, _u16p]),
+    "q3_batch_info": (C.c_int, [_vp, C.c_uint32, _szp, _szp]),
 }
 
 

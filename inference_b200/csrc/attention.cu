@@ -207,8 +207,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     // The position is final here: every kernel triggers its dependents only
     // after its own griddepcontrol.wait, so when this grid runs, the kernel
     // before the QKV GEMV (which advanced the position) has completed.
-    int pos = (a.pos_ptr ? *a.pos_ptr : a.pos_host) + qi;
+    int pos = a.row_pos ? a.row_pos[qi] : (a.pos_ptr ? *a.pos_ptr : a.pos_host) + qi;
     if (pos < 0) pos = 0;
+    const int32_t* page_table = a.row_pos ? a.page_table + static_cast<size_t>(qi) * a.pt_stride : a.page_table;
     const int n_pages = pos / kPage + 1;
     const int pb = static_cast<int>(static_cast<long long>(split) * n_pages / a.splits);
     const int pe = static_cast<int>(static_cast<long long>(split + 1) * n_pages / a.splits);
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
                 }
                 // paged: (column, row, physical page x kv heads + head); flat: (column, head, position)
                 const int y = a.paged ? 0 : kvh;
-                const int z = a.paged ? a.page_table[page] * a.kv_heads + kvh : page * kPage;
+                const int z = a.paged ? page_table[page] * a.kv_heads + kvh : page * kPage;
                 mbar_arrive_expect_tx(&S.full[s], 2 * kTileBytes);
                 tma_load_3d(S.kv[s][0], &a.tk, 0, y, z, &S.full[s], pol);
                 tma_load_3d(S.kv[s][0] + kTileBytes / 2, &a.tk, 64, y, z, &S.full[s], pol);
@@ -271,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
                 if (qb == 0) {
                     __syncwarp();
                     bf16* slot = const_cast<bf16*>(a.k) +
-                                 ((static_cast<size_t>(a.page_table[live_page]) * a.kv_heads + kvh) * kPage +
+                                 ((static_cast<size_t>(page_table[live_page]) * a.kv_heads + kvh) * kPage +
                                   pos % kPage) * kHd;
                     if (lane < 16) reinterpret_cast<uint4*>(slot)[lane] = reinterpret_cast<const uint4*>(S.kn)[lane];
                 }
@@ -659,7 +660,8 @@ bool make_cache_map(CUtensorMap* map, const bf16* base, int paged, int kv_heads,
 
 cudaError_t launch_attention(const AttnArgs& args, cudaStream_t s, bool pdl) {
     AttnArgs a = args;
-    if (!a.paged && a.pos_ptr && a.pool <= 0) return cudaErrorInvalidValue;  // the extent must be known
+    if (!a.paged && (a.pos_ptr || a.row_pos) && a.pool <= 0) return cudaErrorInvalidValue;  // the extent must be known
+    if (a.row_pos && !a.paged) return cudaErrorInvalidValue;
     // paged pool of unknown size: the page table is trusted, as it is for the addresses
     const long long extent = a.pool > 0 ? a.pool
                              : a.paged ? (1ll << 20)

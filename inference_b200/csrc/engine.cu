@@ -28,88 +28,7 @@
 #include <thread>
 #include <vector>
 
-#include "host_util.hpp"
-#include "kernels.cuh"
-#include "nccl_dyn.hpp"
-
-namespace q3 {
-
-namespace {
-
-constexpr int kPageSize = 64;
-
-struct LayerW {
-    bf16 *w_qkv, *w_o, *w_gu, *w_down;  // BF16 engines
-    // FP8 engines: E4M3 matrices of the same shapes and one scale per row
-    uint8_t *f_qkv, *f_o, *f_gu, *f_down;
-    float *s_qkv, *s_o, *s_gu, *s_down;
-    bf16 *in_norm, *post_norm, *q_norm, *k_norm;
-    bf16 *k_pages, *v_pages;
-};
-
-}  // namespace
-}  // namespace q3
-
-struct q3_engine {
-    q3_model_config cfg{};
-    int device = 0, rank = 0, world = 1, sms = 148;
-    cudaStream_t stream = nullptr;
-    // local (per-rank) dimensions
-    int H = 0, qh = 0, kvh = 0, qd = 0, kd = 0, il = 0, vl = 0;
-    uint32_t voff = 0;
-    // weights
-    q3::bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
-    bool fp8 = false;  // Q3_WEIGHTS_FP8_E4M3: GEMV matrices as E4M3 + row scales
-    uint8_t* f_lm = nullptr;
-    float* s_lm = nullptr;
-    std::vector<q3::LayerW> layers;
-    int n_pages = 0;
-    int32_t* page_table = nullptr;
-    float *rope_cos = nullptr, *rope_sin = nullptr;
-    // activations
-    q3::bf16 *hs[2] = {nullptr, nullptr}, *q = nullptr, *attn = nullptr, *g = nullptr, *logits = nullptr;
-    float *vsum = nullptr, *partial = nullptr;
-    // control state
-    int32_t *pos = nullptr, *n_forced = nullptr, *tokens = nullptr, *argmax_hist = nullptr;
-    uint64_t *key_slot = nullptr, *key_send = nullptr, *keys = nullptr;
-    uint32_t *done_counter = nullptr, *err = nullptr;
-    int attn_splits = 1;
-    int o_early = 0;  // o_proj GEMV CTAs that start beside attention (plan_gemv_early)
-    // opt-in variants of the graph path (Q3_TUNE_*)
-    uint32_t tune = 0;
-    // CUDA-graph path timeline: per launch of a step and CTA (q3_engine_trace)
-    bool gtrace = false;
-    unsigned long long* d_gtrace = nullptr;
-    int gtrace_ctas = 0;
-    // batched prefill: token-row buffers of prefill_rows rows (allocated on first use)
-    int prefill_rows = 0;
-    q3::bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pg = nullptr;
-    q3::bf16* pw = nullptr;  // FP8 engines (Q3_TUNE_FP8_PREFILL): one layer matrix expanded to BF16
-    float* pvsum = nullptr;
-    // tensor-parallel exchange through peer memory: this rank's buffer (shared
-    // with the peers by CUDA IPC), the peers' mappings, local counters
-    void* xbuf = nullptr;
-    size_t xbuf_bytes = 0;
-    void* xpeer[q3::kMaxRanks] = {};
-    q3::PeerLinks links{};
-    bool peer_mode = false;
-    // tensor-parallel batched prefill (Q3_TUNE_TP_PREFILL): the partial-row slots
-    // and flags appended to xbuf, and the exchanges run so far (all ranks agree)
-    q3::TpExchange tpx{};
-    uint32_t tp_seq = 0;
-    // graph / comms
-    cudaGraphExec_t graph = nullptr;
-    ncclComm_t comm = nullptr;
-    // NCCL exchange bounds (q3_engine_set_comm_timeout): a host wait on this rank's stream
-    // gives up comm_timeout_s (plus a per-step allowance for the queued steps) after it
-    // starts, aborts the communicator and reports Q3_ERR_NCCL; comm_dead after that
-    double comm_timeout_s = 60.0;
-    size_t queued_steps = 0;
-    bool comm_dead = false;
-    size_t host_pos = 0, host_forced = 0, host_max_pos = 0;
-    size_t weight_bytes = 0;
-    std::vector<void*> allocs;
-};
+#include "engine_state.hpp"
 
 namespace q3 {
 bool engine_tied(const q3_engine* e) { return e->cfg.tied != 0; }
@@ -136,7 +55,6 @@ XbufLayout xbuf_layout(size_t world, size_t H, size_t rows) {
     L.total = L.pf_part_off + 2 * rows * H * 4;
     return L;
 }
-constexpr int kPrefillRows = 512;  // tokens per batched-prefill chunk
 
 int dalloc(q3_engine* e, void** p, size_t bytes) {
     if (bytes == 0) bytes = 16;
@@ -1010,40 +928,39 @@ int q3_engine_step(q3_engine* e, size_t n) {
     return Q3_OK;
 }
 
-// Batched prefill (qwen3.hpp:168-173 runs one decode forward per prompt token,
-// logits discarded): the K/V of the set tokens at positions [pos, pos + n),
-// up to 512 tokens per chunk.  Per layer: row RMSNorm, QKV GEMM (tcgen05),
-// q/k norm + RoPE with the cache writes, attention over each token's prefix,
-// then O (+ residual), RMSNorm of the fp32 sums, gate/up (SwiGLU epilogue) and
-// down (+ residual).  The last layer stops after its attention: its output
-// only feeds the discarded logits.
-int q3_engine_prefill(q3_engine* e, size_t n) {
-    Q3_CHECK(e, "null engine");
-    if (n == 0) return Q3_OK;
-    const size_t p0 = e->host_pos;
-    Q3_CHECK(p0 + n <= e->host_forced, "q3_engine_prefill: tokens not set (set_tokens first)");
-    if (p0 + n >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "q3_engine_prefill: KV cache capacity exceeded");
-    Q3_CUDA(cudaSetDevice(e->device));
-    const bool tp = e->world > 1;
-    if ((e->fp8 && !(e->tune & Q3_TUNE_FP8_PREFILL)) ||
-        (tp && !((e->tune & Q3_TUNE_TP_PREFILL) && (e->peer_mode || e->comm)))) {
-        // FP8-weight engines unless Q3_TUNE_FP8_PREFILL is set, and tensor-parallel ones
-        // unless Q3_TUNE_TP_PREFILL is, prefill through the per-token decode step
-        return q3_engine_step(e, n);
-    }
+namespace {
+
+int ensure_rows_impl(q3_engine* e) {
+    if (e->prefill_rows) return Q3_OK;
     const int H = e->H, qd = e->qd, kd = e->kd, il = e->il;
     const int ldqkv = qd + 2 * kd;
-    if (!e->prefill_rows) {
-        const int rows = static_cast<int>(std::min<size_t>(kPrefillRows, e->cfg.capacity));
-        int rc;
-        if ((rc = dalloc_t(e, &e->px, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
-        if ((rc = dalloc_t(e, &e->pxn, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
-        if ((rc = dalloc_t(e, &e->pqkv, static_cast<size_t>(rows) * ldqkv)) != Q3_OK) return rc;
-        if ((rc = dalloc_t(e, &e->pattn, static_cast<size_t>(rows) * qd)) != Q3_OK) return rc;
-        if ((rc = dalloc_t(e, &e->pg, static_cast<size_t>(rows) * il)) != Q3_OK) return rc;
-        if ((rc = dalloc_t(e, &e->pvsum, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
-        e->prefill_rows = rows;
-    }
+    const int rows = kPrefillRows;
+    int rc;
+    if ((rc = dalloc_t(e, &e->px, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+    if ((rc = dalloc_t(e, &e->pxn, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+    if ((rc = dalloc_t(e, &e->pqkv, static_cast<size_t>(rows) * ldqkv)) != Q3_OK) return rc;
+    if ((rc = dalloc_t(e, &e->pattn, static_cast<size_t>(rows) * qd)) != Q3_OK) return rc;
+    if ((rc = dalloc_t(e, &e->pg, static_cast<size_t>(rows) * il)) != Q3_OK) return rc;
+    if ((rc = dalloc_t(e, &e->pvsum, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+    e->prefill_rows = rows;
+    return Q3_OK;
+}
+
+// Per layer: row RMSNorm, QKV GEMM (tcgen05), q/k norm + RoPE with the cache
+// writes, attention over each row's prefix, then O (+ residual), RMSNorm of the
+// fp32 sums, gate/up (SwiGLU epilogue) and down (+ residual).  Without logits
+// the last layer stops after its attention (its output only feeds logits that
+// the prefill discards); with them the last layer completes and the final
+// RMSNorm and the lm_head GEMM follow.
+int forward_rows_impl(q3_engine* e, const RowsSpec& R) {
+    const bool tp = e->world > 1;
+    const int H = e->H, qd = e->qd, kd = e->kd, il = e->il;
+    const int ldqkv = qd + 2 * kd;
+    const int t = R.n;
+    Q3_CHECK(t > 0 && t <= kPrefillRows, "forward_rows: row count");
+    if (R.logits && (tp || e->fp8 || e->vl % 128 != 0))
+        return fail(Q3_ERR_UNSUPPORTED, "batched logits need a single-GPU BF16 engine with vocab % 128 == 0");
+    Q3_TRY(ensure_rows_impl(e));
     if (e->fp8 && !e->pw) {
         const size_t most = std::max({static_cast<size_t>(ldqkv) * H, static_cast<size_t>(H) * qd,
                                       static_cast<size_t>(2 * il) * H, static_cast<size_t>(H) * il});
@@ -1120,70 +1037,110 @@ int q3_engine_prefill(q3_engine* e, size_t n) {
         }
         return Q3_OK;
     };
+    Q3_CUDA(launch_embed_rows(e->embed, R.tokens, R.p0, t, static_cast<int>(e->cfg.vocab), H, e->px, e->err, s,
+                              R.row_tokens));
+    const int pool = R.k_pools ? R.pool_pages : e->n_pages;
+    for (int l = 0; l < L; ++l) {
+        const LayerW& W = e->layers[l];
+        bf16* kp = R.k_pools ? R.k_pools[l] : W.k_pages;
+        bf16* vp = R.v_pools ? R.v_pools[l] : W.v_pages;
+        Q3_CUDA(launch_rmsnorm_rows(e->px, nullptr, W.in_norm, e->pxn, t, H, eps, s));
+        const bf16* wm = nullptr;
+        Q3_TRY(weight(W.w_qkv, dst_qkv(e, W, 0), &wm));
+        Q3_CUDA(gemm(e->pxn, wm, e->pqkv, nullptr, t, ldqkv, H, ldqkv, GEMM_STORE));
+        PrefillQkvArgs qa{};
+        qa.qkv = e->pqkv;
+        qa.ld = ldqkv;
+        qa.q_heads = e->qh;
+        qa.kv_heads = e->kvh;
+        qa.p0 = R.p0;
+        qa.q_norm = W.q_norm;
+        qa.k_norm = W.k_norm;
+        qa.rope_cos = e->rope_cos;
+        qa.rope_sin = e->rope_sin;
+        qa.k_pages = kp;
+        qa.v_pages = vp;
+        qa.page_table = R.page_table;
+        qa.row_pos = R.row_pos;
+        qa.pt_stride = R.pt_stride;
+        qa.eps = eps;
+        Q3_CUDA(launch_qkv_rows(qa, t, s));
+        AttnArgs aa{};
+        aa.q = e->pqkv;
+        aa.k = kp;
+        aa.v = vp;
+        aa.page_table = R.page_table;
+        aa.row_pos = R.row_pos;
+        aa.pt_stride = R.pt_stride;
+        aa.out = e->pattn;
+        aa.q_heads = e->qh;
+        aa.kv_heads = e->kvh;
+        aa.page_size = kPageSize;
+        aa.paged = 1;
+        aa.pool = pool;
+        aa.pos_host = R.p0;
+        // many queries already fill the GPU: a split gets at least 8 pages
+        const int pages = R.max_pos / kPageSize + 1;
+        aa.splits = attn_splits(e->kvh, ((pages + 7) / 8) * kPageSize - 1, kPageSize, e->sms);
+        aa.err = e->err;
+        aa.n_queries = t;
+        aa.q_stride = ldqkv;
+        aa.out_stride = qd;
+        Q3_CUDA(launch_attention(aa, s, false));
+        if (l == L - 1 && !R.logits) break;
+        Q3_TRY(weight(W.w_o, dst_o(e, W), &wm));
+        if (tp)
+            Q3_TRY(tp_partial(e->pattn, wm, t, qd, e->pvsum));
+        else
+            Q3_CUDA(gemm(e->pattn, wm, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
+        Q3_CUDA(launch_rmsnorm_rows(e->px, e->pvsum, W.post_norm, e->pxn, t, H, eps, s));
+        Q3_TRY(weight(W.w_gu, dst_gu(e, W, 0), &wm));
+        Q3_CUDA(gemm(e->pxn, wm, e->pg, nullptr, t, 2 * il, H, il, GEMM_SWIGLU));
+        Q3_TRY(weight(W.w_down, dst_down(e, W), &wm));
+        if (tp)
+            Q3_TRY(tp_partial(e->pg, wm, t, il, nullptr));
+        else
+            Q3_CUDA(gemm(e->pg, wm, e->px, nullptr, t, H, il, H, GEMM_RESID));
+    }
+    if (R.logits) {
+        // qwen3.hpp:161-163: final RMSNorm, lm_head
+        Q3_CUDA(launch_rmsnorm_rows(e->px, nullptr, e->final_norm, e->pxn, t, H, eps, s));
+        Q3_CUDA(gemm(e->pxn, e->lm_head, R.logits, nullptr, t, e->vl, H, e->vl, GEMM_STORE));
+    }
+    return Q3_OK;
+}
+
+}  // namespace
+
+// Batched prefill (qwen3.hpp:168-173 runs one decode forward per prompt token,
+// logits discarded): the K/V of the set tokens at positions [pos, pos + n), up
+// to kPrefillRows tokens per forward_rows chunk.
+int q3_engine_prefill(q3_engine* e, size_t n) {
+    Q3_CHECK(e, "null engine");
+    if (n == 0) return Q3_OK;
+    const size_t p0 = e->host_pos;
+    Q3_CHECK(p0 + n <= e->host_forced, "q3_engine_prefill: tokens not set (set_tokens first)");
+    if (p0 + n >= e->cfg.capacity) return fail(Q3_ERR_INVALID, "q3_engine_prefill: KV cache capacity exceeded");
+    Q3_CUDA(cudaSetDevice(e->device));
+    const bool tp = e->world > 1;
+    if ((e->fp8 && !(e->tune & Q3_TUNE_FP8_PREFILL)) ||
+        (tp && !((e->tune & Q3_TUNE_TP_PREFILL) && (e->peer_mode || e->comm)))) {
+        // FP8-weight engines unless Q3_TUNE_FP8_PREFILL is set, and tensor-parallel ones
+        // unless Q3_TUNE_TP_PREFILL is, prefill through the per-token decode step
+        return q3_engine_step(e, n);
+    }
     for (size_t done = 0; done < n;) {
-        const int t = static_cast<int>(std::min<size_t>(n - done, static_cast<size_t>(e->prefill_rows)));
-        const int pc = static_cast<int>(p0 + done);
-        Q3_CUDA(launch_embed_rows(e->embed, e->tokens, pc, t, static_cast<int>(e->cfg.vocab), H, e->px, e->err, s));
-        for (int l = 0; l < L; ++l) {
-            const LayerW& W = e->layers[l];
-            Q3_CUDA(launch_rmsnorm_rows(e->px, nullptr, W.in_norm, e->pxn, t, H, eps, s));
-            const bf16* wm = nullptr;
-            Q3_TRY(weight(W.w_qkv, dst_qkv(e, W, 0), &wm));
-            Q3_CUDA(gemm(e->pxn, wm, e->pqkv, nullptr, t, ldqkv, H, ldqkv, GEMM_STORE));
-            PrefillQkvArgs qa{};
-            qa.qkv = e->pqkv;
-            qa.ld = ldqkv;
-            qa.q_heads = e->qh;
-            qa.kv_heads = e->kvh;
-            qa.p0 = pc;
-            qa.q_norm = W.q_norm;
-            qa.k_norm = W.k_norm;
-            qa.rope_cos = e->rope_cos;
-            qa.rope_sin = e->rope_sin;
-            qa.k_pages = W.k_pages;
-            qa.v_pages = W.v_pages;
-            qa.page_table = e->page_table;
-            qa.eps = eps;
-            Q3_CUDA(launch_qkv_rows(qa, t, s));
-            AttnArgs aa{};
-            aa.q = e->pqkv;
-            aa.k = W.k_pages;
-            aa.v = W.v_pages;
-            aa.page_table = e->page_table;
-            aa.out = e->pattn;
-            aa.q_heads = e->qh;
-            aa.kv_heads = e->kvh;
-            aa.page_size = kPageSize;
-            aa.paged = 1;
-            aa.pool = e->n_pages;
-            aa.pos_host = pc;
-            // many queries already fill the GPU: a split gets at least 8 pages
-            const int pages = (pc + t - 1) / kPageSize + 1;
-            aa.splits = attn_splits(e->kvh, ((pages + 7) / 8) * kPageSize - 1, kPageSize, e->sms);
-            aa.err = e->err;
-            aa.n_queries = t;
-            aa.q_stride = ldqkv;
-            aa.out_stride = qd;
-            Q3_CUDA(launch_attention(aa, s, false));
-            if (l == L - 1) break;
-            Q3_TRY(weight(W.w_o, dst_o(e, W), &wm));
-            if (tp)
-                Q3_TRY(tp_partial(e->pattn, wm, t, qd, e->pvsum));
-            else
-                Q3_CUDA(gemm(e->pattn, wm, e->px, e->pvsum, t, H, qd, H, GEMM_RESID));
-            Q3_CUDA(launch_rmsnorm_rows(e->px, e->pvsum, W.post_norm, e->pxn, t, H, eps, s));
-            Q3_TRY(weight(W.w_gu, dst_gu(e, W, 0), &wm));
-            Q3_CUDA(gemm(e->pxn, wm, e->pg, nullptr, t, 2 * il, H, il, GEMM_SWIGLU));
-            Q3_TRY(weight(W.w_down, dst_down(e, W), &wm));
-            if (tp)
-                Q3_TRY(tp_partial(e->pg, wm, t, il, nullptr));
-            else
-                Q3_CUDA(gemm(e->pg, wm, e->px, nullptr, t, H, il, H, GEMM_RESID));
-        }
-        done += static_cast<size_t>(t);
+        RowsSpec R;
+        R.n = static_cast<int>(std::min<size_t>(n - done, static_cast<size_t>(kPrefillRows)));
+        R.tokens = e->tokens;
+        R.p0 = static_cast<int>(p0 + done);
+        R.page_table = e->page_table;
+        R.max_pos = R.p0 + R.n - 1;
+        Q3_TRY(forward_rows_impl(e, R));
+        done += static_cast<size_t>(R.n);
     }
     const int32_t np = static_cast<int32_t>(p0 + n);
-    Q3_CUDA(cudaMemcpyAsync(e->pos, &np, 4, cudaMemcpyHostToDevice, s));
+    Q3_CUDA(cudaMemcpyAsync(e->pos, &np, 4, cudaMemcpyHostToDevice, e->stream));
     e->host_pos = p0 + n;
     if (e->host_pos > e->host_max_pos) e->host_max_pos = e->host_pos;
     return Q3_OK;
@@ -1595,3 +1552,8 @@ int q3_engine_attach_nccl(q3_engine* e, const void* id_in) {
 }
 
 }  // extern "C"
+
+namespace q3 {
+int forward_rows(q3_engine* e, const RowsSpec& r) { return forward_rows_impl(e, r); }
+int ensure_rows(q3_engine* e) { return ensure_rows_impl(e); }
+}  // namespace q3

@@ -181,6 +181,10 @@ struct AttnArgs {
     const float* rope_sin;
     float eps;
     LaunchTrace trace;
+    // batched decode (paged, n_queries rows): query i sits at position row_pos[i] and
+    // uses the page table page_table + i * pt_stride
+    const int32_t* row_pos;
+    int pt_stride;
     // Extent of the cache the tensor maps cover: paged, physical pages in the pool
     // (0 = not known: the page table is trusted); flat, positions (0 = pos + queries).
     int pool;
@@ -225,9 +229,17 @@ struct PrefillQkvArgs {
     bf16 *k_pages, *v_pages;
     const int32_t* page_table;
     float eps;
+    // batched decode: row r sits at position row_pos[r] (not p0 + r) and uses the page
+    // table page_table + r * pt_stride
+    const int32_t* row_pos;
+    int pt_stride;
 };
+// Row r takes token row_tokens[r] when row_tokens is set, else tokens[p0 + r].
 cudaError_t launch_embed_rows(const bf16* table, const int32_t* tokens, int p0, int n, int vocab, int H, bf16* x,
-                              uint32_t* err, cudaStream_t s);
+                              uint32_t* err, cudaStream_t s, const int32_t* row_tokens = nullptr);
+// out[r] = first index of the largest BF16 value of logits[r * ld .. r * ld + n) (the
+// greedy sampler, backend.cu:107-112, per row).
+cudaError_t launch_argmax_rows(const bf16* logits, int rows, int n, int ld, int32_t* out, cudaStream_t s);
 cudaError_t launch_rmsnorm_rows(const bf16* x, const float* vsum, const bf16* w, bf16* xn, int n, int H, float eps,
                                 cudaStream_t s);
 cudaError_t launch_qkv_rows(const PrefillQkvArgs& a, int n, cudaStream_t s);

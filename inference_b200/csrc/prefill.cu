@@ -15,9 +15,9 @@ constexpr int kRowThreads = 256;
 
 __global__ void __launch_bounds__(128) embed_rows_kernel(const bf16* __restrict__ table, const int32_t* __restrict__ tokens,
                                                        int p0, int vocab, int H, bf16* __restrict__ x,
-                                                       uint32_t* err) {
+                                                       uint32_t* err, const int32_t* __restrict__ row_tokens) {
     const int row = blockIdx.x;
-    int t = tokens[p0 + row];
+    int t = row_tokens ? row_tokens[row] : tokens[p0 + row];
     if (t < 0 || t >= vocab) {
         if (threadIdx.x == 0) record_error(err, DEV_BAD_TOKEN);
         t = 0;
@@ -80,9 +80,9 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_rows_kernel(const bf16* _
 // cache slot, v heads copied to theirs.  Warp w handles heads w, w + 8, ...
 __global__ void __launch_bounds__(kRowThreads) qkv_rows_kernel(PrefillQkvArgs a) {
     const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = a.p0 + row;
+    const int pos = a.row_pos ? a.row_pos[row] : a.p0 + row;
     bf16* qkv = a.qkv + static_cast<size_t>(row) * a.ld;
-    const int page = a.page_table[pos / 64];
+    const int page = (a.row_pos ? a.page_table + static_cast<size_t>(row) * a.pt_stride : a.page_table)[pos / 64];
     const int n_heads = a.q_heads + 2 * a.kv_heads;
     for (int h = warp; h < n_heads; h += kRowThreads / 32) {
         if (h >= a.q_heads + a.kv_heads) {
@@ -112,6 +112,26 @@ __global__ void __launch_bounds__(kRowThreads) qkv_rows_kernel(PrefillQkvArgs a)
             dst[i] = f2bf(x * cs - y * sn);
             dst[i + 64] = f2bf(y * cs + x * sn);
         }
+    }
+}
+
+// One CTA per row: the first index of the row's largest BF16 value, through the
+// order-preserving (value, index) keys of the fused lm_head argmax.
+__global__ void __launch_bounds__(kRowThreads) argmax_rows_kernel(const bf16* __restrict__ logits, int n, int ld,
+                                                                int32_t* __restrict__ out) {
+    __shared__ unsigned long long red[kRowThreads / 32];
+    const bf16* row = logits + static_cast<size_t>(blockIdx.x) * ld;
+    uint64_t best = 0;
+    for (int i = threadIdx.x; i < n; i += kRowThreads) best = max(best, argmax_key(bf2f(row[i]), static_cast<uint32_t>(i)));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+        best = max(best, static_cast<uint64_t>(__shfl_xor_sync(0xffffffffu, static_cast<unsigned long long>(best), off)));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t b = 0;
+        for (int w = 0; w < kRowThreads / 32; ++w) b = max(b, static_cast<uint64_t>(red[w]));
+        out[blockIdx.x] = static_cast<int32_t>(argmax_key_index(b));
     }
 }
 
@@ -198,8 +218,14 @@ cudaError_t launch_tp_resid_rows(const TpExchange& x, uint32_t seq, int n, int H
 }
 
 cudaError_t launch_embed_rows(const bf16* table, const int32_t* tokens, int p0, int n, int vocab, int H, bf16* x,
-                              uint32_t* err, cudaStream_t s) {
-    embed_rows_kernel<<<n, 128, 0, s>>>(table, tokens, p0, vocab, H, x, err);
+                              uint32_t* err, cudaStream_t s, const int32_t* row_tokens) {
+    embed_rows_kernel<<<n, 128, 0, s>>>(table, tokens, p0, vocab, H, x, err, row_tokens);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax_rows(const bf16* logits, int rows, int n, int ld, int32_t* out, cudaStream_t s) {
+    if (rows <= 0 || n <= 0 || ld < n) return cudaErrorInvalidValue;
+    argmax_rows_kernel<<<rows, kRowThreads, 0, s>>>(logits, n, ld, out);
     return cudaGetLastError();
 }
 
