@@ -77,6 +77,9 @@ def parse_args(argv=None):
                     help="no benchmark: fixed launches for ncu captures (gemv, attention, gemv8, decode) or the "
                          "per-launch timeline of one decode step (timeline; under torchrun every rank's)")
     ap.add_argument("--position", type=int, default=0, help="--probe decode / timeline: decode position")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="batched decode instead (q3_batch): this many sequences of the workload's prompt, one step "
+                         "= --window tokens of each (default 64); its own JSON line (N = 1)")
     return ap.parse_args(argv)
 
 
@@ -586,6 +589,72 @@ def time_reference_model(kind, cfg, mid, n_tok, what):
             "sample": f"{n_tok} Model::forward calls at context {mid}, {what}"}
 
 
+def run_batch(a, cfg, prompt_len, capacity):
+    """Batched decode (q3_batch): a.batch sequences, each prompt_len tokens of its
+    own seeded ids; after the prefills and a.warmup windows, a.steps windows of
+    a.window steps (one token of every sequence per step) are timed with CUDA
+    events on the engine's stream.  Weights are read once per step for all
+    sequences; every sequence reads its own KV."""
+    import numpy as np
+    import torch
+
+    import inference_b200 as ib
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1 or a.gpus != 1:
+        raise SystemExit("--batch runs on one GPU")
+    B = a.batch
+    window = a.window or 64
+    steps_total = (a.warmup + a.steps) * window
+    if a.prompt:
+        prompt_len = a.prompt
+    max_len = min(capacity, prompt_len + steps_total + 1)
+    pages_per_seq = (max_len + 63) // 64
+    torch.cuda.set_device(0)
+    eng = ib.Engine(cfg, capacity=capacity)
+    eng.init_synthetic(0)
+    bt = ib.Batch(eng, max_seqs=B, pool_pages=B * pages_per_seq)
+    for i in range(B):
+        bt.add(ib.prompt_ids(prompt_len, seed=100 + i, vocab=cfg.vocab), max_len=max_len)
+    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", 0))
+    for _ in range(a.warmup):
+        bt.step(window)
+    eng.sync()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p_start = bt.position(0)
+    with ClockSampler([0]) as clocks:
+        ev0.record(stream)
+        bt.step(window * a.steps)
+        ev1.record(stream)
+        eng.sync()
+    ms = ev0.elapsed_time(ev1)
+    tokens = B * window * a.steps
+    tok_s = tokens / (ms / 1000.0)
+    # bytes per step: every weight once, each sequence's KV at its position, averaged
+    avg_pos = p_start + (window * a.steps - 1) / 2.0
+    step_bytes = cfg.weight_bytes() + B * cfg.kv_bytes_per_position() * (avg_pos + 1)
+    peak, peak_kind = measured_peaks()
+    gbs = step_bytes * (window * a.steps) / (ms / 1000.0) / 1e9
+    line = {
+        "metric": f"batched decode tok/s, {B} sequences (q3_batch)", "value": round(tok_s, 3), "unit": "tok/s",
+        "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 3),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{a.workload}-batch{B}", "model": cfg.name, "prompt": prompt_len,
+                   "decode_tokens_per_sequence_per_step": window, "sequences": B,
+                   "positions": [p_start, p_start + window * a.steps - 1],
+                   "decode_path": "batched rows: tcgen05 GEMMs, per-row split-KV attention, eager launches"},
+        "per_sequence_tok_s": round(tok_s / B, 3),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "bytes_per_step": int(step_bytes),
+                     "peak_source": f"{peak_kind} hbm_gbs"},
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+    bt.close()
+    eng.close()
+    return 0
+
+
 def main(argv=None):
     a = parse_args(argv)
     from inference_b200.config import WORKLOADS
@@ -596,6 +665,8 @@ def main(argv=None):
         return {"gemv": probe_gemv, "attention": probe_attention, "gemv8": probe_gemv8, "decode": probe_decode,
                 "timeline": probe_timeline}[a.probe](a) or 0
     cfg, prompt_len, capacity = WORKLOADS[a.workload]
+    if a.batch:
+        return run_batch(a, cfg, prompt_len, capacity)
     workload = a.workload
     if a.layers:
         cfg = cfg.with_layers(a.layers)

@@ -7,7 +7,9 @@
 // for all rows, per-row q/k norm + RoPE + cache writes, split-KV attention with
 // each row's own position and page table), then the final RMSNorm, the lm_head
 // GEMM and a per-row greedy argmax.  Token histories, positions and page tables
-// live in device memory: steps run back to back with no host round trip.
+// live in device memory, so a step of B rows is one CUDA graph (captured once
+// per B; the attention split count comes from the capacity, not the positions)
+// and steps run back to back with no host round trip.
 //
 // KV memory is a pool of 64-position pages per layer shared by all sequences.
 // A sequence owns ceil(max_len / 64) page-table entries; q3_batch_fork starts a
@@ -17,6 +19,7 @@
 // pool when their last sequence is released.
 #include <algorithm>
 #include <cstring>
+#include <map>
 #include <string>
 #include <vector>
 
@@ -81,6 +84,7 @@ struct q3_batch {
     std::vector<int> refs;       // per physical page
     std::vector<int32_t> free_pages;
     std::vector<int32_t> rows_host;  // the rows of the last uploaded step
+    std::map<int, cudaGraphExec_t> graphs;  // one step of B rows, by B
 };
 
 namespace q3 {
@@ -101,8 +105,70 @@ int balloc_t(q3_batch* b, T** p, size_t n) {
 }
 
 void free_all(q3_batch* b) {
+    for (auto& g : b->graphs) cudaGraphExecDestroy(g.second);
+    b->graphs.clear();
     for (void* p : b->allocs) cudaFree(p);
     b->allocs.clear();
+}
+
+// One step of B rows (row_seq uploaded): prepare, the rows' forward, argmax, advance.
+int record_step(q3_batch* b, int B) {
+    q3_engine* e = b->e;
+    cudaStream_t s = e->stream;
+    batch_prepare_kernel<<<B, 128, 0, s>>>(b->row_seq, B, b->kv_len, b->tok, b->cap, b->tables, b->max_pages,
+                                           b->row_pos, b->row_tok, b->row_pt);
+    Q3_CUDA(cudaGetLastError());
+    RowsSpec R;
+    R.n = B;
+    R.row_tokens = b->row_tok;
+    R.row_pos = b->row_pos;
+    R.page_table = b->row_pt;
+    R.pt_stride = b->max_pages;
+    R.k_pools = b->k_pools.data();
+    R.v_pools = b->v_pools.data();
+    R.pool_pages = b->pool_pages;
+    R.max_pos = b->cap - 1;
+    // one graph serves every position: splits from the rows alone, about two waves of
+    // CTAs (B rows x kv heads x splits), no more than the capacity's pages
+    {
+        const int G = e->qh / e->kvh;
+        const int per_split = B * e->kvh * (G / attn_heads_per_cta(G));
+        const int want = std::max(1, 2 * e->sms / per_split);
+        int sp = 1;
+        while (sp * 2 <= want && sp * 2 <= 16 && sp * 2 <= b->max_pages) sp *= 2;
+        R.attn_splits = std::min(sp, attn_splits(e->kvh, b->cap - 1, kPageSize, e->sms));
+    }
+    R.logits = b->logits;
+    Q3_TRY_STATUS(forward_rows(e, R));
+    Q3_CUDA(launch_argmax_rows(b->logits, B, e->vl, e->vl, b->arg, s));
+    batch_advance_kernel<<<(B + 127) / 128, 128, 0, s>>>(b->row_seq, B, b->kv_len, b->forced, b->tok, b->cap, b->arg);
+    Q3_CUDA(cudaGetLastError());
+    return Q3_OK;
+}
+
+int step_graph(q3_batch* b, int B, cudaGraphExec_t* out) {
+    auto it = b->graphs.find(B);
+    if (it != b->graphs.end()) {
+        *out = it->second;
+        return Q3_OK;
+    }
+    cudaStream_t s = b->e->stream;
+    cudaGraph_t g = nullptr;
+    Q3_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    const int rc = record_step(b, B);
+    const cudaError_t st = cudaStreamEndCapture(s, &g);
+    if (rc != Q3_OK) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("batch graph capture: ") + cudaGetErrorString(st));
+    cudaGraphExec_t x = nullptr;
+    const cudaError_t si = cudaGraphInstantiate(&x, g, 0);
+    cudaGraphDestroy(g);
+    if (si != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("batch graph instantiate: ") + cudaGetErrorString(si));
+    b->graphs[B] = x;
+    *out = x;
+    return Q3_OK;
 }
 
 int take_page(q3_batch* b, int32_t* out) {
@@ -349,14 +415,10 @@ int q3_batch_step(q3_batch* b, size_t n) {
     for (size_t step = 0; step < n; ++step) {
         // the sequences with room for one more token
         std::vector<int32_t> rows;
-        int max_pos = 0;
         for (size_t i = 0; i < b->seqs.size(); ++i) {
             b->seqs[i].row = -1;
             const q3_batch::Seq& q = b->seqs[i];
-            if (q.live && q.kv_len + 1 < q.max_len) {
-                rows.push_back(static_cast<int32_t>(i));
-                max_pos = std::max(max_pos, q.kv_len);
-            }
+            if (q.live && q.kv_len + 1 < q.max_len) rows.push_back(static_cast<int32_t>(i));
         }
         if (rows.empty()) break;
         const int B = static_cast<int>(rows.size());
@@ -365,25 +427,9 @@ int q3_batch_step(q3_batch* b, size_t n) {
             Q3_CUDA(cudaMemcpyAsync(b->row_seq, rows.data(), B * 4, cudaMemcpyHostToDevice, s));
             b->rows_host = rows;
         }
-        batch_prepare_kernel<<<B, 128, 0, s>>>(b->row_seq, B, b->kv_len, b->tok, b->cap, b->tables, b->max_pages,
-                                               b->row_pos, b->row_tok, b->row_pt);
-        Q3_CUDA(cudaGetLastError());
-        RowsSpec R;
-        R.n = B;
-        R.row_tokens = b->row_tok;
-        R.row_pos = b->row_pos;
-        R.page_table = b->row_pt;
-        R.pt_stride = b->max_pages;
-        R.k_pools = b->k_pools.data();
-        R.v_pools = b->v_pools.data();
-        R.pool_pages = b->pool_pages;
-        R.max_pos = max_pos;
-        R.logits = b->logits;
-        Q3_TRY_STATUS(forward_rows(e, R));
-        Q3_CUDA(launch_argmax_rows(b->logits, B, e->vl, e->vl, b->arg, s));
-        batch_advance_kernel<<<(B + 127) / 128, 128, 0, s>>>(b->row_seq, B, b->kv_len, b->forced, b->tok, b->cap,
-                                                            b->arg);
-        Q3_CUDA(cudaGetLastError());
+        cudaGraphExec_t graph = nullptr;
+        Q3_TRY_STATUS(step_graph(b, B, &graph));
+        Q3_CUDA(cudaGraphLaunch(graph, s));
         for (int r = 0; r < B; ++r) {
             q3_batch::Seq& q = b->seqs[rows[r]];
             q.row = r;

@@ -61,6 +61,7 @@ void set_error(const std::string& msg) { g_error = msg; }
 cudaError_t configure_kernels() {
     cudaError_t e = configure_gemv_kernels();
     if (e == cudaSuccess) e = configure_attention_kernels();
+    if (e == cudaSuccess) e = configure_gemm_kernels();
     return e;
 }
 

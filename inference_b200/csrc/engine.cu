@@ -942,6 +942,9 @@ int ensure_rows_impl(q3_engine* e) {
     if ((rc = dalloc_t(e, &e->pattn, static_cast<size_t>(rows) * qd)) != Q3_OK) return rc;
     if ((rc = dalloc_t(e, &e->pg, static_cast<size_t>(rows) * il)) != Q3_OK) return rc;
     if ((rc = dalloc_t(e, &e->pvsum, static_cast<size_t>(rows) * H)) != Q3_OK) return rc;
+    // splits x output tiles <= SMs, output tiles >= N / 256: at most 128 x sms x 256 partials
+    e->split_ws_floats = static_cast<size_t>(128) * e->sms * 256;
+    if ((rc = dalloc_t(e, &e->split_ws, e->split_ws_floats)) != Q3_OK) return rc;
     e->prefill_rows = rows;
     return Q3_OK;
 }
@@ -994,6 +997,9 @@ int forward_rows_impl(q3_engine* e, const RowsSpec& R) {
         g.epi = epi;
         g.bn = gemm_tile_n(m, nn, e->sms);
         g.err = e->err;
+        g.ws = e->split_ws;
+        g.ws_floats = e->split_ws_floats;
+        g.sms = e->sms;
         return launch_gemm(g, s);
     };
     // Tensor parallel: the row-parallel GEMMs (o_proj, down_proj) write fp32 partial
@@ -1081,7 +1087,8 @@ int forward_rows_impl(q3_engine* e, const RowsSpec& R) {
         aa.pos_host = R.p0;
         // many queries already fill the GPU: a split gets at least 8 pages
         const int pages = R.max_pos / kPageSize + 1;
-        aa.splits = attn_splits(e->kvh, ((pages + 7) / 8) * kPageSize - 1, kPageSize, e->sms);
+        aa.splits = R.attn_splits ? R.attn_splits
+                                  : attn_splits(e->kvh, ((pages + 7) / 8) * kPageSize - 1, kPageSize, e->sms);
         aa.err = e->err;
         aa.n_queries = t;
         aa.q_stride = ldqkv;

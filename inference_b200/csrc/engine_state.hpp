@@ -60,6 +60,9 @@ struct q3_engine {
     q3::bf16 *px = nullptr, *pxn = nullptr, *pqkv = nullptr, *pattn = nullptr, *pg = nullptr;
     q3::bf16* pw = nullptr;  // FP8 engines (Q3_TUNE_FP8_PREFILL): one layer matrix expanded to BF16
     float* pvsum = nullptr;
+    // split-K partial tiles of the row GEMMs with one 128-row tile (batched decode, short prompts)
+    float* split_ws = nullptr;
+    size_t split_ws_floats = 0;
     // tensor-parallel exchange through peer memory: this rank's buffer (shared
     // with the peers by CUDA IPC), the peers' mappings, local counters
     void* xbuf = nullptr;
@@ -106,7 +109,8 @@ struct RowsSpec {
     bf16* const* k_pools = nullptr;
     bf16* const* v_pools = nullptr;
     int pool_pages = 0;
-    int max_pos = 0;  // the largest position of any row (sizes the attention splits)
+    int max_pos = 0;      // the largest position of any row (sizes the attention splits)
+    int attn_splits = 0;  // 0: from max_pos, at least 8 pages per split (many rows of one prompt)
     // set: the whole last layer, the final RMSNorm and lm_head into logits [n][vocab]
     bf16* logits = nullptr;
 };

@@ -22,6 +22,9 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cmath>
+#include <atomic>
 #include <mutex>
 
 #include "kernels.cuh"
@@ -114,7 +117,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * BN;
-    const int KT = a.K / kBK;
+    // split-K (blockIdx.z): this CTA's k-tiles [kt0, kt0 + KT)
+    const int kt0 = a.kt_per ? static_cast<int>(blockIdx.z) * a.kt_per : 0;
+    const int KT = a.kt_per ? min(a.kt_per, a.K / kBK - kt0) : a.K / kBK;
+    float* const yf = a.yf ? a.yf + blockIdx.z * a.yf_split : nullptr;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -143,8 +149,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 if (kt >= S && !mbar_wait(&empty[s], ((kt / S) - 1) & 1, a.err, DEV_TMA_WAIT_TIMEOUT)) break;
                 uint8_t* st = smem + s * Cfg::kStage;
                 mbar_arrive_expect_tx(&full[s], Cfg::kStage);
-                tma_load_2d(st, &tmap_x, kt * kBK, m0, &full[s]);
-                tma_load_2d(st + kATile, &tmap_w, kt * kBK, n0, &full[s]);
+                tma_load_2d(st, &tmap_x, (kt0 + kt) * kBK, m0, &full[s]);
+                tma_load_2d(st + kATile, &tmap_w, (kt0 + kt) * kBK, n0, &full[s]);
                 issued = kt + 1;
             }
             // leave no copy in flight: the last round issued into every stage must land
@@ -214,7 +220,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(row) * a.ldy + n / 2) = o;
                 } else if constexpr (EPI == GEMM_F32) {
                     // a row-parallel shard's partial: summed over the ranks, then rounded once
-                    float4* dst = reinterpret_cast<float4*>(a.yf + static_cast<size_t>(row) * a.ldy + n);
+                    float4* dst = reinterpret_cast<float4*>(yf + static_cast<size_t>(row) * a.ldy + n);
 #pragma unroll
                     for (int i = 0; i < 4; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
                 } else {
@@ -266,13 +272,81 @@ bool make_tmap(CUtensorMap* map, const bf16* base, int rows, int K, int box_rows
 }
 
 template <int BN, int EPI>
-cudaError_t launch_bn(const GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, cudaStream_t s) {
+cudaError_t launch_bn(const GemmArgs& a, const CUtensorMap& tx, const CUtensorMap& tw, cudaStream_t s, int splits) {
     auto* fn = gemm_kernel<BN, EPI>;
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmem);
+    // the shared-memory opt-in once per device (not per launch: launches may be captured into a graph)
+    static std::atomic<uint32_t> configured{0};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    const dim3 grid((a.M + kBM - 1) / kBM, a.N / BN);
+    const uint32_t bit = 1u << (dev & 31);
+    if (!(configured.load() & bit)) {
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmem);
+        if (e != cudaSuccess) return e;
+        configured.fetch_or(bit);
+    }
+    const dim3 grid((a.M + kBM - 1) / kBM, a.N / BN, splits);
     fn<<<grid, kGemmThreads, GemmCfg<BN>::kSmem, s>>>(tx, tw, a);
     return cudaGetLastError();
+}
+
+// Split-K: the splits' fp32 partial tiles ws[split][M][N] summed in split order,
+// then the requested epilogue on the sums (the same arithmetic as the GEMM's own
+// epilogues).  One thread per 8 consecutive output columns of a row.
+__global__ void gemm_split_reduce_kernel(GemmArgs a, const float* __restrict__ ws, int splits) {
+    const int per_row = a.N / 8;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= a.M * per_row) return;
+    const int row = i / per_row, n = (i % per_row) * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int z = 0; z < splits; ++z) {
+        const float4* src = reinterpret_cast<const float4*>(ws + (static_cast<size_t>(z) * a.M + row) * a.N + n);
+        const float4 p0 = src[0], p1 = src[1];
+        v[0] += p0.x, v[1] += p0.y, v[2] += p0.z, v[3] += p0.w;
+        v[4] += p1.x, v[5] += p1.y, v[6] += p1.z, v[7] += p1.w;
+    }
+    if (a.epi == GEMM_STORE) {
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+        for (int k = 0; k < 4; ++k)
+            ow[k] = static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(v[2 * k]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(v[2 * k + 1]))) << 16);
+        *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(row) * a.ldy + n) = o;
+    } else if (a.epi == GEMM_SWIGLU) {
+        uint2 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+        for (int k = 0; k < 2; ++k) {
+            float r[2];
+            for (int h = 0; h < 2; ++h) {
+                const float gv = round_bf(v[4 * k + 2 * h]), uv = round_bf(v[4 * k + 2 * h + 1]);
+                r[h] = gv / (1.0f + expf(-gv)) * uv;
+            }
+            ow[k] = static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(r[0]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(r[1]))) << 16);
+        }
+        *reinterpret_cast<uint2*>(a.y + static_cast<size_t>(row) * a.ldy + n / 2) = o;
+    } else if (a.epi == GEMM_F32) {
+        float4* dst = reinterpret_cast<float4*>(a.yf + static_cast<size_t>(row) * a.ldy + n);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+        bf16* h = a.y + static_cast<size_t>(row) * a.ldy + n;
+        uint4 hv = *reinterpret_cast<const uint4*>(h);
+        uint32_t* hw = reinterpret_cast<uint32_t*>(&hv);
+        float sm[8];
+        for (int k = 0; k < 4; ++k) {
+            sm[2 * k] = bf_lo(hw[k]) + round_bf(v[2 * k]);
+            sm[2 * k + 1] = bf_hi(hw[k]) + round_bf(v[2 * k + 1]);
+            hw[k] = static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(sm[2 * k]))) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(f2bf(sm[2 * k + 1]))) << 16);
+        }
+        *reinterpret_cast<uint4*>(h) = hv;
+        if (a.vsum) {
+            float4* vs = reinterpret_cast<float4*>(a.vsum + static_cast<size_t>(row) * a.ldy + n);
+            vs[0] = make_float4(sm[0], sm[1], sm[2], sm[3]);
+            vs[1] = make_float4(sm[4], sm[5], sm[6], sm[7]);
+        }
+    }
 }
 
 }  // namespace
@@ -291,13 +365,32 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+// The shared-memory opt-in of every GEMM variant on the current device, ahead of
+// any stream capture.
+cudaError_t configure_gemm_kernels() {
+    cudaError_t e = cudaSuccess;
+    auto set = [&](const void* fn, int bytes) {
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    };
+    set(reinterpret_cast<const void*>(gemm_kernel<128, GEMM_STORE>), GemmCfg<128>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<256, GEMM_STORE>), GemmCfg<256>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<128, GEMM_SWIGLU>), GemmCfg<128>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<256, GEMM_SWIGLU>), GemmCfg<256>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<128, GEMM_RESID>), GemmCfg<128>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<256, GEMM_RESID>), GemmCfg<256>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<128, GEMM_F32>), GemmCfg<128>::kSmem);
+    set(reinterpret_cast<const void*>(gemm_kernel<256, GEMM_F32>), GemmCfg<256>::kSmem);
+    return e;
+}
+
 // BN = 256 when that still gives at least one wave of CTAs, else 128.
 int gemm_tile_n(int M, int N, int sms) {
     const int mt = (M + kBM - 1) / kBM;
     return (N % 256 == 0 && mt * (N / 256) >= sms) ? 256 : 128;
 }
 
-cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
+cudaError_t launch_gemm(const GemmArgs& args, cudaStream_t s) {
+    GemmArgs a = args;
     if (a.M <= 0 || a.N % 128 || a.K % kBK || a.K <= 0) return cudaErrorInvalidValue;
     if (a.epi == GEMM_F32 && (!a.yf || a.ldy % 4 != 0 || a.ldy < a.N)) return cudaErrorInvalidValue;
     const int BN = a.bn ? a.bn : gemm_tile_n(a.M, a.N, 148);
@@ -305,15 +398,52 @@ cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s) {
     if (a.N % BN) return cudaErrorInvalidValue;
     CUtensorMap tx, tw;
     if (!make_tmap(&tx, a.x, a.M, a.K, kBM) || !make_tmap(&tw, a.w, a.N, a.K, BN)) return cudaErrorInvalidValue;
+    // Split-K for one row tile (a batch of decode rows: the weights stream once and the
+    // output tiles alone would leave SMs idle or a ragged last wave): the split count
+    // whose CTAs fill whole waves best (fewer splits on a tie), every split keeping at
+    // least 4 k-tiles and the partials fitting the workspace
+    int splits = 1;
+    const int tiles = a.N / BN, KT = a.K / kBK, sms = a.sms > 0 ? a.sms : 148;
+    if (a.ws && a.M <= kBM) {
+        auto fill = [&](int sp) {
+            const double waves = static_cast<double>(tiles) * sp / sms;
+            return waves / std::ceil(waves);
+        };
+        double best = fill(1);
+        for (int sp = 2; sp <= 16 && KT / sp >= 4; ++sp) {
+            if (static_cast<size_t>(sp) * a.M * a.N > a.ws_floats) break;
+            if (fill(sp) > best + 0.05) {
+                best = fill(sp);
+                splits = sp;
+            }
+        }
+    }
+    if (splits > 1) {
+        a.kt_per = (KT + splits - 1) / splits;
+        splits = (KT + a.kt_per - 1) / a.kt_per;
+        GemmArgs p = a;  // the splits' partial tiles, [split][M][N] fp32
+        p.epi = GEMM_F32;
+        p.yf = a.ws;
+        p.ldy = a.N;
+        p.yf_split = static_cast<size_t>(a.M) * a.N;
+        const cudaError_t e = BN == 256 ? launch_bn<256, GEMM_F32>(p, tx, tw, s, splits)
+                                        : launch_bn<128, GEMM_F32>(p, tx, tw, s, splits);
+        if (e != cudaSuccess) return e;
+        const int threads = a.M * (a.N / 8);
+        gemm_split_reduce_kernel<<<(threads + 63) / 64, 64, 0, s>>>(a, a.ws, splits);
+        return cudaGetLastError();
+    }
+    a.kt_per = 0;
+    a.yf_split = 0;
     switch (a.epi * 2 + (BN == 256)) {
-        case GEMM_STORE * 2: return launch_bn<128, GEMM_STORE>(a, tx, tw, s);
-        case GEMM_STORE * 2 + 1: return launch_bn<256, GEMM_STORE>(a, tx, tw, s);
-        case GEMM_SWIGLU * 2: return launch_bn<128, GEMM_SWIGLU>(a, tx, tw, s);
-        case GEMM_SWIGLU * 2 + 1: return launch_bn<256, GEMM_SWIGLU>(a, tx, tw, s);
-        case GEMM_RESID * 2: return launch_bn<128, GEMM_RESID>(a, tx, tw, s);
-        case GEMM_RESID * 2 + 1: return launch_bn<256, GEMM_RESID>(a, tx, tw, s);
-        case GEMM_F32 * 2: return launch_bn<128, GEMM_F32>(a, tx, tw, s);
-        case GEMM_F32 * 2 + 1: return launch_bn<256, GEMM_F32>(a, tx, tw, s);
+        case GEMM_STORE * 2: return launch_bn<128, GEMM_STORE>(a, tx, tw, s, 1);
+        case GEMM_STORE * 2 + 1: return launch_bn<256, GEMM_STORE>(a, tx, tw, s, 1);
+        case GEMM_SWIGLU * 2: return launch_bn<128, GEMM_SWIGLU>(a, tx, tw, s, 1);
+        case GEMM_SWIGLU * 2 + 1: return launch_bn<256, GEMM_SWIGLU>(a, tx, tw, s, 1);
+        case GEMM_RESID * 2: return launch_bn<128, GEMM_RESID>(a, tx, tw, s, 1);
+        case GEMM_RESID * 2 + 1: return launch_bn<256, GEMM_RESID>(a, tx, tw, s, 1);
+        case GEMM_F32 * 2: return launch_bn<128, GEMM_F32>(a, tx, tw, s, 1);
+        case GEMM_F32 * 2 + 1: return launch_bn<256, GEMM_F32>(a, tx, tw, s, 1);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -215,10 +215,20 @@ struct GemmArgs {
     int epi;        // GemmEpi
     int bn;         // output tile width 128 / 256, 0 = choose
     uint32_t* err;
+    // Split-K for one 128-row tile with few output tiles (batched decode): ws holds
+    // ws_floats fp32 for the splits' partial tiles; null = no split.  Set by the
+    // caller; launch_gemm picks the split count.
+    float* ws;
+    size_t ws_floats;
+    int sms;
+    // internal (launch_gemm): k-tiles per split, fp32 elements between splits' partials
+    int kt_per;
+    size_t yf_split;
 };
 cudaError_t launch_peer_keys(const PeerLinks& x, unsigned long long* out, uint32_t* err, cudaStream_t s);
 int gemm_tile_n(int M, int N, int sms);
 cudaError_t launch_gemm(const GemmArgs& a, cudaStream_t s);
+cudaError_t configure_gemm_kernels();  // every variant's shared-memory opt-in (before graph capture)
 
 // ---------------------------------------------------------------- prefill rows
 struct PrefillQkvArgs {
