@@ -59,9 +59,10 @@ def parse_args(argv=None):
                     "instead of peer-memory stores fused into the GEMVs")
     ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
                     "batched_poll, no_grid_wait, tp_prefill, fp8_prefill, or all")
-    ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8"],
-                    help="fp8: E4M3 GEMV matrices with per-row power-of-two scales (the FP8-weight model, "
-                         "not the reference's BF16 model; the CUDA graph path)")
+    ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8", "nvfp4"],
+                    help="fp8: E4M3 GEMV matrices with per-row power-of-two scales; nvfp4: E2M1 with E4M3 scales "
+                         "per 16 columns and power-of-two row scales (each the quantized model, not the "
+                         "reference's BF16 model; the CUDA graph path)")
     ap.add_argument("--cpu-sample-seconds", type=float, default=10.0,
                     help="CPU legs: time Model::forward calls for about this long (at least 3 calls)")
     ap.add_argument("--reference-cuda-tokens", type=int, default=32,
@@ -330,10 +331,10 @@ def launch_bytes(cfg, world, pos, weights="bf16"):
     H, hd = cfg.hidden, cfg.head_dim
     qd, kd = cfg.q_heads * hd // world, cfg.kv_heads * hd // world
     il, vl = cfg.inter // world, cfg.vocab // world
-    wb = 1 if weights == "fp8" else 2
+    wb = {"fp8": 1.0, "nvfp4": 0.5625}.get(weights, 2.0)  # bytes per weight (NVFP4: with its block scales)
 
     def mat(n, k):
-        return n * k * wb + (4 * n if wb == 1 else 0) + 2 * k + 2 * n
+        return int(n * k * wb) + (4 * n if wb < 2 else 0) + 2 * k + 2 * n
 
     return {"qkv_gemv": mat(qd + 2 * kd, H), "attention": 2 * (pos + 1) * kd * 2 + 2 * qd * 2,
             "o_gemv": mat(H, qd), "gate_up_gemv": mat(2 * il, H), "down_gemv": mat(H, il), "lm_head": mat(vl, H)}
@@ -691,8 +692,8 @@ def main(argv=None):
     import inference_b200 as ib
 
     eng = ib.Engine(cfg, capacity=capacity, device=local, tp_rank=rank, tp_size=world, weights=a.weights)
-    if a.weights == "fp8":
-        workload += "-fp8"
+    if a.weights != "bf16":
+        workload += "-" + a.weights
     eng.init_synthetic(0)
     tune = [t for t in a.tune.split(",") if t]
     if tune:
@@ -791,7 +792,7 @@ def main(argv=None):
     prefill = {"tokens": n_pre, "ms": round(pre_t, 3), "tok_s": round(n_pre / (pre_t / 1000.0), 1),
                "path": ("batched: tcgen05 GEMMs (TMEM accumulators, TMA), batched split-KV attention"
                         + ("; row-parallel fp32 partials exchanged between ranks" if world > 1 else "")
-                        + ("; E4M3 matrices expanded to their BF16 values first" if a.weights == "fp8" else "")
+                        + ("; packed matrices expanded to their BF16 values first" if a.weights != "bf16" else "")
                         if batched else "per-token decode steps"),
                "tflops": round((gemm_flop + attn_flop) / (pre_t / 1000.0) / 1e12 / world, 1),
                "gemm_tflop": round(gemm_flop / 1e12, 3), "attention_tflop": round(attn_flop / 1e12, 3),

@@ -84,6 +84,22 @@ Q3_API int q3_pack_e4m3(const uint8_t* q_dev, size_t n_out, size_t n_in, uint8_t
 Q3_API int q3_gemv_e4m3(const uint16_t* x_dev, const uint8_t* w8_dev, const float* scale_dev, uint16_t* y_dev,
                         size_t n_out, size_t n_in, void* stream);
 
+/* NVFP4 weights (Q3_WEIGHTS_NVFP4; no reference counterpart): E2M1 values,
+ * an E4M3 scale per 16 columns, a power-of-two scale per row (the smallest
+ * 2^e with max|row| / 6 <= 448 * 2^e); block scale E4M3(amax / 6 * 2^-e),
+ * weights E2M1(w * 2^-e / scale), both round to nearest-even, saturating.
+ * q3_quantize_nvfp4 writes W [n_out, n_in] (BF16, row-major) in the packed
+ * layout of the NVFP4 GEMV (q3_nvfp4_packed_bytes bytes, for this device's
+ * SM count) and the row scales; q3_dequant_nvfp4 gives back the exact BF16
+ * values of the packed matrix; q3_gemv_nvfp4 is y = W x on it.  n_in % 64 == 0. */
+Q3_API size_t q3_nvfp4_packed_bytes(size_t n_out, size_t n_in);
+Q3_API int q3_quantize_nvfp4(const uint16_t* w_dev, size_t n_out, size_t n_in, uint8_t* packed_dev,
+                             float* row_scale_dev, void* stream);
+Q3_API int q3_dequant_nvfp4(const uint8_t* packed_dev, const float* row_scale_dev, size_t n_out, size_t n_in,
+                            uint16_t* out_dev, void* stream);
+Q3_API int q3_gemv_nvfp4(const uint16_t* x_dev, const uint8_t* packed_dev, const float* row_scale_dev, uint16_t* y_dev,
+                         size_t n_out, size_t n_in, void* stream);
+
 /* Batched matmul for the prefill (no Backend counterpart: the reference
  * prefills by calling matmul once per prompt token, qwen3.hpp:168-173):
  * y[m, n] = x[m, k] . W[n, k]^T with W as stored (row-major [out, in]),
@@ -194,12 +210,17 @@ typedef struct q3_model_config {
      * Q3_WEIGHTS_BF16 (0, the reference's format) or Q3_WEIGHTS_FP8_E4M3 (1:
      * E4M3 bytes with one power-of-two scale per row, quantized on the device
      * from the BF16 tensors that init_synthetic / set_weight provide; no
-     * reference counterpart).  Embedding and norm weights stay BF16. */
+     * reference counterpart), or Q3_WEIGHTS_NVFP4 (2, below).  Embedding and
+     * norm weights stay BF16. */
     uint32_t weight_format;
 } q3_model_config;
 
 #define Q3_WEIGHTS_BF16 0
 #define Q3_WEIGHTS_FP8_E4M3 1
+/* NVFP4: E2M1 weights with an E4M3 scale per 16 columns and a power-of-two
+ * scale per row (every dequantized weight an exact BF16 value), quantized on
+ * the device like FP8; the GEMVs read 4.5 bits per weight. */
+#define Q3_WEIGHTS_NVFP4 2
 
 typedef struct q3_engine q3_engine;
 

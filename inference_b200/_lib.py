@@ -24,6 +24,10 @@ SIGNATURES = {
     "q3_embedding": (C.c_int, [_u16p, _sz, _sz, C.c_uint32, _u16p, _vp]),
     "q3_gemv": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _vp]),
     "q3_gemm": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _sz, _vp]),
+    "q3_nvfp4_packed_bytes": (_sz, [_sz, _sz]),
+    "q3_quantize_nvfp4": (C.c_int, [_u16p, _sz, _sz, _vp, _vp, _vp]),
+    "q3_dequant_nvfp4": (C.c_int, [_vp, _vp, _sz, _sz, _u16p, _vp]),
+    "q3_gemv_nvfp4": (C.c_int, [_u16p, _vp, _vp, _u16p, _sz, _sz, _vp]),
     "q3_quantize_e4m3": (C.c_int, [_u16p, _sz, _sz, _sz, _sz, _vp, _vp, _vp]),
     "q3_gemv_e4m3": (C.c_int, [_u16p, _vp, _vp, _u16p, _sz, _sz, _vp]),
     "q3_e4m3_packed_bytes": (_sz, [_sz, _sz]),
@@ -135,4 +139,4 @@ class ModelConfig(C.Structure):
                 ("weight_format", C.c_uint32)]
 
 
-WEIGHT_FORMATS = {"bf16": 0, "fp8": 1}  # Q3_WEIGHTS_BF16, Q3_WEIGHTS_FP8_E4M3
+WEIGHT_FORMATS = {"bf16": 0, "fp8": 1, "nvfp4": 2}  # Q3_WEIGHTS_BF16, Q3_WEIGHTS_FP8_E4M3, Q3_WEIGHTS_NVFP4

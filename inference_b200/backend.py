@@ -83,6 +83,28 @@ class B200Backend:
         n, k = output.numel(), x.numel()
         check(lib().q3_gemv_e4m3(_p(x), _p(packed), _p(scale), _p(output), n, k, self._stream()))
 
+    def quantize_nvfp4(self, weights):
+        """BF16 [n, k] (device) -> (packed NVFP4 bytes in the GEMV's layout, row scales)
+        (q3_quantize_nvfp4)."""
+        torch = _torch()
+        n, k = weights.shape
+        packed = torch.empty(lib().q3_nvfp4_packed_bytes(n, k), dtype=torch.uint8, device=weights.device)
+        scale = torch.empty(n, dtype=torch.float32, device=weights.device)
+        check(lib().q3_quantize_nvfp4(_p(weights), n, k, _p(packed), _p(scale), self._stream()))
+        return packed, scale
+
+    def dequant_nvfp4(self, packed, scale, n: int, k: int):
+        """The exact BF16 values [n, k] of a packed NVFP4 matrix (q3_dequant_nvfp4)."""
+        torch = _torch()
+        out = torch.empty((n, k), dtype=torch.bfloat16, device=packed.device)
+        check(lib().q3_dequant_nvfp4(_p(packed), _p(scale), n, k, _p(out), self._stream()))
+        return out
+
+    def gemv_nvfp4(self, x, packed, scale, output):
+        """output[n] = W[n, :] . x for a packed NVFP4 W (q3_gemv_nvfp4)."""
+        n, k = output.numel(), x.numel()
+        check(lib().q3_gemv_nvfp4(_p(x), _p(packed), _p(scale), _p(output), n, k, self._stream()))
+
     # backend.hpp:28
     def rmsnorm(self, input, weight, output, epsilon: float):
         check(lib().q3_rmsnorm(_p(input), _p(weight), _p(output), input.numel(), epsilon, self._stream()))

@@ -26,14 +26,16 @@ class Qwen3Config:
     # bytes of weights read per decode step on one GPU (all layers + lm_head + norms)
     def weight_bytes(self, weights: str = "bf16") -> int:
         """Bytes one decode step streams: every matrix, the norms, one embedding row.
-        weights="fp8": one byte per GEMV weight plus a 4-byte scale per matrix row."""
+        weights="fp8": one byte per GEMV weight plus a 4-byte scale per matrix row;
+        "nvfp4": half a byte per GEMV weight, a block scale byte per 16, a 4-byte row scale."""
         H, I = self.hidden, self.inter
         qd, kd = self.q_heads * self.head_dim, self.kv_heads * self.head_dim
         mats = self.layer_matmul_params()
         vec = 2 * H + 2 * self.head_dim
-        if weights == "fp8":
+        if weights in ("fp8", "nvfp4"):
             rows = (qd + 2 * kd) + H + 2 * I + H
-            return (mats + 4 * rows + 2 * vec) * self.layers + self.vocab * (H + 4) + 2 * (H + H)
+            per = (lambda n: n // 2 + n // 16) if weights == "nvfp4" else (lambda n: n)
+            return (per(mats) + 4 * rows + 2 * vec) * self.layers + per(self.vocab * H) + 4 * self.vocab + 2 * (H + H)
         return 2 * ((mats + vec) * self.layers + self.vocab * H + H + H)
 
     def layer_matmul_params(self) -> int:

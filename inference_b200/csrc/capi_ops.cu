@@ -150,6 +150,51 @@ int q3_gemv_e4m3(const uint16_t* x, const uint8_t* w8, const float* scale, uint1
     return launch_status(launch_gemv(PRO_PLAIN, EPI_STORE, a, as_stream(stream), false), "q3_gemv_e4m3");
 }
 
+size_t q3_nvfp4_packed_bytes(size_t n_out, size_t n_in) {
+    if (n_out == 0 || n_in == 0 || n_in % 64 != 0 || n_out >= (1u << 30) || n_in > 32768) return 0;
+    return f4_packed_bytes(static_cast<int>(n_out), static_cast<int>(n_in));
+}
+
+int q3_quantize_nvfp4(const uint16_t* w, size_t n_out, size_t n_in, uint8_t* packed, float* row_scale,
+                      void* stream) {
+    Q3_CHECK(w && packed && row_scale, "q3_quantize_nvfp4: null pointer");
+    Q3_CHECK(n_out > 0 && n_in > 0 && n_in % 64 == 0, "q3_quantize_nvfp4: n_in must be a positive multiple of 64");
+    Q3_CHECK(n_in <= 32768 && n_out < (1u << 30), "q3_quantize_nvfp4: shape too large");
+    Q3_CHECK(aligned16(packed), "q3_quantize_nvfp4: packed must be 16-byte aligned");
+    const F8Dst d{packed, row_scale, f4_pack_for(static_cast<int>(n_out), static_cast<int>(n_in), EPI_STORE,
+                                                 current_sms()), 0, 1};
+    return launch_status(launch_quantize_nvfp4(cb(w), n_in, static_cast<int>(n_out), static_cast<int>(n_in), 0,
+                                               static_cast<int>(n_in), d, as_stream(stream)),
+                         "q3_quantize_nvfp4");
+}
+
+int q3_dequant_nvfp4(const uint8_t* packed, const float* row_scale, size_t n_out, size_t n_in, uint16_t* out,
+                     void* stream) {
+    Q3_CHECK(packed && row_scale && out, "q3_dequant_nvfp4: null pointer");
+    Q3_CHECK(n_out > 0 && n_in > 0 && n_in % 64 == 0, "q3_dequant_nvfp4: n_in must be a positive multiple of 64");
+    Q3_CHECK(n_in <= 32768 && n_out < (1u << 30), "q3_dequant_nvfp4: shape too large");
+    Q3_CHECK(aligned16(packed) && aligned16(out), "q3_dequant_nvfp4: 16-byte aligned buffers required");
+    const F8Pack L = f4_pack_for(static_cast<int>(n_out), static_cast<int>(n_in), EPI_STORE, current_sms());
+    return launch_status(launch_dequant_nvfp4(packed, row_scale, L, mb(out), as_stream(stream)), "q3_dequant_nvfp4");
+}
+
+int q3_gemv_nvfp4(const uint16_t* x, const uint8_t* packed, const float* row_scale, uint16_t* y, size_t n_out,
+                  size_t n_in, void* stream) {
+    Q3_CHECK(x && packed && row_scale && y, "q3_gemv_nvfp4: null pointer");
+    Q3_CHECK(n_out > 0 && n_in > 0 && n_in % 64 == 0, "q3_gemv_nvfp4: n_in must be a positive multiple of 64");
+    Q3_CHECK(n_in <= 32768 && n_out < (1u << 30), "q3_gemv_nvfp4: shape too large");
+    Q3_CHECK(aligned16(x) && aligned16(packed), "q3_gemv_nvfp4: x and the packed weights must be 16-byte aligned");
+    GemvArgs a{};
+    a.W8 = packed;
+    a.wscale = row_scale;
+    a.N = static_cast<int>(n_out);
+    a.K = static_cast<int>(n_in);
+    a.plan = plan_gemv(a.N, a.K, EPI_STORE, current_sms(), 0);
+    a.x = cb(x);
+    a.y = mb(y);
+    return launch_status(launch_gemv(PRO_PLAIN, EPI_STORE, a, as_stream(stream), false), "q3_gemv_nvfp4");
+}
+
 int q3_gemm(const uint16_t* x, const uint16_t* w, uint16_t* y, size_t m, size_t n, size_t k, void* stream) {
     Q3_CHECK(x && w && y, "q3_gemm: null pointer");
     Q3_CHECK(m > 0 && n > 0 && k > 0, "q3_gemm: empty shape");

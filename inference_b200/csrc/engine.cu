@@ -72,6 +72,11 @@ int dalloc_t(q3_engine* e, T** p, size_t count) {
     return dalloc(e, reinterpret_cast<void**>(p), count * sizeof(T));
 }
 
+// Bytes of an [N, K] GEMV matrix in the engine's packed weight format.
+size_t packed_bytes(const q3_engine* e, int N, int K) {
+    return e->fp4 ? f4_packed_bytes(N, K) : f8_packed_bytes(N, K);
+}
+
 // Device bytes, zeroed.
 int dalloc_zero(q3_engine* e, uint8_t** p, size_t bytes) {
     int rc = dalloc(e, reinterpret_cast<void**>(p), bytes);
@@ -225,13 +230,13 @@ int gemv(Recorder& r, int pro, int epi, GemvArgs a, WMat W, int N, int K, int ea
     a.N = N;
     a.K = K;
     a.plan = (early_ctas > 0 && !W.q) ? plan_gemv_early(N, K, epi, r.e->sms, early_ctas)
-                                      : plan_gemv(N, K, epi, r.e->sms, W.q ? 1 : 2);
+                                      : plan_gemv(N, K, epi, r.e->sms, W.q ? (r.e->fp4 ? 0 : 1) : 2);
     a.trace = r.trace();
     r.mark(true, 0);
     cudaError_t st = launch_gemv(pro, epi, a, r.e->stream, r.pdl);
     r.mark(false, 0);
     if (r.bytes && (r.klass == 0 || r.klass == 2))
-        *r.bytes += W.q ? static_cast<double>(N) * K + N * 4.0 + K * 2.0 + N * 2.0
+        *r.bytes += W.q ? static_cast<double>(N) * K * (r.e->fp4 ? 0.5625 : 1.0) + N * 4.0 + K * 2.0 + N * 2.0
                         : static_cast<double>(N) * K * 2 + K * 2.0 + N * 2.0;
     if (st != cudaSuccess) return fail(Q3_ERR_CUDA, std::string("gemv launch: ") + cudaGetErrorString(st));
     return Q3_OK;
@@ -473,14 +478,17 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     Q3_CHECK(c.vocab % tp_size == 0, "vocab must divide by the tensor-parallel size");
     Q3_CHECK(c.hidden % 8 == 0 && c.hidden <= 32768, "hidden must be a multiple of 8 (<= 32768)");
     Q3_CHECK(c.capacity < (1u << 24), "capacity too large");
-    Q3_CHECK(c.weight_format == Q3_WEIGHTS_BF16 || c.weight_format == Q3_WEIGHTS_FP8_E4M3,
+    Q3_CHECK(c.weight_format == Q3_WEIGHTS_BF16 || c.weight_format == Q3_WEIGHTS_FP8_E4M3 ||
+                 c.weight_format == Q3_WEIGHTS_NVFP4,
              "q3_engine_create: unknown weight_format");
-    Q3_CHECK(c.weight_format != Q3_WEIGHTS_FP8_E4M3 || (c.hidden % 64 == 0 && (c.inter / tp_size) % 64 == 0),
-             "FP8 weights need hidden and intermediate/tp multiples of 64");
+    Q3_CHECK(c.weight_format == Q3_WEIGHTS_BF16 || (c.hidden % 64 == 0 && (c.inter / tp_size) % 64 == 0 &&
+                                                    (c.q_heads / tp_size * c.head_dim) % 64 == 0),
+             "FP8 / NVFP4 weights need hidden, intermediate/tp and q_heads/tp x head_dim multiples of 64");
 
     auto* e = new q3_engine();
     e->cfg = c;
-    e->fp8 = c.weight_format == Q3_WEIGHTS_FP8_E4M3;
+    e->fp8 = c.weight_format != Q3_WEIGHTS_BF16;
+    e->fp4 = c.weight_format == Q3_WEIGHTS_NVFP4;
     e->device = device;
     e->rank = tp_rank;
     e->world = tp_size;
@@ -509,7 +517,7 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->embed, static_cast<size_t>(c.vocab) * H)) != Q3_OK) return bail(rc);
     if (e->fp8) {
         // the embedding stays BF16 for the lookup; lm_head gets its own E4M3 copy
-        if ((rc = dalloc_zero(e, &e->f_lm, f8_packed_bytes(e->vl, e->H))) != Q3_OK) return bail(rc);
+        if ((rc = dalloc_zero(e, &e->f_lm, packed_bytes(e, e->vl, e->H))) != Q3_OK) return bail(rc);
         if ((rc = dalloc_t(e, &e->s_lm, static_cast<size_t>(e->vl))) != Q3_OK) return bail(rc);
     } else if (c.tied) {
         e->lm_head = e->embed + static_cast<size_t>(e->voff) * H;
@@ -524,11 +532,11 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     for (auto& L : e->layers) {
         L = LayerW{};
         if (e->fp8) {
-            // packed layouts (f8_packed_bytes), zero so the column padding is zero
-            if ((rc = dalloc_zero(e, &L.f_qkv, f8_packed_bytes(static_cast<int>(rows_qkv), e->H))) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_zero(e, &L.f_o, f8_packed_bytes(e->H, e->qd))) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_zero(e, &L.f_gu, f8_packed_bytes(static_cast<int>(rows_gu), e->H))) != Q3_OK) return bail(rc);
-            if ((rc = dalloc_zero(e, &L.f_down, f8_packed_bytes(e->H, e->il))) != Q3_OK) return bail(rc);
+            // packed layouts (packed_bytes), zero so the column padding is zero
+            if ((rc = dalloc_zero(e, &L.f_qkv, packed_bytes(e, static_cast<int>(rows_qkv), e->H))) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_zero(e, &L.f_o, packed_bytes(e, e->H, e->qd))) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_zero(e, &L.f_gu, packed_bytes(e, static_cast<int>(rows_gu), e->H))) != Q3_OK) return bail(rc);
+            if ((rc = dalloc_zero(e, &L.f_down, packed_bytes(e, e->H, e->il))) != Q3_OK) return bail(rc);
             if ((rc = dalloc_t(e, &L.s_qkv, rows_qkv)) != Q3_OK) return bail(rc);
             if ((rc = dalloc_t(e, &L.s_o, H)) != Q3_OK) return bail(rc);
             if ((rc = dalloc_t(e, &L.s_gu, rows_gu)) != Q3_OK) return bail(rc);
@@ -550,11 +558,15 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
             return bail(fail(Q3_ERR_CUDA, "KV cache memset failed"));
     }
     // bytes streamed per decode step by this rank (weights read by the GEMVs + norms + one embedding row)
-    // (FP8: one byte per weight plus a 4-byte scale per row)
+    // (FP8: one byte per weight plus a 4-byte scale per row; NVFP4: half a byte plus a block scale per
+    // 16 weights and a 4-byte scale per row)
     const size_t mat_elems = rows_qkv * H + H * e->qd + rows_gu * H + H * e->il;
     const size_t mat_rows = rows_qkv + H + rows_gu + H;
-    const size_t per_layer = e->fp8 ? mat_elems + mat_rows * 4 + (2 * H + 256) * 2 : (mat_elems + 2 * H + 256) * 2;
-    const size_t lm_bytes = e->fp8 ? static_cast<size_t>(e->vl) * (H + 4) : static_cast<size_t>(e->vl) * H * 2;
+    auto packed_weights = [&](size_t elems) { return e->fp4 ? elems / 2 + elems / 16 : elems; };
+    const size_t per_layer = e->fp8 ? packed_weights(mat_elems) + mat_rows * 4 + (2 * H + 256) * 2
+                                    : (mat_elems + 2 * H + 256) * 2;
+    const size_t lm_bytes = e->fp8 ? packed_weights(static_cast<size_t>(e->vl) * H) + static_cast<size_t>(e->vl) * 4
+                                   : static_cast<size_t>(e->vl) * H * 2;
     e->weight_bytes = per_layer * c.layers + lm_bytes + H * 2 + H * 2;
 
     // ---- page table (identity for a single sequence) and RoPE tables
@@ -676,27 +688,34 @@ struct Staging {
 
 int quant(q3_engine* e, const bf16* src, size_t ld_src, size_t rows, size_t full_cols, size_t c0, size_t cols,
           const F8Dst& d) {
-    Q3_CUDA(launch_quantize_e4m3(src, ld_src, static_cast<int>(rows), static_cast<int>(full_cols), static_cast<int>(c0),
-                                 static_cast<int>(cols), d, e->stream));
+    if (d.pack.fmt == 1)
+        Q3_CUDA(launch_quantize_nvfp4(src, ld_src, static_cast<int>(rows), static_cast<int>(full_cols),
+                                      static_cast<int>(c0), static_cast<int>(cols), d, e->stream));
+    else
+        Q3_CUDA(launch_quantize_e4m3(src, ld_src, static_cast<int>(rows), static_cast<int>(full_cols),
+                                     static_cast<int>(c0), static_cast<int>(cols), d, e->stream));
     return Q3_OK;
 }
 
-// The FP8 matrices as quantize destinations, each in the packed layout of the
+// The packed matrices as quantize destinations, each in the packed layout of the
 // GEMV that reads it (record_step's shapes and epilogues).
+F8Pack pack_for(const q3_engine* e, int N, int K, int epi) {
+    return e->fp4 ? f4_pack_for(N, K, epi, e->sms) : f8_pack_for(N, K, epi, e->sms);
+}
 F8Dst dst_qkv(const q3_engine* e, const LayerW& L, int row0) {
-    return F8Dst{L.f_qkv, L.s_qkv, f8_pack_for(e->qd + 2 * e->kd, e->H, EPI_QKV, e->sms), row0, 1};
+    return F8Dst{L.f_qkv, L.s_qkv, pack_for(e, e->qd + 2 * e->kd, e->H, EPI_QKV), row0, 1};
 }
 F8Dst dst_o(const q3_engine* e, const LayerW& L) {
-    return F8Dst{L.f_o, L.s_o, f8_pack_for(e->H, e->qd, e->world > 1 ? EPI_PARTIAL : EPI_RESID_F32, e->sms), 0, 1};
+    return F8Dst{L.f_o, L.s_o, pack_for(e, e->H, e->qd, e->world > 1 ? EPI_PARTIAL : EPI_RESID_F32), 0, 1};
 }
 F8Dst dst_gu(const q3_engine* e, const LayerW& L, int up) {  // gate row j -> row 2 j, up row j -> 2 j + 1
-    return F8Dst{L.f_gu, L.s_gu, f8_pack_for(2 * e->il, e->H, EPI_SWIGLU, e->sms), up, 2};
+    return F8Dst{L.f_gu, L.s_gu, pack_for(e, 2 * e->il, e->H, EPI_SWIGLU), up, 2};
 }
 F8Dst dst_down(const q3_engine* e, const LayerW& L) {
-    return F8Dst{L.f_down, L.s_down, f8_pack_for(e->H, e->il, e->world > 1 ? EPI_PARTIAL : EPI_RESID, e->sms), 0, 1};
+    return F8Dst{L.f_down, L.s_down, pack_for(e, e->H, e->il, e->world > 1 ? EPI_PARTIAL : EPI_RESID), 0, 1};
 }
 F8Dst dst_lm(const q3_engine* e) {
-    return F8Dst{e->f_lm, e->s_lm, f8_pack_for(e->vl, e->H, EPI_ARGMAX, e->sms), 0, 1};
+    return F8Dst{e->f_lm, e->s_lm, pack_for(e, e->vl, e->H, EPI_ARGMAX), 0, 1};
 }
 
 // FP8 engines: each GEMV matrix generated at full row width in BF16 (so a
@@ -980,7 +999,10 @@ int forward_rows_impl(q3_engine* e, const RowsSpec& R) {
     auto weight = [&](const bf16* w, const F8Dst& d, const bf16** out) -> int {
         *out = w;
         if (!e->fp8) return Q3_OK;
-        Q3_CUDA(launch_dequant_e4m3(d.base, d.scale, d.pack, e->pw, s));
+        if (d.pack.fmt == 1)
+            Q3_CUDA(launch_dequant_nvfp4(d.base, d.scale, d.pack, e->pw, s));
+        else
+            Q3_CUDA(launch_dequant_e4m3(d.base, d.scale, d.pack, e->pw, s));
         *out = e->pw;
         return Q3_OK;
     };

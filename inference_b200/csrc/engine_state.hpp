@@ -33,7 +33,8 @@ struct q3_engine {
     uint32_t voff = 0;
     // weights
     q3::bf16 *embed = nullptr, *lm_head = nullptr, *final_norm = nullptr;
-    bool fp8 = false;  // Q3_WEIGHTS_FP8_E4M3: GEMV matrices as E4M3 + row scales
+    bool fp8 = false;  // packed GEMV matrices (Q3_WEIGHTS_FP8_E4M3 or Q3_WEIGHTS_NVFP4) + row scales
+    bool fp4 = false;  // ... and they are NVFP4
     uint8_t* f_lm = nullptr;
     float* s_lm = nullptr;
     std::vector<q3::LayerW> layers;

@@ -26,6 +26,11 @@
 //     |x| >= max|x| 2^-29; the few smaller ones round as f16 subnormals).
 //     Row sums are multiplied back by 2^s and by the row's scale in the
 //     epilogue.
+//   * NVFP4 weights (F4) take the same path with 16-row x 512-column items:
+//     each lane's 16 columns of a 64-column block are one NVFP4 block, so
+//     its E2M1 nibbles turn into f16 by a byte-permute lookup (integer pipe,
+//     not the conversion unit) and one f16x2 multiply by the block's E4M3
+//     scale gives the exact weights (at most six significant bits).
 #include <algorithm>
 #include <cmath>
 
@@ -64,24 +69,32 @@ constexpr size_t kSmemBudgetF8 = 226 * 1024;
 constexpr int kF8Rows = kF8TileRows;          // rows per FP8 tile (the mma M dimension)
 constexpr int kF8Cols = kF8TileCols;          // columns per FP8 item
 constexpr int kF8Slot = kF8Rows * kF8Cols;    // bytes per FP8 ring slot (one packed item)
+constexpr int kF4Slot = kF8Rows * kF4RowBytes;  // bytes per NVFP4 ring slot (nibbles + block scales)
 
 struct SmemLayout {
     size_t stage_off, x_off, part_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline size_t slot_bytes(const GemvPlan& p) {
-    return p.wb == 1 ? static_cast<size_t>(kF8Slot) : static_cast<size_t>(p.kc) * 2;
+// plan.wb: 2 = BF16, 1 = E4M3, 0 = NVFP4 (WF = 2 - wb in the kernel)
+__host__ __device__ inline size_t slot_bytes_of(int wb, int kc) {
+    return wb == 2 ? static_cast<size_t>(kc) * 2 : wb == 1 ? static_cast<size_t>(kF8Slot)
+                                                          : static_cast<size_t>(kF4Slot);
 }
+__host__ __device__ inline size_t slot_bytes(const GemvPlan& p) { return slot_bytes_of(p.wb, p.kc); }
 
-__host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K, int max_rows) {
+// `wb` a compile-time constant in the kernel (its weight format)
+__host__ __device__ inline SmemLayout smem_layout_wb(const GemvPlan& p, int wb, int K, int max_rows) {
     SmemLayout L;
     L.stage_off = 0;
-    L.x_off = static_cast<size_t>(kWarps) * p.stages * slot_bytes(p);
+    L.x_off = static_cast<size_t>(kWarps) * p.stages * slot_bytes_of(wb, p.kc);
     L.part_off = L.x_off + (static_cast<size_t>(K) * 2 + 15) / 16 * 16;
     L.bar_off = L.part_off + (static_cast<size_t>(max_rows) * p.nch * 4 + 15) / 16 * 16;
     L.misc_off = L.bar_off + static_cast<size_t>(kWarps) * p.stages * 8;
     L.total = L.misc_off + 128;
     return L;
+}
+__host__ __device__ inline SmemLayout smem_layout(const GemvPlan& p, int K, int max_rows) {
+    return smem_layout_wb(p, p.wb, K, max_rows);
 }
 
 __device__ __forceinline__ size_t kv_slot(const GemvArgs& a, int pos, int head) {
@@ -134,6 +147,43 @@ __device__ __forceinline__ void mma_e4m3_f16(float (&d)[4], uint32_t wg, uint32_
     // not volatile: a pure function of its operands, free to be scheduled among the conversions
     asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Two E2M1 weights (one byte: column 2 i in the low nibble) as an f16x2, by a
+// byte-permute lookup of the f16 high byte (the low byte of every E2M1 value in
+// f16 is zero): magnitudes 0, 0.5, 1, 1.5, 2, 3, 4, 6 -> 0x00, 0x38, 0x3C,
+// 0x3E, 0x40, 0x42, 0x44, 0x46, entry 0 also filling the low bytes; the signs
+// go to bits 15 and 31.
+__device__ __forceinline__ uint32_t e2m1x2_f16x2(uint32_t byte) {
+    const uint32_t sel = ((byte & 0x7u) << 4) | ((byte & 0x70u) << 8);
+    uint32_t v;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(v) : "r"(0x3E3C3800u), "r"(0x46444240u), "r"(sel));
+    return v | ((byte & 0x8u) << 12) | ((byte & 0x80u) << 24);
+}
+
+__device__ __forceinline__ uint32_t mul_f16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// An E4M3 scale byte as (s, s) in f16 (exact).
+__device__ __forceinline__ uint32_t e4m3_f16x2_splat(uint32_t q) {
+    uint32_t d;
+    asm("{\n\t.reg .b16 p;\n\tcvt.u16.u32 p, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, p;\n\t}" : "=r"(d) : "r"(q | (q << 8)));
+    return d;
+}
+
+// The mma of four consecutive columns of NVFP4 rows g and g + 8: h / h8 hold the
+// two bytes (four nibbles) of each row, sa / sb the rows' block scales as f16x2.
+__device__ __forceinline__ void mma_nvfp4(float (&d)[4], uint32_t h, uint32_t h8, uint32_t sa, uint32_t sb,
+                                          uint32_t b0, uint32_t b1) {
+    const uint32_t a0 = mul_f16x2(e2m1x2_f16x2(h & 0xFFu), sa), a2 = mul_f16x2(e2m1x2_f16x2((h >> 8) & 0xFFu), sa);
+    const uint32_t a1 = mul_f16x2(e2m1x2_f16x2(h8 & 0xFFu), sb), a3 = mul_f16x2(e2m1x2_f16x2((h8 >> 8) & 0xFFu), sb);
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
         "{%0, %1, %2, %3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -203,11 +253,16 @@ __device__ __forceinline__ void peer_wait(const PeerLinks& x, unsigned long long
     __syncthreads();
 }
 
-// F8: weights are E4M3 bytes (a.W8) with a scale per row (a.wscale); the ring
-// slots hold the same 4 KB, twice the columns.
-template <int PRO, int EPI, bool F8>
+// WF (weight format): 0 BF16; 1 E4M3 bytes (a.W8) with a scale per row (a.wscale),
+// ring slots of 4 KB holding twice the columns; 2 NVFP4 (a.W8 in the NVFP4 pack,
+// row scales in a.wscale), slots of 16 rows x 512 columns with their block scales.
+template <int PRO, int EPI, int WF>
 __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(const __grid_constant__ GemvArgs a) {
-    constexpr int WB = F8 ? 1 : 2;  // bytes per weight
+    constexpr bool F8 = WF != 0;  // packed 16-row tiles on the tensor cores (E4M3 or NVFP4)
+    constexpr bool F4 = WF == 2;
+    constexpr int WB = F8 ? 1 : 2;  // bytes per weight (BF16 items)
+    constexpr int kUnit = F4 ? kF4RowBytes : kF8Cols;  // bytes of one row of a packed item
+    constexpr int kSlot = kF8Rows * kUnit;
     extern __shared__ __align__(128) uint8_t smem[];
     const GemvPlan& p = a.plan;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -226,13 +281,14 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
     const int r0 = u0 * p.row_gran, r1 = u1 * p.row_gran;
     const int nrows = r1 - r0;
     const int max_rows = p.max_units * p.row_gran;
-    const SmemLayout L = smem_layout(p, a.K, max_rows);
+    constexpr int kWb = 2 - WF;  // the plan's wb of this weight format
+    const SmemLayout L = smem_layout_wb(p, kWb, a.K, max_rows);
     bf16* xs = reinterpret_cast<bf16*>(smem + L.x_off);
     float* part = reinterpret_cast<float*>(smem + L.part_off);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bar_off) + warp * p.stages;
     float* misc = reinterpret_cast<float*>(smem + L.misc_off);
     unsigned long long* cta_key = reinterpret_cast<unsigned long long*>(misc + 16);
-    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * slot_bytes(p);
+    uint8_t* ring = smem + L.stage_off + static_cast<size_t>(warp) * p.stages * slot_bytes_of(kWb, p.kc);
 
     // items: (row, chunk) pairs; FP8: (16-row tile, 256-column chunk) pairs
     const int n_items = (F8 ? (nrows + kF8Rows - 1) / kF8Rows : nrows) * p.nch;
@@ -256,11 +312,11 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             const int tile = item / p.nch;
             const int rows = min(kF8Rows, nrows - tile * kF8Rows);
             if (lane == 0) {
-                const uint32_t bytes = static_cast<uint32_t>(rows * kF8Cols);
+                const uint32_t bytes = static_cast<uint32_t>(rows * kUnit);
                 mbar_arrive_expect_tx(&bars[slot], bytes);
-                bulk_g2s(ring + static_cast<size_t>(slot) * kF8Slot,
+                bulk_g2s(ring + static_cast<size_t>(slot) * kSlot,
                          a.W8 + (static_cast<size_t>(r0) * p.nch + static_cast<size_t>(tile) * kF8Rows * p.nch +
-                                 static_cast<size_t>(c) * rows) * kF8Cols,
+                                 static_cast<size_t>(c) * rows) * kUnit,
                          bytes, &bars[slot], pol);
             }
         } else {
@@ -524,9 +580,29 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             failed = failed || !ok;
             const int item = i0 + j;
             const int tile = item / p.nch, c = item % p.nch;
-            if (ok) {
+            if (ok && F4) {
                 const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
-                const uint8_t* ws = ring + static_cast<size_t>(slot) * kF8Slot;
+                const uint8_t* ws = ring + static_cast<size_t>(slot) * kSlot;
+                const uint8_t* sc = ws + min(kF8Rows, nrows - tile * kF8Rows) * 256;  // the item's block scales
+                const uint4* xq = reinterpret_cast<const uint4*>(xs) + c * (p.kc / 8);
+#pragma unroll 2
+                for (int blk = 0; blk < cols / 64; ++blk) {
+                    // lane (g, t): block 4 blk + t of rows g and g + 8 (8 bytes each, 32-byte units
+                    // swizzled by the row), its scales, and the matching 16 x values
+                    const int unit = ((blk ^ g) << 5) + (t << 3);
+                    const uint2 wa = *reinterpret_cast<const uint2*>(ws + g * 256 + unit);
+                    const uint2 wb = *reinterpret_cast<const uint2*>(ws + (g + 8) * 256 + unit);
+                    const uint32_t sa = e4m3_f16x2_splat(sc[g * 32 + 4 * blk + t]);
+                    const uint32_t sb = e4m3_f16x2_splat(sc[(g + 8) * 32 + 4 * blk + t]);
+                    const uint4 x0 = xq[blk * 8 + 2 * t], x1 = xq[blk * 8 + 2 * t + 1];
+                    mma_nvfp4(d, wa.x, wb.x, sa, sb, x0.x, x0.y);
+                    mma_nvfp4(e, wa.x >> 16, wb.x >> 16, sa, sb, x0.z, x0.w);
+                    mma_nvfp4(d, wa.y, wb.y, sa, sb, x1.x, x1.y);
+                    mma_nvfp4(e, wa.y >> 16, wb.y >> 16, sa, sb, x1.z, x1.w);
+                }
+            } else if (ok) {
+                const int cols = (c == p.nch - 1) ? a.K - c * p.kc : p.kc;
+                const uint8_t* ws = ring + static_cast<size_t>(slot) * kSlot;
                 const uint4* xq = reinterpret_cast<const uint4*>(xs) + c * (kF8Cols / 8);
 #pragma unroll 4
                 for (int blk = 0; blk < cols / 64; ++blk) {
@@ -718,7 +794,7 @@ __global__ void peer_keys_kernel(const PeerLinks x, unsigned long long* out, uin
 
 template <int PRO, int EPI>
 cudaError_t launch_t(const GemvArgs& a, cudaStream_t s, bool pdl) {
-    auto* fn = a.W8 ? gemv_kernel<PRO, EPI, true> : gemv_kernel<PRO, EPI, false>;
+    auto* fn = !a.W8 ? gemv_kernel<PRO, EPI, 0> : a.plan.wb == 0 ? gemv_kernel<PRO, EPI, 2> : gemv_kernel<PRO, EPI, 1>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.plan.grid);
     cfg.blockDim = dim3(kThreads);
@@ -741,8 +817,9 @@ cudaError_t launch_peer_keys(const PeerLinks& x, unsigned long long* out, uint32
 
 template <int PRO, int EPI>
 cudaError_t configure_pair() {
-    for (const void* f : {reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, false>),
-                          reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, true>)}) {
+    for (const void* f : {reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, 0>),
+                          reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, 1>),
+                          reinterpret_cast<const void*>(gemv_kernel<PRO, EPI, 2>)}) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxDynSmem);
         // the whole carve-out as shared memory, so a CTA of the next (PDL-launched) kernel fits beside
         // this one where the two footprints allow
@@ -774,15 +851,20 @@ cudaError_t configure_gemv_kernels() {
 
 F8Pack f8_pack_for(int N, int K, int epi, int sms) {
     const GemvPlan p = plan_gemv(N, K, epi, sms, 1);
-    return F8Pack{N, K, (K + kF8TileCols - 1) / kF8TileCols, p.grid, p.row_gran};
+    return F8Pack{N, K, (K + kF8TileCols - 1) / kF8TileCols, p.grid, p.row_gran, 0};
+}
+
+F8Pack f4_pack_for(int N, int K, int epi, int sms) {
+    const GemvPlan p = plan_gemv(N, K, epi, sms, 0);
+    return F8Pack{N, K, (K + kF4TileCols - 1) / kF4TileCols, p.grid, p.row_gran, 1};
 }
 
 GemvPlan plan_gemv(int N, int K, int epi, int sms, int wb) {
     GemvPlan p{};
     p.row_gran = (epi == EPI_SWIGLU) ? 2 : 1;
     p.wb = wb;
-    // BF16: 4 KB row segments; FP8: 16-row tiles of 256 columns
-    const int chunk = wb == 1 ? kF8Cols : kChunk;
+    // BF16: 4 KB row segments; FP8: 16-row tiles of 256 columns; NVFP4: of 512
+    const int chunk = wb == 2 ? kChunk : wb == 1 ? kF8Cols : kF4TileCols;
     p.kc = K < chunk ? K : chunk;
     p.nch = (K + p.kc - 1) / p.kc;
     const int units = N / p.row_gran;
@@ -794,7 +876,7 @@ GemvPlan plan_gemv(int N, int K, int epi, int sms, int wb) {
     p.grid = std::max(1, grid);
     p.max_units = (units + p.grid - 1) / p.grid;
     const int max_rows = p.max_units * p.row_gran;
-    const size_t budget = wb == 1 ? kSmemBudgetF8 : kSmemBudget;
+    const size_t budget = wb == 2 ? kSmemBudget : kSmemBudgetF8;
     for (p.stages = Q3_GEMV_MAX_STAGES; p.stages > 2; --p.stages)
         if (smem_layout(p, K, max_rows).total <= budget) break;
     p.smem = smem_layout(p, K, max_rows).total;
@@ -827,8 +909,9 @@ GemvPlan plan_gemv_early(int N, int K, int epi, int sms, int early_ctas) {
 }
 
 cudaError_t launch_gemv(int pro, int epi, const GemvArgs& a, cudaStream_t s, bool pdl) {
-    // the plan's item width must match the weight format; FP8 rows are whole 64-column blocks
-    if (a.plan.wb != (a.W8 ? 1 : 2) || (a.W8 && (a.K % 64 != 0 || !a.wscale))) return cudaErrorInvalidValue;
+    // the plan's item width must match the weight format; packed rows are whole 64-column blocks
+    if ((a.W8 ? a.plan.wb == 2 : a.plan.wb != 2) || (a.W8 && (a.K % 64 != 0 || !a.wscale)))
+        return cudaErrorInvalidValue;
 #define Q3_CASE(P, E) \
     if (pro == P && epi == E) return launch_t<P, E>(a, s, pdl);
     Q3_CASE(PRO_PLAIN, EPI_STORE)

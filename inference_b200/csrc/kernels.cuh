@@ -308,23 +308,65 @@ cudaError_t configure_gemv_kernels();
 // group j ^ (r & 7), so the tensor-core fragment loads hit distinct banks.
 struct F8Pack {
     int N, K, nch, grid, row_gran;  // N == 0: plain row-major with pitch K
+    int fmt;                        // 0: E4M3 (256-column chunks); 1: NVFP4 (512-column chunks)
 };
 constexpr int kF8TileRows = 16;
 constexpr int kF8TileCols = 256;
-__host__ __device__ inline size_t f8_offset(const F8Pack& L, int row, int col) {
-    if (L.N == 0) return static_cast<size_t>(row) * L.K + col;
+// The band of GEMV rows holding `row` (the plan's uniform split into whole
+// row_gran units), and the row's tile t, row rr in the tile and the tile's rows.
+__host__ __device__ inline void pack_tile(const F8Pack& L, int row, int& r0, int& t, int& rr, int& rows_t) {
     const int U = L.N / L.row_gran, u = row / L.row_gran;
     int b = static_cast<int>(static_cast<long long>(u) * L.grid / U);
     while (b + 1 < L.grid && static_cast<int>(static_cast<long long>(b + 1) * U / L.grid) <= u) ++b;
     const int u0 = static_cast<int>(static_cast<long long>(b) * U / L.grid);
     const int u1 = static_cast<int>(static_cast<long long>(b + 1) * U / L.grid);
-    const int r0 = u0 * L.row_gran, nrows = (u1 - u0) * L.row_gran;
-    const int rl = row - r0, t = rl / kF8TileRows, rr = rl % kF8TileRows;
-    const int rows_t = nrows - t * kF8TileRows < kF8TileRows ? nrows - t * kF8TileRows : kF8TileRows;
+    r0 = u0 * L.row_gran;
+    const int nrows = (u1 - u0) * L.row_gran;
+    const int rl = row - r0;
+    t = rl / kF8TileRows;
+    rr = rl % kF8TileRows;
+    rows_t = nrows - t * kF8TileRows < kF8TileRows ? nrows - t * kF8TileRows : kF8TileRows;
+}
+__host__ __device__ inline size_t f8_offset(const F8Pack& L, int row, int col) {
+    if (L.N == 0) return static_cast<size_t>(row) * L.K + col;
+    int r0, t, rr, rows_t;
+    pack_tile(L, row, r0, t, rr, rows_t);
     const int c = col / kF8TileCols, g = (col % kF8TileCols) / 16;
     return (static_cast<size_t>(r0) * L.nch + static_cast<size_t>(t) * kF8TileRows * L.nch +
             static_cast<size_t>(c) * rows_t + rr) * kF8TileCols + ((g ^ (rr & 7)) << 4) + (col & 15);
 }
+// NVFP4 (fmt 1): E2M1 weights in 512-column chunks, one E4M3 scale per 16 columns.
+// Item (tile, chunk) = rows_t x 256 bytes of nibbles, then rows_t x 32 block
+// scales.  In row rr of an item: columns 64 u .. 64 u + 63 (unit u) sit in the
+// 32 bytes at (u ^ (rr & 7)) * 32, the unit's 16-column block j at byte 8 j of
+// them, column 2 i of the block in the low nibble of byte i; block b of the
+// chunk has its scale at byte rows_t * 256 + rr * 32 + b.
+constexpr int kF4TileCols = 512;
+constexpr int kF4RowBytes = 256 + 32;
+__host__ __device__ inline size_t f4_item_base(const F8Pack& L, int row, int col, int& rr, int& rows_t) {
+    int r0, t;
+    pack_tile(L, row, r0, t, rr, rows_t);
+    const int c = col / kF4TileCols;
+    return (static_cast<size_t>(r0) * L.nch + static_cast<size_t>(t) * kF8TileRows * L.nch +
+            static_cast<size_t>(c) * rows_t) * kF4RowBytes;
+}
+// The byte holding column col (a multiple of 2: the low nibble; col + 1 the high one).
+__host__ __device__ inline size_t f4_nibble_offset(const F8Pack& L, int row, int col) {
+    int rr, rows_t;
+    const size_t base = f4_item_base(L, row, col, rr, rows_t);
+    const int cc = col % kF4TileCols, u = cc / 64;
+    return base + static_cast<size_t>(rr) * 256 + ((u ^ (rr & 7)) << 5) + ((cc % 64) / 16) * 8 + (cc % 16) / 2;
+}
+// The scale byte of column col's 16-column block.
+__host__ __device__ inline size_t f4_scale_offset(const F8Pack& L, int row, int col) {
+    int rr, rows_t;
+    const size_t base = f4_item_base(L, row, col, rr, rows_t);
+    return base + static_cast<size_t>(rows_t) * 256 + static_cast<size_t>(rr) * 32 + (col % kF4TileCols) / 16;
+}
+inline size_t f4_packed_bytes(int N, int K) {
+    return static_cast<size_t>(N) * ((K + kF4TileCols - 1) / kF4TileCols) * kF4RowBytes;
+}
+F8Pack f4_pack_for(int N, int K, int epi, int num_sms);
 inline size_t f8_packed_bytes(int N, int K) {
     return static_cast<size_t>(N) * ((K + kF8TileCols - 1) / kF8TileCols) * kF8TileCols;
 }
@@ -351,6 +393,17 @@ cudaError_t launch_pack_e4m3(const uint8_t* q, const F8Pack& pack, uint8_t* pack
 // The packed matrix's exact BF16 values times the row scales, row-major [N, K] (K % 16 == 0).
 cudaError_t launch_dequant_e4m3(const uint8_t* packed, const float* scale, const F8Pack& pack, bf16* out,
                                 cudaStream_t s);
+// NVFP4 with power-of-two row scales: for each of `rows` rows of src the row scale
+// is 2^e, e the smallest integer with max|row| / 6 <= 448 * 2^e; each block b of
+// 16 columns of [c0, c0 + cols) gets the E4M3 scale s = E4M3(amax_b / 6 * 2^-e)
+// and its weights E2M1(w * 2^-e / s) (nearest, ties to even, saturating at 6;
+// 0 when s is 0), written to columns 0 .. cols - 1 of the destination rows of
+// an NVFP4 pack (c0 and cols multiples of 16).
+cudaError_t launch_quantize_nvfp4(const bf16* src, size_t ld_src, int rows, int full_cols, int c0, int cols,
+                                  const F8Dst& dst, cudaStream_t s);
+// The NVFP4-packed matrix's exact BF16 values (E2M1 x block scale x row scale), row-major [N, K].
+cudaError_t launch_dequant_nvfp4(const uint8_t* packed, const float* scale, const F8Pack& pack, bf16* out,
+                                 cudaStream_t s);
 cudaError_t configure_attention_kernels();
 int num_sms(int device);
 

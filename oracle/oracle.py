@@ -86,6 +86,12 @@ class Oracle:
         L.q3o_e4m3_value.restype = C.c_float
         L.q3o_quantize_e4m3.argtypes = [_u16p, _sz, _sz, _u8p, _f32p]
         L.q3o_model_quantize_fp8.argtypes = [C.c_void_p]
+        L.q3o_e2m1.argtypes = [C.c_float]
+        L.q3o_e2m1.restype = C.c_uint8
+        L.q3o_e2m1_value.argtypes = [C.c_uint8]
+        L.q3o_e2m1_value.restype = C.c_float
+        L.q3o_quantize_nvfp4.argtypes = [_u16p, _sz, _sz, _u8p, _u8p, _f32p]
+        L.q3o_model_quantize_nvfp4.argtypes = [C.c_void_p]
 
     # -- synthetic inputs
     def normal(self, seed, tensor_id, rows, cols, row0=0, col0=0, full_cols=None):
@@ -171,6 +177,23 @@ class Oracle:
         self.lib.q3o_quantize_e4m3(w, w.shape[0], w.shape[1], q, sc)
         return q, sc
 
+    # -- NVFP4 weights (E2M1, E4M3 block scales of 16 columns, power-of-two row scales)
+    def e2m1(self, x: float) -> int:
+        return int(self.lib.q3o_e2m1(x))
+
+    def e2m1_value(self, q: int) -> float:
+        return float(self.lib.q3o_e2m1_value(q))
+
+    def quantize_nvfp4(self, w):
+        """w [rows, cols] BF16 bits -> (q [rows, cols] E2M1 codes, block scales [rows, cols / 16]
+        E4M3 codes, row scales [rows] float32)."""
+        w = np.ascontiguousarray(w, np.uint16)
+        q = np.empty(w.shape, np.uint8)
+        bs = np.empty((w.shape[0], w.shape[1] // 16), np.uint8)
+        rs = np.empty(w.shape[0], np.float32)
+        self.lib.q3o_quantize_nvfp4(w, w.shape[0], w.shape[1], q, bs, rs)
+        return q, bs, rs
+
     # -- model
     def model(self, cfg: ModelConfig, seed: int = 0) -> "OracleModel":
         return OracleModel(self, cfg, seed)
@@ -194,6 +217,11 @@ class OracleModel:
     def quantize_fp8(self) -> "OracleModel":
         """Replace every GEMV matrix by its E4M3 round trip (the FP8-weight engine's model)."""
         self.o.lib.q3o_model_quantize_fp8(self.h)
+        return self
+
+    def quantize_nvfp4(self) -> "OracleModel":
+        """Replace every GEMV matrix by its NVFP4 round trip (the NVFP4-weight engine's model)."""
+        self.o.lib.q3o_model_quantize_nvfp4(self.h)
         return self
 
     def logits(self) -> np.ndarray:

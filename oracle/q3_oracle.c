@@ -327,6 +327,80 @@ static void fp8_roundtrip(uint16_t* w, size_t rows, size_t cols) {
     free(q);
 }
 
+/* ---------------------------------------------------------------- NVFP4 weights
+ * (the build's 4-bit weight format; no reference counterpart).  E2M1 values
+ * (1 sign, 2 exponent, 1 mantissa bit: 0, 0.5, 1, 1.5, 2, 3, 4, 6) with one
+ * E4M3 scale per block of 16 consecutive columns, and per row a power-of-two
+ * scale 2^e_r, e_r the smallest integer with max|w_r| / 6 <= 448 * 2^e_r (so
+ * every block scale fits E4M3).  Block b of row r: code = E4M3(amax_b / 6 *
+ * 2^-e_r) (nearest, ties to even, the FP8 encoder above), s = its value; each
+ * weight w -> E2M1(w * 2^-e_r / s) (nearest, ties to even, saturating at
+ * +-6; 0 when s is 0).  A dequantized weight E2M1 * s * 2^e_r has at most six
+ * significant bits: exactly a BF16 value. */
+Q3O_API uint8_t q3o_e2m1(float x) {
+    const uint8_t s = signbit(x) ? 0x8 : 0x0;
+    const float a = fabsf(x);
+    uint8_t c;
+    if (a <= 0.25f) c = 0;          /* the ties go to the even code */
+    else if (a < 0.75f) c = 1;
+    else if (a <= 1.25f) c = 2;
+    else if (a < 1.75f) c = 3;
+    else if (a <= 2.5f) c = 4;
+    else if (a < 3.5f) c = 5;
+    else if (a <= 5.0f) c = 6;
+    else c = 7;                     /* 6, saturating */
+    return (uint8_t)(s | c);
+}
+
+Q3O_API float q3o_e2m1_value(uint8_t q) {
+    static const float mag[8] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f};
+    const float v = mag[q & 7];
+    return (q & 8) ? -v : v;
+}
+
+/* Row r: q[r, c] E2M1 codes (one per byte), bscale[r, c / 16] E4M3 codes,
+ * rscale[r] = 2^e_r.  cols % 16 == 0. */
+Q3O_API void q3o_quantize_nvfp4(const uint16_t* w, size_t rows, size_t cols, uint8_t* q, uint8_t* bscale,
+                                float* rscale) {
+    for (size_t r = 0; r < rows; ++r) {
+        const uint16_t* wr = w + r * cols;
+        float mx = 0.0f;
+        for (size_t c = 0; c < cols; ++c) mx = fmaxf(mx, fabsf(bf2f(wr[c])));
+        int e = 0;
+        if (mx > 0.0f) {
+            int k;
+            const float f = frexpf(mx, &k);          /* mx = f * 2^k; 6 * 448 = 2688 = 0.65625 * 2^12 */
+            e = (f <= 0.65625f) ? k - 12 : k - 11;
+        }
+        rscale[r] = ldexpf(1.0f, e);
+        for (size_t b = 0; b < cols / 16; ++b) {
+            float amax = 0.0f;
+            for (size_t j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(bf2f(wr[16 * b + j])));
+            const uint8_t sc = q3o_e4m3(ldexpf(amax / 6.0f, -e));
+            const float sv = q3o_e4m3_value(sc);
+            bscale[r * (cols / 16) + b] = sc;
+            for (size_t j = 0; j < 16; ++j) {
+                const float x = bf2f(wr[16 * b + j]);
+                q[r * cols + 16 * b + j] = sv > 0.0f ? q3o_e2m1(ldexpf(x, -e) / sv) : (uint8_t)(signbit(x) ? 8 : 0);
+            }
+        }
+    }
+}
+
+/* In place: w <- bf16(dequant(quant(w))) (exact, see above). */
+static void nvfp4_roundtrip(uint16_t* w, size_t rows, size_t cols) {
+    uint8_t* q = (uint8_t*)malloc(cols);
+    uint8_t* bs = (uint8_t*)malloc(cols / 16);
+    float rs;
+    for (size_t r = 0; r < rows; ++r) {
+        q3o_quantize_nvfp4(w + r * cols, 1, cols, q, bs, &rs);
+        for (size_t c = 0; c < cols; ++c)
+            w[r * cols + c] = f2bf(q3o_e2m1_value(q[c]) * q3o_e4m3_value(bs[c / 16]) * rs);
+    }
+    free(q);
+    free(bs);
+}
+
 /* ---------------------------------------------------------------- model */
 
 typedef struct {
@@ -430,6 +504,29 @@ Q3O_API void q3o_model_quantize_fp8(q3o_model* m) {
         fp8_roundtrip(L->gate, I, H);
         fp8_roundtrip(L->up, I, H);
         fp8_roundtrip(L->down, H, I);
+    }
+}
+
+/* The model an NVFP4-weight engine computes: every GEMV matrix replaced by its
+ * NVFP4 round trip (the embedding lookup keeps the BF16 table). */
+Q3O_API void q3o_model_quantize_nvfp4(q3o_model* m) {
+    const q3o_config* c = &m->cfg;
+    size_t H = c->hidden, I = c->inter, hd = c->head_dim;
+    size_t qd = c->q_heads * hd, kd = c->kv_heads * hd;
+    if (m->lm_head == m->embed) {
+        m->lm_head = (uint16_t*)malloc(c->vocab * H * 2);
+        memcpy(m->lm_head, m->embed, c->vocab * H * 2);
+    }
+    nvfp4_roundtrip(m->lm_head, c->vocab, H);
+    for (size_t l = 0; l < c->layers; ++l) {
+        q3o_layer* L = &m->layer[l];
+        nvfp4_roundtrip(L->q_proj, qd, H);
+        nvfp4_roundtrip(L->k_proj, kd, H);
+        nvfp4_roundtrip(L->v_proj, kd, H);
+        nvfp4_roundtrip(L->o_proj, H, qd);
+        nvfp4_roundtrip(L->gate, I, H);
+        nvfp4_roundtrip(L->up, I, H);
+        nvfp4_roundtrip(L->down, H, I);
     }
 }
 
