@@ -57,8 +57,8 @@ def parse_args(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--nccl", action="store_true", help="tensor parallel: exchange partial sums with NCCL "
                     "instead of peer-memory stores fused into the GEMVs")
-    ap.add_argument("--tune", default="", help="comma list of opt-in decode variants (q3_engine_set_tuning): "
-                    "batched_poll, no_grid_wait, tp_prefill, fp8_prefill, or all")
+    ap.add_argument("--tune", default="", help="comma list of opt-in prefill variants (q3_engine_set_tuning): "
+                    "tp_prefill, fp8_prefill, or all")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "fp8", "nvfp4"],
                     help="fp8: E4M3 GEMV matrices with per-row power-of-two scales; nvfp4: E2M1 with E4M3 scales "
                          "per 16 columns and power-of-two row scales (each the quantized model, not the "

@@ -286,32 +286,22 @@ Q3_API int q3_engine_generate(q3_engine* e, const uint32_t* prompt_host, size_t 
  * after one prefill. */
 Q3_API int q3_engine_set_position(q3_engine* e, size_t pos);
 
-/* Opt-in variants of the CUDA-graph decode path (no counterpart in the
- * reference), as bit flags; 0, the default, selects the kernels described
- * above.  Every flag keeps the step's arithmetic and its order, so tokens
- * and logits are bit-identical with and without it.  Setting them
- * re-records the step graph at the next step.
- *   Q3_TUNE_PEER_BATCHED_POLL: tensor parallel through peer memory -- the
- *     RMSNorm prologue that sums the ranks' partial rows issues the loads of
- *     up to four ranks at once instead of one rank per round trip;
- *   Q3_TUNE_PEER_NO_GRID_WAIT: those prologues start on the (value, tag)
- *     pairs alone, without griddepcontrol.wait on the producing GEMV;
+/* Opt-in variants of the prefill (no counterpart in the reference), as bit
+ * flags; 0, the default, prefills tensor-parallel and packed-weight engines
+ * through one decode step per prompt token.
  *   Q3_TUNE_TP_PREFILL: tensor-parallel engines prefill with the batched
  *     tcgen05 GEMMs on their shards (row-parallel outputs exchanged as fp32
- *     partials) instead of one decode step per prompt token.  Unlike the
- *     other flags this changes the fp32 order of the prefill's sums (GEMM
+ *     partials).  This changes the fp32 order of the prefill's sums (GEMM
  *     instead of GEMV), exactly as the single-GPU batched prefill does;
- *   Q3_TUNE_FP8_PREFILL: FP8-weight engines prefill with the batched tcgen05
- *     GEMMs too, each matrix first expanded into a BF16 scratch copy (E4M3
- *     times a power-of-two row scale is an exact BF16 value, so the GEMMs
- *     see exactly the FP8 model's weights), instead of one decode step per
- *     prompt token.  The same change of fp32 order as above.
+ *   Q3_TUNE_FP8_PREFILL: FP8- and NVFP4-weight engines prefill with the
+ *     batched tcgen05 GEMMs too, each matrix first expanded into a BF16
+ *     scratch copy (its dequantized values are exact BF16 values, so the
+ *     GEMMs see exactly the quantized model's weights).  The same change of
+ *     fp32 order as above.
  * Unknown bits return Q3_ERR_INVALID. */
-#define Q3_TUNE_PEER_BATCHED_POLL 0x1u
-#define Q3_TUNE_PEER_NO_GRID_WAIT 0x2u
 #define Q3_TUNE_TP_PREFILL 0x10u
 #define Q3_TUNE_FP8_PREFILL 0x20u
-#define Q3_TUNE_ALL 0x33u /* bits 0x4 and 0x8 are unused (invalid) */
+#define Q3_TUNE_ALL 0x30u /* the lower bits are unused (invalid) */
 Q3_API int q3_engine_set_tuning(q3_engine* e, uint32_t flags);
 Q3_API int q3_engine_tuning(q3_engine* e, uint32_t* flags);
 

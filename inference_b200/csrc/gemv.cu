@@ -213,28 +213,6 @@ __device__ __forceinline__ void ld_pairs(const unsigned long long* p, unsigned l
     asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 
-// Re-reads the 8 (value, tag) pairs at p into q, which holds a first read,
-// until all carry `tag`; bounded like every peer wait, and it gives up at once
-// once another wait has recorded a failure.
-__device__ __forceinline__ void poll_pairs(const unsigned long long* p, unsigned long long (&q)[8], uint32_t tag,
-                                           uint32_t* err) {
-    for (uint32_t polls = 0;; ++polls) {
-        bool all = true;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) all = all && static_cast<uint32_t>(q[e] >> 32) == tag;
-        if (all) return;
-        if ((polls & 1023) == 1023 && *reinterpret_cast<volatile uint32_t*>(err)) return;
-        if (polls > kPeerPolls) {
-            record_error(err, DEV_PEER_WAIT_TIMEOUT);
-            return;
-        }
-        __nanosleep(32);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) ld_pairs(p + 2 * e, q[2 * e], q[2 * e + 1]);
-    }
-}
-constexpr int kPollBatch = 4;  // ranks whose pairs one thread has in flight at once (Q3_TUNE_PEER_BATCHED_POLL)
-
 // Consumer side: every CTA waits (bounded) until all ranks filled the slot of
 // exchange s, the one the kernel before produced.
 __device__ __forceinline__ void peer_wait(const PeerLinks& x, unsigned long long s, uint32_t* err) {
@@ -345,22 +323,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
             if (tid + k * kThreads < kv8) wpre[k] = reinterpret_cast<const uint4*>(a.norm_w)[tid + k * kThreads];
     }
 
-    // Q3_TUNE_PEER_NO_GRID_WAIT: an RMSNorm prologue over the ranks' partial rows
-    // needs nothing from the kernel just before it (the producing GEMV) beyond
-    // those rows, whose tags say when they are there.  What it reads besides
-    // (the residual rows, the position, the step counter) was written, and
-    // what it overwrites (the other residual buffer, q and the raw k rows, a V
-    // slot, the SwiGLU rows, the logits) was last read, two or more launches
-    // back, by a launch that has done so before this grid starts: either the
-    // chain of waits covers it (a kernel that waits triggers its dependents
-    // only after its wait), or a kernel without the wait stands in between,
-    // whose CTAs read every partial row of the launch before them -- rows that
-    // launch's CTAs store only after their own reads (x is read in the
-    // prologue, partial rows are stored in the epilogue).  The layer-0 QKV GEMV
-    // (the embedding prologue) keeps its wait: the position it reads is
-    // advanced by the lm_head launch just before it.
-    const bool grid_wait = !(pro == PRO_RESID_NORM && a.peer.world && (a.tune & Q3_TUNE_PEER_NO_GRID_WAIT));
-    if (grid_wait) pdl_wait();
+    pdl_wait();
     pdl_trigger();
     if (tracing && tid == 0) tr_c1 = clock64();
     // the residual rows this thread updates in the epilogue (first pass), read now
@@ -431,32 +394,7 @@ __global__ void __launch_bounds__(kThreads, Q3_GEMV_MIN_BLOCKS) gemv_kernel(cons
                 ss += v1.x * v1.x + v1.y * v1.y + v1.z * v1.z + v1.w * v1.w;
             } else if (pro == PRO_RESID_NORM) {
                 float4 v0, v1;
-                if (parts && (a.tune & Q3_TUNE_PEER_BATCHED_POLL)) {
-                    // the same sums in the same order, with the first reads of kPollBatch
-                    // ranks in flight together (one round trip per batch, not per rank)
-                    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                    for (int rg = 0; rg < a.peer.world; rg += kPollBatch) {
-                        unsigned long long q[kPollBatch][8];
-#pragma unroll
-                        for (int b = 0; b < kPollBatch; ++b) {
-                            if (rg + b < a.peer.world) {
-                                const unsigned long long* pr = parts + static_cast<size_t>(rg + b) * a.peer.H + 8 * i;
-#pragma unroll
-                                for (int e = 0; e < 4; ++e) ld_pairs(pr + 2 * e, q[b][2 * e], q[b][2 * e + 1]);
-                            }
-                        }
-#pragma unroll
-                        for (int b = 0; b < kPollBatch; ++b) {
-                            if (rg + b < a.peer.world) {
-                                poll_pairs(parts + static_cast<size_t>(rg + b) * a.peer.H + 8 * i, q[b], tag, a.err);
-#pragma unroll
-                                for (int e = 0; e < 8; ++e) acc[e] += __uint_as_float(static_cast<uint32_t>(q[b][e]));
-                            }
-                        }
-                    }
-                    v0 = make_float4(acc[0], acc[1], acc[2], acc[3]);
-                    v1 = make_float4(acc[4], acc[5], acc[6], acc[7]);
-                } else if (parts) {
+                if (parts) {
                     // sum of the ranks' partials in rank order (the same bits on every rank),
                     // each pair read until it carries this exchange's tag (bounded)
                     float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};

@@ -136,9 +136,8 @@ class Engine:
 
         return generate_text(self, tokenizer, prompt)
 
-    # opt-in variants of the CUDA-graph decode path (include/q3_sm100a.h, q3_engine_set_tuning)
-    TUNE_FLAGS = {"batched_poll": 0x1, "no_grid_wait": 0x2,
-                  "tp_prefill": 0x10, "fp8_prefill": 0x20}
+    # opt-in variants of the prefill (include/q3_sm100a.h, q3_engine_set_tuning)
+    TUNE_FLAGS = {"tp_prefill": 0x10, "fp8_prefill": 0x20}
 
     @property
     def tuning(self) -> int:

@@ -1,13 +1,14 @@
-"""Opt-in variants of the decode path (q3_engine_set_tuning).
+"""Determinism of the decode path (race detection) and the opt-in prefill
+variants (q3_engine_set_tuning).
 
-The decode variants reorder no arithmetic, so every logit, argmax and KV slot
-must be bit-identical to the default kernels: on 2 GPUs, the peer-exchange
-prologue with batched rank reads and without the grid-dependency wait.
-The batched prefills of tensor-parallel and of FP8-weight engines change the
-fp32 order of the prefill's sums (GEMMs instead of GEMVs, as the single-GPU
-prefill does), so they are held to the oracle like test_gpu_prefill.py: KV
-slots of the prefilled positions and the teacher-forced logits of the decode
-steps after it.
+Every cross-CTA and cross-rank combination in the decode kernels runs in a
+fixed order, so two independent runs on the same weights and ids must agree
+bit for bit in every logit, argmax and KV slot -- on one GPU and across 2
+tensor-parallel ranks.  The batched prefills of tensor-parallel and of
+packed-weight engines change the fp32 order of the prefill's sums (GEMMs
+instead of GEMVs, as the single-GPU prefill does), so they are held to the
+oracle like test_gpu_prefill.py: KV slots of the prefilled positions and the
+teacher-forced logits of the decode steps after it.
 """
 import datetime
 import os
@@ -20,7 +21,6 @@ from gpu_util import assert_logits_close, assert_within_spread, bf, paired_no_wo
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-DECODE_FLAGS = 0x1 | 0x2  # batched_poll | no_grid_wait
 TP_PREFILL = 0x10
 
 
@@ -35,12 +35,11 @@ def _cos(a, b):
                                                            (8, 32, 4096, 12288)])
 @pytest.mark.parametrize("weights", ["bf16", "fp8"])
 def test_decode_is_deterministic(kv_heads, q_heads, hidden, inter, weights):
-    """Race detection: two engines on the same weights and ids, one with the
-    (on one GPU inert) peer-exchange flags set, produce bit-identical logits,
-    argmax and KV slots at every step, at positions from 0 to the end of an
-    8192-slot cache (every page boundary the windows cross, up to 8 pages per
-    split).  Every cross-CTA combination in the kernels is in a fixed order, so
-    any difference is a race."""
+    """Race detection: two engines on the same weights and ids produce
+    bit-identical logits, argmax and KV slots at every step, at positions from
+    0 to the end of an 8192-slot cache (every page boundary the windows cross,
+    up to 8 pages per split).  Every cross-CTA combination in the kernels is in
+    a fixed order, so any difference is a race."""
     from inference_b200 import Engine, Qwen3Config, prompt_ids
 
     cfg = Qwen3Config(f"gqa{q_heads // kv_heads}-kv{kv_heads}-h{hidden}-l2", hidden=hidden, inter=inter, layers=2,
@@ -48,12 +47,10 @@ def test_decode_is_deterministic(kv_heads, q_heads, hidden, inter, weights):
     cap = 8192
     ids = prompt_ids(cap, seed=1)
     runs = {}
-    for flags in (0, DECODE_FLAGS):
+    for run in (0, 1):
         logits, kv = [], []
         with Engine(cfg, capacity=cap, weights=weights) as e:
             e.init_synthetic(0)
-            e.tuning = flags
-            assert e.tuning == flags
             e.set_tokens(ids)
 
             def window(n):
@@ -70,8 +67,8 @@ def test_decode_is_deterministic(kv_heads, q_heads, hidden, inter, weights):
             e.fill_kv(8180)
             window(11)         # 8180..8190: 128 pages, 8 per split
             hist = e.argmax_history(8191)
-        runs[flags] = (logits, kv, hist)
-    base, tuned = runs[0], runs[DECODE_FLAGS]
+        runs[run] = (logits, kv, hist)
+    base, tuned = runs[0], runs[1]
     for i, (a, b) in enumerate(zip(base[0], tuned[0])):
         assert np.array_equal(a, b), f"step {i}: logits differ"
     for i, ((k0, v0), (k1, v1)) in enumerate(zip(base[1], tuned[1])):
@@ -210,13 +207,14 @@ def _run_tp(tmp_path, tag, name, mode, flags, n_pre, world=2):
 
 @pytest.mark.timeout(600)
 @pytest.mark.parametrize("name", ["qwen3_0p6b", "qwen3_8b_l2"])
-def test_tp_decode_variants_bit_identical(tmp_path, name):
+def test_tp_decode_is_deterministic(tmp_path, name):
+    """Two independent 2-rank runs (peer exchange): bit-identical on every rank."""
     import torch
 
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     base = _run_tp(tmp_path, "base", name, "peer", 0, 0)
-    tuned = _run_tp(tmp_path, "tuned", name, "peer", DECODE_FLAGS, 0)
+    tuned = _run_tp(tmp_path, "again", name, "peer", 0, 0)
     for r in range(2):
         for key in base[r]:
             assert np.array_equal(base[r][key], tuned[r][key]), (r, key)
