@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "engine_state.hpp"
+#include "page_pool.hpp"
 
 namespace q3 {
 namespace {
@@ -81,8 +82,7 @@ struct q3_batch {
         int row = -1;                // its row in the last step (logits), -1 if none
     };
     std::vector<Seq> seqs;
-    std::vector<int> refs;       // per physical page
-    std::vector<int32_t> free_pages;
+    q3::PagePool pool{0};
     std::vector<int32_t> rows_host;  // the rows of the last uploaded step
     std::map<int, cudaGraphExec_t> graphs;  // one step of B rows, by B
 };
@@ -171,18 +171,6 @@ int step_graph(q3_batch* b, int B, cudaGraphExec_t* out) {
     return Q3_OK;
 }
 
-int take_page(q3_batch* b, int32_t* out) {
-    if (b->free_pages.empty()) return fail(Q3_ERR_OOM, "q3_batch: KV page pool exhausted");
-    *out = b->free_pages.back();
-    b->free_pages.pop_back();
-    b->refs[*out] = 1;
-    return Q3_OK;
-}
-
-void drop_page(q3_batch* b, int32_t p) {
-    if (--b->refs[p] == 0) b->free_pages.push_back(p);
-}
-
 int seq_slot(q3_batch* b, uint32_t id, q3_batch::Seq** out) {
     if (id >= b->seqs.size() || !b->seqs[id].live) return fail(Q3_ERR_INVALID, "q3_batch: no such sequence");
     *out = &b->seqs[id];
@@ -263,8 +251,7 @@ int q3_batch_create(q3_engine* e, uint32_t max_seqs, uint32_t pool_pages, q3_bat
         cudaMemset(b->tok, 0, S * b->cap * 4) != cudaSuccess)
         return bail(fail(Q3_ERR_CUDA, "q3_batch_create: cudaMemset failed"));
     b->seqs.resize(S);
-    b->refs.assign(pool_pages, 0);
-    for (int p = static_cast<int>(pool_pages) - 1; p >= 0; --p) b->free_pages.push_back(p);
+    b->pool = PagePool(static_cast<int>(pool_pages));
     *out = b;
     return Q3_OK;
 }
@@ -292,15 +279,7 @@ int q3_batch_add(q3_batch* b, const uint32_t* prompt, size_t n, size_t max_len, 
     Q3_TRY_STATUS(free_slot(b, &slot));
     q3_batch::Seq q;
     const int pages = static_cast<int>((max_len + kPageSize - 1) / kPageSize);
-    for (int i = 0; i < pages; ++i) {
-        int32_t p = 0;
-        const int rc = take_page(b, &p);
-        if (rc != Q3_OK) {
-            for (int32_t t : q.pages) drop_page(b, t);
-            return rc;
-        }
-        q.pages.push_back(p);
-    }
+    if (!b->pool.take_n(pages, q.pages)) return fail(Q3_ERR_OOM, "q3_batch: KV page pool exhausted");
     q.live = true;
     q.kv_len = static_cast<int>(n) - 1;
     q.forced = static_cast<int>(n);
@@ -341,30 +320,19 @@ int q3_batch_fork(q3_batch* b, uint32_t src, uint32_t* id) {
     q.kv_len = from->kv_len;
     q.forced = std::max(from->forced, from->kv_len + 1);
     q.max_len = from->max_len;
-    const int full = from->kv_len / kPageSize;  // pages entirely before the position: shared, never written again
-    for (size_t i = 0; i < from->pages.size(); ++i) {
-        if (static_cast<int>(i) < full) {
-            ++b->refs[from->pages[i]];
-            q.pages.push_back(from->pages[i]);
-            continue;
-        }
-        int32_t p = 0;
-        const int rc = take_page(b, &p);
-        if (rc != Q3_OK) {
-            for (int32_t t : q.pages) drop_page(b, t);
-            return rc;
-        }
-        q.pages.push_back(p);
-    }
-    // the partial page (positions full * 64 .. kv_len - 1) is copied, every layer
-    if (from->kv_len % kPageSize) {
+    // pages entirely before the position: shared, never written again; the rest fresh
+    int copy = -1;
+    if (!b->pool.fork(from->pages, from->kv_len, kPageSize, q.pages, &copy))
+        return fail(Q3_ERR_OOM, "q3_batch: KV page pool exhausted");
+    // the partial page (its positions before kv_len) is copied, every layer
+    if (copy >= 0) {
         const size_t bytes = b->page_elems * 2;
         for (size_t l = 0; l < e->layers.size(); ++l) {
-            Q3_CUDA(cudaMemcpyAsync(b->k_pools[l] + q.pages[full] * b->page_elems,
-                                    b->k_pools[l] + from->pages[full] * b->page_elems, bytes,
+            Q3_CUDA(cudaMemcpyAsync(b->k_pools[l] + q.pages[copy] * b->page_elems,
+                                    b->k_pools[l] + from->pages[copy] * b->page_elems, bytes,
                                     cudaMemcpyDeviceToDevice, e->stream));
-            Q3_CUDA(cudaMemcpyAsync(b->v_pools[l] + q.pages[full] * b->page_elems,
-                                    b->v_pools[l] + from->pages[full] * b->page_elems, bytes,
+            Q3_CUDA(cudaMemcpyAsync(b->v_pools[l] + q.pages[copy] * b->page_elems,
+                                    b->v_pools[l] + from->pages[copy] * b->page_elems, bytes,
                                     cudaMemcpyDeviceToDevice, e->stream));
         }
     }
@@ -402,7 +370,7 @@ int q3_batch_release(q3_batch* b, uint32_t id) {
     Q3_CUDA(cudaSetDevice(b->e->device));
     // steps in flight may still read its pages
     Q3_CUDA(cudaStreamSynchronize(b->e->stream));
-    for (int32_t p : q->pages) drop_page(b, p);
+    b->pool.drop_all(q->pages);
     *q = q3_batch::Seq();
     return Q3_OK;
 }
@@ -467,7 +435,7 @@ int q3_batch_logits(q3_batch* b, uint32_t id, uint16_t* out) {
 
 int q3_batch_info(q3_batch* b, uint32_t id, size_t* position, size_t* free_pages) {
     Q3_CHECK(b, "q3_batch_info: null argument");
-    if (free_pages) *free_pages = b->free_pages.size();
+    if (free_pages) *free_pages = static_cast<size_t>(b->pool.free_count());
     if (position) {
         q3_batch::Seq* q = nullptr;
         Q3_TRY_STATUS(seq_slot(b, id, &q));
