@@ -93,6 +93,10 @@ Q3_API int q3_gemv_e4m3(const uint16_t* x_dev, const uint8_t* w8_dev, const floa
  * SM count) and the row scales; q3_dequant_nvfp4 gives back the exact BF16
  * values of the packed matrix; q3_gemv_nvfp4 is y = W x on it.  n_in % 64 == 0. */
 Q3_API size_t q3_nvfp4_packed_bytes(size_t n_out, size_t n_in);
+/* Byte offset in that layout (for num_sms SMs) of the byte holding weight
+ * (row, col) -- the low nibble for an even col -- or, with scale != 0, of
+ * the E4M3 scale of col's 16-column block; SIZE_MAX when out of range. */
+Q3_API size_t q3_nvfp4_packed_offset(size_t n_out, size_t n_in, int num_sms, size_t row, size_t col, int scale);
 Q3_API int q3_quantize_nvfp4(const uint16_t* w_dev, size_t n_out, size_t n_in, uint8_t* packed_dev,
                              float* row_scale_dev, void* stream);
 Q3_API int q3_dequant_nvfp4(const uint8_t* packed_dev, const float* row_scale_dev, size_t n_out, size_t n_in,

@@ -25,6 +25,7 @@ SIGNATURES = {
     "q3_gemv": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _vp]),
     "q3_gemm": (C.c_int, [_u16p, _u16p, _u16p, _sz, _sz, _sz, _vp]),
     "q3_nvfp4_packed_bytes": (_sz, [_sz, _sz]),
+    "q3_nvfp4_packed_offset": (_sz, [_sz, _sz, C.c_int, _sz, _sz, C.c_int]),
     "q3_quantize_nvfp4": (C.c_int, [_u16p, _sz, _sz, _vp, _vp, _vp]),
     "q3_dequant_nvfp4": (C.c_int, [_vp, _vp, _sz, _sz, _u16p, _vp]),
     "q3_gemv_nvfp4": (C.c_int, [_u16p, _vp, _vp, _u16p, _sz, _sz, _vp]),

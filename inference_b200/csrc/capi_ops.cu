@@ -155,6 +155,15 @@ size_t q3_nvfp4_packed_bytes(size_t n_out, size_t n_in) {
     return f4_packed_bytes(static_cast<int>(n_out), static_cast<int>(n_in));
 }
 
+size_t q3_nvfp4_packed_offset(size_t n_out, size_t n_in, int num_sms, size_t row, size_t col, int scale) {
+    if (n_out == 0 || n_in == 0 || n_in % 64 != 0 || n_in > 32768 || n_out >= (1u << 30) || num_sms <= 0 ||
+        row >= n_out || col >= n_in)
+        return SIZE_MAX;
+    const F8Pack L = f4_pack_for(static_cast<int>(n_out), static_cast<int>(n_in), EPI_STORE, num_sms);
+    return scale ? f4_scale_offset(L, static_cast<int>(row), static_cast<int>(col))
+                 : f4_nibble_offset(L, static_cast<int>(row), static_cast<int>(col));
+}
+
 int q3_quantize_nvfp4(const uint16_t* w, size_t n_out, size_t n_in, uint8_t* packed, float* row_scale,
                       void* stream) {
     Q3_CHECK(w && packed && row_scale, "q3_quantize_nvfp4: null pointer");

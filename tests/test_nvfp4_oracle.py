@@ -52,3 +52,35 @@ def test_nvfp4_dequantized_weights_are_bf16_and_close(oracle):
     assert (np.abs(deq - x) <= 0.25 * amax + 1e-30).all()
     # every block scale fits E4M3 (no saturation at 448)
     assert (s <= 448.0).all()
+
+
+@pytest.mark.parametrize("n,k,sms", [(300, 512, 148), (37, 64, 4), (4096, 192, 148), (66, 1024, 7), (19, 2560, 3)])
+def test_packed_nvfp4_layout_is_a_tiled_bijection(n, k, sms):
+    """q3_nvfp4_packed_offset (the NVFP4 GEMV's weight layout, the same
+    functions the device quantizer and expansion use): every pair of columns
+    has its own byte and every 16-column block its own scale byte, all inside
+    q3_nvfp4_packed_bytes; a block's nibbles are 8 contiguous bytes; and each
+    16-row x 512-column item of a CTA's row band is one contiguous run of
+    rows x 288 bytes (one bulk copy), nibbles first, scales after."""
+    from inference_b200 import lib
+
+    L = lib()
+    size = L.q3_nvfp4_packed_bytes(n, k)
+    assert size == n * ((k + 511) // 512) * 288
+    nib = np.array([[L.q3_nvfp4_packed_offset(n, k, sms, r, c, 0) for c in range(0, k, 2)] for r in range(n)],
+                   np.int64)
+    sc = np.array([[L.q3_nvfp4_packed_offset(n, k, sms, r, c, 1) for c in range(0, k, 16)] for r in range(n)],
+                  np.int64)
+    every = np.concatenate([nib.ravel(), sc.ravel()])
+    assert every.min() >= 0 and every.max() < size
+    assert len(np.unique(every)) == every.size  # nibble and scale bytes all distinct
+    # a column and its odd neighbour share a byte
+    assert L.q3_nvfp4_packed_offset(n, k, sms, 0, 1, 0) == L.q3_nvfp4_packed_offset(n, k, sms, 0, 0, 0)
+    # a 16-column block: 8 contiguous bytes
+    for j in range(1, 8):
+        assert (nib[:, j::8] == nib[:, 0::8][:, :nib[:, j::8].shape[1]] + j).all()
+    # items: the bytes of rows sharing a tile and a 512-column chunk form one contiguous run
+    used = np.zeros(size, bool)
+    used[every] = True
+    assert used[: n * (k // 512) * 288].all() if k % 512 == 0 else True
+    assert L.q3_nvfp4_packed_offset(n, k, sms, n, 0, 0) == 2**64 - 1  # out of range
