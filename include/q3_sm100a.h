@@ -172,9 +172,9 @@ Q3_API int q3_argmax(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, 
  * synchronisation.  Its scratch is a 32 KB array compiled into the library
  * (kept by every GPU that loads it until the process exits), so n is limited
  * to 16,777,216 logits; larger inputs return Q3_ERR_INVALID.  The first call
- * on a device looks up the array's device address and caches it: make that
- * call before any stream capture, and do not use the library across a
- * cudaDeviceReset of the device.  Calls share the array, so calls that
+ * on a device looks up the array's device address (cudaGetSymbolAddress) and
+ * caches it, so do not use the library across a cudaDeviceReset of the
+ * device.  Calls share the array, so calls that
  * overlap on the GPU (unordered streams) race. */
 Q3_API int q3_argmax_noalloc(const uint16_t* logits_dev, size_t n, uint32_t* index_dev, void* stream);
 

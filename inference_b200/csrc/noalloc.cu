@@ -17,8 +17,7 @@
 //
 // The array's host-side name is not a device address.  The first call on each
 // device, with that device current, resolves the address once with
-// cudaGetSymbolAddress; make that first call before any stream capture.  The
-// address is cached for the life of the process: the library must not be used
+// cudaGetSymbolAddress.  The address is cached for the life of the process: the library must not be used
 // across a cudaDeviceReset of that device (the reset frees the module's
 // memory, and later calls would launch with the stale address).
 #include <mutex>
