@@ -132,10 +132,11 @@ def test_tuning_rejects_unknown_bits():
             e.tuning = 0x400
         with pytest.raises(ValueError):
             e.tuning = ["no_such_flag"]
-        with pytest.raises(Q3Error):
-            e.tuning = 0x4  # a retired bit
+        for retired in (0x1, 0x2, 0x4, 0x8):
+            with pytest.raises(Q3Error):
+                e.tuning = retired
         e.tuning = ["all"]
-        assert e.tuning == 0x33
+        assert e.tuning == 0x30
         e.tuning = 0
         assert e.tuning == 0
 
