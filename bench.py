@@ -643,7 +643,7 @@ def run_batch(a, cfg, prompt_len, capacity):
         "config": {"workload": f"{a.workload}-batch{B}", "model": cfg.name, "prompt": prompt_len,
                    "decode_tokens_per_sequence_per_step": window, "sequences": B,
                    "positions": [p_start, p_start + window * a.steps - 1],
-                   "decode_path": "batched rows: tcgen05 GEMMs, per-row split-KV attention, eager launches"},
+                   "decode_path": "batched rows: tcgen05 GEMMs, per-row split-KV attention, one CUDA graph per row count"},
         "per_sequence_tok_s": round(tok_s / B, 3),
         "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(gbs / peak, 4), "bytes_per_step": int(step_bytes),
