@@ -32,7 +32,7 @@ typedef enum q3_status {
     Q3_ERR_INVALID = 1,     /* bad shape, alignment or argument */
     Q3_ERR_CUDA = 2,        /* a CUDA runtime call failed */
     Q3_ERR_UNSUPPORTED = 3, /* valid request this build does not handle */
-    Q3_ERR_OOM = 4,         /* device allocation failed */
+    Q3_ERR_OOM = 4,         /* device (or host) allocation failed */
     Q3_ERR_DEVICE = 5,      /* a kernel recorded an error (e.g. a bounded wait ran out) */
     Q3_ERR_NCCL = 6,        /* a NCCL call failed */
 } q3_status;

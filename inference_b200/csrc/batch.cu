@@ -8,8 +8,8 @@
 // each row's own position and page table), then the final RMSNorm, the lm_head
 // GEMM and a per-row greedy argmax.  Token histories, positions and page tables
 // live in device memory, so a step of B rows is one CUDA graph (captured once
-// per B; the attention split count comes from the capacity, not the positions)
-// and steps run back to back with no host round trip.
+// per B; the attention split count comes from B and the capacity, not from the
+// positions) and steps run back to back with no host round trip.
 //
 // KV memory is a pool of 64-position pages per layer shared by all sequences.
 // A sequence owns ceil(max_len / 64) page-table entries; q3_batch_fork starts a
@@ -287,8 +287,16 @@ int q3_batch_add(q3_batch* b, const uint32_t* prompt, size_t n, size_t max_len, 
     b->seqs[slot] = q;
     std::vector<int32_t> ids(prompt, prompt + n);
     int32_t* tok_row = b->tok + static_cast<size_t>(slot) * b->cap;
-    Q3_CUDA(cudaMemcpyAsync(tok_row, ids.data(), n * 4, cudaMemcpyHostToDevice, e->stream));
-    Q3_TRY_STATUS(upload_state(b, slot));
+    // a failure below leaves no sequence behind: the slot is freed and its pages returned
+    auto undo = [&](int rc) {
+        b->pool.drop_all(b->seqs[slot].pages);
+        b->seqs[slot] = q3_batch::Seq();
+        return rc;
+    };
+    const cudaError_t up = cudaMemcpyAsync(tok_row, ids.data(), n * 4, cudaMemcpyHostToDevice, e->stream);
+    if (up != cudaSuccess) return undo(fail(Q3_ERR_CUDA, std::string("q3_batch_add: ") + cudaGetErrorString(up)));
+    int rc = upload_state(b, slot);
+    if (rc != Q3_OK) return undo(rc);
     // Model::prefill (qwen3.hpp:168-173): positions [0, n - 1) through the batched rows
     for (int done = 0; done < static_cast<int>(n) - 1;) {
         RowsSpec R;
@@ -300,7 +308,10 @@ int q3_batch_add(q3_batch* b, const uint32_t* prompt, size_t n, size_t max_len, 
         R.v_pools = b->v_pools.data();
         R.pool_pages = b->pool_pages;
         R.max_pos = done + R.n - 1;
-        Q3_TRY_STATUS(forward_rows(e, R));
+        if ((rc = forward_rows(e, R)) != Q3_OK) {
+            cudaStreamSynchronize(e->stream);  // launches already queued may still write its pages
+            return undo(rc);
+        }
         done += R.n;
     }
     *id = slot;
@@ -324,23 +335,36 @@ int q3_batch_fork(q3_batch* b, uint32_t src, uint32_t* id) {
     int copy = -1;
     if (!b->pool.fork(from->pages, from->kv_len, kPageSize, q.pages, &copy))
         return fail(Q3_ERR_OOM, "q3_batch: KV page pool exhausted");
+    b->seqs[slot] = q;
+    // a failure below leaves no sequence behind: the slot is freed and its references dropped
+    auto undo = [&](int rc) {
+        cudaStreamSynchronize(e->stream);
+        b->pool.drop_all(b->seqs[slot].pages);
+        b->seqs[slot] = q3_batch::Seq();
+        return rc;
+    };
+    cudaError_t st = cudaSuccess;
     // the partial page (its positions before kv_len) is copied, every layer
     if (copy >= 0) {
         const size_t bytes = b->page_elems * 2;
-        for (size_t l = 0; l < e->layers.size(); ++l) {
-            Q3_CUDA(cudaMemcpyAsync(b->k_pools[l] + q.pages[copy] * b->page_elems,
-                                    b->k_pools[l] + from->pages[copy] * b->page_elems, bytes,
-                                    cudaMemcpyDeviceToDevice, e->stream));
-            Q3_CUDA(cudaMemcpyAsync(b->v_pools[l] + q.pages[copy] * b->page_elems,
-                                    b->v_pools[l] + from->pages[copy] * b->page_elems, bytes,
-                                    cudaMemcpyDeviceToDevice, e->stream));
+        for (size_t l = 0; l < e->layers.size() && st == cudaSuccess; ++l) {
+            st = cudaMemcpyAsync(b->k_pools[l] + q.pages[copy] * b->page_elems,
+                                 b->k_pools[l] + from->pages[copy] * b->page_elems, bytes, cudaMemcpyDeviceToDevice,
+                                 e->stream);
+            if (st == cudaSuccess)
+                st = cudaMemcpyAsync(b->v_pools[l] + q.pages[copy] * b->page_elems,
+                                     b->v_pools[l] + from->pages[copy] * b->page_elems, bytes,
+                                     cudaMemcpyDeviceToDevice, e->stream);
         }
     }
-    Q3_CUDA(cudaMemcpyAsync(b->tok + static_cast<size_t>(slot) * b->cap, b->tok + static_cast<size_t>(src) * b->cap,
-                            static_cast<size_t>(b->cap) * 4, cudaMemcpyDeviceToDevice, e->stream));
-    b->seqs[slot] = q;
-    Q3_TRY_STATUS(upload_state(b, slot));
-    Q3_CUDA(cudaStreamSynchronize(e->stream));
+    if (st == cudaSuccess)
+        st = cudaMemcpyAsync(b->tok + static_cast<size_t>(slot) * b->cap, b->tok + static_cast<size_t>(src) * b->cap,
+                             static_cast<size_t>(b->cap) * 4, cudaMemcpyDeviceToDevice, e->stream);
+    if (st != cudaSuccess) return undo(fail(Q3_ERR_CUDA, std::string("q3_batch_fork: ") + cudaGetErrorString(st)));
+    const int rc = upload_state(b, slot);
+    if (rc != Q3_OK) return undo(rc);
+    if ((st = cudaStreamSynchronize(e->stream)) != cudaSuccess)
+        return undo(fail(Q3_ERR_CUDA, std::string("q3_batch_fork: ") + cudaGetErrorString(st)));
     *id = slot;
     return Q3_OK;
 }

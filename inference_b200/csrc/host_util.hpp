@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <exception>
+#include <new>
 #include <string>
 
 #include "../../include/q3_sm100a.h"
@@ -46,5 +48,22 @@ size_t engine_capacity(const q3_engine* e);
         const int rc_ = (x);           \
         if (rc_ != Q3_OK) return rc_;  \
     } while (0)
+
+// Runs the body of a C entry point whose host work allocates in proportion to
+// its input (files, text): no C++ exception crosses the C ABI.  A failed host
+// allocation becomes Q3_ERR_OOM, any other exception Q3_ERR_INVALID with its
+// message.
+template <class F>
+int guarded(const char* fn, F&& body) noexcept {
+    try {
+        return body();
+    } catch (const std::bad_alloc&) {
+        return fail(Q3_ERR_OOM, std::string(fn) + ": host allocation failed");
+    } catch (const std::exception& ex) {
+        return fail(Q3_ERR_INVALID, std::string(fn) + ": " + ex.what());
+    } catch (...) {
+        return fail(Q3_ERR_INVALID, std::string(fn) + ": unexpected exception");
+    }
+}
 
 }  // namespace q3

@@ -232,15 +232,7 @@ bool collect(const std::string& path_in, std::vector<Tensor>& out, std::string& 
     return scan_file(path, out, err);
 }
 
-}  // namespace
-}  // namespace q3
-
-using namespace q3;
-
-extern "C" {
-
-int q3_safetensors_list(const char* path, char* out, size_t capacity, size_t* needed) {
-    Q3_CHECK(path && needed, "q3_safetensors_list: null argument");
+int list_impl(const char* path, char* out, size_t capacity, size_t* needed) {
     std::vector<q3::Tensor> ts;
     std::string err;
     if (!collect(path, ts, err)) return fail(Q3_ERR_INVALID, err);
@@ -258,8 +250,7 @@ int q3_safetensors_list(const char* path, char* out, size_t capacity, size_t* ne
     return Q3_OK;
 }
 
-int q3_engine_load_safetensors(q3_engine* e, const char* path, size_t* n_loaded) {
-    Q3_CHECK(e && path, "q3_engine_load_safetensors: null argument");
+int load_impl(q3_engine* e, const char* path, size_t* n_loaded) {
     std::vector<q3::Tensor> ts;
     std::string err;
     if (!collect(path, ts, err)) return fail(Q3_ERR_INVALID, err);
@@ -274,12 +265,15 @@ int q3_engine_load_safetensors(q3_engine* e, const char* path, size_t* n_loaded)
             const int fd = open(t.file.c_str(), O_RDONLY);
             Q3_CHECK(fd >= 0, "cannot open " + t.file);
             struct stat st {};
-            fstat(fd, &st);
-            m->size = static_cast<size_t>(st.st_size);
-            m->base = mmap(nullptr, m->size, PROT_READ, MAP_PRIVATE, fd, 0);
+            if (fstat(fd, &st) == 0 && st.st_size > 0) {
+                m->size = static_cast<size_t>(st.st_size);
+                m->base = mmap(nullptr, m->size, PROT_READ, MAP_PRIVATE, fd, 0);
+            }
             close(fd);
             Q3_CHECK(m->base != MAP_FAILED, "cannot map " + t.file);
         }
+        // the file may have changed since its header was read
+        Q3_CHECK(t.offset <= m->size && t.bytes <= m->size - t.offset, t.name + ": data past the end of " + t.file);
         // BF16 data must be 2-byte aligned for the row copies
         Q3_CHECK(t.offset % 2 == 0, t.name + ": misaligned data");
         const uint16_t* src = reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(m->base) + t.offset);
@@ -303,6 +297,23 @@ int q3_engine_load_safetensors(q3_engine* e, const char* path, size_t* n_loaded)
     Q3_CUDA(cudaDeviceSynchronize());
     if (n_loaded) *n_loaded = loaded.size();
     return Q3_OK;
+}
+
+}  // namespace
+}  // namespace q3
+
+using namespace q3;
+
+extern "C" {
+
+int q3_safetensors_list(const char* path, char* out, size_t capacity, size_t* needed) {
+    Q3_CHECK(path && needed, "q3_safetensors_list: null argument");
+    return guarded("q3_safetensors_list", [&]() -> int { return list_impl(path, out, capacity, needed); });
+}
+
+int q3_engine_load_safetensors(q3_engine* e, const char* path, size_t* n_loaded) {
+    Q3_CHECK(e && path, "q3_engine_load_safetensors: null argument");
+    return guarded("q3_engine_load_safetensors", [&]() -> int { return load_impl(e, path, n_loaded); });
 }
 
 }  // extern "C"

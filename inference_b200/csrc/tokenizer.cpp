@@ -29,6 +29,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <fstream>
+#include <memory>
 #include <queue>
 #include <sstream>
 #include <string>
@@ -321,11 +322,15 @@ int load(const std::string& path_in, q3_tokenizer& t) {
     const Json* rx = pat ? pat->get("Regex") : nullptr;
     if (!rx || rx->kind != Json::Str || rx->str != kQwen2Pattern)
         return fail(Q3_ERR_UNSUPPORTED, path + ": pre-tokenizer pattern is not the Qwen2 split pattern");
+    // ids are integers below 2^24 (Qwen3's vocabularies hold ~152k)
+    auto valid_id = [](const Json* v) {
+        return v && v->kind == Json::Num && v->num >= 0 && v->num < 16777216.0 &&
+               v->num == static_cast<double>(static_cast<uint32_t>(v->num));
+    };
     uint32_t max_id = 0;
     t.vocab.reserve(vocab->obj.size());
     for (const auto& kv : vocab->obj) {
-        if (kv.second.kind != Json::Num || kv.second.num < 0 || kv.second.num >= 16777216.0)
-            return fail(Q3_ERR_INVALID, path + ": bad vocabulary id for " + kv.first);
+        if (!valid_id(&kv.second)) return fail(Q3_ERR_INVALID, path + ": bad vocabulary id for " + kv.first);
         const uint32_t id = static_cast<uint32_t>(kv.second.num);
         t.vocab.emplace(kv.first, id);
         max_id = std::max(max_id, id);
@@ -335,7 +340,7 @@ int load(const std::string& path_in, q3_tokenizer& t) {
         for (const Json& a : added->arr) {
             const Json* id = a.get("id");
             const Json* content = a.get("content");
-            if (!id || id->kind != Json::Num || !content || content->kind != Json::Str || content->str.empty())
+            if (!valid_id(id) || !content || content->kind != Json::Str || content->str.empty())
                 return fail(Q3_ERR_INVALID, path + ": malformed added token");
             const uint32_t v = static_cast<uint32_t>(id->num);
             t.special.emplace_back(content->str, v);
@@ -495,63 +500,9 @@ int copy_out(const std::string& s, char* out, size_t capacity, size_t* needed) {
     return Q3_OK;
 }
 
-}  // namespace
-}  // namespace q3
-
-using namespace q3;
-
-extern "C" {
-
-int q3_tokenizer_load(const char* path, q3_tokenizer** out) {
-    Q3_CHECK(path && out, "q3_tokenizer_load: null argument");
-    *out = nullptr;
-    auto* t = new q3_tokenizer();
-    const int rc = load(path, *t);
-    if (rc != Q3_OK) {
-        delete t;
-        return rc;
-    }
-    *out = t;
-    return Q3_OK;
-}
-
-int q3_tokenizer_destroy(q3_tokenizer* t) {
-    delete t;
-    return Q3_OK;
-}
-
-int q3_tokenizer_encode(const q3_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t capacity,
-                        size_t* n_ids) {
-    Q3_CHECK(t && (text || len == 0) && n_ids, "q3_tokenizer_encode: null argument");
-    std::vector<uint32_t> v;
-    const int rc = encode(*t, std::string(text ? text : "", len), v);
-    if (rc != Q3_OK) return rc;
-    *n_ids = v.size();
-    if (!ids) return Q3_OK;
-    Q3_CHECK(capacity >= v.size(), "q3_tokenizer_encode: ids buffer too small");
-    std::copy(v.begin(), v.end(), ids);
-    return Q3_OK;
-}
-
-int q3_tokenizer_decode(const q3_tokenizer* t, const uint32_t* ids, size_t n, char* out, size_t capacity,
-                        size_t* needed) {
-    Q3_CHECK(t && (ids || n == 0), "q3_tokenizer_decode: null argument");
-    std::string s;
-    const int rc = decode(*t, ids, n, s);
-    if (rc != Q3_OK) return rc;
-    return copy_out(s, out, capacity, needed);
-}
-
-int q3_chat_template(const char* prompt, size_t len, char* out, size_t capacity, size_t* needed) {
-    Q3_CHECK(prompt || len == 0, "q3_chat_template: null argument");
-    return copy_out(chat_template(std::string(prompt ? prompt : "", len)), out, capacity, needed);
-}
-
-int q3_engine_generate_text(q3_engine* e, const q3_tokenizer* t, const char* prompt, size_t len, char** out,
-                            size_t* out_len) {
-    Q3_CHECK(e && t && (prompt || len == 0) && out && out_len, "q3_engine_generate_text: null argument");
-    *out = nullptr;
-    *out_len = 0;
+// q3_engine_generate_text after its argument checks.
+int generate_text(q3_engine* e, const q3_tokenizer* t, const char* prompt, size_t len, char** out,
+                  size_t* out_len) {
     std::vector<uint32_t> ids;
     Q3_TRY_STATUS(encode(*t, chat_template(std::string(prompt ? prompt : "", len)), ids));
     // generator.cpp:42-44 (q3_engine_generate checks it too)
@@ -569,6 +520,72 @@ int q3_engine_generate_text(q3_engine* e, const q3_tokenizer* t, const char* pro
     *out = buf;
     *out_len = s.size();
     return Q3_OK;
+}
+
+}  // namespace
+}  // namespace q3
+
+using namespace q3;
+
+extern "C" {
+
+int q3_tokenizer_load(const char* path, q3_tokenizer** out) {
+    Q3_CHECK(path && out, "q3_tokenizer_load: null argument");
+    *out = nullptr;
+    return guarded("q3_tokenizer_load", [&]() -> int {
+        auto t = std::make_unique<q3_tokenizer>();
+        const int rc = load(path, *t);
+        if (rc == Q3_OK) *out = t.release();
+        return rc;
+    });
+}
+
+int q3_tokenizer_destroy(q3_tokenizer* t) {
+    delete t;
+    return Q3_OK;
+}
+
+int q3_tokenizer_encode(const q3_tokenizer* t, const char* text, size_t len, uint32_t* ids, size_t capacity,
+                        size_t* n_ids) {
+    Q3_CHECK(t && (text || len == 0) && n_ids, "q3_tokenizer_encode: null argument");
+    return guarded("q3_tokenizer_encode", [&]() -> int {
+        std::vector<uint32_t> v;
+        const int rc = encode(*t, std::string(text ? text : "", len), v);
+        if (rc != Q3_OK) return rc;
+        *n_ids = v.size();
+        if (!ids) return Q3_OK;
+        Q3_CHECK(capacity >= v.size(), "q3_tokenizer_encode: ids buffer too small");
+        std::copy(v.begin(), v.end(), ids);
+        return Q3_OK;
+    });
+}
+
+int q3_tokenizer_decode(const q3_tokenizer* t, const uint32_t* ids, size_t n, char* out, size_t capacity,
+                        size_t* needed) {
+    Q3_CHECK(t && (ids || n == 0), "q3_tokenizer_decode: null argument");
+    return guarded("q3_tokenizer_decode", [&]() -> int {
+        std::string s;
+        const int rc = decode(*t, ids, n, s);
+        if (rc != Q3_OK) return rc;
+        return copy_out(s, out, capacity, needed);
+    });
+}
+
+int q3_chat_template(const char* prompt, size_t len, char* out, size_t capacity, size_t* needed) {
+    Q3_CHECK(prompt || len == 0, "q3_chat_template: null argument");
+    return guarded("q3_chat_template",
+                   [&]() -> int {
+                       return copy_out(chat_template(std::string(prompt ? prompt : "", len)), out, capacity, needed);
+                   });
+}
+
+int q3_engine_generate_text(q3_engine* e, const q3_tokenizer* t, const char* prompt, size_t len, char** out,
+                            size_t* out_len) {
+    Q3_CHECK(e && t && (prompt || len == 0) && out && out_len, "q3_engine_generate_text: null argument");
+    *out = nullptr;
+    *out_len = 0;
+    return guarded("q3_engine_generate_text",
+                   [&]() -> int { return generate_text(e, t, prompt, len, out, out_len); });
 }
 
 void q3_string_free(char* s) { std::free(s); }

@@ -173,3 +173,22 @@ def test_encode_decode_buffers_and_errors(tmp_path):
         assert n.value == len(t.tokenize(text))
         assert list(t.tokenize("")) == []
         assert t.decode([]) == ""
+
+
+@pytest.mark.parametrize("where", ["vocab", "added"])
+@pytest.mark.parametrize("bad_id", [-1, 1.5, 2 ** 24, 1e300, "7"])
+def test_hostile_ids_are_rejected(tmp_path, where, bad_id):
+    """Vocabulary and added-token ids must be integers in [0, 2^24): anything
+    else is Q3_ERR_INVALID, never a huge allocation or an undefined cast."""
+    from inference_b200 import Q3Error, Tokenizer
+
+    with open(SYNTH, encoding="utf-8") as f:
+        j = json.load(f)
+    if where == "vocab":
+        word = next(iter(j["model"]["vocab"]))
+        j["model"]["vocab"][word] = bad_id
+    else:
+        j["added_tokens"].append({"id": bad_id, "content": "<|hostile|>", "special": True})
+    (tmp_path / "tokenizer.json").write_text(json.dumps(j), encoding="utf-8")
+    with pytest.raises(Q3Error, match="INVALID"):
+        Tokenizer(str(tmp_path))
