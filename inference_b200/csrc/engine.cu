@@ -436,15 +436,14 @@ int check_device_error(q3_engine* e) {
 
 // Host rope tables exactly as make_rope_cache (rope_cache.hpp:29-41): fp32,
 // inv_freq = 1/pow(theta, 2i/hd), cos/sin(float(p) * inv_freq).
-void rope_tables(size_t max_pos, size_t hd, float theta, std::vector<float>& c, std::vector<float>& s) {
+// c and s hold max_pos * hd / 2 floats each.
+void rope_tables(size_t max_pos, size_t hd, float theta, float* c, float* s) {
     const size_t half = hd / 2;
     std::vector<float> inv(half);
     for (size_t i = 0; i < half; ++i) {
         const float ex = 2.0F * static_cast<float>(i) / static_cast<float>(hd);
         inv[i] = 1.0F / std::pow(theta, ex);
     }
-    c.resize(max_pos * half);
-    s.resize(max_pos * half);
     for (size_t p = 0; p < max_pos; ++p)
         for (size_t i = 0; i < half; ++i) {
             const float ang = static_cast<float>(p) * inv[i];
@@ -575,8 +574,8 @@ int q3_engine_create(const q3_model_config* cfg, int device, int tp_rank, int tp
     if ((rc = dalloc_t(e, &e->page_table, pt.size())) != Q3_OK) return bail(rc);
     if (cudaMemcpy(e->page_table, pt.data(), pt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
         return bail(fail(Q3_ERR_CUDA, "page table upload failed"));
-    std::vector<float> cs, sn;
-    rope_tables(c.capacity, 128, c.theta, cs, sn);
+    std::vector<float> cs(static_cast<size_t>(c.capacity) * 64), sn(cs.size());
+    rope_tables(c.capacity, 128, c.theta, cs.data(), sn.data());
     if ((rc = dalloc_t(e, &e->rope_cos, cs.size())) != Q3_OK) return bail(rc);
     if ((rc = dalloc_t(e, &e->rope_sin, sn.size())) != Q3_OK) return bail(rc);
     if (cudaMemcpy(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -1486,11 +1485,8 @@ int q3_engine_profile_step(q3_engine* e, int klass, double* ms, size_t* launches
 }
 
 int q3_rope_tables(size_t max_pos, size_t head_dim, float theta, float* cos_host, float* sin_host) {
-    Q3_CHECK(cos_host && sin_host && head_dim % 2 == 0, "q3_rope_tables: bad argument");
-    std::vector<float> c, s;
-    rope_tables(max_pos, head_dim, theta, c, s);
-    std::memcpy(cos_host, c.data(), c.size() * 4);
-    std::memcpy(sin_host, s.data(), s.size() * 4);
+    Q3_CHECK(cos_host && sin_host && head_dim % 2 == 0 && head_dim <= 65536, "q3_rope_tables: bad argument");
+    rope_tables(max_pos, head_dim, theta, cos_host, sin_host);
     return Q3_OK;
 }
 
