@@ -194,7 +194,9 @@ class CpuSampler:
     Model::forward calls there."""
 
     def __init__(self, cfg, pos, max_tokens, threads):
-        os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+        # every host thread, whatever the launcher set (torchrun sets 1 per rank);
+        # read by the OpenMP runtime when the library below is loaded
+        os.environ["OMP_NUM_THREADS"] = str(threads)
         from oracle import ModelConfig
 
         mc = ModelConfig.make(cfg.hidden, cfg.inter, cfg.layers, cfg.q_heads, cfg.kv_heads, 128, cfg.vocab,
@@ -227,6 +229,14 @@ class CpuSampler:
         self.m.close()
 
 
+def host_threads():
+    """The CPUs this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def cpu_token_cap(cfg, seconds):
     # KV capacity for a time-bounded sample: generous for small models, which run fastest
     return max(8, int(seconds * (400 if cfg.hidden <= 1024 else 60 if cfg.hidden <= 2560 else 30)))
@@ -237,7 +247,7 @@ def run_reference(a, cfg, prompt_len, capacity, workload):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    threads = os.cpu_count() or 1
+    threads = host_threads()
     mid = prompt_len + (capacity - prompt_len) // 2
     per_step = max(1.0, a.cpu_sample_seconds / 2)
     cs = CpuSampler(cfg, mid, cpu_token_cap(cfg, per_step), threads)
@@ -824,7 +834,7 @@ def main(argv=None):
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        threads = os.cpu_count() or 1
+        threads = host_threads()
         try:
             cs = CpuSampler(cfg, mid, cpu_token_cap(cfg, a.cpu_sample_seconds) + 1, threads)
             cs.sample(0, min_tokens=1)
