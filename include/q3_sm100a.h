@@ -412,6 +412,8 @@ Q3_API int q3_engine_set_comm_timeout(q3_engine* e, double seconds);
  * ---------------------------------------------------------------------- */
 typedef struct q3_batch q3_batch;
 
+/* A batch holds its own KV pages and token histories and uses the engine's
+ * weights, stream and row buffers: destroy it before its engine. */
 Q3_API int q3_batch_create(q3_engine* e, uint32_t max_seqs, uint32_t pool_pages, q3_batch** out);
 Q3_API int q3_batch_destroy(q3_batch* b);
 

@@ -4,6 +4,7 @@ the q3_batch_* C ABI).  The reference decodes one sequence at a time
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -20,6 +21,10 @@ class Batch:
         h = C.c_void_p()
         check(lib().q3_batch_create(engine.h, max_seqs, pool_pages, C.byref(h)))
         self.h = h
+        # Engine.close destroys its live batches before itself (q3_batch_destroy first)
+        if not hasattr(engine, "_batches"):
+            engine._batches = weakref.WeakSet()
+        engine._batches.add(self)
 
     def close(self):
         if getattr(self, "h", None):

@@ -27,8 +27,10 @@ def _ptr(a: np.ndarray) -> int:
 class Engine:
     def __init__(self, cfg: Qwen3Config, capacity: int, device: int = 0, tp_rank: int = 0, tp_size: int = 1,
                  weights: str = "bf16"):
-        """weights: "bf16" (the reference's format) or "fp8" (E4M3 GEMV matrices with a
-        power-of-two scale per row, quantized on the device from the BF16 tensors)."""
+        """weights: "bf16" (the reference's format), "fp8" (E4M3 GEMV matrices with a
+        power-of-two scale per row) or "nvfp4" (E2M1 with an E4M3 scale per 16 columns
+        and a power-of-two scale per row); both quantized on the device from the BF16
+        tensors."""
         if weights not in WEIGHT_FORMATS:
             raise ValueError(f"weights must be one of {sorted(WEIGHT_FORMATS)}")
         self.cfg, self.capacity, self.tp_rank, self.tp_size = cfg, capacity, tp_rank, tp_size
@@ -42,6 +44,9 @@ class Engine:
     # ---- lifecycle
     def close(self):
         if getattr(self, "h", None):
+            # batches decode on this engine's weights and stream: they go first
+            for b in list(getattr(self, "_batches", ())):
+                b.close()
             lib().q3_engine_destroy(self.h)
             self.h = None
 
