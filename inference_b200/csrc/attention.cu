@@ -6,7 +6,7 @@
 // head of its GQA group and round-trips fp32 partials through HBM.  Here:
 //   * grid = (splits, kv_heads, query-head blocks), cluster = (splits, 1, 1):
 //     the splits of one (kv head, block) form a thread-block cluster; one CTA
-//     handles up to four query heads of the GQA group, so K/V cross HBM once;
+//     handles up to eight query heads of the GQA group, so K/V cross HBM once;
 //   * the context's pages are divided evenly over the splits from the device
 //     position at run time, so one launch shape (one CUDA graph) serves every
 //     position;
@@ -14,10 +14,9 @@
 //     ring with 3-D TMA tensor copies (128-byte swizzle: two 64-column boxes
 //     per 64-row tile, from the paged pool or the reference's [capacity, kvh,
 //     128] layout alike), so ldmatrix reads conflict-free rows with no pass
-//     over the tile first;
-//     Pages older than the current position are fetched before
-//     griddepcontrol.wait -- only the page receiving this token's K/V waits
-//     for the QKV kernel;
+//     over the tile first; pages older than the current position are fetched
+//     before griddepcontrol.wait -- only the page receiving this token's K/V
+//     waits for the QKV kernel;
 //   * each consumer warp owns 16 of a page's 64 tokens and does its math on the
 //     tensor cores with the tokens as the 16-row M dimension and the CTA's
 //     query heads (up to 8) as N: S^T = K Q^T, online softmax in fp32 on the
@@ -243,13 +242,15 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(const __grid_constant
     } else {
         // ------------------------------------------------------------ consumers
         // Tensor cores (mma.sync m16n8k16, BF16 -> FP32): warp w owns tokens
-        // 16w .. 16w + 15 of each 64-token page.  S = Q K^T with Q as the A
-        // operand (rows = the CTA's HG query heads, padded to 16 with zeros),
-        // online softmax on the accumulator fragments, then O += P V with P
-        // reused as the A operand, split into BF16 hi + lo parts so the
-        // probabilities keep ~16 bits.  Each warp first XOR-swizzles its own
-        // 16 rows of the K and V tiles in place (16-byte chunk c of row r to
-        // c ^ (r & 7)), so every ldmatrix phase hits 8 distinct bank groups.
+        // 16w .. 16w + 15 of each 64-token page, the M dimension.  S^T = K Q^T
+        // with the warp's key rows as the A operand (ldmatrix) and the CTA's HG
+        // query heads as N (columns past HG are zero), online softmax on the
+        // accumulator fragments, then O^T += V^T P^T with V^T from
+        // ldmatrix.trans and P, split into BF16 hi + lo parts so the
+        // probabilities keep ~16 bits, moved into the B operand by movmatrix.
+        // The tiles arrive 128-byte swizzled by the TMA (16-byte chunk c of row
+        // r at c ^ (r & 7), tile_off), so every ldmatrix phase hits 8 distinct
+        // bank groups.
         const bool fused = a.k_raw != nullptr;
         const bool has_live = fused && live_page >= pb && live_page < pe;
         NormRope nq, nk;

@@ -105,8 +105,11 @@ def test_qk_norm_rope(be, oracle, golden_ops, qh, kvh, pos):
     assert_bf16_close(host(kt), golden_ops[f"qknr_k/{qh}_{kvh}_{pos}"], atol=1e-2)
 
 
+# the last four have few kv heads and at least 16 pages: clusters of 16 splits where the
+# GPU can hold one such cluster per kv head (the per-rank shapes of 4- and 8-way tensor
+# parallelism), else 8
 ATTN_CASES = G.ATTN + [(16, 8, 63), (16, 8, 64), (16, 8, 65), (32, 8, 127), (64, 8, 1000), (8, 8, 5), (16, 16, 200),
-                       (32, 4, 700), (8, 1, 333), (64, 8, 8191)]
+                       (32, 4, 700), (8, 1, 333), (64, 8, 8191), (8, 1, 2047), (8, 2, 4095), (2, 1, 1000), (1, 1, 1500)]
 
 
 @pytest.mark.parametrize("qh,kvh,pos", ATTN_CASES)
@@ -123,7 +126,8 @@ def test_attention_reference_layout(be, oracle, golden_ops, qh, kvh, pos):
         assert_bf16_close(mine, golden_ops[key], rtol=1e-2, atol=2e-3)
 
 
-@pytest.mark.parametrize("qh,kvh,pos", [(16, 8, 0), (16, 8, 100), (32, 8, 4095), (64, 8, 2000), (8, 2, 64)])
+@pytest.mark.parametrize("qh,kvh,pos", [(16, 8, 0), (16, 8, 100), (32, 8, 4095), (64, 8, 2000), (8, 2, 64),
+                                        (4, 1, 3000)])
 def test_attention_paged_matches_flat(be, qh, kvh, pos):
     """The paged layout under a shuffled page table gives the same bits as the
     reference layout: the page table is only an address map."""
